@@ -1,0 +1,92 @@
+// bnn_device.cuh - small device helpers shared by the W1A8 kernels.
+//
+// Everything FP32 here is written with explicit round-to-nearest intrinsics
+// (__fmul_rn/__fadd_rn/__fdiv_rn) so no multiply-add is ever contracted,
+// matching the reference's "-ffp-contract=off, volatile per-op rounding"
+// rule (bnn-accelerator/soft-bnn-accelerator.c:123-140). The library is
+// compiled without fast-math and with -ftz=false, so subnormals survive.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+
+namespace bnn {
+
+constexpr uint32_t kGroup = 128;        // weights per binary16 scale
+constexpr uint32_t kRowBlock = 8;       // output rows per repacked weight block
+constexpr uint32_t kWordsPerGroup = 32; // sliced activation words per group
+constexpr uint32_t kActStride = 36;     // smem words per group (144 B: bank spread)
+
+// binary16 bit pattern -> binary32. cvt.f32.f16 is exact for every binary16
+// value including subnormals and signed zero (HalfToFloat, soft :92-121).
+__device__ __forceinline__ float h2f(uint16_t h) {
+    return __half2float(__ushort_as_half(h));
+}
+
+// d = c + sum_i a.u8[i] * b.s8[i]: unsigned weight-mask bytes times signed
+// activation bytes, exact in int32.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ float load_f32_any(const unsigned char* p) {
+    if ((reinterpret_cast<uintptr_t>(p) & 3u) == 0)
+        return *reinterpret_cast<const float*>(p);
+    uint32_t v = (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) |
+                 ((uint32_t)p[3] << 24);
+    return __uint_as_float(v);
+}
+
+__device__ __forceinline__ void store_f32_any(unsigned char* p, float f) {
+    if ((reinterpret_cast<uintptr_t>(p) & 3u) == 0) {
+        *reinterpret_cast<float*>(p) = f;
+        return;
+    }
+    uint32_t v = __float_as_uint(f);
+    p[0] = (unsigned char)v;
+    p[1] = (unsigned char)(v >> 8);
+    p[2] = (unsigned char)(v >> 16);
+    p[3] = (unsigned char)(v >> 24);
+}
+
+__device__ __forceinline__ void store_i16_any(unsigned char* p, int16_t x) {
+    if ((reinterpret_cast<uintptr_t>(p) & 1u) == 0) {
+        *reinterpret_cast<int16_t*>(p) = x;
+        return;
+    }
+    uint16_t v = (uint16_t)x;
+    p[0] = (unsigned char)v;
+    p[1] = (unsigned char)(v >> 8);
+}
+
+// Smallest positive binary32 subnormal (FLT_TRUE_MIN).
+__device__ __forceinline__ float flt_true_min() { return __uint_as_float(1u); }
+
+// Row scale of the full-row absmax quantiser (QuantizeRow, soft :187-195).
+__device__ __forceinline__ float row_scale_from_absmax(float absmax) {
+    if (absmax == 0.0f)
+        return 1.0f;
+    float s = __fdiv_rn(absmax, 127.0f);
+    return s == 0.0f ? flt_true_min() : s;
+}
+
+// One element of QuantizeRow (soft :197-208): RN division, round half away
+// from zero, clamp to [-127, 127].
+__device__ __forceinline__ int8_t quantize_one(float x, float s) {
+    float r = roundf(__fdiv_rn(x, s));
+    r = fminf(fmaxf(r, -127.0f), 127.0f);
+    return (int8_t)(int)r;
+}
+
+// Pack four activation bytes for one (group, word t, bit slice j): byte i is
+// q[32t + 8i + j] of the group, the activation that meets bit (8i + j) of the
+// group's 32-bit weight word t.
+__device__ __forceinline__ uint32_t pack_slice(const int8_t* qg, uint32_t t, uint32_t j) {
+    const int8_t* b = qg + 32u * t + j;
+    return (uint32_t)(uint8_t)b[0] | ((uint32_t)(uint8_t)b[8] << 8) |
+           ((uint32_t)(uint8_t)b[16] << 16) | ((uint32_t)(uint8_t)b[24] << 24);
+}
+
+}  // namespace bnn

@@ -1,0 +1,57 @@
+// bnn_internal.h - private handle layouts shared by the C-ABI translation units.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "bnn_b200_accel.h"
+
+struct bnn_accel_device {
+    int ordinal;              // CUDA device ordinal
+    cudaStream_t stream;      // every call of this handle runs on it, then syncs
+    size_t matrix_count;
+    size_t buffer_count;
+    // Per-job scratch: sliced int8 activations, group totals, row scales.
+    void* scratch;
+    size_t scratch_bytes;
+    int* d_status;            // prep-kernel verdict (device)
+    int* h_status;            // pinned host mirror
+};
+
+struct bnn_accel_matrix {
+    BNN_Device owner;
+    uint32_t in_features;
+    uint32_t out_features;
+    uint32_t groups;
+    uint4* wbits;             // repacked 8-row blocks
+    uint16_t* scales;         // [N][G] binary16
+};
+
+struct bnn_accel_buffer {
+    BNN_Device owner;
+    size_t bytes;
+    unsigned char* data;      // device memory
+};
+
+namespace bnn {
+
+// Makes `ordinal` current for the lifetime of the guard, restoring the
+// caller's device afterwards.
+class DeviceGuard {
+  public:
+    explicit DeviceGuard(int ordinal) {
+        ok_ = cudaGetDevice(&prev_) == cudaSuccess && cudaSetDevice(ordinal) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (prev_ >= 0)
+            cudaSetDevice(prev_);
+    }
+    bool ok() const { return ok_; }
+
+  private:
+    int prev_ = -1;
+    bool ok_ = false;
+};
+
+}  // namespace bnn

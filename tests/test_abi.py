@@ -1,0 +1,98 @@
+"""The C-ABI boundary, checked without a GPU.
+
+  * libbnn_b200.so loads and exports every function include/bnn_b200_accel.h
+    declares (and the engine/kernel headers' entry points);
+  * struct layouts and enum values of include/bnn_b200_accel.h equal the
+    reference header's (bnn-accelerator/bnn-accelerator.h), so callers
+    compiled against either link against the library unchanged;
+  * without a CUDA device the library refuses to open one (no CPU fallback).
+"""
+import ctypes
+import re
+import shutil
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from conftest import ROOT, gpu_present
+
+LIB = ROOT / "bnn-train-infer_b200" / "lib" / "libbnn_b200.so"
+REF_HEADER_DIR = Path("/root/reference/bnn-accelerator")
+
+PROBE = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include HEADER
+#define S(t) printf(#t " size %zu\n", sizeof(t));
+#define O(t, f) printf(#t "." #f " %zu\n", offsetof(t, f));
+#define E(e) printf(#e " %d\n", (int)(e));
+int main(void) {
+  S(BNN_Caps) O(BNN_Caps, api_version) O(BNN_Caps, max_in_features) O(BNN_Caps, max_out_features)
+  O(BNN_Caps, max_rows) O(BNN_Caps, group_size) O(BNN_Caps, supported_ops)
+  S(BNN_MatrixDesc) O(BNN_MatrixDesc, in_features) O(BNN_MatrixDesc, out_features)
+  O(BNN_MatrixDesc, group_size) O(BNN_MatrixDesc, weight_bits) O(BNN_MatrixDesc, weight_bytes)
+  O(BNN_MatrixDesc, scale_fp16) O(BNN_MatrixDesc, scale_count)
+  S(BNN_BufferView) O(BNN_BufferView, buffer) O(BNN_BufferView, type) O(BNN_BufferView, offset)
+  O(BNN_BufferView, row_stride)
+  S(BNN_Job) O(BNN_Job, operation) O(BNN_Job, matrix) O(BNN_Job, input) O(BNN_Job, output)
+  O(BNN_Job, rows)
+  S(BNN_Status) S(BNN_Operation) S(BNN_Type)
+  E(BNN_API_VERSION) E(BNN_OK) E(BNN_EINVAL) E(BNN_ENOMEM) E(BNN_ENOTSUP) E(BNN_ERANGE)
+  E(BNN_EBUSY) E(BNN_EIO) E(BNN_ETIMEOUT) E(BNN_OP_GEMV) E(BNN_OP_GEMM) E(BNN_OP_DOT_GROUPS)
+  E(BNN_OP_GEMV_F32) E(BNN_OP_GEMM_F32) E(BNN_TYPE_I8) E(BNN_TYPE_F32) E(BNN_TYPE_I16)
+  E(BNN_CAP_GEMV) E(BNN_CAP_GEMM) E(BNN_CAP_DOT_GROUPS) E(BNN_CAP_GEMV_F32) E(BNN_CAP_GEMM_F32)
+  return 0;
+}
+"""
+
+
+def declared_functions(header):
+    text = header.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:[A-Za-z_][\w\s\*]*?)\b((?:BNN|BNND|bnn_b200)_\w+)\s*\(",
+                                 text, flags=re.M)))
+
+
+def test_library_loads_and_exports_declared_symbols():
+    assert LIB.exists(), "build libbnn_b200.so first (make -C bnn-train-infer_b200)"
+    dll = ctypes.CDLL(str(LIB))
+    headers = sorted((ROOT / "include").glob("*.h"))
+    assert headers
+    missing = []
+    for h in headers:
+        for name in declared_functions(h):
+            if not hasattr(dll, name):
+                missing.append(f"{h.name}:{name}")
+    assert not missing, missing
+    accel_funcs = declared_functions(ROOT / "include" / "bnn_b200_accel.h")
+    assert len(accel_funcs) == 11, accel_funcs
+
+
+def _probe(tmp_path, include_dir, header_name):
+    cc = shutil.which("gcc") or "cc"
+    src = tmp_path / f"probe_{header_name}.c"
+    src.write_text(PROBE.replace("HEADER", f'"{header_name}"'))
+    exe = tmp_path / f"probe_{header_name}"
+    subprocess.run([cc, "-std=c11", "-I", str(include_dir), str(src), "-o", str(exe)], check=True)
+    return subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
+
+
+def test_abi_matches_reference_header(tmp_path):
+    if not (REF_HEADER_DIR / "bnn-accelerator.h").exists():
+        pytest.skip("reference header not mounted on this host")
+    ours = _probe(tmp_path, ROOT / "include", "bnn_b200_accel.h")
+    ref = _probe(tmp_path, REF_HEADER_DIR, "bnn-accelerator.h")
+    assert ours == ref
+
+
+def test_no_device_means_no_fallback():
+    if gpu_present():
+        pytest.skip("a GPU is present")
+    from bnn_b200 import accel
+    api = accel.Api()
+    h = ctypes.c_void_p(1)
+    assert api.BNN_DeviceOpen(0, ctypes.byref(h)) == accel.ENOTSUP
+    assert not h.value
+    assert api.status_string(accel.ETIMEOUT) == "device timeout"
+    assert api.status_string(99) == "unknown status"

@@ -1,0 +1,222 @@
+"""Parity of libbnn_b200.so with the reference on a B200 (marked gpu).
+
+Every comparison is bit-exact: DOT_GROUPS is integer, and the FP32 ops
+follow the same per-op rounding as the soft backend, so the bar of the
+reference's own conformance test (memcmp of outputs) applies.
+
+  * the reference's unmodified conformance program
+    (tests/accelerator/test_bnn_accelerator.c), linked against
+    libbnn_b200.so by oracle/Makefile;
+  * the reference golden vectors (RTL regression case) through the API;
+  * the single-op sweep shapes (Qwen3-1.7B linears), GEMV_F32 and
+    DOT_GROUPS, with 2048x151669 chunked like bnn-sw-v2/linear.c:161-216;
+  * multi-row GEMM/GEMM_F32, unaligned views, rejection and recovery.
+"""
+import subprocess
+
+import numpy as np
+import pytest
+
+from bnn_b200 import accel, synth
+
+pytestmark = pytest.mark.gpu
+
+MAX_OUT = 8192
+
+
+def bits_equal(a, b):
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    return a.shape == b.shape and a.tobytes() == b.tobytes()
+
+
+def test_reference_conformance_program(oracle_mod):
+    exe = oracle_mod.ref_tool("b200_conformance")
+    if exe is None:
+        pytest.skip("oracle/_ref/b200_conformance not built (make -C oracle ref-b200)")
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert "successful jobs" in out.stdout
+
+
+def test_golden_rtl_case(b200_device, golden):
+    z = accel.run_op(b200_device, accel.OP_GEMM, golden["bits"], golden["scales"], golden["q_full"])
+    assert bits_equal(z.view(np.uint32), golden["golden_full_i8"])
+    zt = accel.run_op(b200_device, accel.OP_GEMM, golden["bits"][:, :16], golden["scales"][:, :1],
+                      golden["q_tile"])
+    assert bits_equal(zt.view(np.uint32), golden["golden_tile_i8"])
+    yt = accel.run_op(b200_device, accel.OP_GEMM_F32, golden["bits"][:, :16],
+                      golden["scales"][:, :1], golden["x_tile"])
+    assert bits_equal(yt.view(np.uint32), golden["golden_tile_f32"])
+
+
+def chunked_gemv_f32(device, bits, scales, x):
+    """GEMV_F32 over out_features > 8192 the way linear.c does it: one input
+    buffer, chunks of <= max_out_features rows, one read per chunk."""
+    n, kb = bits.shape
+    k = kb * 8
+    mats = [accel.Matrix(device, bits[o:o + MAX_OUT], scales[o:o + MAX_OUT])
+            for o in range(0, n, MAX_OUT)]
+    bi, bo = accel.Buffer(device, k * 4), accel.Buffer(device, min(n, MAX_OUT) * 4)
+    y = np.empty(n, dtype=np.float32)
+    try:
+        bi.write(np.ascontiguousarray(x, dtype=np.float32))
+        for i, m in enumerate(mats):
+            assert device.execute(accel.OP_GEMV_F32, m, bi, bo, rows=1) == accel.OK
+            y[i * MAX_OUT:i * MAX_OUT + m.n] = bo.read(m.n * 4).view(np.float32)
+    finally:
+        bi.free()
+        bo.free()
+        for m in mats:
+            m.destroy()
+    return y
+
+
+@pytest.mark.parametrize("k,n", synth.SWEEP_SHAPES)
+def test_sweep_gemv_f32(b200_device, oracle_mod, k, n):
+    rng = synth.rng_for(1, salt=k * 7 + n)
+    bits, scales = synth.w1_matrix(rng, k, n)
+    x = synth.activations(rng, 1, k)
+    want, _, _ = oracle_mod.gemm_f32(bits, scales, x)
+    got = chunked_gemv_f32(b200_device, bits, scales, x[0])
+    assert bits_equal(got.view(np.uint32), want[0].view(np.uint32))
+
+
+@pytest.mark.parametrize("k,n", synth.SWEEP_SHAPES[:4] + [(2048, 8192)])
+def test_sweep_dot_groups(b200_device, oracle_mod, k, n):
+    rng = synth.rng_for(1, salt=k * 11 + n)
+    bits, scales = synth.w1_matrix(rng, k, n)
+    q, _ = oracle_mod.quantize_rows(synth.activations(rng, 1, k))
+    want = oracle_mod.dot_groups(bits, scales, q)
+    got = accel.run_op(b200_device, accel.OP_DOT_GROUPS, bits, scales, q)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("m", [2, 3, 8, 9, 16, 64, 130, 512])
+def test_gemm_f32_rows(b200_device, oracle_mod, m):
+    rng = synth.rng_for(3, salt=m)
+    k, n = 2048, 320
+    bits, scales = synth.w1_matrix(rng, k, n)
+    x = synth.activations(rng, m, k)
+    want, q, _ = oracle_mod.gemm_f32(bits, scales, x)
+    got = accel.run_op(b200_device, accel.OP_GEMM_F32, bits, scales, x)
+    assert bits_equal(got.view(np.uint32), want.view(np.uint32))
+    z = accel.run_op(b200_device, accel.OP_GEMM, bits, scales, q)
+    assert bits_equal(z.view(np.uint32), oracle_mod.gemm_i8(bits, scales, q).view(np.uint32))
+
+
+@pytest.mark.parametrize("op", [accel.OP_GEMM_F32, accel.OP_GEMM, accel.OP_DOT_GROUPS])
+def test_unaligned_views(b200_device, oracle_mod, op):
+    rng = synth.rng_for(4, salt=op)
+    k, n, m = 384, 17, 3
+    bits, scales = synth.w1_matrix(rng, k, n)
+    mat = accel.Matrix(b200_device, bits, scales)
+    f32 = op == accel.OP_GEMM_F32
+    x = synth.activations(rng, m, k) if f32 else synth.i8_activations(rng, m, k)
+    in_row = x[0].nbytes
+    in_stride, in_off = in_row + 7, 3
+    g = k // 128
+    out_row = n * g * 2 if op == accel.OP_DOT_GROUPS else n * 4
+    out_stride, out_off = out_row + 11, 5
+    raw_in = np.full(in_off + m * in_stride + 9, 0xFF if f32 else 0x80, dtype=np.uint8)
+    for r in range(m):
+        raw_in[in_off + r * in_stride:in_off + r * in_stride + in_row] = x[r].view(np.uint8)
+    sentinel = np.full(out_off + m * out_stride + 13, 0xA5, dtype=np.uint8)
+    bi, bo = accel.Buffer(b200_device, raw_in.nbytes), accel.Buffer(b200_device, sentinel.nbytes)
+    try:
+        bi.write(raw_in)
+        bo.write(sentinel)
+        st = b200_device.execute(op, mat, bi, bo, rows=m, in_offset=in_off, in_stride=in_stride,
+                                 out_offset=out_off, out_stride=out_stride)
+        assert st == accel.OK
+        got = bo.read()
+        if f32:
+            want, _, _ = oracle_mod.gemm_f32(bits, scales, x)
+        elif op == accel.OP_GEMM:
+            want = oracle_mod.gemm_i8(bits, scales, x)
+        else:
+            want = oracle_mod.dot_groups(bits, scales, x)
+        expect = sentinel.copy()
+        for r in range(m):
+            expect[out_off + r * out_stride:out_off + r * out_stride + out_row] = \
+                np.ascontiguousarray(want[r]).view(np.uint8).reshape(-1)
+        assert bits_equal(got, expect)
+        assert bits_equal(bi.read(), raw_in)  # input untouched
+    finally:
+        bi.free()
+        bo.free()
+        mat.destroy()
+
+
+@pytest.mark.parametrize("bad", [np.nan, np.inf, -np.inf])
+def test_nonfinite_rejected_output_untouched_then_recovers(b200_device, oracle_mod, bad):
+    rng = synth.rng_for(5)
+    k, n, m = 384, 17, 3
+    bits, scales = synth.w1_matrix(rng, k, n)
+    mat = accel.Matrix(b200_device, bits, scales)
+    x = synth.activations(rng, m, k)
+    bi, bo = accel.Buffer(b200_device, x.nbytes), accel.Buffer(b200_device, m * n * 4)
+    try:
+        sentinel = np.full(m * n * 4, 0x5A, dtype=np.uint8)
+        bo.write(sentinel)
+        xb = x.copy()
+        xb[m - 1, k - 1] = bad  # last element of the last row
+        bi.write(xb)
+        assert b200_device.execute(accel.OP_GEMM_F32, mat, bi, bo, rows=m) == accel.ERANGE
+        assert bits_equal(bo.read(), sentinel)
+        bi.write(x)
+        assert b200_device.execute(accel.OP_GEMM_F32, mat, bi, bo, rows=m) == accel.OK
+        want, _, _ = oracle_mod.gemm_f32(bits, scales, x)
+        assert bits_equal(bo.read().view(np.float32).reshape(m, n).view(np.uint32),
+                          want.view(np.uint32))
+    finally:
+        bi.free()
+        bo.free()
+        mat.destroy()
+
+
+def test_minus128_rejected_then_recovers(b200_device, oracle_mod):
+    rng = synth.rng_for(6)
+    k, n, m = 384, 3, 3
+    bits, scales = synth.w1_matrix(rng, k, n)
+    mat = accel.Matrix(b200_device, bits, scales)
+    q = synth.i8_activations(rng, m, k)
+    bi, bo = accel.Buffer(b200_device, q.nbytes), accel.Buffer(b200_device, m * n * (k // 128) * 2)
+    try:
+        for pos in (0, 127, 128, 383):
+            sentinel = np.full(bo.nbytes, 0x5A, dtype=np.uint8)
+            bo.write(sentinel)
+            qb = q.copy()
+            qb[1, pos] = -128
+            bi.write(qb)
+            assert b200_device.execute(accel.OP_DOT_GROUPS, mat, bi, bo, rows=m) == accel.ERANGE
+            assert bits_equal(bo.read(), sentinel)
+        bi.write(q)
+        assert b200_device.execute(accel.OP_DOT_GROUPS, mat, bi, bo, rows=m) == accel.OK
+        assert np.array_equal(bo.read().view(np.int16).reshape(m, n, k // 128),
+                              oracle_mod.dot_groups(bits, scales, q))
+    finally:
+        bi.free()
+        bo.free()
+        mat.destroy()
+
+
+def test_extremes_and_special_scales(b200_device, oracle_mod):
+    """|D| = 16256 extremes, subnormal/zero/negative-zero/max binary16 scales,
+    and subnormal activations (scale underflow to FLT_TRUE_MIN)."""
+    rng = synth.rng_for(7)
+    k, n = 384, 17
+    bits, _ = synth.w1_matrix(rng, k, n)
+    pool = np.array([0x3C00, 0xBC00, 0x0001, 0x8001, 0x03FF, 0x0400, 0x0000, 0x8000, 0x7BFF],
+                    dtype=np.uint16)
+    scales = pool[rng.integers(0, pool.size, size=(n, k // 128))]
+    signs = np.unpackbits(bits[0], bitorder="little").astype(np.int8) * 2 - 1
+    q = np.stack([signs * 127, -signs * 127]).astype(np.int8)
+    d = accel.run_op(b200_device, accel.OP_DOT_GROUPS, bits, scales, q)
+    assert np.all(d[0, 0] == 16256) and np.all(d[1, 0] == -16256)
+    assert np.array_equal(d, oracle_mod.dot_groups(bits, scales, q))
+    for mul in (1.0, 2.0 ** -140, 2.0 ** -149, 2.0 ** 120):
+        x = (synth.activations(rng, 3, k) * np.float32(mul)).astype(np.float32)
+        want, _, _ = oracle_mod.gemm_f32(bits, scales, x)
+        got = accel.run_op(b200_device, accel.OP_GEMM_F32, bits, scales, x)
+        assert bits_equal(got.view(np.uint32), want.view(np.uint32))
