@@ -26,5 +26,5 @@ def load() -> ctypes.CDLL:
             raise RuntimeError(
                 f"libbnn_b200.so not found at {path}; build it with "
                 "`make -C bnn-train-infer_b200` (the B200 path has no CPU fallback)")
-        _handle = ctypes.CDLL(str(path), mode=ctypes.RTLD_GLOBAL)
+        _handle = ctypes.CDLL(str(path))
     return _handle

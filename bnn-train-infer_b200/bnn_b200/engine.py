@@ -1,0 +1,139 @@
+"""Python binding of the device-resident engine (include/bnn_b200_engine.h).
+
+Mirrors the reference engine's BNNE_* calls (bnn-sw-v2/bnn-engine.h) with a
+BNND_ prefix. `EngineApi(cdll, prefix)` also binds the reference engine's
+own BNNE_* functions from a library that exports them, which is how the
+tests drive both engines with identical calls.
+"""
+import ctypes
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_uint32, c_uint64, c_void_p
+
+import numpy as np
+
+from . import _lib
+from .accel import Api, Device
+
+OK, EINVAL, ENOMEM, ENOTSUP, ERANGE, EIO, EFORMAT, ECOMPUTE = 0, -1, -2, -3, -4, -5, -6, -7
+TASK_CLASSIFY, TASK_LLM = 1, 2
+
+
+class ModelInfo(ctypes.Structure):
+    _fields_ = [("task", c_int), ("input_size", c_uint32), ("n_classes", c_uint32),
+                ("n_vocab", c_uint32), ("n_ctx_train", c_uint32), ("eos_token", c_int32),
+                ("n_layers", c_uint32), ("hidden", c_uint32), ("heads", c_uint32),
+                ("kv_heads", c_uint32), ("head_dim", c_uint32), ("ffn", c_uint32),
+                ("weight_count", c_uint64)]
+
+
+class ContextParams(ctypes.Structure):
+    _fields_ = [("n_ctx", c_uint32), ("n_batch", c_uint32), ("exact", c_int)]
+
+
+class EngineError(RuntimeError):
+    def __init__(self, status, detail):
+        self.status = status
+        super().__init__(f"status {status}: {detail}")
+
+
+class EngineApi:
+    def __init__(self, cdll=None):
+        self.dll = cdll if cdll is not None else _lib.load()
+        d = self.dll
+        sig = {
+            "BNND_ModelLoad": (c_int, [c_void_p, c_char_p, POINTER(c_void_p)]),
+            "BNND_ModelFree": (None, [c_void_p]),
+            "BNND_ModelGetInfo": (c_int, [c_void_p, POINTER(ModelInfo)]),
+            "BNND_ContextParamsInit": (None, [POINTER(ContextParams)]),
+            "BNND_ContextCreate": (c_int, [c_void_p, POINTER(ContextParams), POINTER(c_void_p)]),
+            "BNND_ContextFree": (None, [c_void_p]),
+            "BNND_Decode": (c_int, [c_void_p, c_void_p, c_uint32, c_void_p]),
+            "BNND_DecodeArgmax": (c_int, [c_void_p, c_void_p, c_uint32, c_void_p]),
+            "BNND_Generate": (c_int, [c_void_p, c_uint32, c_void_p]),
+            "BNND_ContextPos": (c_uint32, [c_void_p]),
+            "BNND_ContextTruncate": (c_int, [c_void_p, c_uint32]),
+            "BNND_Classify": (c_int, [c_void_p, c_void_p, c_uint32, c_void_p]),
+            "BNND_LastError": (c_char_p, []),
+            "BNND_ContextStream": (c_void_p, [c_void_p]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(d, name)
+            fn.restype = res
+            fn.argtypes = args
+            setattr(self, name[5:], fn)
+
+    def last_error(self):
+        return (self.LastError() or b"").decode(errors="replace")
+
+    def check(self, st):
+        if st != OK:
+            raise EngineError(st, self.last_error())
+
+
+class Model:
+    def __init__(self, device: Device, path, api: EngineApi = None):
+        self.api = api or EngineApi(device.api.dll)
+        self.device = device
+        h = c_void_p()
+        self.api.check(self.api.ModelLoad(device.handle, str(path).encode(), ctypes.byref(h)))
+        self.handle = h
+        info = ModelInfo()
+        self.api.check(self.api.ModelGetInfo(h, ctypes.byref(info)))
+        self.info = info
+
+    def free(self):
+        if self.handle:
+            self.api.ModelFree(self.handle)
+            self.handle = None
+
+
+class Context:
+    def __init__(self, model: Model, n_ctx=0, n_batch=1, exact=True):
+        self.model = model
+        self.api = model.api
+        p = ContextParams(n_ctx, n_batch, 1 if exact else 0)
+        h = c_void_p()
+        self.api.check(self.api.ContextCreate(model.handle, ctypes.byref(p), ctypes.byref(h)))
+        self.handle = h
+        self.rows = max(1, n_batch)
+
+    @property
+    def pos(self):
+        return self.api.ContextPos(self.handle)
+
+    def decode(self, tokens, want_logits=True):
+        """tokens int32 [rows][n] (or [n] for one row); returns logits [rows][V] or None."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32).reshape(self.rows, -1))
+        v = self.model.info.n_vocab
+        out = np.empty((self.rows, v), dtype=np.float32) if want_logits else None
+        st = self.api.Decode(self.handle, t.ctypes.data, t.shape[1],
+                             out.ctypes.data if out is not None else None)
+        self.api.check(st)
+        return out
+
+    def decode_argmax(self, tokens):
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32).reshape(self.rows, -1))
+        nxt = np.empty(self.rows, dtype=np.int32)
+        self.api.check(self.api.DecodeArgmax(self.handle, t.ctypes.data, t.shape[1], nxt.ctypes.data))
+        return nxt
+
+    def generate(self, steps):
+        out = np.empty((self.rows, steps), dtype=np.int32)
+        self.api.check(self.api.Generate(self.handle, steps, out.ctypes.data))
+        return out
+
+    def truncate(self, pos):
+        self.api.check(self.api.ContextTruncate(self.handle, pos))
+
+    def classify(self, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty((x.shape[0], self.model.info.n_classes), dtype=np.float32)
+        self.api.check(self.api.Classify(self.handle, x.ctypes.data, x.shape[0], out.ctypes.data))
+        return out
+
+    def stream(self):
+        return self.api.ContextStream(self.handle)
+
+    def free(self):
+        if self.handle:
+            self.api.ContextFree(self.handle)
+            self.handle = None

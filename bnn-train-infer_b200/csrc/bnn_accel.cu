@@ -141,6 +141,10 @@ BNN_Status BNN_DeviceOpen(uint32_t device_index, BNN_Device* out_device) {
     if (!d)
         return BNN_ENOMEM;
     d->ordinal = ordinal;
+    if (cudaDeviceGetAttribute(&d->sm_count, cudaDevAttrMultiProcessorCount, ordinal) != cudaSuccess) {
+        delete d;
+        return BNN_EIO;
+    }
     if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess) {
         delete d;
         return BNN_EIO;
@@ -226,7 +230,8 @@ static BNN_Status bnn_b200_matrix_create_limited(BNN_Device device, const BNN_Ma
     if (!m)
         return BNN_ENOMEM;
     const uint32_t groups = desc->in_features / kGroupSize;
-    const size_t nblocks = (desc->out_features + bnn::kRowBlock - 1) / bnn::kRowBlock;
+    size_t nblocks = (desc->out_features + bnn::kRowBlock - 1) / bnn::kRowBlock;
+    nblocks = (nblocks + bnn::kBlockPad - 1) / bnn::kBlockPad * bnn::kBlockPad;
     const size_t packed_bytes = nblocks * groups * bnn::kRowBlock * 16u;
     uint8_t* raw = nullptr;
     if (cudaMalloc(&m->wbits, packed_bytes) != cudaSuccess ||
@@ -245,7 +250,7 @@ static BNN_Status bnn_b200_matrix_create_limited(BNN_Device device, const BNN_Ma
     if (ok) {
         const size_t chunks = nblocks * groups * bnn::kRowBlock;
         const unsigned grid = (unsigned)std::min<size_t>((chunks + 255) / 256, 148u * 16u);
-        bnn::w1a8_repack_kernel<<<grid, 256, 0, s>>>(raw, desc->out_features, groups, m->wbits);
+        bnn::w1a8_repack_kernel<<<grid, 256, 0, s>>>(raw, desc->out_features, groups, nblocks, m->wbits);
         ok = cudaGetLastError() == cudaSuccess && cudaStreamSynchronize(s) == cudaSuccess;
     }
     cudaFree(raw);
@@ -436,12 +441,7 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
     }
 
     const int mode = job->operation == BNN_OP_DOT_GROUPS ? 0 : 1;
-    const size_t c_smem = bnn::contract_smem_bytes(G, mode);
-    const uint32_t nblocks = (m->out_features + bnn::kRowBlock - 1) / bnn::kRowBlock;
-    if (mode == 0)
-        cudaFuncSetAttribute(bnn::w1a8_contract_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c_smem);
-    else
-        cudaFuncSetAttribute(bnn::w1a8_contract_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c_smem);
+    const bnn::ContractLaunch cl = bnn::plan_contract(device->sm_count, m->out_features, G, M, mode);
     const uint32_t rows_per_launch = 65535u * bnn::kRowsPerCta;
     for (uint32_t r0 = 0; r0 < M; r0 += rows_per_launch) {
         const uint32_t rows = std::min<uint32_t>(M - r0, rows_per_launch);
@@ -457,11 +457,11 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
         ca.m = rows;
         ca.out = job->output.buffer->data + job->output.offset + (size_t)r0 * out_stride;
         ca.out_stride = out_stride;
-        dim3 grid(nblocks, (rows + bnn::kRowsPerCta - 1) / bnn::kRowsPerCta);
-        if (mode == 0)
-            bnn::w1a8_contract_kernel<0><<<grid, bnn::kContractThreads, c_smem, s>>>(ca);
-        else
-            bnn::w1a8_contract_kernel<1><<<grid, bnn::kContractThreads, c_smem, s>>>(ca);
+        ca.residual = nullptr;
+        ca.tiles = cl.tiles;
+        ca.stages = cl.stages;
+        if (bnn::launch_contract(cl, (rows + bnn::kRowsPerCta - 1) / bnn::kRowsPerCta, mode, ca, s) != cudaSuccess)
+            return BNN_EIO;
     }
     if (cudaGetLastError() != cudaSuccess)
         return BNN_EIO;
@@ -510,7 +510,10 @@ BNN_Status bnn_b200_sync(BNN_Device device) {
         cudaGetLastError();
         return BNN_EIO;
     }
-    return *device->h_status ? BNN_ERANGE : BNN_OK;
+    const int st = *device->h_status;
+    if (st & bnn::kStatusTimeout)
+        return BNN_ETIMEOUT;
+    return st ? BNN_ERANGE : BNN_OK;
 }
 
 void* bnn_b200_device_stream(BNN_Device device) {

@@ -9,6 +9,7 @@
 
 struct bnn_accel_device {
     int ordinal;              // CUDA device ordinal
+    int sm_count;             // streaming multiprocessors of that device
     cudaStream_t stream;      // every call of this handle runs on it, then syncs
     size_t matrix_count;
     size_t buffer_count;

@@ -1,0 +1,958 @@
+// engine.cu - device-resident Qwen3 / bnn-mlp engine (BNND_*, include/bnn_b200_engine.h).
+//
+// Load path mirrors the reference's (bnn-sw-v2/engine.c:16-78, qwen3.c:144-274,
+// bnn-mlp.c:62-151): the same GGUF keys and tensor names, the same shape
+// checks and status codes, Q1_0 decoded as bnne_q1_0_read does
+// (linear.c:26-62) and uploaded through the BNN_* matrix path (repacked on
+// the device). Linears that share an input are concatenated by rows
+// (q|k|v, gate|up): every output row is computed independently, so this is
+// bit-identical to separate calls.
+//
+// A decode step (qwen3_step, qwen3.c:396-512) is a fixed kernel sequence over
+// device-resident state, captured once per context as a CUDA graph; the
+// position and input token live in device memory so one graph serves every
+// step. Per layer:
+//   rmsnorm_quant -> W1A8(q|k|v) -> qk_norm_rope(+KV append) -> attention
+//   -> quant -> W1A8(o, x += o) -> rmsnorm_quant -> W1A8(gate|up)
+//   -> swiglu_quant -> W1A8(down, x += d)
+// then rmsnorm_quant -> W1A8(lm_head) -> argmax -> step_end.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "bnn_b200_engine.h"
+#include "bnn_b200_ext.h"
+#include "bnn_internal.h"
+#include "engine_kernels.cuh"
+#include "gguf_reader.h"
+#include "w1a8_kernels.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+BNND_Status fail(BNND_Status st, const char* fmt, ...) {
+    char buf[256];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return st;
+}
+
+BNND_Status from_accel(BNN_Status st, const char* what) {
+    if (st == BNN_OK)
+        return BNND_OK;
+    BNND_Status r = BNND_ECOMPUTE;
+    if (st == BNN_ENOMEM) r = BNND_ENOMEM;
+    else if (st == BNN_ENOTSUP) r = BNND_ENOTSUP;
+    else if (st == BNN_ERANGE) r = BNND_ERANGE;
+    else if (st == BNN_EIO || st == BNN_ETIMEOUT) r = BNND_EIO;
+    return fail(r, "%s: %s", what, BNN_StatusString(st));
+}
+
+#define CUDA_OR(expr, status)                                                              \
+    do {                                                                                   \
+        cudaError_t e_ = (expr);                                                           \
+        if (e_ != cudaSuccess) {                                                           \
+            cudaGetLastError();                                                            \
+            return fail(status, "%s: %s", #expr, cudaGetErrorString(e_));                  \
+        }                                                                                  \
+    } while (0)
+
+// Device allocation owned by a model or context.
+struct DevMem {
+    void* p = nullptr;
+    ~DevMem() {
+        if (p)
+            cudaFree(p);
+    }
+    template <typename T>
+    T* as() const { return static_cast<T*>(p); }
+};
+
+BNND_Status dev_alloc(DevMem& m, size_t bytes) {
+    if (bytes == 0)
+        bytes = 16;
+    if (cudaMalloc(&m.p, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        m.p = nullptr;
+        return fail(BNND_ENOMEM, "device allocation of %zu bytes failed", bytes);
+    }
+    return BNND_OK;
+}
+
+float half_bits_to_float(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16, mant = h & 0x3ffu;
+    int exp = (h >> 10) & 0x1f;
+    uint32_t bits;
+    if (exp == 0x1f) {
+        bits = sign | 0x7f800000u | (mant << 13);
+    } else if (exp == 0) {
+        if (mant == 0) {
+            bits = sign;
+        } else {
+            int e = 1;
+            while ((mant & 0x400u) == 0) {
+                mant <<= 1;
+                --e;
+            }
+            bits = sign | ((uint32_t)(e + 112) << 23) | ((mant & 0x3ffu) << 13);
+        }
+    } else {
+        bits = sign | ((uint32_t)(exp + 112) << 23) | (mant << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+// A W1 linear on the device: matrix handle plus its launch plan.
+struct Linear {
+    BNN_Matrix m = nullptr;
+    uint32_t in = 0, out = 0;
+    ~Linear() { BNN_MatrixDestroy(m); }
+};
+
+// Host staging for one (possibly row-concatenated) W1 matrix.
+struct HostW1 {
+    uint32_t in = 0, out = 0;
+    std::vector<uint8_t> bits;
+    std::vector<uint16_t> scales;
+};
+
+BNND_Status read_q1_0(const bnn::GgufFile& g, const std::string& name, uint32_t in, uint32_t out,
+                      HostW1* dst) {
+    const bnn::GgufTensor* t = g.tensor(name);
+    if (!t || t->type != 41 || t->dims.size() != 2 || t->dims[0] != in || t->dims[1] != out ||
+        in % 128 != 0)
+        return fail(BNND_EFORMAT, "unexpected Q1_0 tensor '%s' shape or type", name.c_str());
+    if (dst->bits.empty())
+        dst->in = in;
+    if (dst->in != in)
+        return fail(BNND_EFORMAT, "tensor '%s' input width differs", name.c_str());
+    const size_t groups = in / 128, row_bytes = in / 8;
+    const size_t r0 = dst->out;
+    dst->out += out;
+    dst->bits.resize((size_t)dst->out * row_bytes);
+    dst->scales.resize((size_t)dst->out * groups);
+    for (size_t o = 0; o < out; ++o) {
+        for (size_t grp = 0; grp < groups; ++grp) {
+            const uint8_t* blk = t->data + (o * groups + grp) * 18;
+            const uint16_t sc = (uint16_t)(blk[0] | (blk[1] << 8));
+            if (!std::isfinite(half_bits_to_float(sc)))
+                return fail(BNND_EFORMAT, "Q1_0 scale in '%s' is not finite", name.c_str());
+            dst->scales[(r0 + o) * groups + grp] = sc;
+            std::memcpy(&dst->bits[(r0 + o) * row_bytes + grp * 16], blk + 2, 16);
+        }
+    }
+    return BNND_OK;
+}
+
+BNND_Status upload_w1(BNN_Device dev, const HostW1& h, Linear* l) {
+    BNN_MatrixDesc d;
+    d.in_features = h.in;
+    d.out_features = h.out;
+    d.group_size = 128;
+    d.weight_bits = h.bits.data();
+    d.weight_bytes = h.bits.size();
+    d.scale_fp16 = h.scales.data();
+    d.scale_count = h.scales.size();
+    l->in = h.in;
+    l->out = h.out;
+    return from_accel(bnn_b200_matrix_create_unbounded(dev, &d, &l->m), "matrix upload");
+}
+
+BNND_Status read_f32(const bnn::GgufFile& g, const std::string& name, size_t count, DevMem* dst,
+                     std::vector<float>* host = nullptr) {
+    const bnn::GgufTensor* t = g.tensor(name);
+    if (!t || (t->type != 0 && t->type != 1))
+        return fail(BNND_EFORMAT, "missing or invalid F32/F16 tensor '%s'", name.c_str());
+    size_t n = 1;
+    for (uint64_t d : t->dims)
+        n *= (size_t)d;
+    if (n != count)
+        return fail(BNND_EFORMAT, "tensor '%s' has %zu elements, expected %zu", name.c_str(), n, count);
+    std::vector<float> v(n);
+    for (size_t i = 0; i < n; ++i) {
+        if (t->type == 0) {
+            std::memcpy(&v[i], t->data + 4 * i, 4);
+        } else {
+            uint16_t h = (uint16_t)(t->data[2 * i] | (t->data[2 * i + 1] << 8));
+            v[i] = half_bits_to_float(h);
+        }
+        if (!std::isfinite(v[i]))
+            return fail(BNND_EFORMAT, "non-finite value in tensor '%s'", name.c_str());
+    }
+    BNND_Status st = dev_alloc(*dst, n * 4);
+    if (st != BNND_OK)
+        return st;
+    CUDA_OR(cudaMemcpy(dst->p, v.data(), n * 4, cudaMemcpyHostToDevice), BNND_EIO);
+    if (host)
+        *host = std::move(v);
+    return BNND_OK;
+}
+
+struct QwenLayer {
+    Linear qkv, o, gu, down;
+    DevMem attn_norm, ffn_norm, q_norm, k_norm;
+};
+
+struct MlpLayer {
+    Linear w;
+    DevMem post_scale, post_bias;
+    int relu = 0;
+};
+
+}  // namespace
+
+struct bnnd_model {
+    BNN_Device dev = nullptr;
+    BNND_ModelInfo info{};
+    // qwen3
+    float eps = 0, rope_base = 0, rope_freq_scale = 1, rope_mscale = 1;
+    int32_t rope_corr0 = 0, rope_corr1 = 0;
+    int rope_yarn = 0;
+    std::vector<std::unique_ptr<QwenLayer>> layers;
+    Linear lm_head;
+    DevMem out_norm;
+    // bnn-mlp
+    std::vector<std::unique_ptr<MlpLayer>> mlp;
+    uint32_t mlp_max_dim = 0;
+};
+
+struct bnnd_context {
+    BNND_Model model = nullptr;
+    BNND_ContextParams params{};
+    uint32_t rows = 1, n_ctx = 0, pos = 0;
+    cudaStream_t stream = nullptr;
+    DevMem x, act, totals, rscale, qkv, y, gu, logits, kcache, vcache, rope_cos, rope_sin;
+    DevMem pos_d, tok_in, tok_next, tok_seq, hist, hist_count, status;
+    DevMem mlp_a, mlp_b;
+    size_t tok_seq_cap = 0;
+    uint32_t hist_cap = 0;
+    bnn::ContractLaunch plan_qkv{}, plan_o{}, plan_gu{}, plan_down{}, plan_head{};
+    std::vector<bnn::ContractLaunch> plan_mlp;
+    cudaGraphExec_t graph_logits = nullptr, graph_prefill = nullptr;
+    int* h_status = nullptr;
+    int32_t* h_tokens = nullptr;
+    bool have_logits = false;
+
+    ~bnnd_context() {
+        if (graph_logits)
+            cudaGraphExecDestroy(graph_logits);
+        if (graph_prefill)
+            cudaGraphExecDestroy(graph_prefill);
+        if (h_status)
+            cudaFreeHost(h_status);
+        if (h_tokens)
+            cudaFreeHost(h_tokens);
+    }
+};
+
+namespace {
+
+// qwen3_init_rope_params (qwen3.c:116-142): same formulas, same types.
+BNND_Status rope_params(const bnn::GgufFile& g, bnnd_model* m) {
+    float factor = 0.0f;
+    g.get_f32("qwen3.rope.scaling.factor", &factor);
+    if (factor <= 0.0f)
+        factor = 1.0f;
+    std::string type;
+    g.get_str("qwen3.rope.scaling.type", &type);
+    uint64_t original = 0;
+    g.get_u64("qwen3.rope.scaling.original_context_length", &original);
+    if (original == 0)
+        original = m->info.n_ctx_train;
+    const float freq_scale = 1.0f / factor;
+    const int yarn = type == "yarn";
+    int32_t corr0 = 0, corr1 = (int32_t)(m->info.head_dim - 1);
+    float mscale = 1.0f;
+    if (yarn && original) {
+        const double base = m->rope_base, orig = (double)original, pi = 3.14159265358979323846;
+        const double start = std::floor((double)m->info.head_dim * std::log(orig / (32.0 * 2.0 * pi)) /
+                                        (2.0 * std::log(base)));
+        const double end = std::ceil((double)m->info.head_dim * std::log(orig / (2.0 * pi)) /
+                                     (2.0 * std::log(base)));
+        auto clamp = [&](double v) {
+            const int32_t hi = (int32_t)m->info.head_dim - 1;
+            if (v <= 0.0) return (int32_t)0;
+            if (v >= (double)hi) return hi;
+            return (int32_t)v;
+        };
+        corr0 = clamp(start);
+        corr1 = clamp(end);
+        mscale = 1.0f + 0.1f * logf(1.0f / freq_scale);
+    }
+    if (!(freq_scale > 0.0f) || !std::isfinite(mscale))
+        return fail(BNND_EFORMAT, "invalid Qwen3 rope scaling");
+    m->rope_freq_scale = freq_scale;
+    m->rope_mscale = mscale;
+    m->rope_corr0 = corr0;
+    m->rope_corr1 = corr1;
+    m->rope_yarn = yarn;
+    return BNND_OK;
+}
+
+BNND_Status load_qwen3(const bnn::GgufFile& g, bnnd_model* m) {
+    uint64_t L = 0, C = 0, FF = 0, H = 0, Hk = 0, kl = 0, vl = 0, ctx = 0;
+    g.get_u64("qwen3.block_count", &L);
+    g.get_u64("qwen3.embedding_length", &C);
+    g.get_u64("qwen3.feed_forward_length", &FF);
+    g.get_u64("qwen3.attention.head_count", &H);
+    g.get_u64("qwen3.attention.head_count_kv", &Hk);
+    g.get_u64("qwen3.attention.key_length", &kl);
+    g.get_u64("qwen3.attention.value_length", &vl);
+    g.get_u64("qwen3.context_length", &ctx);
+    float eps = 0.0f, base = 0.0f;
+    g.get_f32("qwen3.attention.layer_norm_rms_epsilon", &eps);
+    g.get_f32("qwen3.rope.freq_base", &base);
+    const bnn::GgufTensor* emb = g.tensor("token_embd.weight");
+    if (!emb || emb->type != 41 || emb->dims.size() != 2)
+        return fail(BNND_EFORMAT, "missing token_embd.weight");
+    // Same admissible ranges as qwen3_load (qwen3.c:155-189).
+    if (L == 0 || L > 128 || C == 0 || C > UINT32_MAX || FF == 0 || FF > UINT32_MAX || H == 0 ||
+        H > 256 || Hk == 0 || Hk > 256 || kl == 0 || kl > UINT32_MAX || kl != vl || ctx == 0 ||
+        ctx > UINT32_MAX || eps <= 0.0f || base <= 0.0f || emb->dims[0] != C || emb->dims[1] == 0 ||
+        emb->dims[1] > (1u << 20))
+        return fail(BNND_EFORMAT, "unsupported Qwen3 dimensions");
+    const uint32_t HD = (uint32_t)kl, V = (uint32_t)emb->dims[1];
+    if (HD > C || H * HD != C || H % Hk != 0 || C % 128 != 0 || FF % 128 != 0 || HD % 2 != 0)
+        return fail(BNND_EFORMAT, "inconsistent Qwen3 dimensions");
+    const uint32_t KV = (uint32_t)(Hk * HD);
+    if (KV % 128 != 0)
+        return fail(BNND_EFORMAT, "Qwen3 KV width is not group aligned");
+    if (HD > 1024)
+        return fail(BNND_ENOTSUP, "head_dim above 1024 is not supported");
+    BNND_ModelInfo& info = m->info;
+    info.task = BNND_TASK_LLM;
+    info.n_layers = (uint32_t)L;
+    info.hidden = (uint32_t)C;
+    info.ffn = (uint32_t)FF;
+    info.heads = (uint32_t)H;
+    info.kv_heads = (uint32_t)Hk;
+    info.head_dim = HD;
+    info.n_vocab = V;
+    info.n_ctx_train = (uint32_t)ctx;
+    uint64_t eos = 0;
+    info.eos_token = g.get_u64("tokenizer.ggml.eos_token_id", &eos) ? (int32_t)eos : -1;
+    m->eps = eps;
+    m->rope_base = base;
+    BNND_Status st = rope_params(g, m);
+    if (st != BNND_OK)
+        return st;
+    st = read_f32(g, "output_norm.weight", C, &m->out_norm);
+    if (st != BNND_OK)
+        return st;
+    {
+        HostW1 head;
+        st = read_q1_0(g, "token_embd.weight", (uint32_t)C, V, &head);
+        if (st == BNND_OK)
+            st = upload_w1(m->dev, head, &m->lm_head);
+        if (st != BNND_OK)
+            return st;
+    }
+    uint64_t weights = (uint64_t)C * V;
+    for (uint32_t l = 0; l < L; ++l) {
+        auto layer = std::make_unique<QwenLayer>();
+        const std::string p = "blk." + std::to_string(l) + ".";
+        if ((st = read_f32(g, p + "attn_norm.weight", C, &layer->attn_norm)) != BNND_OK ||
+            (st = read_f32(g, p + "ffn_norm.weight", C, &layer->ffn_norm)) != BNND_OK ||
+            (st = read_f32(g, p + "attn_q_norm.weight", HD, &layer->q_norm)) != BNND_OK ||
+            (st = read_f32(g, p + "attn_k_norm.weight", HD, &layer->k_norm)) != BNND_OK)
+            return st;
+        HostW1 qkv, o, gu, down;
+        if ((st = read_q1_0(g, p + "attn_q.weight", C, C, &qkv)) != BNND_OK ||
+            (st = read_q1_0(g, p + "attn_k.weight", C, KV, &qkv)) != BNND_OK ||
+            (st = read_q1_0(g, p + "attn_v.weight", C, KV, &qkv)) != BNND_OK ||
+            (st = read_q1_0(g, p + "attn_output.weight", C, C, &o)) != BNND_OK ||
+            (st = read_q1_0(g, p + "ffn_gate.weight", C, FF, &gu)) != BNND_OK ||
+            (st = read_q1_0(g, p + "ffn_up.weight", C, FF, &gu)) != BNND_OK ||
+            (st = read_q1_0(g, p + "ffn_down.weight", FF, C, &down)) != BNND_OK)
+            return st;
+        if ((st = upload_w1(m->dev, qkv, &layer->qkv)) != BNND_OK ||
+            (st = upload_w1(m->dev, o, &layer->o)) != BNND_OK ||
+            (st = upload_w1(m->dev, gu, &layer->gu)) != BNND_OK ||
+            (st = upload_w1(m->dev, down, &layer->down)) != BNND_OK)
+            return st;
+        weights += (uint64_t)C * (C + 2 * KV) + (uint64_t)C * C + 3ull * C * FF;
+        m->layers.push_back(std::move(layer));
+    }
+    info.weight_count = weights;
+    return BNND_OK;
+}
+
+BNND_Status load_mlp(const bnn::GgufFile& g, bnnd_model* m) {
+    uint64_t blocks = 0, in = 0, classes = 0, pixels = 0;
+    float stdv = 1.0f;
+    g.get_u64("bnn-mlp.block_count", &blocks);
+    g.get_u64("bnn-mlp.input_features", &in);
+    g.get_u64("bnn-mlp.class_count", &classes);
+    g.get_u64("bnn-mlp.input_pixels", &pixels);
+    if (!g.get_f32("bnn-mlp.input_std", &stdv))
+        stdv = 0.0f;
+    // Same checks as bnn_mlp_load (bnn-mlp.c:62-70).
+    if (blocks == 0 || blocks > 64 || in == 0 || in > UINT32_MAX || in % 128 != 0 || classes == 0 ||
+        classes > UINT32_MAX || (pixels && pixels > in) || !(stdv > 0.0f))
+        return fail(BNND_EFORMAT, "unsupported bnn-mlp metadata");
+    uint32_t expected = (uint32_t)in, max_dim = (uint32_t)in;
+    uint64_t weights = 0;
+    for (uint32_t i = 0; i < blocks; ++i) {
+        auto layer = std::make_unique<MlpLayer>();
+        const std::string p = "blk." + std::to_string(i) + ".";
+        const bnn::GgufTensor* t = g.tensor(p + "weight");
+        if (!t || t->dims.size() != 2 || t->dims[0] == 0 || t->dims[1] == 0 || t->dims[0] > UINT32_MAX ||
+            t->dims[1] > UINT32_MAX)
+            return fail(BNND_EFORMAT, "missing or invalid Q1_0 tensor '%sweight'", p.c_str());
+        const uint32_t lin = (uint32_t)t->dims[0], lout = (uint32_t)t->dims[1];
+        if (lin != expected)
+            return fail(BNND_EFORMAT, "layer %u input width %u does not match previous output %u", i, lin,
+                        expected);
+        HostW1 w;
+        BNND_Status st = read_q1_0(g, p + "weight", lin, lout, &w);
+        if (st == BNND_OK)
+            st = upload_w1(m->dev, w, &layer->w);
+        if (st == BNND_OK)
+            st = read_f32(g, p + "post_scale", lout, &layer->post_scale);
+        if (st == BNND_OK)
+            st = read_f32(g, p + "post_bias", lout, &layer->post_bias);
+        if (st != BNND_OK)
+            return st;
+        std::string act;
+        if (!g.get_str("bnn-mlp.block." + std::to_string(i) + ".activation", &act) || act.empty())
+            layer->relu = i + 1 < blocks;
+        else if (act == "relu")
+            layer->relu = 1;
+        else if (act == "none")
+            layer->relu = 0;
+        else
+            return fail(BNND_EFORMAT, "invalid activation for bnn-mlp block %u", i);
+        max_dim = std::max(max_dim, lout);
+        expected = lout;
+        weights += (uint64_t)lin * lout;
+        m->mlp.push_back(std::move(layer));
+    }
+    if (expected != classes)
+        return fail(BNND_EFORMAT, "last bnn-mlp layer width %u does not match class_count %u", expected,
+                    (uint32_t)classes);
+    m->info.task = BNND_TASK_CLASSIFY;
+    m->info.input_size = (uint32_t)in;
+    m->info.n_classes = (uint32_t)classes;
+    m->info.eos_token = -1;
+    m->info.weight_count = weights;
+    m->mlp_max_dim = max_dim;
+    return BNND_OK;
+}
+
+// qwen3_init_rope_tables (qwen3.c:298-319), computed on the host with the
+// same libm calls so the tables are bit-identical.
+void rope_tables(const bnnd_model* m, uint32_t n_ctx, std::vector<float>* cs, std::vector<float>* sn) {
+    const uint32_t hd = m->info.head_dim, half = hd / 2;
+    cs->resize((size_t)n_ctx * half);
+    sn->resize((size_t)n_ctx * half);
+    for (uint32_t pos = 0; pos < n_ctx; ++pos) {
+        for (uint32_t j = 0; j < half; ++j) {
+            const float theta_extrap = (float)pos * powf(m->rope_base, -2.0f * (float)j / (float)hd);
+            float theta = m->rope_freq_scale * theta_extrap;
+            if (m->rope_yarn) {
+                const float span = (float)(m->rope_corr1 - m->rope_corr0);
+                const float denom = span > 0.001f ? span : 0.001f;
+                const float y = ((float)j - (float)m->rope_corr0) / denom;
+                const float ramp = 1.0f - fminf(1.0f, fmaxf(0.0f, y));
+                theta = (m->rope_freq_scale * theta_extrap) * (1.0f - ramp) + theta_extrap * ramp;
+            }
+            (*cs)[(size_t)pos * half + j] = cosf(theta) * m->rope_mscale;
+            (*sn)[(size_t)pos * half + j] = sinf(theta) * m->rope_mscale;
+        }
+    }
+}
+
+cudaError_t launch_linear(const bnn::ContractLaunch& cl, const Linear& l, const uint32_t* act,
+                          const int32_t* totals, const float* rs, uint32_t rows, float* out,
+                          const float* residual, int* status, cudaStream_t s) {
+    bnn::ContractArgs a;
+    a.wbits = l.m->wbits;
+    a.scales = l.m->scales;
+    a.act = act;
+    a.totals = totals;
+    a.row_scale = rs;
+    a.status = status;
+    a.n = l.out;
+    a.groups = l.in / 128;
+    a.m = rows;
+    a.out = reinterpret_cast<unsigned char*>(out);
+    a.out_stride = (size_t)l.out * 4u;
+    a.residual = residual;
+    a.tiles = cl.tiles;
+    a.stages = cl.stages;
+    return bnn::launch_contract(cl, (rows + bnn::kRowsPerCta - 1) / bnn::kRowsPerCta, 1, a, s);
+}
+
+bnn::eng::QuantOut qout(bnnd_context* c, uint32_t k) {
+    bnn::eng::QuantOut q;
+    q.act = c->act.as<uint32_t>();
+    q.totals = c->totals.as<int32_t>();
+    q.row_scale = c->rscale.as<float>();
+    q.act_groups = k / 128;
+    return q;
+}
+
+// Enqueues one decode step for every row (tokens already in tok_in).
+cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
+    const bnnd_model* m = c->model;
+    const BNND_ModelInfo& in = m->info;
+    const uint32_t C = in.hidden, F = in.ffn, HD = in.head_dim, KV = in.kv_heads * HD, R = c->rows;
+    cudaStream_t s = c->stream;
+    int* status = c->status.as<int>();
+    const int exact = c->params.exact;
+    const size_t norm_smem = (size_t)C * 9u;
+    bnn::eng::embed_kernel<<<R, 256, 0, s>>>(c->tok_in.as<int32_t>(), m->lm_head.m->wbits,
+                                             m->lm_head.m->scales, C, c->x.as<float>());
+    for (uint32_t l = 0; l < in.n_layers; ++l) {
+        const QwenLayer& L = *m->layers[l];
+        bnn::eng::rmsnorm_quant_kernel<<<R, 512, norm_smem, s>>>(c->x.as<float>(), L.attn_norm.as<float>(),
+                                                                 m->eps, C, qout(c, C), status, exact);
+        launch_linear(c->plan_qkv, L.qkv, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(),
+                      R, c->qkv.as<float>(), nullptr, status, s);
+        bnn::eng::QkArgs qa;
+        qa.qkv = c->qkv.as<float>();
+        qa.q_norm = L.q_norm.as<float>();
+        qa.k_norm = L.k_norm.as<float>();
+        qa.rope_cos = c->rope_cos.as<float>();
+        qa.rope_sin = c->rope_sin.as<float>();
+        qa.pos = c->pos_d.as<uint32_t>();
+        const size_t layer_cache = (size_t)R * c->n_ctx * KV;
+        qa.kcache = c->kcache.as<float>() + (size_t)l * layer_cache;
+        qa.vcache = c->vcache.as<float>() + (size_t)l * layer_cache;
+        qa.c = C;
+        qa.kv = KV;
+        qa.hd = HD;
+        qa.heads = in.heads;
+        qa.kv_heads = in.kv_heads;
+        qa.n_ctx = c->n_ctx;
+        qa.eps = m->eps;
+        qa.exact = exact;
+        qa.status = status;
+        bnn::eng::qk_norm_rope_kernel<<<dim3(in.heads + in.kv_heads, R), HD, HD * 8, s>>>(qa);
+        bnn::eng::AttnArgs aa;
+        aa.qkv = c->qkv.as<float>();
+        aa.kcache = qa.kcache;
+        aa.vcache = qa.vcache;
+        aa.pos = qa.pos;
+        aa.y = c->y.as<float>();
+        aa.c = C;
+        aa.kv = KV;
+        aa.hd = HD;
+        aa.heads = in.heads;
+        aa.kv_heads = in.kv_heads;
+        aa.n_ctx = c->n_ctx;
+        aa.scale = 1.0f / sqrtf((float)HD);
+        aa.exact = exact;
+        aa.status = status;
+        bnn::eng::attention_kernel<<<dim3(in.heads, R), 256, (size_t)(HD + c->n_ctx) * 4, s>>>(aa);
+        bnn::eng::quant_kernel<<<R, 512, (size_t)C * 5u, s>>>(c->y.as<float>(), C, qout(c, C));
+        launch_linear(c->plan_o, L.o, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(), R,
+                      c->x.as<float>(), c->x.as<float>(), status, s);
+        bnn::eng::rmsnorm_quant_kernel<<<R, 512, norm_smem, s>>>(c->x.as<float>(), L.ffn_norm.as<float>(),
+                                                                 m->eps, C, qout(c, C), status, exact);
+        launch_linear(c->plan_gu, L.gu, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(), R,
+                      c->gu.as<float>(), nullptr, status, s);
+        bnn::eng::swiglu_quant_kernel<<<R, 512, (size_t)F * 5u, s>>>(c->gu.as<float>(), F, qout(c, F));
+        launch_linear(c->plan_down, L.down, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(),
+                      R, c->x.as<float>(), c->x.as<float>(), status, s);
+    }
+    if (with_logits) {
+        bnn::eng::rmsnorm_quant_kernel<<<R, 512, norm_smem, s>>>(c->x.as<float>(), m->out_norm.as<float>(),
+                                                                 m->eps, C, qout(c, C), status, exact);
+        launch_linear(c->plan_head, m->lm_head, c->act.as<uint32_t>(), c->totals.as<int32_t>(),
+                      c->rscale.as<float>(), R, c->logits.as<float>(), nullptr, status, s);
+        bnn::eng::argmax_kernel<<<R, 1024, 0, s>>>(c->logits.as<float>(), in.n_vocab, c->tok_next.as<int32_t>(),
+                                                  status);
+    }
+    bnn::eng::step_end_kernel<<<1, 32 * ((R + 31) / 32), 0, s>>>(
+        R, c->pos_d.as<uint32_t>(), c->tok_in.as<int32_t>(), c->tok_next.as<int32_t>(), c->hist.as<int32_t>(),
+        c->hist_count.as<uint32_t>(), c->hist_cap, with_logits ? 1 : 0);
+    return cudaGetLastError();
+}
+
+BNND_Status capture_step(bnnd_context* c, bool with_logits, cudaGraphExec_t* out) {
+    cudaGraph_t graph = nullptr;
+    CUDA_OR(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), BNND_EIO);
+    cudaError_t e = enqueue_step(c, with_logits);
+    cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
+    if (e != cudaSuccess || e2 != cudaSuccess) {
+        if (graph)
+            cudaGraphDestroy(graph);
+        cudaGetLastError();
+        return fail(BNND_EIO, "decode step capture failed: %s",
+                    cudaGetErrorString(e != cudaSuccess ? e : e2));
+    }
+    e = cudaGraphInstantiate(out, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(BNND_EIO, "decode graph instantiation failed: %s", cudaGetErrorString(e));
+    }
+    return BNND_OK;
+}
+
+BNND_Status create_llm_context(bnnd_context* c) {
+    const bnnd_model* m = c->model;
+    const BNND_ModelInfo& in = m->info;
+    const uint32_t C = in.hidden, F = in.ffn, KV = in.kv_heads * in.head_dim, R = c->rows;
+    const uint32_t gmax = std::max(C, F) / 128;
+    BNND_Status st;
+    const size_t cache = (size_t)in.n_layers * R * c->n_ctx * KV * 4u;
+    if ((st = dev_alloc(c->x, (size_t)R * C * 4)) || (st = dev_alloc(c->act, (size_t)R * gmax * 128)) ||
+        (st = dev_alloc(c->totals, (size_t)R * gmax * 4)) || (st = dev_alloc(c->rscale, (size_t)R * 4)) ||
+        (st = dev_alloc(c->qkv, (size_t)R * (C + 2 * KV) * 4)) || (st = dev_alloc(c->y, (size_t)R * C * 4)) ||
+        (st = dev_alloc(c->gu, (size_t)R * 2 * F * 4)) ||
+        (st = dev_alloc(c->logits, (size_t)R * in.n_vocab * 4)) || (st = dev_alloc(c->kcache, cache)) ||
+        (st = dev_alloc(c->vcache, cache)) || (st = dev_alloc(c->pos_d, (size_t)R * 4)) ||
+        (st = dev_alloc(c->tok_in, (size_t)R * 4)) || (st = dev_alloc(c->tok_next, (size_t)R * 4)) ||
+        (st = dev_alloc(c->hist_count, 4)) || (st = dev_alloc(c->status, 4)))
+        return st;
+    c->hist_cap = c->n_ctx;
+    if ((st = dev_alloc(c->hist, (size_t)c->hist_cap * R * 4)))
+        return st;
+    std::vector<float> cs, sn;
+    rope_tables(m, c->n_ctx, &cs, &sn);
+    if ((st = dev_alloc(c->rope_cos, cs.size() * 4)) || (st = dev_alloc(c->rope_sin, sn.size() * 4)))
+        return st;
+    CUDA_OR(cudaMemcpy(c->rope_cos.p, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), BNND_EIO);
+    CUDA_OR(cudaMemcpy(c->rope_sin.p, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), BNND_EIO);
+    CUDA_OR(cudaMemset(c->pos_d.p, 0, (size_t)R * 4), BNND_EIO);
+    CUDA_OR(cudaMemset(c->tok_in.p, 0, (size_t)R * 4), BNND_EIO);
+    CUDA_OR(cudaMemset(c->hist_count.p, 0, 4), BNND_EIO);
+    CUDA_OR(cudaMemset(c->status.p, 0, 4), BNND_EIO);
+    const int sms = m->dev->sm_count;
+    c->plan_qkv = bnn::plan_contract(sms, C + 2 * KV, C / 128, R, 1);
+    c->plan_o = bnn::plan_contract(sms, C, C / 128, R, 1);
+    c->plan_gu = bnn::plan_contract(sms, 2 * F, C / 128, R, 1);
+    c->plan_down = bnn::plan_contract(sms, C, F / 128, R, 1);
+    c->plan_head = bnn::plan_contract(sms, in.n_vocab, C / 128, R, 1);
+    const size_t norm_smem = (size_t)std::max(C, F) * 9u;
+    cudaFuncSetAttribute(bnn::eng::rmsnorm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)norm_smem);
+    cudaFuncSetAttribute(bnn::eng::quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)norm_smem);
+    cudaFuncSetAttribute(bnn::eng::swiglu_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)norm_smem);
+    cudaFuncSetAttribute(bnn::eng::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)((in.head_dim + c->n_ctx) * 4));
+    if ((st = capture_step(c, true, &c->graph_logits)) || (st = capture_step(c, false, &c->graph_prefill)))
+        return st;
+    return BNND_OK;
+}
+
+BNND_Status create_mlp_context(bnnd_context* c) {
+    const bnnd_model* m = c->model;
+    const uint32_t R = c->rows, D = m->mlp_max_dim;
+    BNND_Status st;
+    if ((st = dev_alloc(c->mlp_a, (size_t)R * D * 4)) || (st = dev_alloc(c->mlp_b, (size_t)R * D * 4)) ||
+        (st = dev_alloc(c->act, (size_t)R * D)) || (st = dev_alloc(c->totals, (size_t)R * (D / 128 + 1) * 4)) ||
+        (st = dev_alloc(c->rscale, (size_t)R * 4)) || (st = dev_alloc(c->status, 4)))
+        return st;
+    for (const auto& l : m->mlp)
+        c->plan_mlp.push_back(bnn::plan_contract(m->dev->sm_count, l->w.out, l->w.in / 128, R, 1));
+    cudaFuncSetAttribute(bnn::eng::quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(D * 5));
+    return BNND_OK;
+}
+
+// Reads and clears the device status word after the stream drains.
+BNND_Status finish(bnnd_context* c, const char* what) {
+    CUDA_OR(cudaMemcpyAsync(c->h_status, c->status.p, 4, cudaMemcpyDeviceToHost, c->stream), BNND_EIO);
+    CUDA_OR(cudaStreamSynchronize(c->stream), BNND_EIO);
+    const int st = *c->h_status;
+    if (st) {
+        cudaMemsetAsync(c->status.p, 0, 4, c->stream);
+        cudaStreamSynchronize(c->stream);
+        if (st & bnn::kStatusTimeout)
+            return fail(BNND_EIO, "%s: device wait timed out", what);
+        return fail(BNND_ECOMPUTE, "%s: model produced NaN or Inf values", what);
+    }
+    return BNND_OK;
+}
+
+BNND_Status set_pos(bnnd_context* c, uint32_t pos) {
+    std::vector<uint32_t> p(c->rows, pos);
+    CUDA_OR(cudaMemcpyAsync(c->pos_d.p, p.data(), p.size() * 4, cudaMemcpyHostToDevice, c->stream), BNND_EIO);
+    CUDA_OR(cudaStreamSynchronize(c->stream), BNND_EIO);
+    c->pos = pos;
+    return BNND_OK;
+}
+
+// Shared body of BNND_Decode / BNND_DecodeArgmax.
+BNND_Status decode(bnnd_context* c, const int32_t* tokens, uint32_t n, float* logits, int32_t* next) {
+    g_last_error.clear();
+    if (!c || !tokens || n == 0)
+        return BNND_EINVAL;
+    const bnnd_model* m = c->model;
+    if (m->info.task != BNND_TASK_LLM)
+        return fail(BNND_ENOTSUP, "model is not a language model");
+    if (c->pos > c->n_ctx || n > c->n_ctx - c->pos)
+        return fail(BNND_ERANGE, "decode exceeds context length");
+    const size_t count = (size_t)n * c->rows;
+    for (size_t i = 0; i < count; ++i)
+        if (tokens[i] < 0 || (uint32_t)tokens[i] >= m->info.n_vocab)
+            return fail(BNND_ERANGE, "token ID is outside vocabulary");
+    bnn::DeviceGuard guard(m->dev->ordinal);
+    if (c->tok_seq_cap < count) {
+        c->tok_seq = DevMem();
+        BNND_Status st = dev_alloc(c->tok_seq, count * 4);
+        if (st != BNND_OK)
+            return st;
+        c->tok_seq_cap = count;
+    }
+    // Step-major layout: entry [i][row] is row's i-th token.
+    std::vector<int32_t> seq(count);
+    for (uint32_t r = 0; r < c->rows; ++r)
+        for (uint32_t i = 0; i < n; ++i)
+            seq[(size_t)i * c->rows + r] = tokens[(size_t)r * n + i];
+    const uint32_t start = c->pos;
+    CUDA_OR(cudaMemcpyAsync(c->tok_seq.p, seq.data(), count * 4, cudaMemcpyHostToDevice, c->stream), BNND_EIO);
+    const bool want = logits || next;
+    for (uint32_t i = 0; i < n; ++i) {
+        CUDA_OR(cudaMemcpyAsync(c->tok_in.p, c->tok_seq.as<int32_t>() + (size_t)i * c->rows, c->rows * 4,
+                                cudaMemcpyDeviceToDevice, c->stream),
+                BNND_EIO);
+        const bool last = i + 1 == n;
+        CUDA_OR(cudaGraphLaunch(last && want ? c->graph_logits : c->graph_prefill, c->stream), BNND_EIO);
+    }
+    if (logits)
+        CUDA_OR(cudaMemcpyAsync(logits, c->logits.p, (size_t)c->rows * m->info.n_vocab * 4,
+                                cudaMemcpyDeviceToHost, c->stream),
+                BNND_EIO);
+    if (next)
+        CUDA_OR(cudaMemcpyAsync(next, c->tok_next.p, (size_t)c->rows * 4, cudaMemcpyDeviceToHost, c->stream),
+                BNND_EIO);
+    BNND_Status st = finish(c, "BNND_Decode");
+    if (st != BNND_OK) {
+        set_pos(c, start);  // the KV cache returns to the position before the call
+        return st;
+    }
+    c->pos = start + n;
+    c->have_logits = want;
+    return BNND_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+BNND_Status BNND_ModelLoad(BNN_Device device, const char* gguf_path, BNND_Model* out_model) {
+    if (out_model)
+        *out_model = nullptr;
+    g_last_error.clear();
+    if (!device || !gguf_path || !out_model)
+        return BNND_EINVAL;
+    bnn::GgufFile g;
+    if (!g.open(gguf_path))
+        return fail(BNND_EFORMAT, "%s: %s", gguf_path, g.error().c_str());
+    std::string arch;
+    if (!g.get_str("general.architecture", &arch))
+        return fail(BNND_EFORMAT, "%s: missing general.architecture", gguf_path);
+    auto* m = new (std::nothrow) bnnd_model();
+    if (!m)
+        return fail(BNND_ENOMEM, "out of memory");
+    m->dev = device;
+    bnn::DeviceGuard guard(device->ordinal);
+    BNND_Status st;
+    if (arch == "qwen3")
+        st = load_qwen3(g, m);
+    else if (arch == "bnn-mlp")
+        st = load_mlp(g, m);
+    else
+        st = fail(BNND_ENOTSUP, "unsupported GGUF architecture '%s'", arch.c_str());
+    if (st != BNND_OK) {
+        delete m;
+        return st;
+    }
+    *out_model = m;
+    return BNND_OK;
+}
+
+void BNND_ModelFree(BNND_Model model) {
+    if (!model)
+        return;
+    bnn::DeviceGuard guard(model->dev->ordinal);
+    delete model;
+}
+
+BNND_Status BNND_ModelGetInfo(BNND_Model model, BNND_ModelInfo* out_info) {
+    if (!model || !out_info)
+        return BNND_EINVAL;
+    *out_info = model->info;
+    return BNND_OK;
+}
+
+void BNND_ContextParamsInit(BNND_ContextParams* params) {
+    if (params) {
+        params->n_ctx = 0;
+        params->n_batch = 1;
+        params->exact = 1;
+    }
+}
+
+BNND_Status BNND_ContextCreate(BNND_Model model, const BNND_ContextParams* params, BNND_Context* out_ctx) {
+    if (out_ctx)
+        *out_ctx = nullptr;
+    g_last_error.clear();
+    if (!model || !out_ctx)
+        return BNND_EINVAL;
+    auto c = std::unique_ptr<bnnd_context>(new (std::nothrow) bnnd_context());
+    if (!c)
+        return fail(BNND_ENOMEM, "out of memory");
+    c->model = model;
+    BNND_ContextParamsInit(&c->params);
+    if (params)
+        c->params = *params;
+    c->rows = c->params.n_batch ? c->params.n_batch : 1;
+    if (c->rows > 1024)
+        return fail(BNND_ERANGE, "n_batch above 1024 is not supported");
+    bnn::DeviceGuard guard(model->dev->ordinal);
+    c->stream = model->dev->stream;
+    if (cudaMallocHost(&c->h_status, 4) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(BNND_ENOMEM, "pinned allocation failed");
+    }
+    BNND_Status st;
+    if (model->info.task == BNND_TASK_LLM) {
+        c->n_ctx = c->params.n_ctx ? c->params.n_ctx : model->info.n_ctx_train;
+        if (c->n_ctx == 0 || c->n_ctx > model->info.n_ctx_train)
+            return fail(BNND_ERANGE, "context length %u exceeds model capacity %u", c->n_ctx,
+                        model->info.n_ctx_train);
+        st = create_llm_context(c.get());
+    } else {
+        st = create_mlp_context(c.get());
+    }
+    if (st != BNND_OK)
+        return st;
+    *out_ctx = c.release();
+    return BNND_OK;
+}
+
+void BNND_ContextFree(BNND_Context ctx) {
+    if (!ctx)
+        return;
+    bnn::DeviceGuard guard(ctx->model->dev->ordinal);
+    cudaStreamSynchronize(ctx->stream);
+    delete ctx;
+}
+
+BNND_Status BNND_Decode(BNND_Context ctx, const int32_t* tokens, uint32_t n_tokens, float* logits) {
+    return decode(ctx, tokens, n_tokens, logits, nullptr);
+}
+
+BNND_Status BNND_DecodeArgmax(BNND_Context ctx, const int32_t* tokens, uint32_t n_tokens,
+                              int32_t* next_tokens) {
+    if (!next_tokens)
+        return BNND_EINVAL;
+    return decode(ctx, tokens, n_tokens, nullptr, next_tokens);
+}
+
+BNND_Status BNND_Generate(BNND_Context c, uint32_t steps, int32_t* out_tokens) {
+    g_last_error.clear();
+    if (!c || steps == 0)
+        return BNND_EINVAL;
+    if (c->model->info.task != BNND_TASK_LLM)
+        return fail(BNND_ENOTSUP, "model is not a language model");
+    if (!c->have_logits)
+        return fail(BNND_EINVAL, "BNND_Generate needs a preceding decode with logits");
+    // Each step consumes one position; the last generated token is not fed back.
+    if (c->pos > c->n_ctx || steps - 1 > c->n_ctx - c->pos)
+        return fail(BNND_ERANGE, "generation exceeds context length");
+    if (steps > c->hist_cap)
+        return fail(BNND_ERANGE, "too many steps for one call");
+    bnn::DeviceGuard guard(c->model->dev->ordinal);
+    const uint32_t start = c->pos;
+    // The first generated token is the argmax already computed.
+    CUDA_OR(cudaMemsetAsync(c->hist_count.p, 0, 4, c->stream), BNND_EIO);
+    CUDA_OR(cudaMemcpyAsync(c->hist.p, c->tok_next.p, (size_t)c->rows * 4, cudaMemcpyDeviceToDevice, c->stream),
+            BNND_EIO);
+    CUDA_OR(cudaMemcpyAsync(c->tok_in.p, c->tok_next.p, (size_t)c->rows * 4, cudaMemcpyDeviceToDevice, c->stream),
+            BNND_EIO);
+    const uint32_t one = 1;
+    CUDA_OR(cudaMemcpyAsync(c->hist_count.p, &one, 4, cudaMemcpyHostToDevice, c->stream), BNND_EIO);
+    for (uint32_t i = 1; i < steps; ++i)
+        CUDA_OR(cudaGraphLaunch(c->graph_logits, c->stream), BNND_EIO);
+    if (out_tokens)
+        CUDA_OR(cudaMemcpyAsync(out_tokens, c->hist.p, (size_t)steps * c->rows * 4, cudaMemcpyDeviceToHost,
+                                c->stream),
+                BNND_EIO);
+    BNND_Status st = finish(c, "BNND_Generate");
+    if (st != BNND_OK) {
+        set_pos(c, start);
+        return st;
+    }
+    c->pos = start + steps - 1;
+    if (out_tokens) {
+        // Device history is step-major; the API returns row-major [rows][steps].
+        std::vector<int32_t> tmp(out_tokens, out_tokens + (size_t)steps * c->rows);
+        for (uint32_t s = 0; s < steps; ++s)
+            for (uint32_t r = 0; r < c->rows; ++r)
+                out_tokens[(size_t)r * steps + s] = tmp[(size_t)s * c->rows + r];
+    }
+    return BNND_OK;
+}
+
+uint32_t BNND_ContextPos(BNND_Context ctx) { return ctx ? ctx->pos : 0; }
+
+BNND_Status BNND_ContextTruncate(BNND_Context ctx, uint32_t pos) {
+    g_last_error.clear();
+    if (!ctx)
+        return BNND_EINVAL;
+    if (pos > ctx->pos)
+        return fail(BNND_EINVAL, "truncate position is beyond current position");
+    if (ctx->model->info.task != BNND_TASK_LLM) {
+        ctx->pos = pos;
+        return BNND_OK;
+    }
+    bnn::DeviceGuard guard(ctx->model->dev->ordinal);
+    ctx->have_logits = false;
+    return set_pos(ctx, pos);
+}
+
+BNND_Status BNND_Classify(BNND_Context c, const float* input, uint32_t n_samples, float* logits) {
+    g_last_error.clear();
+    if (!c || !input || !logits || n_samples == 0)
+        return BNND_EINVAL;
+    const bnnd_model* m = c->model;
+    if (m->info.task != BNND_TASK_CLASSIFY)
+        return fail(BNND_ENOTSUP, "model is not a classifier");
+    if (n_samples > c->rows)
+        return fail(BNND_ERANGE, "sample count exceeds context batch size");
+    const size_t inputs = (size_t)n_samples * m->info.input_size;
+    for (size_t i = 0; i < inputs; ++i)
+        if (!std::isfinite(input[i]))
+            return fail(BNND_EINVAL, "input contains NaN or Inf");
+    bnn::DeviceGuard guard(m->dev->ordinal);
+    cudaStream_t s = c->stream;
+    float* cur = c->mlp_a.as<float>();
+    float* nxt = c->mlp_b.as<float>();
+    CUDA_OR(cudaMemcpyAsync(cur, input, inputs * 4, cudaMemcpyHostToDevice, s), BNND_EIO);
+    for (size_t i = 0; i < m->mlp.size(); ++i) {
+        const MlpLayer& L = *m->mlp[i];
+        bnn::eng::quant_kernel<<<n_samples, 512, (size_t)L.w.in * 5u, s>>>(cur, L.w.in, qout(c, L.w.in));
+        const bnn::ContractLaunch& cl = c->plan_mlp[i];
+        CUDA_OR(launch_linear(cl, L.w, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(),
+                              n_samples, nxt, nullptr, c->status.as<int>(), s),
+                BNND_EIO);
+        bnn::eng::mlp_post_kernel<<<64, 256, 0, s>>>(nxt, L.post_scale.as<float>(), L.post_bias.as<float>(),
+                                                     L.w.out, n_samples, L.relu);
+        std::swap(cur, nxt);
+    }
+    const size_t outputs = (size_t)n_samples * m->info.n_classes;
+    bnn::eng::finite_check_kernel<<<16, 256, 0, s>>>(cur, outputs, c->status.as<int>(), bnn::eng::kStatusNonFinite);
+    CUDA_OR(cudaMemcpyAsync(logits, cur, outputs * 4, cudaMemcpyDeviceToHost, s), BNND_EIO);
+    return finish(c, "BNND_Classify");
+}
+
+const char* BNND_LastError(void) { return g_last_error.c_str(); }
+
+void* BNND_ContextStream(BNND_Context ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
+
+}  // extern "C"

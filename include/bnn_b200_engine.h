@@ -1,0 +1,117 @@
+/*
+ * bnn_b200_engine.h - device-resident W1A8 engine (libbnn_b200.so).
+ *
+ * The reference engine (bnn-sw-v2/bnn-engine.h) runs its model glue on the
+ * host and crosses the accelerator boundary once per linear (215 times per
+ * Qwen3-1.7B token, bnn-sw-v2/linear.c:161-216). This engine keeps the whole
+ * step on the B200: embedding, RMSNorm, the W1A8 linears, q/k-norm, RoPE,
+ * the KV cache, attention, SwiGLU, lm_head and the greedy argmax. Its API
+ * mirrors BNNE_* (same task model, same status values, same argument and
+ * range rules) under a BNND_ prefix so both engines can be linked into one
+ * program. A context holds `n_batch` independent rows (sequences) decoded
+ * in lockstep; the reference's single-sequence context is n_batch = 1.
+ *
+ * Numerics: the linears are the bit-exact BNN_* contraction. In the default
+ * exact mode the glue reproduces qwen3.c's FP32 operation order (sequential
+ * sums, per-op rounding, host-computed RoPE tables) so logits match the
+ * reference engine; the one known difference is expf, which is correctly
+ * rounded here while glibc's misrounds ~0.004% of inputs by one ulp.
+ */
+#ifndef BNN_B200_ENGINE_H
+#define BNN_B200_ENGINE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "bnn_b200_accel.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct bnnd_model* BNND_Model;
+typedef struct bnnd_context* BNND_Context;
+
+/* Same values as BNNE_Status (bnn-sw-v2/bnn-engine.h:36-45). */
+typedef enum {
+    BNND_OK = 0,
+    BNND_EINVAL = -1,
+    BNND_ENOMEM = -2,
+    BNND_ENOTSUP = -3,
+    BNND_ERANGE = -4,
+    BNND_EIO = -5,
+    BNND_EFORMAT = -6,
+    BNND_ECOMPUTE = -7
+} BNND_Status;
+
+typedef enum { BNND_TASK_CLASSIFY = 1, BNND_TASK_LLM = 2 } BNND_Task;
+
+/* Mirrors BNNE_ModelInfo (bnn-engine.h:52-68) plus the Qwen3 shape. */
+typedef struct {
+    BNND_Task task;
+    uint32_t input_size; /* classify: features per sample */
+    uint32_t n_classes;
+    uint32_t n_vocab;    /* llm */
+    uint32_t n_ctx_train;
+    int32_t eos_token;   /* -1 if not declared */
+    uint32_t n_layers, hidden, heads, kv_heads, head_dim, ffn;
+    uint64_t weight_count; /* W1 weights streamed per token (llm) or sample (classify) */
+} BNND_ModelInfo;
+
+/* n_ctx: KV capacity (0 = the model's training context); n_batch: rows per
+ * call (sequences for llm, samples for classify; 0 = 1); exact: 1 = the
+ * reference's operation order for all FP32 glue (default), 0 = parallel
+ * reductions for the norm and attention sums. */
+typedef struct {
+    uint32_t n_ctx;
+    uint32_t n_batch;
+    int exact;
+} BNND_ContextParams;
+
+/* Replaces BNNE_ModelLoad (bnn-engine.h:95): parses the GGUF (architectures
+ * "qwen3" and "bnn-mlp") and uploads every tensor to the device of `device`,
+ * Q1_0 weights repacked into the contraction kernel's layout. */
+BNND_Status BNND_ModelLoad(BNN_Device device, const char* gguf_path, BNND_Model* out_model);
+void BNND_ModelFree(BNND_Model model);
+BNND_Status BNND_ModelGetInfo(BNND_Model model, BNND_ModelInfo* out_info);
+
+void BNND_ContextParamsInit(BNND_ContextParams* params);
+BNND_Status BNND_ContextCreate(BNND_Model model, const BNND_ContextParams* params, BNND_Context* out_ctx);
+void BNND_ContextFree(BNND_Context ctx);
+
+/* Replaces BNNE_Decode (bnn-engine.h:139): appends n_tokens per row
+ * (tokens [n_batch][n_tokens], row-major) at the current position, one step
+ * per token; logits (NULL for prefill only) receive [n_batch][n_vocab] of the
+ * last token. Range and finiteness rules of BNNE_Decode apply. */
+BNND_Status BNND_Decode(BNND_Context ctx, const int32_t* tokens, uint32_t n_tokens, float* logits);
+
+/* Like BNND_Decode but returns only the greedy next token of each row
+ * (first maximum, lowest index on ties, as bnn-infer-v2.c:48-54). */
+BNND_Status BNND_DecodeArgmax(BNND_Context ctx, const int32_t* tokens, uint32_t n_tokens,
+                              int32_t* next_tokens);
+
+/* Greedy generation entirely on the device: feeds each row's last argmax
+ * back as input for `steps` steps (one CUDA graph launch per step) and writes
+ * the generated ids to out_tokens [n_batch][steps] (host) when non-NULL.
+ * Requires a preceding BNND_Decode/BNND_DecodeArgmax. */
+BNND_Status BNND_Generate(BNND_Context ctx, uint32_t steps, int32_t* out_tokens);
+
+uint32_t BNND_ContextPos(BNND_Context ctx);
+/* Replaces BNNE_ContextTruncate (bnn-engine.h:144). */
+BNND_Status BNND_ContextTruncate(BNND_Context ctx, uint32_t pos);
+
+/* Replaces BNNE_Classify (bnn-engine.h:131) for bnn-mlp: input
+ * [n_samples][input_size], logits [n_samples][n_classes]. */
+BNND_Status BNND_Classify(BNND_Context ctx, const float* input, uint32_t n_samples, float* logits);
+
+/* Thread-local text of the last failure (BNNE_LastError, bnn-engine.h:157). */
+const char* BNND_LastError(void);
+
+/* The CUDA stream the context's work runs on (cudaStream_t as void*). */
+void* BNND_ContextStream(BNND_Context ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,108 @@
+"""ctypes face of the reference engine compiled from its own sources.
+
+TEST INFRASTRUCTURE ONLY (tests/, smoke(), bench.py's CPU-baseline leg).
+oracle/_ref/libbnn_engine_soft.so is bnn-sw-v2 (engine, qwen3, bnn-mlp,
+gguf, tokenizer) + the soft backend, built by oracle/Makefile with
+-Bsymbolic so its BNN_* calls stay inside it even when libbnn_b200.so is
+loaded in the same process. Calls follow bnn-sw-v2/bnn-engine.h.
+"""
+import ctypes
+from ctypes import POINTER, c_char_p, c_int, c_int32, c_uint32, c_uint64, c_void_p
+from pathlib import Path
+
+import numpy as np
+
+LIB = Path(__file__).resolve().parent / "_ref" / "libbnn_engine_soft.so"
+
+
+class BnneModelInfo(ctypes.Structure):  # bnn-engine.h:52-68
+    _fields_ = [("task", c_int), ("arch", c_char_p), ("load_ns", c_uint64),
+                ("input_rank", c_uint32), ("input_dims", c_uint32 * 4), ("input_size", c_uint32),
+                ("n_classes", c_uint32), ("n_vocab", c_uint32), ("n_ctx_train", c_uint32),
+                ("bos_token", c_int32), ("eos_token", c_int32)]
+
+
+class BnneContextParams(ctypes.Structure):  # bnn-engine.h:70-74
+    _fields_ = [("n_ctx", c_uint32), ("n_batch", c_uint32), ("enable_stats", c_int)]
+
+
+_dll = None
+
+
+def available():
+    return LIB.exists()
+
+
+def dll():
+    global _dll
+    if _dll is None:
+        d = ctypes.CDLL(str(LIB))
+        d.BNN_DeviceOpen.argtypes = [c_uint32, POINTER(c_void_p)]
+        d.BNN_DeviceClose.argtypes = [c_void_p]
+        d.BNNE_ModelLoad.argtypes = [c_void_p, c_char_p, POINTER(c_void_p)]
+        d.BNNE_ModelFree.argtypes = [c_void_p]
+        d.BNNE_ModelGetInfo.argtypes = [c_void_p, POINTER(BnneModelInfo)]
+        d.BNNE_ContextParamsInit.argtypes = [POINTER(BnneContextParams)]
+        d.BNNE_ContextCreate.argtypes = [c_void_p, POINTER(BnneContextParams), POINTER(c_void_p)]
+        d.BNNE_ContextFree.argtypes = [c_void_p]
+        d.BNNE_Decode.argtypes = [c_void_p, c_void_p, c_uint32, c_void_p]
+        d.BNNE_Classify.argtypes = [c_void_p, c_void_p, c_uint32, c_void_p]
+        d.BNNE_ContextTruncate.argtypes = [c_void_p, c_uint32]
+        d.BNNE_LastError.restype = c_char_p
+        _dll = d
+    return _dll
+
+
+class RefEngine:
+    """One soft device + one model + one context of the reference engine."""
+
+    def __init__(self, path, n_ctx=0, n_batch=0):
+        d = dll()
+        self.dev, self.model, self.ctx = c_void_p(), c_void_p(), c_void_p()
+        assert d.BNN_DeviceOpen(0, ctypes.byref(self.dev)) == 0
+        st = d.BNNE_ModelLoad(self.dev, str(path).encode(), ctypes.byref(self.model))
+        if st != 0:
+            raise RuntimeError(f"BNNE_ModelLoad: {st} {d.BNNE_LastError()}")
+        self.info = BnneModelInfo()
+        d.BNNE_ModelGetInfo(self.model, ctypes.byref(self.info))
+        p = BnneContextParams()
+        d.BNNE_ContextParamsInit(ctypes.byref(p))
+        p.n_ctx, p.n_batch, p.enable_stats = n_ctx, n_batch, 0
+        st = d.BNNE_ContextCreate(self.model, ctypes.byref(p), ctypes.byref(self.ctx))
+        if st != 0:
+            raise RuntimeError(f"BNNE_ContextCreate: {st} {d.BNNE_LastError()}")
+
+    def decode(self, tokens, want_logits=True):
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32).reshape(-1))
+        out = np.empty(self.info.n_vocab, dtype=np.float32) if want_logits else None
+        st = dll().BNNE_Decode(self.ctx, t.ctypes.data, t.size, out.ctypes.data if out is not None else None)
+        if st != 0:
+            raise RuntimeError(f"BNNE_Decode: {st} {dll().BNNE_LastError()}")
+        return out
+
+    def greedy(self, prompt, steps):
+        """The CLI's loop (bnn-infer-v2.c:245-280) without EOG stopping:
+        prefill, then argmax/feed `steps - 1` times; returns `steps` ids."""
+        logits = self.decode(prompt)
+        out = [int(np.argmax(logits))]  # numpy argmax = first maximum
+        for _ in range(steps - 1):
+            logits = self.decode([out[-1]])
+            out.append(int(np.argmax(logits)))
+        return out
+
+    def classify(self, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty((x.shape[0], self.info.n_classes), dtype=np.float32)
+        st = dll().BNNE_Classify(self.ctx, x.ctypes.data, x.shape[0], out.ctypes.data)
+        if st != 0:
+            raise RuntimeError(f"BNNE_Classify: {st} {dll().BNNE_LastError()}")
+        return out
+
+    def truncate(self, pos):
+        assert dll().BNNE_ContextTruncate(self.ctx, pos) == 0
+
+    def close(self):
+        d = dll()
+        d.BNNE_ContextFree(self.ctx)
+        d.BNNE_ModelFree(self.model)
+        d.BNN_DeviceClose(self.dev)
