@@ -1,0 +1,382 @@
+#!/usr/bin/env python3
+"""Benchmark: Qwen3-1.7B-shape W1A8 greedy decode tokens/s on B200.
+
+Workload: random-init Qwen3-1.7B architecture
+(28 layers, hidden 2048, 16 q / 8 kv heads of 128, SwiGLU 6144, vocab 151669,
+tied Q1_0 embedding/lm_head, RMSNorm gains ~N(1, 0.02), rope theta 1e6), a
+32-token seeded prompt, greedy decode at ctx 1024, batch 1. A step is one
+decoded token: one pass of the device-resident engine over the whole model
+(241.9 MB of Q1_0 weights streamed from HBM per token, larger than L2).
+
+value     tokens/s of BNND_Generate with everything resident on the device,
+          timed with CUDA events on the engine's stream (max over ranks).
+e2e       the same through the public per-token call BNND_DecodeArgmax with
+          host token ids in and the host argmax out every step (4 B each way).
+roofline  the W1A8 contraction kernel (the step's dominant kernel), from an
+          instrumented replay of the same step graph: algorithmic bytes
+          (N*K*0.140625 + 4K + 4N per linear) / its device time, against the
+          measured HBM copy bandwidth in MEASURED_PEAKS.json.
+cpu_baseline  the reference engine itself (bnn-sw-v2 + soft backend, compiled
+          from its sources into oracle/_ref) decoding one token of the same
+          model on one host core.
+
+--impl reference runs only the reference's CPU path: one soft-engine process
+per host core (it is single-threaded), each decoding tokens of the same
+model, and reports their aggregate tokens/s.
+
+Multi-GPU (torchrun, one rank per GPU): every rank decodes its own replica
+(independent sequences, no collective on the data path): weak scaling.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT / "bnn-train-infer_b200"), str(ROOT / "oracle")]
+
+METRIC = "qwen3_1p7b_w1a8_decode_tokens_per_s"
+PROMPT_TOKENS = 32
+CTX = 1024
+MODEL_SEED = 20261203  # rng_for(config index 2)
+PROMPT_SEED = 20261203 + 7
+WORKLOAD = ("configs[2]: Qwen3-1.7B-shape W1A8 greedy decode, random-init weights, "
+            "32-token seeded prompt, ctx 1024, batch 1")
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def model_path(cache):
+    cache = Path(cache)
+    cache.mkdir(parents=True, exist_ok=True)
+    p = cache / f"qwen3_1p7b_seed{MODEL_SEED}.gguf"
+    if not p.exists():
+        from bnn_b200 import gguf
+        tmp = p.with_suffix(f".tmp{os.getpid()}")
+        t0 = time.time()
+        gguf.qwen3_model(tmp, gguf.QWEN3_1_7B, seed=MODEL_SEED)
+        os.replace(tmp, p)
+        log(f"generated {p} in {time.time() - t0:.1f}s")
+    return p
+
+
+def prompt_ids(vocab):
+    import numpy as np
+    return np.random.default_rng(PROMPT_SEED).integers(0, vocab, size=PROMPT_TOKENS).astype(np.int32)
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile(prefix="clocks", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        self.out.close()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in Path(self.out.name).read_text().splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        finally:
+            os.unlink(self.out.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "samples": len(rows), "reasons": reasons}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the contraction kernel from the committed ncu
+    summary (profiles/roofline_traffic.json), if one matches this workload."""
+    p = ROOT / "profiles" / "roofline_traffic.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return d.get(METRIC)
+    except (ValueError, OSError):
+        return None
+
+
+def cpu_baseline_sample(path, prompt):
+    """One decode step of the same model through the reference engine (soft
+    backend, one core). Returns (tokens/s, seconds) or None."""
+    import ref_engine
+    if not ref_engine.available():
+        return None
+    ref = ref_engine.RefEngine(path, n_ctx=CTX)
+    try:
+        t0 = time.perf_counter()
+        ref.decode(prompt[:1])
+        dt = time.perf_counter() - t0
+    finally:
+        ref.close()
+    return 1.0 / dt, dt
+
+
+def run_b200(args):
+    import numpy as np
+    import torch
+    from bnn_b200 import accel, engine
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    torch.cuda.set_device(local)
+
+    if rank == 0 or world == 1:
+        path = model_path(args.model_cache)
+    if dist:
+        dist.barrier()
+        path = model_path(args.model_cache)
+
+    dev = accel.Device(local)
+    api = engine.EngineApi(dev.api.dll)
+    t0 = time.time()
+    model = engine.Model(dev, path, api)
+    log(f"[rank {rank}] model loaded in {time.time() - t0:.1f}s")
+    info = model.info
+    prompt = prompt_ids(info.n_vocab)
+    ctx = engine.Context(model, n_ctx=CTX, n_batch=1, exact=not args.fast)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    launches_per_step = ctx.step_launches()
+
+    def timed(fn):
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        e1.synchronize()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if dist:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    # ---- device-resident value
+    ctx.decode_argmax(prompt)                    # prefill (untimed)
+    ctx.generate(args.warmup)                    # warm-up steps
+    need = PROMPT_TOKENS + args.warmup + args.steps + 2
+    if need > CTX:
+        raise SystemExit(f"prompt + warmup + steps must fit ctx {CTX}")
+    gen = api.Generate
+    with ClockSampler(local) as clocks:
+        ms = timed(lambda: api.check(gen(ctx.handle, args.steps + 1, None)))
+    clk = clocks.summary()
+    value = args.steps * world / (ms / 1e3)   # first of the steps+1 ids was the warm-up's pick
+
+    # ---- end to end through the public per-token call (host ids in/out)
+    ctx.truncate(0)
+    nxt = ctx.decode_argmax(prompt)
+    for _ in range(args.warmup):
+        nxt = ctx.decode_argmax(nxt)
+    host_tok = np.empty(1, dtype=np.int32)
+
+    def e2e_loop():
+        tok = nxt.copy()
+        for _ in range(args.steps):
+            tok = ctx.decode_argmax(tok)
+        host_tok[:] = tok
+
+    ms_e2e = timed(e2e_loop)
+    e2e_value = args.steps * world / (ms_e2e / 1e3)
+
+    # ---- roofline of the dominant kernel (instrumented replay of the same step)
+    ctx.truncate(0)
+    ctx.decode_argmax(prompt)
+    stats, total_ms = ctx.profile(args.profile_steps)
+    by_kernel = {}
+    for name, (launches, kms, kbytes) in stats.items():
+        key = "w1a8_contract_kernel" if name.startswith("w1a8_gemv:") else name
+        l0, m0, b0 = by_kernel.get(key, (0, 0.0, 0.0))
+        by_kernel[key] = (l0 + launches, m0 + kms, b0 + kbytes)
+    dominant = max(by_kernel, key=lambda k: by_kernel[k][1])
+    launches, kms, kbytes = by_kernel["w1a8_contract_kernel"]
+    peak, peak_kind = measured_peaks()
+    achieved = kbytes / (kms / 1e3) / 1e9
+    traffic = ncu_traffic()
+    roofline = {
+        "kernel": "w1a8_contract_kernel", "dominant_kernel": dominant, "bound": "hbm",
+        "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+        "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+        "traffic": traffic, "launches_per_step": launches,
+        "bytes_per_launch": round(kbytes / (launches * args.profile_steps), 1),
+        "us_per_launch": round(kms * 1e3 / (launches * args.profile_steps), 3),
+        "share_of_step": round(kms / total_ms, 4),
+        "step_ms_instrumented": round(total_ms / args.profile_steps, 4),
+        "kernel_share": {k: round(v[1] / total_ms, 4) for k, v in sorted(by_kernel.items(), key=lambda kv: -kv[1][1])},
+    }
+
+    out = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            sample = cpu_baseline_sample(path, prompt)
+            if sample:
+                cpu = {"value": round(sample[0], 6), "unit": "tokens/s", "cores": 1, "kind": "reference",
+                       "sample": f"one decode step (position 0, with lm_head) of the same model through the "
+                                 f"reference engine + soft backend built from its sources, 1 thread: "
+                                 f"{sample[1]:.2f} s"}
+        weight_bytes = info.weight_count * 0.140625
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded random-init weights and prompt; no checkpoint offline)",
+            "config": {"workload": WORKLOAD, "prompt_tokens": PROMPT_TOKENS, "ctx": CTX, "batch_per_gpu": 1,
+                       "layers": info.n_layers, "hidden": info.hidden, "ffn": info.ffn, "vocab": info.n_vocab,
+                       "numerics": "fast" if args.fast else "exact (reference operation order)",
+                       "weight_bytes_per_token": int(weight_bytes),
+                       "l2": "inputs larger than L2: 242 MB of weights streamed per token vs 126 MB L2",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 4, "call": "BNND_DecodeArgmax per token, host ids in and out"},
+            "clocks": clk,
+            "gpu_launches": int(launches_per_step * (args.steps + 1)),
+        }
+    ctx.free()
+    model.free()
+    dev.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
+def _ref_worker(path, n_tokens, conn):
+    import ref_engine
+    ref = ref_engine.RefEngine(path, n_ctx=CTX)
+    import numpy as np
+    prompt = prompt_ids(ref.info.n_vocab)
+    logits = ref.decode(prompt[:1])  # the first step doubles as warm-up
+    tok = int(np.argmax(logits))
+    t0 = time.perf_counter()
+    for _ in range(n_tokens):
+        tok = int(np.argmax(ref.decode([tok])))
+    dt = time.perf_counter() - t0
+    ref.close()
+    conn.send((n_tokens, dt))
+    conn.close()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    import multiprocessing as mp
+    import ref_engine
+    if not ref_engine.available():
+        return {"impl": "reference", "unavailable": "oracle/_ref/libbnn_engine_soft.so not built"}
+    path = model_path(args.model_cache)
+    cores = os.cpu_count() or 1
+    procs = max(1, min(cores, args.ref_procs, args.steps))
+    per = max(1, math.ceil(args.steps / procs))
+    ctxm = mp.get_context("spawn")
+    pipes, workers = [], []
+    for _ in range(procs):
+        a, b = ctxm.Pipe(duplex=False)
+        w = ctxm.Process(target=_ref_worker, args=(str(path), per, b))
+        w.start()
+        pipes.append(a)
+        workers.append(w)
+    results = [p.recv() for p in pipes]
+    for w in workers:
+        w.join()
+    tokens = sum(r[0] for r in results)
+    slowest = max(r[1] for r in results)
+    value = tokens / slowest
+    sample = (f"{procs} reference soft-engine processes (single-threaded each) on {cores} host cores, "
+              f"{per} timed decode step(s) each after one untimed step; aggregate tokens / slowest process")
+    return {
+        "metric": METRIC, "value": round(value, 6), "unit": "tokens/s", "n_gpus": 0, "steps": tokens,
+        "warmup": procs, "ms_per_step": round(slowest * 1e3 / per, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "prompt_tokens": PROMPT_TOKENS, "ctx": CTX},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(value, 6), "unit": "tokens/s", "cores": procs, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": round(value, 6), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--fast", action="store_true", help="tree reductions instead of the reference order")
+    ap.add_argument("--profile-steps", type=int, default=4)
+    ap.add_argument("--ref-procs", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--model-cache", default=os.environ.get("BNN_MODEL_CACHE", "/tmp/bnn_b200_models"))
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    out = run_reference(args) if args.impl == "reference" else run_b200(args)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

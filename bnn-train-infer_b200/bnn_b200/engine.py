@@ -29,6 +29,11 @@ class ContextParams(ctypes.Structure):
     _fields_ = [("n_ctx", c_uint32), ("n_batch", c_uint32), ("exact", c_int)]
 
 
+class KernelStat(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 32), ("launches", c_uint32), ("ms", ctypes.c_double),
+                ("bytes", ctypes.c_double)]
+
+
 class EngineError(RuntimeError):
     def __init__(self, status, detail):
         self.status = status
@@ -54,6 +59,9 @@ class EngineApi:
             "BNND_Classify": (c_int, [c_void_p, c_void_p, c_uint32, c_void_p]),
             "BNND_LastError": (c_char_p, []),
             "BNND_ContextStream": (c_void_p, [c_void_p]),
+            "BNND_ContextProfile": (c_int, [c_void_p, c_uint32, c_void_p, c_uint32, POINTER(c_uint32),
+                                            POINTER(ctypes.c_double)]),
+            "BNND_StepLaunches": (c_uint32, [c_void_p]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(d, name)
@@ -132,6 +140,23 @@ class Context:
 
     def stream(self):
         return self.api.ContextStream(self.handle)
+
+    def step_launches(self):
+        return self.api.StepLaunches(self.handle)
+
+    def profile(self, steps):
+        """Per-kernel device time over `steps` instrumented greedy steps:
+        ({name: (launches_per_step, ms, bytes)}, total_ms)."""
+        cap = 64
+        stats = (KernelStat * cap)()
+        count, total = c_uint32(), ctypes.c_double()
+        self.api.check(self.api.ContextProfile(self.handle, steps, stats, cap, ctypes.byref(count),
+                                               ctypes.byref(total)))
+        out = {}
+        for i in range(count.value):
+            s = stats[i]
+            out[s.name.decode()] = (s.launches, s.ms, s.bytes)
+        return out, total.value
 
     def free(self):
         if self.handle:

@@ -428,7 +428,8 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
     pa.row_scale = rscale;
     pa.status = device->d_status;
     const size_t prep_smem = bnn::prep_smem_bytes(K);
-    cudaFuncSetAttribute(bnn::w1a8_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
+    cudaFuncSetAttribute(bnn::w1a8_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)bnn::prep_smem_bytes(kMaxFeatures));
     for (uint32_t r0 = 0; r0 < M; r0 += 65535u * 1024u) {
         const uint32_t rows = std::min<uint32_t>(M - r0, 65535u * 1024u);
         bnn::PrepArgs chunk = pa;

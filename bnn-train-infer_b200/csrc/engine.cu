@@ -57,6 +57,48 @@ BNND_Status from_accel(BNN_Status st, const char* what) {
     return fail(r, "%s: %s", what, BNN_StatusString(st));
 }
 
+
+
+// Timestamps between launches while capturing an instrumented step.
+struct StepRecorder {
+    cudaStream_t stream = nullptr;
+    std::vector<cudaEvent_t> events;  // events[i] precedes launch i
+    std::vector<std::string> names;   // names[i] labels launch i
+    std::vector<double> bytes;        // algorithmic bytes of launch i
+    size_t next = 0;
+    bool overflow = false;
+    void mark(const char* name, double b) {
+        if (next + 1 >= events.size()) {
+            overflow = true;
+            return;
+        }
+        names[next] = name;
+        bytes[next] = b;
+        ++next;
+        cudaEventRecordWithFlags(events[next], stream, cudaEventRecordExternal);
+    }
+};
+thread_local StepRecorder* g_rec = nullptr;
+thread_local double g_next_bytes = 0.0;  // bytes of the launch being reported
+
+// First failing launch of an enqueue sequence (name + error), for diagnostics.
+struct LaunchCheck {
+    const char* what = nullptr;
+    cudaError_t err = cudaSuccess;
+    void operator()(const char* name, cudaError_t e = cudaGetLastError()) {
+        if (e != cudaSuccess && err == cudaSuccess) {
+            err = e;
+            what = name;
+        }
+        ++launches;
+        if (g_rec)
+            g_rec->mark(name, g_next_bytes);
+        g_next_bytes = 0.0;
+    }
+    uint32_t launches = 0;
+};
+thread_local LaunchCheck* g_check = nullptr;
+
 #define CUDA_OR(expr, status)                                                              \
     do {                                                                                   \
         cudaError_t e_ = (expr);                                                           \
@@ -239,9 +281,13 @@ struct bnnd_context {
     uint32_t hist_cap = 0;
     bnn::ContractLaunch plan_qkv{}, plan_o{}, plan_gu{}, plan_down{}, plan_head{};
     std::vector<bnn::ContractLaunch> plan_mlp;
-    cudaGraphExec_t graph_logits = nullptr, graph_prefill = nullptr;
+    cudaGraphExec_t graph_logits = nullptr, graph_prefill = nullptr, graph_profile = nullptr;
+    StepRecorder recorder;
+    uint32_t step_launches = 0;
     int* h_status = nullptr;
-    int32_t* h_tokens = nullptr;
+    int32_t* h_tokens = nullptr;   // pinned staging of input ids
+    size_t h_tokens_cap = 0;
+    int32_t* h_next = nullptr;     // pinned staging of greedy picks
     bool have_logits = false;
 
     ~bnnd_context() {
@@ -249,10 +295,16 @@ struct bnnd_context {
             cudaGraphExecDestroy(graph_logits);
         if (graph_prefill)
             cudaGraphExecDestroy(graph_prefill);
+        if (graph_profile)
+            cudaGraphExecDestroy(graph_profile);
+        for (cudaEvent_t e : recorder.events)
+            cudaEventDestroy(e);
         if (h_status)
             cudaFreeHost(h_status);
         if (h_tokens)
             cudaFreeHost(h_tokens);
+        if (h_next)
+            cudaFreeHost(h_next);
     }
 };
 
@@ -491,6 +543,7 @@ cudaError_t launch_linear(const bnn::ContractLaunch& cl, const Linear& l, const 
     a.residual = residual;
     a.tiles = cl.tiles;
     a.stages = cl.stages;
+    g_next_bytes = ((double)l.out * l.in * 0.140625 + 4.0 * l.in + 4.0 * l.out) * rows;
     return bnn::launch_contract(cl, (rows + bnn::kRowsPerCta - 1) / bnn::kRowsPerCta, 1, a, s);
 }
 
@@ -505,6 +558,8 @@ bnn::eng::QuantOut qout(bnnd_context* c, uint32_t k) {
 
 // Enqueues one decode step for every row (tokens already in tok_in).
 cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
+    LaunchCheck local;
+    LaunchCheck& ck = g_check ? *g_check : local;
     const bnnd_model* m = c->model;
     const BNND_ModelInfo& in = m->info;
     const uint32_t C = in.hidden, F = in.ffn, HD = in.head_dim, KV = in.kv_heads * HD, R = c->rows;
@@ -514,12 +569,14 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
     const size_t norm_smem = (size_t)C * 9u;
     bnn::eng::embed_kernel<<<R, 256, 0, s>>>(c->tok_in.as<int32_t>(), m->lm_head.m->wbits,
                                              m->lm_head.m->scales, C, c->x.as<float>());
+    ck("embed_kernel");
     for (uint32_t l = 0; l < in.n_layers; ++l) {
         const QwenLayer& L = *m->layers[l];
         bnn::eng::rmsnorm_quant_kernel<<<R, 512, norm_smem, s>>>(c->x.as<float>(), L.attn_norm.as<float>(),
                                                                  m->eps, C, qout(c, C), status, exact);
-        launch_linear(c->plan_qkv, L.qkv, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(),
-                      R, c->qkv.as<float>(), nullptr, status, s);
+        ck("rmsnorm_quant_kernel");
+        ck("w1a8_gemv:qkv", launch_linear(c->plan_qkv, L.qkv, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(),
+                      R, c->qkv.as<float>(), nullptr, status, s));
         bnn::eng::QkArgs qa;
         qa.qkv = c->qkv.as<float>();
         qa.q_norm = L.q_norm.as<float>();
@@ -540,6 +597,7 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
         qa.exact = exact;
         qa.status = status;
         bnn::eng::qk_norm_rope_kernel<<<dim3(in.heads + in.kv_heads, R), HD, HD * 8, s>>>(qa);
+        ck("qk_norm_rope_kernel");
         bnn::eng::AttnArgs aa;
         aa.qkv = c->qkv.as<float>();
         aa.kcache = qa.kcache;
@@ -556,41 +614,58 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
         aa.exact = exact;
         aa.status = status;
         bnn::eng::attention_kernel<<<dim3(in.heads, R), 256, (size_t)(HD + c->n_ctx) * 4, s>>>(aa);
+        ck("attention_kernel");
         bnn::eng::quant_kernel<<<R, 512, (size_t)C * 5u, s>>>(c->y.as<float>(), C, qout(c, C));
-        launch_linear(c->plan_o, L.o, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(), R,
-                      c->x.as<float>(), c->x.as<float>(), status, s);
+        ck("quant_kernel");
+        ck("w1a8_gemv:o", launch_linear(c->plan_o, L.o, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(), R,
+                      c->x.as<float>(), c->x.as<float>(), status, s));
         bnn::eng::rmsnorm_quant_kernel<<<R, 512, norm_smem, s>>>(c->x.as<float>(), L.ffn_norm.as<float>(),
                                                                  m->eps, C, qout(c, C), status, exact);
-        launch_linear(c->plan_gu, L.gu, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(), R,
-                      c->gu.as<float>(), nullptr, status, s);
+        ck("rmsnorm_quant_kernel");
+        ck("w1a8_gemv:gate_up", launch_linear(c->plan_gu, L.gu, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(), R,
+                      c->gu.as<float>(), nullptr, status, s));
         bnn::eng::swiglu_quant_kernel<<<R, 512, (size_t)F * 5u, s>>>(c->gu.as<float>(), F, qout(c, F));
-        launch_linear(c->plan_down, L.down, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(),
-                      R, c->x.as<float>(), c->x.as<float>(), status, s);
+        ck("swiglu_quant_kernel");
+        ck("w1a8_gemv:down", launch_linear(c->plan_down, L.down, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(),
+                      R, c->x.as<float>(), c->x.as<float>(), status, s));
     }
     if (with_logits) {
         bnn::eng::rmsnorm_quant_kernel<<<R, 512, norm_smem, s>>>(c->x.as<float>(), m->out_norm.as<float>(),
                                                                  m->eps, C, qout(c, C), status, exact);
-        launch_linear(c->plan_head, m->lm_head, c->act.as<uint32_t>(), c->totals.as<int32_t>(),
-                      c->rscale.as<float>(), R, c->logits.as<float>(), nullptr, status, s);
+        ck("rmsnorm_quant_kernel");
+        ck("w1a8_gemv:lm_head", launch_linear(c->plan_head, m->lm_head, c->act.as<uint32_t>(), c->totals.as<int32_t>(),
+                      c->rscale.as<float>(), R, c->logits.as<float>(), nullptr, status, s));
         bnn::eng::argmax_kernel<<<R, 1024, 0, s>>>(c->logits.as<float>(), in.n_vocab, c->tok_next.as<int32_t>(),
                                                   status);
+        ck("argmax_kernel");
     }
     bnn::eng::step_end_kernel<<<1, 32 * ((R + 31) / 32), 0, s>>>(
         R, c->pos_d.as<uint32_t>(), c->tok_in.as<int32_t>(), c->tok_next.as<int32_t>(), c->hist.as<int32_t>(),
         c->hist_count.as<uint32_t>(), c->hist_cap, with_logits ? 1 : 0);
-    return cudaGetLastError();
+    ck("step_end_kernel");
+    const cudaError_t tail = cudaGetLastError();
+    if (tail != cudaSuccess && ck.err == cudaSuccess)
+        ck.err = tail;
+    if (with_logits)
+        c->step_launches = ck.launches;
+    return ck.err;
 }
 
 BNND_Status capture_step(bnnd_context* c, bool with_logits, cudaGraphExec_t* out) {
     cudaGraph_t graph = nullptr;
     CUDA_OR(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), BNND_EIO);
+    LaunchCheck ck;
+    g_check = &ck;
+    if (g_rec)
+        cudaEventRecordWithFlags(g_rec->events[0], c->stream, cudaEventRecordExternal);
     cudaError_t e = enqueue_step(c, with_logits);
+    g_check = nullptr;
     cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
     if (e != cudaSuccess || e2 != cudaSuccess) {
         if (graph)
             cudaGraphDestroy(graph);
         cudaGetLastError();
-        return fail(BNND_EIO, "decode step capture failed: %s",
+        return fail(BNND_EIO, "decode step capture failed at %s: %s", ck.what ? ck.what : "end",
                     cudaGetErrorString(e != cudaSuccess ? e : e2));
     }
     e = cudaGraphInstantiate(out, graph, 0);
@@ -637,12 +712,13 @@ BNND_Status create_llm_context(bnnd_context* c) {
     c->plan_gu = bnn::plan_contract(sms, 2 * F, C / 128, R, 1);
     c->plan_down = bnn::plan_contract(sms, C, F / 128, R, 1);
     c->plan_head = bnn::plan_contract(sms, in.n_vocab, C / 128, R, 1);
-    const size_t norm_smem = (size_t)std::max(C, F) * 9u;
-    cudaFuncSetAttribute(bnn::eng::rmsnorm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)norm_smem);
-    cudaFuncSetAttribute(bnn::eng::quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)norm_smem);
-    cudaFuncSetAttribute(bnn::eng::swiglu_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)norm_smem);
-    cudaFuncSetAttribute(bnn::eng::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)((in.head_dim + c->n_ctx) * 4));
+    // Per-function limits, set to the most any context of this library needs.
+    if (std::max(C, F) * 9u > 200u * 1024u || (in.head_dim + c->n_ctx) * 4u > 200u * 1024u)
+        return fail(BNND_ENOTSUP, "hidden/ffn width or context too large for one block");
+    cudaFuncSetAttribute(bnn::eng::rmsnorm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(bnn::eng::quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(bnn::eng::swiglu_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(bnn::eng::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if ((st = capture_step(c, true, &c->graph_logits)) || (st = capture_step(c, false, &c->graph_prefill)))
         return st;
     return BNND_OK;
@@ -656,9 +732,10 @@ BNND_Status create_mlp_context(bnnd_context* c) {
         (st = dev_alloc(c->act, (size_t)R * D)) || (st = dev_alloc(c->totals, (size_t)R * (D / 128 + 1) * 4)) ||
         (st = dev_alloc(c->rscale, (size_t)R * 4)) || (st = dev_alloc(c->status, 4)))
         return st;
+    CUDA_OR(cudaMemset(c->status.p, 0, 4), BNND_EIO);
     for (const auto& l : m->mlp)
         c->plan_mlp.push_back(bnn::plan_contract(m->dev->sm_count, l->w.out, l->w.in / 128, R, 1));
-    cudaFuncSetAttribute(bnn::eng::quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(D * 5));
+    cudaFuncSetAttribute(bnn::eng::quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     return BNND_OK;
 }
 
@@ -707,13 +784,21 @@ BNND_Status decode(bnnd_context* c, const int32_t* tokens, uint32_t n, float* lo
             return st;
         c->tok_seq_cap = count;
     }
-    // Step-major layout: entry [i][row] is row's i-th token.
-    std::vector<int32_t> seq(count);
+    if (c->h_tokens_cap < count) {
+        if (c->h_tokens)
+            cudaFreeHost(c->h_tokens);
+        c->h_tokens = nullptr;
+        c->h_tokens_cap = 0;
+        CUDA_OR(cudaMallocHost(&c->h_tokens, count * 4), BNND_ENOMEM);
+        c->h_tokens_cap = count;
+    }
+    // Step-major layout in pinned staging: entry [i][row] is row's i-th token.
+    int32_t* seq = c->h_tokens;
     for (uint32_t r = 0; r < c->rows; ++r)
         for (uint32_t i = 0; i < n; ++i)
             seq[(size_t)i * c->rows + r] = tokens[(size_t)r * n + i];
     const uint32_t start = c->pos;
-    CUDA_OR(cudaMemcpyAsync(c->tok_seq.p, seq.data(), count * 4, cudaMemcpyHostToDevice, c->stream), BNND_EIO);
+    CUDA_OR(cudaMemcpyAsync(c->tok_seq.p, seq, count * 4, cudaMemcpyHostToDevice, c->stream), BNND_EIO);
     const bool want = logits || next;
     for (uint32_t i = 0; i < n; ++i) {
         CUDA_OR(cudaMemcpyAsync(c->tok_in.p, c->tok_seq.as<int32_t>() + (size_t)i * c->rows, c->rows * 4,
@@ -727,9 +812,11 @@ BNND_Status decode(bnnd_context* c, const int32_t* tokens, uint32_t n, float* lo
                                 cudaMemcpyDeviceToHost, c->stream),
                 BNND_EIO);
     if (next)
-        CUDA_OR(cudaMemcpyAsync(next, c->tok_next.p, (size_t)c->rows * 4, cudaMemcpyDeviceToHost, c->stream),
+        CUDA_OR(cudaMemcpyAsync(c->h_next, c->tok_next.p, (size_t)c->rows * 4, cudaMemcpyDeviceToHost, c->stream),
                 BNND_EIO);
     BNND_Status st = finish(c, "BNND_Decode");
+    if (st == BNND_OK && next)
+        std::memcpy(next, c->h_next, (size_t)c->rows * 4);
     if (st != BNND_OK) {
         set_pos(c, start);  // the KV cache returns to the position before the call
         return st;
@@ -815,7 +902,8 @@ BNND_Status BNND_ContextCreate(BNND_Model model, const BNND_ContextParams* param
         return fail(BNND_ERANGE, "n_batch above 1024 is not supported");
     bnn::DeviceGuard guard(model->dev->ordinal);
     c->stream = model->dev->stream;
-    if (cudaMallocHost(&c->h_status, 4) != cudaSuccess) {
+    if (cudaMallocHost(&c->h_status, 4) != cudaSuccess ||
+        cudaMallocHost(&c->h_next, (size_t)c->rows * 4) != cudaSuccess) {
         cudaGetLastError();
         return fail(BNND_ENOMEM, "pinned allocation failed");
     }
@@ -950,6 +1038,84 @@ BNND_Status BNND_Classify(BNND_Context c, const float* input, uint32_t n_samples
     CUDA_OR(cudaMemcpyAsync(logits, cur, outputs * 4, cudaMemcpyDeviceToHost, s), BNND_EIO);
     return finish(c, "BNND_Classify");
 }
+
+BNND_Status BNND_ContextProfile(BNND_Context c, uint32_t steps, BNND_KernelStat* stats, uint32_t capacity,
+                                uint32_t* count, double* total_ms) {
+    g_last_error.clear();
+    if (count)
+        *count = 0;
+    if (!c || steps == 0 || (!stats && capacity))
+        return BNND_EINVAL;
+    if (c->model->info.task != BNND_TASK_LLM)
+        return fail(BNND_ENOTSUP, "model is not a language model");
+    if (!c->have_logits)
+        return fail(BNND_EINVAL, "BNND_ContextProfile needs a preceding decode with logits");
+    if (c->pos > c->n_ctx || steps > c->n_ctx - c->pos)
+        return fail(BNND_ERANGE, "profiling exceeds context length");
+    bnn::DeviceGuard guard(c->model->dev->ordinal);
+    StepRecorder& rec = c->recorder;
+    if (!c->graph_profile) {
+        const size_t n_events = (size_t)c->step_launches + 2;
+        rec.stream = c->stream;
+        rec.events.resize(n_events);
+        rec.names.assign(n_events, std::string());
+        rec.bytes.assign(n_events, 0.0);
+        for (cudaEvent_t& e : rec.events)
+            CUDA_OR(cudaEventCreate(&e), BNND_EIO);
+        rec.next = 0;
+        g_rec = &rec;
+        BNND_Status st = capture_step(c, true, &c->graph_profile);
+        g_rec = nullptr;
+        if (st != BNND_OK)
+            return st;
+        if (rec.overflow)
+            return fail(BNND_EIO, "profile recorder overflow");
+    }
+    const uint32_t start = c->pos;
+    CUDA_OR(cudaMemcpyAsync(c->tok_in.p, c->tok_next.p, (size_t)c->rows * 4, cudaMemcpyDeviceToDevice, c->stream),
+            BNND_EIO);
+    std::vector<std::string> names;
+    std::vector<BNND_KernelStat> acc;
+    double total = 0.0;
+    for (uint32_t step = 0; step < steps; ++step) {
+        CUDA_OR(cudaGraphLaunch(c->graph_profile, c->stream), BNND_EIO);
+        CUDA_OR(cudaStreamSynchronize(c->stream), BNND_EIO);
+        for (size_t i = 0; i < rec.next; ++i) {
+            float ms = 0.0f;
+            CUDA_OR(cudaEventElapsedTime(&ms, rec.events[i], rec.events[i + 1]), BNND_EIO);
+            total += ms;
+            size_t k = 0;
+            while (k < names.size() && names[k] != rec.names[i])
+                ++k;
+            if (k == names.size()) {
+                names.push_back(rec.names[i]);
+                BNND_KernelStat z{};
+                std::snprintf(z.name, sizeof z.name, "%s", rec.names[i].c_str());
+                acc.push_back(z);
+            }
+            if (step == 0)
+                acc[k].launches += 1;
+            acc[k].ms += ms;
+            acc[k].bytes += rec.bytes[i];
+        }
+    }
+    BNND_Status st = finish(c, "BNND_ContextProfile");
+    if (st != BNND_OK) {
+        set_pos(c, start);
+        return st;
+    }
+    c->pos = start + steps;
+    const uint32_t n = (uint32_t)std::min<size_t>(acc.size(), capacity);
+    for (uint32_t i = 0; i < n; ++i)
+        stats[i] = acc[i];
+    if (count)
+        *count = n;
+    if (total_ms)
+        *total_ms = total;
+    return BNND_OK;
+}
+
+uint32_t BNND_StepLaunches(BNND_Context ctx) { return ctx ? ctx->step_launches : 0; }
 
 const char* BNND_LastError(void) { return g_last_error.c_str(); }
 

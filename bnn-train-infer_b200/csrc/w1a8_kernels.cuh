@@ -395,7 +395,9 @@ inline ContractLaunch plan_contract(int sm_count, uint32_t n, uint32_t groups, u
     c.tiles = (nblocks + c.consumers - 1) / c.consumers;
     int occ = 1;
     const void* fn = mode == 0 ? (const void*)w1a8_contract_kernel<0> : (const void*)w1a8_contract_kernel<1>;
-    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
+    // The attribute is per function, shared by every matrix's launches: set it
+    // to the whole budget rather than this plan's need.
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBudget);
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, (int)(c.consumers + 1) * 32, c.smem) != cudaSuccess ||
         occ < 1)
         occ = 1;

@@ -107,6 +107,27 @@ BNND_Status BNND_Classify(BNND_Context ctx, const float* input, uint32_t n_sampl
 /* Thread-local text of the last failure (BNNE_LastError, bnn-engine.h:157). */
 const char* BNND_LastError(void);
 
+/* Device time per kernel of the decode step, for measurement. Has no
+ * counterpart in the reference (its BNNE_Stats splits host wall time only,
+ * bnn-engine.h:76-87). */
+typedef struct {
+    char name[32];      /* kernel (W1A8 linears as "w1a8_gemv:<linear>") */
+    uint32_t launches;  /* launches per step */
+    double ms;          /* device time summed over the profiled steps */
+    double bytes;       /* algorithmic bytes summed over the profiled steps; for
+                           a linear N*K*0.140625 + 4K + 4N per launch and row */
+} BNND_KernelStat;
+
+/* Runs `steps` greedy decode steps (as BNND_Generate, advancing the context)
+ * through an instrumented copy of the step graph with a timestamp between
+ * every pair of launches, and returns one entry per kernel name (at most
+ * `capacity`, *count set to the number written) plus the summed step time. */
+BNND_Status BNND_ContextProfile(BNND_Context ctx, uint32_t steps, BNND_KernelStat* stats,
+                                uint32_t capacity, uint32_t* count, double* total_ms);
+
+/* Number of kernel launches in one decode step with logits. */
+uint32_t BNND_StepLaunches(BNND_Context ctx);
+
 /* The CUDA stream the context's work runs on (cudaStream_t as void*). */
 void* BNND_ContextStream(BNND_Context ctx);
 
