@@ -40,6 +40,30 @@ int bnn_b200_device_ordinal(BNN_Device device);
  * pointers to their own kernels). */
 void* bnn_b200_buffer_device_ptr(BNN_Buffer buffer);
 
+/* GEMM_F32 that allocates nothing. No counterpart in the reference.
+ *
+ * For callers that cannot let a library allocate device memory while they
+ * run: programs whose framework allocator already holds the GPU's free
+ * memory, or hot loops that cannot absorb cudaMalloc's implicit device-wide
+ * synchronisation. BNN_Execute may cudaMalloc its per-job scratch; this call
+ * uses a fixed scratch array compiled into the library instead (136 KiB on
+ * every GPU that loads it, held until the process exits).
+ *
+ * x: device pointer to rows x in_features packed FP32 inputs; y: device
+ * pointer to rows x out_features packed FP32 outputs. Same quantisation and
+ * arithmetic as BNN_OP_GEMM_F32 (bit-identical results), synchronous on the
+ * matrix's device. Limits: rows <= 16 and in_features <= 8192; larger jobs
+ * return BNN_ERANGE without running (use BNN_Execute). Other statuses as
+ * BNN_Execute: BNN_EINVAL for NULL arguments or rows == 0, BNN_ERANGE for a
+ * NaN/Inf input (y untouched), BNN_ENOTSUP when the FP rounding mode is not
+ * to-nearest, BNN_EIO on a CUDA failure.
+ *
+ * The first call on a device looks up the scratch's device address there
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the one scratch array and it keeps the last call's
+ * contents: calls that overlap on the GPU race and must be serialised. */
+BNN_Status bnn_b200_gemm_f32_noalloc(BNN_Matrix matrix, const float* x, uint32_t rows, float* y);
+
 #ifdef __cplusplus
 }
 #endif
