@@ -4,9 +4,9 @@
 // Argument checks follow the reference soft backend's order exactly so every
 // misuse returns the same status code (soft-bnn-accelerator.c:310-603); the
 // work itself runs on the device:
-//   BNN_MatrixCreate -> device copy of the bits, repacked by w1a8_repack_kernel
+//   BNN_MatrixCreate -> device copy of bits and scales, packed by w1a8_pack_kernel
 //   BNN_Execute      -> w1a8_prep_kernel (validate + quantise every row), then
-//                       w1a8_contract_kernel, then one synchronous status read.
+//                       w1a8_gemv_kernel, then one synchronous status read.
 // A rejected input is detected by the prep kernel before the contraction
 // kernel writes anything, so the output stays untouched (bnn-accelerator.h:201).
 #include <cfenv>
@@ -19,7 +19,7 @@
 
 #include "bnn_b200_ext.h"
 #include "bnn_internal.h"
-#include "w1a8_kernels.cuh"
+#include "w1a8_prep.cuh"
 
 namespace {
 
@@ -232,31 +232,32 @@ static BNN_Status bnn_b200_matrix_create_limited(BNN_Device device, const BNN_Ma
     const uint32_t groups = desc->in_features / kGroupSize;
     size_t nblocks = (desc->out_features + bnn::kRowBlock - 1) / bnn::kRowBlock;
     nblocks = (nblocks + bnn::kBlockPad - 1) / bnn::kBlockPad * bnn::kBlockPad;
-    const size_t packed_bytes = nblocks * groups * bnn::kRowBlock * 16u;
+    const size_t packed_bytes = nblocks * bnn::block_bytes(groups);
     uint8_t* raw = nullptr;
-    if (cudaMalloc(&m->wbits, packed_bytes) != cudaSuccess ||
-        cudaMalloc(&m->scales, scale_bytes) != cudaSuccess ||
-        cudaMalloc(&raw, weight_bytes) != cudaSuccess) {
+    uint16_t* raw_scales = nullptr;
+    if (cudaMalloc(&m->wblocks, packed_bytes) != cudaSuccess || cudaMalloc(&raw, weight_bytes) != cudaSuccess ||
+        cudaMalloc(&raw_scales, scale_bytes) != cudaSuccess) {
         cudaGetLastError();
-        if (m->wbits) cudaFree(m->wbits);
-        if (m->scales) cudaFree(m->scales);
+        if (m->wblocks) cudaFree(m->wblocks);
         if (raw) cudaFree(raw);
+        if (raw_scales) cudaFree(raw_scales);
         delete m;
         return BNN_ENOMEM;
     }
     cudaStream_t s = device->stream;
     bool ok = cudaMemcpyAsync(raw, desc->weight_bits, weight_bytes, cudaMemcpyHostToDevice, s) == cudaSuccess &&
-              cudaMemcpyAsync(m->scales, desc->scale_fp16, scale_bytes, cudaMemcpyHostToDevice, s) == cudaSuccess;
+              cudaMemcpyAsync(raw_scales, desc->scale_fp16, scale_bytes, cudaMemcpyHostToDevice, s) == cudaSuccess;
     if (ok) {
         const size_t chunks = nblocks * groups * bnn::kRowBlock;
         const unsigned grid = (unsigned)std::min<size_t>((chunks + 255) / 256, 148u * 16u);
-        bnn::w1a8_repack_kernel<<<grid, 256, 0, s>>>(raw, desc->out_features, groups, nblocks, m->wbits);
+        bnn::w1a8_pack_kernel<<<grid, 256, 0, s>>>(raw, raw_scales, desc->out_features, groups, nblocks,
+                                                   m->wblocks);
         ok = cudaGetLastError() == cudaSuccess && cudaStreamSynchronize(s) == cudaSuccess;
     }
     cudaFree(raw);
+    cudaFree(raw_scales);
     if (!ok) {
-        cudaFree(m->wbits);
-        cudaFree(m->scales);
+        cudaFree(m->wblocks);
         delete m;
         return BNN_EIO;
     }
@@ -279,8 +280,7 @@ void BNN_MatrixDestroy(BNN_Matrix matrix) {
     bnn::DeviceGuard guard(matrix->owner->ordinal);
     cudaStreamSynchronize(matrix->owner->stream);
     --matrix->owner->matrix_count;
-    cudaFree(matrix->wbits);
-    cudaFree(matrix->scales);
+    cudaFree(matrix->wblocks);
     delete matrix;
 }
 
@@ -441,27 +441,26 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
         bnn::w1a8_prep_kernel<<<rows, bnn::kPrepThreads, prep_smem, s>>>(chunk);
     }
 
-    const int mode = job->operation == BNN_OP_DOT_GROUPS ? 0 : 1;
-    const bnn::ContractLaunch cl = bnn::plan_contract(device->sm_count, m->out_features, G, M, mode);
+    const int epi = job->operation == BNN_OP_DOT_GROUPS ? bnn::kEpiDotGroups : bnn::kEpiView;
+    const bnn::GemvLaunch cl = bnn::plan_gemv(device->sm_count, m->out_features, G, M, bnn::kProSliced, epi);
     const uint32_t rows_per_launch = 65535u * bnn::kRowsPerCta;
     for (uint32_t r0 = 0; r0 < M; r0 += rows_per_launch) {
         const uint32_t rows = std::min<uint32_t>(M - r0, rows_per_launch);
-        bnn::ContractArgs ca;
-        ca.wbits = m->wbits;
-        ca.scales = m->scales;
-        ca.act = act + (size_t)r0 * G * bnn::kWordsPerGroup;
-        ca.totals = totals + (size_t)r0 * G;
-        ca.row_scale = in_type == BNN_TYPE_F32 ? rscale + r0 : nullptr;
-        ca.status = device->d_status;
-        ca.n = m->out_features;
-        ca.groups = G;
-        ca.m = rows;
-        ca.out = job->output.buffer->data + job->output.offset + (size_t)r0 * out_stride;
-        ca.out_stride = out_stride;
-        ca.residual = nullptr;
-        ca.tiles = cl.tiles;
-        ca.stages = cl.stages;
-        if (bnn::launch_contract(cl, (rows + bnn::kRowsPerCta - 1) / bnn::kRowsPerCta, mode, ca, s) != cudaSuccess)
+        bnn::GemvArgs ga = {};
+        ga.wblocks = m->wblocks;
+        ga.n = m->out_features;
+        ga.groups = G;
+        ga.m = rows;
+        ga.tiles = cl.tiles;
+        ga.stages = cl.stages;
+        ga.blocks_per_tile = cl.blocks_per_tile;
+        ga.act = act + (size_t)r0 * G * bnn::kWordsPerGroup;
+        ga.totals = totals + (size_t)r0 * G;
+        ga.row_scale = in_type == BNN_TYPE_F32 ? rscale + r0 : nullptr;
+        ga.out = job->output.buffer->data + job->output.offset + (size_t)r0 * out_stride;
+        ga.out_stride = out_stride;
+        ga.status = device->d_status;
+        if (bnn::launch_gemv(cl, rows, ga, s, false) != cudaSuccess)
             return BNN_EIO;
     }
     if (cudaGetLastError() != cudaSuccess)

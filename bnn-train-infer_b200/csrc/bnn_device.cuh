@@ -61,6 +61,15 @@ __device__ __forceinline__ void store_i16_any(unsigned char* p, int16_t x) {
     p[1] = (unsigned char)(v >> 8);
 }
 
+// Programmatic dependent launch. launch_dependents lets the next kernel of
+// the stream be scheduled as soon as every CTA of this one has started;
+// wait blocks until the preceding kernel has completed and its writes are
+// visible. Both are no-ops for kernels launched without the PDL attribute.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Smallest positive binary32 subnormal (FLT_TRUE_MIN).
 __device__ __forceinline__ float flt_true_min() { return __uint_as_float(1u); }
 

@@ -25,8 +25,7 @@ struct bnn_accel_matrix {
     uint32_t in_features;
     uint32_t out_features;
     uint32_t groups;
-    uint4* wbits;             // repacked 8-row blocks
-    uint16_t* scales;         // [N][G] binary16
+    unsigned char* wblocks;   // packed 8-row blocks: sign bits + scales (w1a8_gemv.cuh)
 };
 
 struct bnn_accel_buffer {

@@ -23,7 +23,7 @@
 
 #include "bnn_b200_ext.h"
 #include "bnn_internal.h"
-#include "w1a8_kernels.cuh"
+#include "w1a8_prep.cuh"
 
 namespace {
 
@@ -103,23 +103,23 @@ extern "C" BNN_Status bnn_b200_gemm_f32_noalloc(BNN_Matrix matrix, const float* 
                          (int)bnn::prep_smem_bytes(kNoAllocMaxK));
     bnn::w1a8_prep_kernel<<<rows, bnn::kPrepThreads, bnn::prep_smem_bytes(K), s>>>(pa);
 
-    const bnn::ContractLaunch cl = bnn::plan_contract(device->sm_count, matrix->out_features, G, rows, 1);
-    bnn::ContractArgs ca;
-    ca.wbits = matrix->wbits;
-    ca.scales = matrix->scales;
-    ca.act = act;
-    ca.totals = totals;
-    ca.row_scale = rscale;
-    ca.status = status;
-    ca.n = matrix->out_features;
-    ca.groups = G;
-    ca.m = rows;
-    ca.out = reinterpret_cast<unsigned char*>(y);
-    ca.out_stride = (size_t)matrix->out_features * 4u;
-    ca.residual = nullptr;
-    ca.tiles = cl.tiles;
-    ca.stages = cl.stages;
-    if (bnn::launch_contract(cl, (rows + bnn::kRowsPerCta - 1) / bnn::kRowsPerCta, 1, ca, s) != cudaSuccess)
+    const bnn::GemvLaunch cl =
+        bnn::plan_gemv(device->sm_count, matrix->out_features, G, rows, bnn::kProSliced, bnn::kEpiView);
+    bnn::GemvArgs ga = {};
+    ga.wblocks = matrix->wblocks;
+    ga.n = matrix->out_features;
+    ga.groups = G;
+    ga.m = rows;
+    ga.tiles = cl.tiles;
+    ga.stages = cl.stages;
+    ga.blocks_per_tile = cl.blocks_per_tile;
+    ga.act = act;
+    ga.totals = totals;
+    ga.row_scale = rscale;
+    ga.out = reinterpret_cast<unsigned char*>(y);
+    ga.out_stride = (size_t)matrix->out_features * 4u;
+    ga.status = status;
+    if (bnn::launch_gemv(cl, rows, ga, s, false) != cudaSuccess)
         return BNN_EIO;
     int verdict = 0;
     if (cudaMemcpyAsync(&verdict, status, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||

@@ -12,10 +12,13 @@
 // device-resident state, captured once per context as a CUDA graph; the
 // position and input token live in device memory so one graph serves every
 // step. Per layer:
-//   rmsnorm_quant -> W1A8(q|k|v) -> qk_norm_rope(+KV append) -> attention
-//   -> quant -> W1A8(o, x += o) -> rmsnorm_quant -> W1A8(gate|up)
-//   -> swiglu_quant -> W1A8(down, x += d)
-// then rmsnorm_quant -> W1A8(lm_head) -> argmax -> step_end.
+//   W1A8(RMSNorm -> q|k|v) -> qk_norm_rope(+KV append) -> attention
+//   -> W1A8(quantise y -> o, x += o) -> W1A8(RMSNorm -> gate|up -> SwiGLU h)
+//   -> W1A8(quantise h -> down, x += d)
+// then W1A8(RMSNorm -> lm_head) -> argmax -> step_end. The RMSNorm and the
+// row quantisation run inside each linear's prologue; the W1A8 linears are
+// launched with programmatic dependent launch so their weight streaming
+// overlaps the preceding kernel.
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -30,7 +33,7 @@
 #include "bnn_internal.h"
 #include "engine_kernels.cuh"
 #include "gguf_reader.h"
-#include "w1a8_kernels.cuh"
+#include "w1a8_gemv.cuh"
 
 namespace {
 
@@ -197,6 +200,23 @@ BNND_Status read_q1_0(const bnn::GgufFile& g, const std::string& name, uint32_t 
     return BNND_OK;
 }
 
+// Reorders a [gate(F); up(F)] row stack into alternating 8-row blocks
+// (gate 0-7, up 0-7, gate 8-15, ...) for the SwiGLU epilogue, which pairs
+// block 2p (gate) with block 2p+1 (up). Row order does not change any output.
+void interleave_blocks(HostW1* h, uint32_t f) {
+    const size_t rb = h->in / 8, sg = h->in / 128;
+    std::vector<uint8_t> bits(h->bits.size());
+    std::vector<uint16_t> scales(h->scales.size());
+    for (uint32_t row = 0; row < 2 * f; ++row) {
+        const uint32_t up = row >= f, r = up ? row - f : row;
+        const size_t dst = (size_t)(r / 8) * 16 + (up ? 8 : 0) + r % 8;
+        std::memcpy(&bits[dst * rb], &h->bits[(size_t)row * rb], rb);
+        std::memcpy(&scales[dst * sg], &h->scales[(size_t)row * sg], sg * 2);
+    }
+    h->bits.swap(bits);
+    h->scales.swap(scales);
+}
+
 BNND_Status upload_w1(BNN_Device dev, const HostW1& h, Linear* l) {
     BNN_MatrixDesc d;
     d.in_features = h.in;
@@ -274,13 +294,14 @@ struct bnnd_context {
     BNND_ContextParams params{};
     uint32_t rows = 1, n_ctx = 0, pos = 0;
     cudaStream_t stream = nullptr;
-    DevMem x, act, totals, rscale, qkv, y, gu, logits, kcache, vcache, rope_cos, rope_sin;
+    DevMem x, qkv, y, h, logits, kcache, vcache, rope_cos, rope_sin;
     DevMem pos_d, tok_in, tok_next, tok_seq, hist, hist_count, status;
     DevMem mlp_a, mlp_b;
     size_t tok_seq_cap = 0;
     uint32_t hist_cap = 0;
-    bnn::ContractLaunch plan_qkv{}, plan_o{}, plan_gu{}, plan_down{}, plan_head{};
-    std::vector<bnn::ContractLaunch> plan_mlp;
+    bnn::GemvLaunch plan_qkv{}, plan_o{}, plan_gu{}, plan_down{}, plan_head{};
+    std::vector<bnn::GemvLaunch> plan_mlp;
+    bool pdl = true;  // launch the W1A8 linears with programmatic dependent launch
     cudaGraphExec_t graph_logits = nullptr, graph_prefill = nullptr, graph_profile = nullptr;
     StepRecorder recorder;
     uint32_t step_launches = 0;
@@ -382,6 +403,8 @@ BNND_Status load_qwen3(const bnn::GgufFile& g, bnnd_model* m) {
         return fail(BNND_EFORMAT, "Qwen3 KV width is not group aligned");
     if (HD > 1024)
         return fail(BNND_ENOTSUP, "head_dim above 1024 is not supported");
+    if (C > bnn::kMaxPrologueK || FF > bnn::kMaxPrologueK)
+        return fail(BNND_ENOTSUP, "hidden or ffn width above %u is not supported", bnn::kMaxPrologueK);
     BNND_ModelInfo& info = m->info;
     info.task = BNND_TASK_LLM;
     info.n_layers = (uint32_t)L;
@@ -428,6 +451,7 @@ BNND_Status load_qwen3(const bnn::GgufFile& g, bnnd_model* m) {
             (st = read_q1_0(g, p + "ffn_up.weight", C, FF, &gu)) != BNND_OK ||
             (st = read_q1_0(g, p + "ffn_down.weight", FF, C, &down)) != BNND_OK)
             return st;
+        interleave_blocks(&gu, (uint32_t)FF);
         if ((st = upload_w1(m->dev, qkv, &layer->qkv)) != BNND_OK ||
             (st = upload_w1(m->dev, o, &layer->o)) != BNND_OK ||
             (st = upload_w1(m->dev, gu, &layer->gu)) != BNND_OK ||
@@ -453,6 +477,8 @@ BNND_Status load_mlp(const bnn::GgufFile& g, bnnd_model* m) {
     if (blocks == 0 || blocks > 64 || in == 0 || in > UINT32_MAX || in % 128 != 0 || classes == 0 ||
         classes > UINT32_MAX || (pixels && pixels > in) || !(stdv > 0.0f))
         return fail(BNND_EFORMAT, "unsupported bnn-mlp metadata");
+    if (in > bnn::kMaxPrologueK)
+        return fail(BNND_ENOTSUP, "bnn-mlp input width above %u is not supported", bnn::kMaxPrologueK);
     uint32_t expected = (uint32_t)in, max_dim = (uint32_t)in;
     uint64_t weights = 0;
     for (uint32_t i = 0; i < blocks; ++i) {
@@ -463,6 +489,8 @@ BNND_Status load_mlp(const bnn::GgufFile& g, bnnd_model* m) {
             t->dims[1] > UINT32_MAX)
             return fail(BNND_EFORMAT, "missing or invalid Q1_0 tensor '%sweight'", p.c_str());
         const uint32_t lin = (uint32_t)t->dims[0], lout = (uint32_t)t->dims[1];
+        if (lout > bnn::kMaxPrologueK && i + 1 < blocks)
+            return fail(BNND_ENOTSUP, "bnn-mlp hidden width above %u is not supported", bnn::kMaxPrologueK);
         if (lin != expected)
             return fail(BNND_EFORMAT, "layer %u input width %u does not match previous output %u", i, lin,
                         expected);
@@ -525,35 +553,28 @@ void rope_tables(const bnnd_model* m, uint32_t n_ctx, std::vector<float>* cs, st
     }
 }
 
-cudaError_t launch_linear(const bnn::ContractLaunch& cl, const Linear& l, const uint32_t* act,
-                          const int32_t* totals, const float* rs, uint32_t rows, float* out,
-                          const float* residual, int* status, cudaStream_t s) {
-    bnn::ContractArgs a;
-    a.wbits = l.m->wbits;
-    a.scales = l.m->scales;
-    a.act = act;
-    a.totals = totals;
-    a.row_scale = rs;
-    a.status = status;
+// One W1A8 linear: FP32 input rows x (stride l.in), RMSNorm gains when the
+// plan's prologue normalises, output rows of `out_stride` bytes.
+cudaError_t launch_linear(const bnnd_context* c, const bnn::GemvLaunch& cl, const Linear& l, const float* x,
+                          const float* gain, uint32_t rows, float* out, size_t out_stride, int* status) {
+    bnn::GemvArgs a = {};
+    a.wblocks = l.m->wblocks;
     a.n = l.out;
     a.groups = l.in / 128;
     a.m = rows;
-    a.out = reinterpret_cast<unsigned char*>(out);
-    a.out_stride = (size_t)l.out * 4u;
-    a.residual = residual;
     a.tiles = cl.tiles;
     a.stages = cl.stages;
+    a.blocks_per_tile = cl.blocks_per_tile;
+    a.x = x;
+    a.x_stride = l.in;
+    a.gain = gain;
+    a.eps = c->model->eps;
+    a.exact = c->params.exact;
+    a.out = reinterpret_cast<unsigned char*>(out);
+    a.out_stride = out_stride;
+    a.status = status;
     g_next_bytes = ((double)l.out * l.in * 0.140625 + 4.0 * l.in + 4.0 * l.out) * rows;
-    return bnn::launch_contract(cl, (rows + bnn::kRowsPerCta - 1) / bnn::kRowsPerCta, 1, a, s);
-}
-
-bnn::eng::QuantOut qout(bnnd_context* c, uint32_t k) {
-    bnn::eng::QuantOut q;
-    q.act = c->act.as<uint32_t>();
-    q.totals = c->totals.as<int32_t>();
-    q.row_scale = c->rscale.as<float>();
-    q.act_groups = k / 128;
-    return q;
+    return bnn::launch_gemv(cl, rows, a, c->stream, c->pdl);
 }
 
 // Enqueues one decode step for every row (tokens already in tok_in).
@@ -566,17 +587,14 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
     cudaStream_t s = c->stream;
     int* status = c->status.as<int>();
     const int exact = c->params.exact;
-    const size_t norm_smem = (size_t)C * 9u;
-    bnn::eng::embed_kernel<<<R, 256, 0, s>>>(c->tok_in.as<int32_t>(), m->lm_head.m->wbits,
-                                             m->lm_head.m->scales, C, c->x.as<float>());
+    bnn::eng::embed_kernel<<<R, 256, 0, s>>>(c->tok_in.as<int32_t>(), m->lm_head.m->wblocks, C, c->x.as<float>());
     ck("embed_kernel");
+    const size_t qkv_pitch = (size_t)(C + 2 * KV) * 4u;
     for (uint32_t l = 0; l < in.n_layers; ++l) {
         const QwenLayer& L = *m->layers[l];
-        bnn::eng::rmsnorm_quant_kernel<<<R, 512, norm_smem, s>>>(c->x.as<float>(), L.attn_norm.as<float>(),
-                                                                 m->eps, C, qout(c, C), status, exact);
-        ck("rmsnorm_quant_kernel");
-        ck("w1a8_gemv:qkv", launch_linear(c->plan_qkv, L.qkv, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(),
-                      R, c->qkv.as<float>(), nullptr, status, s));
+        // attn_norm + q|k|v projections (prologue: RMSNorm + quantise)
+        ck("w1a8_gemv:qkv", launch_linear(c, c->plan_qkv, L.qkv, c->x.as<float>(), L.attn_norm.as<float>(), R,
+                                          c->qkv.as<float>(), qkv_pitch, status));
         bnn::eng::QkArgs qa;
         qa.qkv = c->qkv.as<float>();
         qa.q_norm = L.q_norm.as<float>();
@@ -615,26 +633,19 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
         aa.status = status;
         bnn::eng::attention_kernel<<<dim3(in.heads, R), 256, (size_t)(HD + c->n_ctx) * 4, s>>>(aa);
         ck("attention_kernel");
-        bnn::eng::quant_kernel<<<R, 512, (size_t)C * 5u, s>>>(c->y.as<float>(), C, qout(c, C));
-        ck("quant_kernel");
-        ck("w1a8_gemv:o", launch_linear(c->plan_o, L.o, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(), R,
-                      c->x.as<float>(), c->x.as<float>(), status, s));
-        bnn::eng::rmsnorm_quant_kernel<<<R, 512, norm_smem, s>>>(c->x.as<float>(), L.ffn_norm.as<float>(),
-                                                                 m->eps, C, qout(c, C), status, exact);
-        ck("rmsnorm_quant_kernel");
-        ck("w1a8_gemv:gate_up", launch_linear(c->plan_gu, L.gu, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(), R,
-                      c->gu.as<float>(), nullptr, status, s));
-        bnn::eng::swiglu_quant_kernel<<<R, 512, (size_t)F * 5u, s>>>(c->gu.as<float>(), F, qout(c, F));
-        ck("swiglu_quant_kernel");
-        ck("w1a8_gemv:down", launch_linear(c->plan_down, L.down, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(),
-                      R, c->x.as<float>(), c->x.as<float>(), status, s));
+        // attn_output, x += o (prologue: quantise the attention output)
+        ck("w1a8_gemv:o", launch_linear(c, c->plan_o, L.o, c->y.as<float>(), nullptr, R, c->x.as<float>(),
+                                        (size_t)C * 4u, status));
+        // ffn_norm + gate|up + SwiGLU -> h
+        ck("w1a8_gemv:gate_up", launch_linear(c, c->plan_gu, L.gu, c->x.as<float>(), L.ffn_norm.as<float>(), R,
+                                              c->h.as<float>(), (size_t)F * 4u, status));
+        // ffn_down, x += d (prologue: quantise h)
+        ck("w1a8_gemv:down", launch_linear(c, c->plan_down, L.down, c->h.as<float>(), nullptr, R, c->x.as<float>(),
+                                           (size_t)C * 4u, status));
     }
     if (with_logits) {
-        bnn::eng::rmsnorm_quant_kernel<<<R, 512, norm_smem, s>>>(c->x.as<float>(), m->out_norm.as<float>(),
-                                                                 m->eps, C, qout(c, C), status, exact);
-        ck("rmsnorm_quant_kernel");
-        ck("w1a8_gemv:lm_head", launch_linear(c->plan_head, m->lm_head, c->act.as<uint32_t>(), c->totals.as<int32_t>(),
-                      c->rscale.as<float>(), R, c->logits.as<float>(), nullptr, status, s));
+        ck("w1a8_gemv:lm_head", launch_linear(c, c->plan_head, m->lm_head, c->x.as<float>(), m->out_norm.as<float>(),
+                                              R, c->logits.as<float>(), (size_t)in.n_vocab * 4u, status));
         bnn::eng::argmax_kernel<<<R, 1024, 0, s>>>(c->logits.as<float>(), in.n_vocab, c->tok_next.as<int32_t>(),
                                                   status);
         ck("argmax_kernel");
@@ -681,13 +692,10 @@ BNND_Status create_llm_context(bnnd_context* c) {
     const bnnd_model* m = c->model;
     const BNND_ModelInfo& in = m->info;
     const uint32_t C = in.hidden, F = in.ffn, KV = in.kv_heads * in.head_dim, R = c->rows;
-    const uint32_t gmax = std::max(C, F) / 128;
     BNND_Status st;
     const size_t cache = (size_t)in.n_layers * R * c->n_ctx * KV * 4u;
-    if ((st = dev_alloc(c->x, (size_t)R * C * 4)) || (st = dev_alloc(c->act, (size_t)R * gmax * 128)) ||
-        (st = dev_alloc(c->totals, (size_t)R * gmax * 4)) || (st = dev_alloc(c->rscale, (size_t)R * 4)) ||
-        (st = dev_alloc(c->qkv, (size_t)R * (C + 2 * KV) * 4)) || (st = dev_alloc(c->y, (size_t)R * C * 4)) ||
-        (st = dev_alloc(c->gu, (size_t)R * 2 * F * 4)) ||
+    if ((st = dev_alloc(c->x, (size_t)R * C * 4)) || (st = dev_alloc(c->qkv, (size_t)R * (C + 2 * KV) * 4)) ||
+        (st = dev_alloc(c->y, (size_t)R * C * 4)) || (st = dev_alloc(c->h, (size_t)R * F * 4)) ||
         (st = dev_alloc(c->logits, (size_t)R * in.n_vocab * 4)) || (st = dev_alloc(c->kcache, cache)) ||
         (st = dev_alloc(c->vcache, cache)) || (st = dev_alloc(c->pos_d, (size_t)R * 4)) ||
         (st = dev_alloc(c->tok_in, (size_t)R * 4)) || (st = dev_alloc(c->tok_next, (size_t)R * 4)) ||
@@ -707,17 +715,16 @@ BNND_Status create_llm_context(bnnd_context* c) {
     CUDA_OR(cudaMemset(c->hist_count.p, 0, 4), BNND_EIO);
     CUDA_OR(cudaMemset(c->status.p, 0, 4), BNND_EIO);
     const int sms = m->dev->sm_count;
-    c->plan_qkv = bnn::plan_contract(sms, C + 2 * KV, C / 128, R, 1);
-    c->plan_o = bnn::plan_contract(sms, C, C / 128, R, 1);
-    c->plan_gu = bnn::plan_contract(sms, 2 * F, C / 128, R, 1);
-    c->plan_down = bnn::plan_contract(sms, C, F / 128, R, 1);
-    c->plan_head = bnn::plan_contract(sms, in.n_vocab, C / 128, R, 1);
-    // Per-function limits, set to the most any context of this library needs.
-    if (std::max(C, F) * 9u > 200u * 1024u || (in.head_dim + c->n_ctx) * 4u > 200u * 1024u)
-        return fail(BNND_ENOTSUP, "hidden/ffn width or context too large for one block");
-    cudaFuncSetAttribute(bnn::eng::rmsnorm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    cudaFuncSetAttribute(bnn::eng::quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    cudaFuncSetAttribute(bnn::eng::swiglu_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    c->plan_qkv = bnn::plan_gemv(sms, C + 2 * KV, C / 128, R, bnn::kProRmsNorm, bnn::kEpiView);
+    c->plan_o = bnn::plan_gemv(sms, C, C / 128, R, bnn::kProQuant, bnn::kEpiResidual);
+    c->plan_gu = bnn::plan_gemv(sms, 2 * F, C / 128, R, bnn::kProRmsNorm, bnn::kEpiSwiGLU);
+    c->plan_down = bnn::plan_gemv(sms, C, F / 128, R, bnn::kProQuant, bnn::kEpiResidual);
+    c->plan_head = bnn::plan_gemv(sms, in.n_vocab, C / 128, R, bnn::kProRmsNorm, bnn::kEpiView);
+    for (const bnn::GemvLaunch* p : {&c->plan_qkv, &c->plan_o, &c->plan_gu, &c->plan_down, &c->plan_head})
+        if (p->smem > bnn::kGemvSmemBudget)
+            return fail(BNND_ENOTSUP, "hidden/ffn width too large for the contraction kernel");
+    if ((in.head_dim + c->n_ctx) * 4u > 200u * 1024u)
+        return fail(BNND_ENOTSUP, "context too large for one attention block");
     cudaFuncSetAttribute(bnn::eng::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if ((st = capture_step(c, true, &c->graph_logits)) || (st = capture_step(c, false, &c->graph_prefill)))
         return st;
@@ -729,13 +736,15 @@ BNND_Status create_mlp_context(bnnd_context* c) {
     const uint32_t R = c->rows, D = m->mlp_max_dim;
     BNND_Status st;
     if ((st = dev_alloc(c->mlp_a, (size_t)R * D * 4)) || (st = dev_alloc(c->mlp_b, (size_t)R * D * 4)) ||
-        (st = dev_alloc(c->act, (size_t)R * D)) || (st = dev_alloc(c->totals, (size_t)R * (D / 128 + 1) * 4)) ||
-        (st = dev_alloc(c->rscale, (size_t)R * 4)) || (st = dev_alloc(c->status, 4)))
+        (st = dev_alloc(c->status, 4)))
         return st;
     CUDA_OR(cudaMemset(c->status.p, 0, 4), BNND_EIO);
-    for (const auto& l : m->mlp)
-        c->plan_mlp.push_back(bnn::plan_contract(m->dev->sm_count, l->w.out, l->w.in / 128, R, 1));
-    cudaFuncSetAttribute(bnn::eng::quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    for (const auto& l : m->mlp) {
+        c->plan_mlp.push_back(
+            bnn::plan_gemv(m->dev->sm_count, l->w.out, l->w.in / 128, R, bnn::kProQuant, bnn::kEpiView));
+        if (c->plan_mlp.back().smem > bnn::kGemvSmemBudget)
+            return fail(BNND_ENOTSUP, "layer width too large for the contraction kernel");
+    }
     return BNND_OK;
 }
 
@@ -749,6 +758,8 @@ BNND_Status finish(bnnd_context* c, const char* what) {
         cudaStreamSynchronize(c->stream);
         if (st & bnn::kStatusTimeout)
             return fail(BNND_EIO, "%s: device wait timed out", what);
+        if (st == bnn::kStatusBadInput)  // a linear's FP32 input held NaN/Inf (BNN_ERANGE)
+            return fail(BNND_ERANGE, "%s: linear input contains NaN or Inf", what);
         return fail(BNND_ECOMPUTE, "%s: model produced NaN or Inf values", what);
     }
     return BNND_OK;
@@ -1024,17 +1035,15 @@ BNND_Status BNND_Classify(BNND_Context c, const float* input, uint32_t n_samples
     CUDA_OR(cudaMemcpyAsync(cur, input, inputs * 4, cudaMemcpyHostToDevice, s), BNND_EIO);
     for (size_t i = 0; i < m->mlp.size(); ++i) {
         const MlpLayer& L = *m->mlp[i];
-        bnn::eng::quant_kernel<<<n_samples, 512, (size_t)L.w.in * 5u, s>>>(cur, L.w.in, qout(c, L.w.in));
-        const bnn::ContractLaunch& cl = c->plan_mlp[i];
-        CUDA_OR(launch_linear(cl, L.w, c->act.as<uint32_t>(), c->totals.as<int32_t>(), c->rscale.as<float>(),
-                              n_samples, nxt, nullptr, c->status.as<int>(), s),
+        CUDA_OR(launch_linear(c, c->plan_mlp[i], L.w, cur, nullptr, n_samples, nxt, (size_t)L.w.out * 4u,
+                              c->status.as<int>()),
                 BNND_EIO);
         bnn::eng::mlp_post_kernel<<<64, 256, 0, s>>>(nxt, L.post_scale.as<float>(), L.post_bias.as<float>(),
                                                      L.w.out, n_samples, L.relu);
         std::swap(cur, nxt);
     }
     const size_t outputs = (size_t)n_samples * m->info.n_classes;
-    bnn::eng::finite_check_kernel<<<16, 256, 0, s>>>(cur, outputs, c->status.as<int>(), bnn::eng::kStatusNonFinite);
+    bnn::eng::finite_check_kernel<<<16, 256, 0, s>>>(cur, outputs, c->status.as<int>(), bnn::kStatusNonFinite);
     CUDA_OR(cudaMemcpyAsync(logits, cur, outputs * 4, cudaMemcpyDeviceToHost, s), BNND_EIO);
     return finish(c, "BNND_Classify");
 }

@@ -4,15 +4,14 @@
 // FP32 operation order (bnn-sw-v2/qwen3/qwen3.c, bnn-mlp/bnn-mlp.c), using
 // explicit round-to-nearest intrinsics so nothing is fused or reassociated:
 //   embed_kernel            qwen3_embed               qwen3.c:374-385
-//   rmsnorm_quant_kernel    qwen3_rmsnorm + QuantizeRow  qwen3.c:361-372, soft :175-211
 //   qk_norm_rope_kernel     per-head q/k RMSNorm, RoPE, KV append  qwen3.c:418-438
 //   attention_kernel        causal softmax attention  qwen3.c:440-478
-//   swiglu_quant_kernel     SwiGLU + QuantizeRow      qwen3.c:491-495
-//   quant_kernel            QuantizeRow of a vector (attention output)
 //   argmax_kernel           greedy pick + finite check  bnn-infer-v2.c:48-54, engine.c:262-267
 //   mlp_post_kernel         post_scale/bias + ReLU    bnn-mlp.c:189-193
-// In exact mode every long sum is accumulated serially in index order, as
-// the reference does; fast mode uses a fixed-order tree instead.
+// RMSNorm before a linear, the row quantisation and SwiGLU run inside the
+// W1A8 linears (w1a8_gemv.cuh prologues/epilogues). In exact mode every long
+// sum is accumulated serially in index order, as the reference does; fast
+// mode uses a fixed-order tree instead.
 #pragma once
 
 #include <cstdint>
@@ -41,7 +40,7 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 // Sum of `vals[0..n)` (shared memory). exact: serial in index order by
 // thread 0 (the reference's loop); otherwise a fixed-order tree. The result
 // is returned to every thread.
-__device__ float block_sum_ordered(const float* vals, uint32_t n, bool exact, float* red) {
+static __device__ float block_sum_ordered(const float* vals, uint32_t n, bool exact, float* red) {
     __syncthreads();
     if (exact) {
         if (threadIdx.x == 0) {
@@ -72,122 +71,21 @@ __device__ float block_sum_ordered(const float* vals, uint32_t n, bool exact, fl
     return red[0];
 }
 
-// QuantizeRow of a shared-memory vector and the sliced layout + totals the
-// contraction kernel consumes (all threads of the block participate).
-__device__ void quantize_and_slice(const float* v, uint32_t k, int8_t* qs, uint32_t* act,
-                                   int32_t* totals, float* row_scale, float* red) {
-    float amax = 0.0f;
-    for (uint32_t i = threadIdx.x; i < k; i += blockDim.x)
-        amax = fmaxf(amax, fabsf(v[i]));
-    amax = block_max(amax, red);
-    const float s = row_scale_from_absmax(amax);
-    const RowQuantizer quant(s);
-    for (uint32_t i = threadIdx.x; i < k; i += blockDim.x)
-        qs[i] = quant(v[i]);
-    __syncthreads();
-    const uint32_t groups = k / kGroup;
-    for (uint32_t w = threadIdx.x; w < groups * kWordsPerGroup; w += blockDim.x) {
-        const uint32_t g = w / kWordsPerGroup, tj = w % kWordsPerGroup;
-        act[w] = pack_slice(qs + g * kGroup, tj >> 3, tj & 7u);
-    }
-    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (uint32_t g = warp; g < groups; g += nw) {
-        const int8_t* qg = qs + g * kGroup + lane * 4u;
-        int t = (int)qg[0] + (int)qg[1] + (int)qg[2] + (int)qg[3];
-        for (int o = 16; o > 0; o >>= 1)
-            t += __shfl_xor_sync(0xffffffffu, t, o);
-        if (lane == 0)
-            totals[g] = t;
-    }
-    if (threadIdx.x == 0)
-        *row_scale = s;
-}
-
-struct QuantOut {
-    uint32_t* act;      // [rows][act_groups][32]
-    int32_t* totals;    // [rows][act_groups]
-    float* row_scale;   // [rows]
-    uint32_t act_groups;  // row pitch of act/totals, in groups
-};
-
-// qwen3_embed: x[c] = bit ? scale : -scale, read from the repacked lm_head
-// (token_embd and lm_head are the same tied matrix).
-__global__ void embed_kernel(const int32_t* tokens, const uint4* wbits, const uint16_t* scales,
-                             uint32_t c, float* x) {
+// qwen3_embed: x[c] = bit ? scale : -scale, read from lm_head's packed
+// blocks (token_embd and lm_head are the same tied matrix).
+__global__ void embed_kernel(const int32_t* tokens, const unsigned char* wblocks, uint32_t c, float* x) {
     const uint32_t row = blockIdx.x;
     const uint32_t tok = (uint32_t)tokens[row];
     const uint32_t groups = c / kGroup;
-    const uint32_t blk = tok / kRowBlock, r = tok % kRowBlock;
+    const uint32_t r = tok % kRowBlock;
+    const unsigned char* blk = wblocks + (size_t)(tok / kRowBlock) * groups * 144u;
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(blk + (size_t)groups * 128u) + (size_t)r * groups;
     for (uint32_t k = threadIdx.x; k < c; k += blockDim.x) {
         const uint32_t g = k / kGroup, b = k % kGroup;
-        const uint4 u = wbits[((size_t)blk * groups + g) * kRowBlock + r];
-        const uint32_t words[4] = {u.x, u.y, u.z, u.w};
-        const uint32_t bit = (words[b >> 5] >> (b & 31)) & 1u;
-        const float sc = h2f(scales[(size_t)tok * groups + g]);
-        x[(size_t)row * c + k] = bit ? sc : -sc;
+        const uint32_t word = reinterpret_cast<const uint32_t*>(blk + (g * kRowBlock + r) * 16u)[b >> 5];
+        const float scale = h2f(sc[g]);
+        x[(size_t)row * c + k] = ((word >> (b & 31)) & 1u) ? scale : -scale;
     }
-}
-
-// qwen3_rmsnorm (sum of squares, sqrtf(sum/n + eps), x / rms * gain) then the
-// full-row quantiser of the next linear's input. One block per row.
-__global__ void rmsnorm_quant_kernel(const float* x, const float* gain, float eps, uint32_t c,
-                                     QuantOut q, int* status, int exact) {
-    extern __shared__ __align__(16) unsigned char e_smem[];
-    float* xs = reinterpret_cast<float*>(e_smem);
-    float* sq = xs + c;
-    int8_t* qs = reinterpret_cast<int8_t*>(sq + c);
-    __shared__ float red[64];
-    const uint32_t row = blockIdx.x;
-    for (uint32_t i = threadIdx.x; i < c; i += blockDim.x) {
-        const float v = x[(size_t)row * c + i];
-        xs[i] = v;
-        sq[i] = __fmul_rn(v, v);
-    }
-    const float sum = block_sum_ordered(sq, c, exact != 0, red);
-    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)c), eps));
-    if (!isfinite(rms) || rms == 0.0f) {
-        if (threadIdx.x == 0)
-            atomicOr(status, kStatusNonFinite);
-        return;
-    }
-    for (uint32_t i = threadIdx.x; i < c; i += blockDim.x)
-        xs[i] = __fmul_rn(__fdiv_rn(xs[i], rms), gain[i]);
-    __syncthreads();
-    quantize_and_slice(xs, c, qs, q.act + (size_t)row * q.act_groups * kWordsPerGroup,
-                       q.totals + (size_t)row * q.act_groups, q.row_scale + row, red);
-}
-
-// QuantizeRow of a plain vector (the attention output feeding attn_output).
-__global__ void quant_kernel(const float* v, uint32_t k, QuantOut q) {
-    extern __shared__ __align__(16) unsigned char e_smem[];
-    float* vs = reinterpret_cast<float*>(e_smem);
-    int8_t* qs = reinterpret_cast<int8_t*>(vs + k);
-    __shared__ float red[64];
-    const uint32_t row = blockIdx.x;
-    for (uint32_t i = threadIdx.x; i < k; i += blockDim.x)
-        vs[i] = v[(size_t)row * k + i];
-    __syncthreads();
-    quantize_and_slice(vs, k, qs, q.act + (size_t)row * q.act_groups * kWordsPerGroup,
-                       q.totals + (size_t)row * q.act_groups, q.row_scale + row, red);
-}
-
-// SwiGLU (silu(g) = g / (1 + expf(-g)), times up) then QuantizeRow for ffn_down.
-// gu: [rows][2F], gate in [0, F), up in [F, 2F).
-__global__ void swiglu_quant_kernel(const float* gu, uint32_t f, QuantOut q) {
-    extern __shared__ __align__(16) unsigned char e_smem[];
-    float* hs = reinterpret_cast<float*>(e_smem);
-    int8_t* qs = reinterpret_cast<int8_t*>(hs + f);
-    __shared__ float red[64];
-    const uint32_t row = blockIdx.x;
-    const float* g = gu + (size_t)row * 2u * f;
-    for (uint32_t i = threadIdx.x; i < f; i += blockDim.x) {
-        const float v = g[i];
-        const float silu = __fdiv_rn(v, __fadd_rn(1.0f, expf_cr(-v)));
-        hs[i] = __fmul_rn(silu, g[f + i]);
-    }
-    __syncthreads();
-    quantize_and_slice(hs, f, qs, q.act + (size_t)row * q.act_groups * kWordsPerGroup,
-                       q.totals + (size_t)row * q.act_groups, q.row_scale + row, red);
 }
 
 struct QkArgs {

@@ -1,0 +1,534 @@
+// w1a8_gemv.cuh - the W1A8 contraction (ComputeRow, soft-bnn-accelerator.c:219-276).
+//
+// Packed weight layout (written once by w1a8_pack_kernel): blocks of 8 output
+// rows; block b is G*144 bytes:
+//     [G][8][16 B]  sign bits of row 8b+r, group g, public bit order
+//     [8][G]        binary16 scales of row 8b+r, group g
+// A tile of B = 1, 2 or 4 consecutive blocks is one contiguous range that the
+// producer warp streams into shared memory with a single 1D bulk copy, bits
+// and scales together. Allocations are padded to kBlockPad blocks.
+//
+// Activations are int8 "sliced" words: per row and group 32 words, word
+// (t, j) = t*8 + j packs q[g*128 + 32t + 8i + j], i = 0..3. Masking weight
+// word t with (0x01010101 << j) keeps, in byte i, the weight bit that meets
+// exactly that activation, scaled by 2^j; dp4a sums 2^j * q over those four
+// weights, the eight slices are kept apart, and
+//     pos = sum_j acc_j >> j,   D = 2 * pos - total    (soft :251-258).
+// The FP32 epilogue then runs acc = fl(acc + fl(F32(scale_g) * D_g)) in
+// increasing g, one lane per (activation row, output row) (soft :260-274).
+//
+// Prologues (where the int8 activations come from):
+//   kProSliced   pre-sliced words/totals/row scales in global memory (BNN_Execute)
+//   kProQuant    FP32 rows, quantised in the CTA (QuantizeRow, soft :175-211)
+//   kProRmsNorm  FP32 rows, RMSNorm (qwen3.c:361-372) then quantised
+// Epilogues (what is written):
+//   kEpiDotGroups  int16 D into a BNN view          (DOT_GROUPS)
+//   kEpiView       FP32 Z or Z*s into a BNN view    (GEMV/GEMM[_F32])
+//   kEpiResidual   x[n] = fl(x[n] + Y)              (qwen3.c:482-483, 498-499)
+//   kEpiSwiGLU     h = fl(fl(g / fl(1 + exp(-g))) * u) over gate/up block pairs
+//                  (qwen3.c:491-495); the matrix stores gate and up rows in
+//                  alternating 8-row blocks
+//
+// Pipeline: persistent CTAs of 4 compute warps + 1 producer warp. The
+// producer starts streaming weights at once (they never depend on earlier
+// kernels), before the compute warps wait for the preceding kernel
+// (programmatic dependent launch) and build the activations. 4/B warps share
+// one block, each taking a subset of its groups (the integer D's meet in
+// shared memory, so the FP32 order is unchanged); small matrices use B = 1 so
+// that every SM gets blocks. All waits are bounded.
+#pragma once
+
+#include <cstdint>
+#include "bnn_device.cuh"
+#include "bnn_sync.cuh"
+#include "exact_sum.cuh"
+
+namespace bnn {
+
+constexpr int kRowsPerCta = 8;      // activation rows per CTA (grid y covers more)
+constexpr int kStatusBadInput = 1;  // an input row had NaN/Inf (F32) or -128 (I8)
+constexpr int kStatusNonFinite = 4; // a normalisation divisor was not finite
+constexpr uint32_t kBlockPad = 4;
+constexpr uint32_t kComputeWarps = 4;
+
+enum Prologue : int { kProSliced = 0, kProQuant = 1, kProRmsNorm = 2 };
+enum Epilogue : int { kEpiDotGroups = 0, kEpiView = 1, kEpiResidual = 2, kEpiSwiGLU = 3 };
+
+__host__ __device__ inline size_t block_bytes(uint32_t groups) { return (size_t)groups * 144u; }
+
+// Public [N][K/8] bits + [N][G] scales -> packed blocks (rows past N zero).
+static __global__ void w1a8_pack_kernel(const uint8_t* __restrict__ bits, const uint16_t* __restrict__ scales,
+                                        uint32_t n, uint32_t groups, size_t nblocks,
+                                        unsigned char* __restrict__ out) {
+    const size_t bb = block_bytes(groups);
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t first = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    const size_t chunks = nblocks * groups * kRowBlock;
+    for (size_t i = first; i < chunks; i += stride) {
+        const size_t r = i % kRowBlock, g = (i / kRowBlock) % groups, b = i / (kRowBlock * groups);
+        const size_t row = b * kRowBlock + r;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (row < n) {
+            const uint8_t* src = bits + row * (groups * 16u) + g * 16u;
+            uint32_t w[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+                w[t] = (uint32_t)src[4 * t] | ((uint32_t)src[4 * t + 1] << 8) |
+                       ((uint32_t)src[4 * t + 2] << 16) | ((uint32_t)src[4 * t + 3] << 24);
+            v = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        *reinterpret_cast<uint4*>(out + b * bb + (g * kRowBlock + r) * 16u) = v;
+    }
+    const size_t nscales = nblocks * kRowBlock * groups;
+    for (size_t i = first; i < nscales; i += stride) {
+        const size_t g = i % groups, r = (i / groups) % kRowBlock, b = i / (kRowBlock * groups);
+        const size_t row = b * kRowBlock + r;
+        const uint16_t sc = row < n ? scales[row * groups + g] : (uint16_t)0;
+        *reinterpret_cast<uint16_t*>(out + b * bb + (size_t)groups * 128u + (r * groups + g) * 2u) = sc;
+    }
+}
+
+struct GemvArgs {
+    const unsigned char* wblocks;  // packed blocks (see header)
+    uint32_t n, groups, m;         // packed output rows, K/128, activation rows
+    uint32_t tiles, stages;        // tiles of B blocks; shared-memory ring depth
+    uint32_t blocks_per_tile;      // B = 1, 2 or 4
+    // kProSliced
+    const uint32_t* act;           // [M][G][32]
+    const int32_t* totals;         // [M][G]
+    const float* row_scale;        // [M]; nullptr: the I8 ops return Z unscaled
+    // kProQuant / kProRmsNorm
+    const float* x;                // FP32 rows
+    size_t x_stride;               // floats between rows
+    const float* gain;             // kProRmsNorm gains [K]
+    float eps;
+    int exact;                     // 1: the reference's serial sum for RMSNorm
+    // output
+    unsigned char* out;            // first logical output row
+    size_t out_stride;             // bytes between output rows
+    int* status;
+};
+
+struct GemvSmem {
+    size_t bars, rs, act, tot, xbuf, qbuf, seg, dsm, epi, stage, total;
+};
+
+__host__ __device__ inline GemvSmem gemv_smem_plan(uint32_t groups, uint32_t mrows, uint32_t bpt,
+                                                   uint32_t stages, int pro, int epi) {
+    GemvSmem p;
+    p.bars = 0;     // full[stages], empty[stages] (stages <= 8)
+    p.rs = 128;     // row scales + status flags
+    p.act = 256;
+    p.tot = p.act + (size_t)mrows * groups * kActStride * 4u;
+    p.xbuf = (p.tot + (size_t)mrows * groups * 4u + 15) & ~(size_t)15;  // float4 stores
+    p.qbuf = p.xbuf + (pro != kProSliced ? (size_t)groups * kGroup * 4u : 0);  // FP32 row
+    p.seg = p.qbuf + (pro != kProSliced ? (size_t)groups * kGroup : 0);          // int8 row
+    p.dsm = p.seg + (pro == kProRmsNorm ? 32u * kSegMax * sizeof(SumSeg) + 128u : 0);
+    p.epi = p.dsm + (epi != kEpiDotGroups ? (size_t)bpt * mrows * kRowBlock * groups * 2u : 0);
+    p.epi = (p.epi + 15) & ~(size_t)15;
+    p.stage = p.epi + (epi == kEpiSwiGLU ? (size_t)bpt * mrows * kRowBlock * 4u : 0);
+    p.stage = (p.stage + 127) & ~(size_t)127;
+    p.total = p.stage + (size_t)stages * bpt * block_bytes(groups);
+    return p;
+}
+
+// Integer part of one (row, group) unit for one activation row.
+__device__ __forceinline__ int group_dot(const uint32_t (&mk)[32], const uint32_t* act_s, int total) {
+    int acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        acc[j] = 0;
+    const uint4* a4 = reinterpret_cast<const uint4*>(act_s);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const uint4 lo = a4[t * 2], hi = a4[t * 2 + 1];
+        acc[0] = dp4a_us(mk[t * 8 + 0], lo.x, acc[0]);
+        acc[1] = dp4a_us(mk[t * 8 + 1], lo.y, acc[1]);
+        acc[2] = dp4a_us(mk[t * 8 + 2], lo.z, acc[2]);
+        acc[3] = dp4a_us(mk[t * 8 + 3], lo.w, acc[3]);
+        acc[4] = dp4a_us(mk[t * 8 + 4], hi.x, acc[4]);
+        acc[5] = dp4a_us(mk[t * 8 + 5], hi.y, acc[5]);
+        acc[6] = dp4a_us(mk[t * 8 + 6], hi.z, acc[6]);
+        acc[7] = dp4a_us(mk[t * 8 + 7], hi.w, acc[7]);
+    }
+    // 128 * pos = sum_j acc_j * 2^(7-j): acc_j is an exact multiple of 2^j.
+    int pos128 = acc[7];
+#pragma unroll
+    for (int j = 6; j >= 0; --j)
+        pos128 += acc[j] << (7 - j);
+    return (pos128 >> 6) - total;
+}
+
+// The reference's RMSNorm sum fl(...fl(fl(x0*x0) + x1*x1)...) in index order:
+// exact mode reproduces it bit for bit with warp 0 (exact_sum.cuh); fast mode
+// uses a fixed-order tree over the compute threads. Returns it to every
+// compute thread.
+static __device__ float rms_sum(const float* xs, uint32_t k, bool exact, uint32_t nthreads, float* red,
+                                SumSeg* seg, int* cnt) {
+    const uint32_t tid = threadIdx.x;
+    if (exact) {
+        if (tid < 32) {
+            const float s = exact_sumsq_warp(xs, (int)k, seg, cnt);
+            if (tid == 0)
+                red[0] = s;
+        }
+    } else {
+        float s = 0.0f;
+        for (uint32_t i = tid; i < k; i += nthreads)
+            s = __fadd_rn(s, __fmul_rn(xs[i], xs[i]));
+        for (int o = 16; o > 0; o >>= 1)
+            s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+        if ((tid & 31) == 0)
+            red[1 + (tid >> 5)] = s;
+        named_barrier(1, nthreads);
+        if (tid == 0) {
+            float t = 0.0f;
+            for (uint32_t w = 0; w < nthreads / 32; ++w)
+                t = __fadd_rn(t, red[1 + w]);
+            red[0] = t;
+        }
+    }
+    named_barrier(1, nthreads);
+    return red[0];
+}
+
+template <int PRO, int EPI>
+__global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
+    griddep_launch_dependents();
+    extern __shared__ __align__(128) unsigned char sm[];
+    const uint32_t G = a.groups;
+    const uint32_t consumers = kComputeWarps;
+    const uint32_t cthreads = consumers * 32;
+    const uint32_t bpt = a.blocks_per_tile, wpb = kComputeWarps / bpt;
+    const uint32_t m0 = blockIdx.y * kRowsPerCta;
+    const uint32_t mrows = min((uint32_t)kRowsPerCta, a.m - m0);
+    const GemvSmem plan = gemv_smem_plan(G, mrows, bpt, a.stages, PRO, EPI);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + plan.bars);
+    uint64_t* empty = full + a.stages;
+    float* rs_s = reinterpret_cast<float*>(sm + plan.rs);          // [8] row scales
+    int* flags = reinterpret_cast<int*>(sm + plan.rs + 32);        // [0] abort
+    float* red = reinterpret_cast<float*>(sm + plan.rs + 64);      // reduction slots (16)
+    uint32_t* act_s = reinterpret_cast<uint32_t*>(sm + plan.act);
+    int32_t* tot_s = reinterpret_cast<int32_t*>(sm + plan.tot);
+    float* xbuf = reinterpret_cast<float*>(sm + plan.xbuf);
+    uint32_t* qbuf = reinterpret_cast<uint32_t*>(sm + plan.qbuf);
+    SumSeg* seg = reinterpret_cast<SumSeg*>(sm + plan.seg);
+    int* seg_cnt = reinterpret_cast<int*>(sm + plan.seg + 32u * kSegMax * sizeof(SumSeg));
+    int16_t* dsm = reinterpret_cast<int16_t*>(sm + plan.dsm);
+    float* epi_s = reinterpret_cast<float*>(sm + plan.epi);
+    unsigned char* stage0 = sm + plan.stage;
+    const uint32_t bb = (uint32_t)block_bytes(G);
+    const uint32_t tile_bytes = bpt * bb;
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    if (tid == 0) {
+        for (uint32_t s = 0; s < a.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], consumers);
+        }
+        fence_barrier_init();
+        flags[0] = 0;
+    }
+    __syncthreads();
+
+    if (warp == consumers) {  // producer warp: weights never depend on earlier kernels
+        if (lane == 0) {
+            uint32_t i = 0;
+            for (uint32_t tile = blockIdx.x; tile < a.tiles; tile += gridDim.x, ++i) {
+                const uint32_t s = i % a.stages;
+                if (i >= a.stages && !mbar_wait(&empty[s], ((i / a.stages) - 1) & 1)) {
+                    atomicOr(a.status, kStatusTimeout);
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[s], tile_bytes);
+                bulk_g2s(stage0 + (size_t)s * tile_bytes, a.wblocks + (size_t)tile * tile_bytes, tile_bytes,
+                         &full[s]);
+            }
+            // No bulk copy may still be in flight when the CTA exits.
+            for (uint32_t j = i > a.stages ? i - a.stages : 0; j < i; ++j)
+                if (!mbar_wait(&full[j % a.stages], (j / a.stages) & 1))
+                    atomicOr(a.status, kStatusTimeout);
+        }
+        return;
+    }
+
+    // ---- consumers: wait for the producers of our activations, then build them
+    griddep_wait();
+    if (tid == 0 && *a.status != 0)
+        flags[0] = 1;  // an earlier kernel failed: skip the work, keep the protocol
+    if (PRO == kProSliced) {
+        for (uint32_t i = tid; i < mrows * G * (kWordsPerGroup / 4); i += cthreads) {
+            const uint32_t mm = i / (G * 8), rest = i % (G * 8), g = rest / 8, c = rest % 8;
+            const uint4* src =
+                reinterpret_cast<const uint4*>(a.act + ((size_t)(m0 + mm) * G + g) * kWordsPerGroup);
+            reinterpret_cast<uint4*>(act_s + (mm * G + g) * kActStride)[c] = src[c];
+        }
+        for (uint32_t i = tid; i < mrows * G; i += cthreads)
+            tot_s[i] = a.totals[(size_t)m0 * G + i];
+        if (tid < mrows)
+            rs_s[tid] = a.row_scale ? a.row_scale[m0 + tid] : 1.0f;
+        named_barrier(1, cthreads);
+    } else {
+        const uint32_t K = G * kGroup;
+        for (uint32_t mm = 0; mm < mrows; ++mm) {
+            const float4* xr = reinterpret_cast<const float4*>(a.x + (size_t)(m0 + mm) * a.x_stride);
+            int bad = 0;
+            for (uint32_t i = tid; i < K / 4; i += cthreads) {
+                const float4 v = xr[i];
+                bad |= !isfinite(v.x) | !isfinite(v.y) | !isfinite(v.z) | !isfinite(v.w);
+                reinterpret_cast<float4*>(xbuf)[i] = v;
+            }
+            // A linear rejects non-finite input (ValidateF32Input, soft :294-308);
+            // before RMSNorm it shows up as a non-finite divisor instead.
+            if (bad && PRO == kProQuant)
+                flags[0] = 2;
+            named_barrier(1, cthreads);
+            if (PRO == kProRmsNorm) {
+                const float sum = rms_sum(xbuf, K, a.exact != 0, cthreads, red, seg, seg_cnt);
+                const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)K), a.eps));
+                if (!isfinite(rms) || rms == 0.0f) {
+                    if (tid == 0) {
+                        flags[0] = 1;
+                        atomicOr(a.status, kStatusNonFinite);
+                    }
+                } else {
+                    for (uint32_t i = tid; i < K; i += cthreads)
+                        xbuf[i] = __fmul_rn(__fdiv_rn(xbuf[i], rms), a.gain[i]);
+                }
+                named_barrier(1, cthreads);
+            }
+            float amax = 0.0f;
+            for (uint32_t i = tid; i < K; i += cthreads)
+                amax = fmaxf(amax, fabsf(xbuf[i]));
+            for (int o = 16; o > 0; o >>= 1)
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            if (lane == 0)
+                red[1 + warp] = amax;
+            named_barrier(1, cthreads);
+            amax = red[1];
+            for (uint32_t w = 1; w < consumers; ++w)
+                amax = fmaxf(amax, red[1 + w]);
+            const float s = row_scale_from_absmax(amax);
+            const RowQuantizer quant(s);
+            // Quantise four consecutive values per thread (coalesced); a warp's
+            // 32 lanes cover exactly one group per pass, so each pass's group
+            // total is one warp reduction, done for all passes together.
+            constexpr uint32_t kMaxPasses = 16;  // K <= 8192
+            int part[kMaxPasses];
+            uint32_t passes = 0;
+            for (uint32_t qi = tid; qi < K / 4; qi += cthreads, ++passes) {
+                const float4 v = reinterpret_cast<const float4*>(xbuf)[qi];
+                const int8_t q0 = quant(v.x), q1 = quant(v.y), q2 = quant(v.z), q3 = quant(v.w);
+                qbuf[qi] = (uint32_t)(uint8_t)q0 | ((uint32_t)(uint8_t)q1 << 8) | ((uint32_t)(uint8_t)q2 << 16) |
+                           ((uint32_t)(uint8_t)q3 << 24);
+                part[passes & (kMaxPasses - 1)] = (int)q0 + (int)q1 + (int)q2 + (int)q3;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (uint32_t p = 0; p < kMaxPasses; ++p)
+                    if (p < passes)
+                        part[p] += __shfl_xor_sync(0xffffffffu, part[p], o);
+            if (lane == 0)
+                for (uint32_t p = 0; p < passes; ++p)
+                    tot_s[mm * G + p * consumers + warp] = part[p];
+            named_barrier(1, cthreads);
+            // Slice: word (t, j) of group g takes byte (j & 3) of the four
+            // int8 words holding q[32t + 8i + j], i = 0..3.
+            for (uint32_t w = tid; w < G * kWordsPerGroup; w += cthreads) {
+                const uint32_t g = w / kWordsPerGroup, tj = w % kWordsPerGroup, t = tj >> 3, j = tj & 7;
+                const uint32_t* qw = qbuf + g * 32u + 8u * t + (j >> 2);
+                const uint32_t b = j & 3u;
+                const uint32_t lo = __byte_perm(qw[0], qw[2], b | ((4u + b) << 4));
+                const uint32_t hi = __byte_perm(qw[4], qw[6], b | ((4u + b) << 4));
+                act_s[(mm * G + g) * kActStride + tj] = __byte_perm(lo, hi, 0x5410);
+            }
+            if (tid == 0)
+                rs_s[mm] = s;
+            named_barrier(1, cthreads);  // xbuf and red are reused by the next row
+        }
+        if (tid == 0 && flags[0] == 2)
+            atomicOr(a.status, kStatusBadInput);
+        named_barrier(1, cthreads);
+    }
+    const bool abort = flags[0] != 0;
+
+    // ---- contraction over this CTA's tiles
+    const uint32_t r = lane & 7;
+    const uint32_t my_block = warp / wpb, part = warp % wpb;
+    int16_t* blk_d = dsm + (size_t)my_block * mrows * kRowBlock * G;
+    uint32_t i = 0;
+    for (uint32_t tile = blockIdx.x; tile < a.tiles; tile += gridDim.x, ++i) {
+        const uint32_t s = i % a.stages;
+        const bool ready = mbar_wait(&full[s], (i / a.stages) & 1);
+        if (!ready && lane == 0)
+            atomicOr(a.status, kStatusTimeout);
+        const bool work = ready && !abort;
+        const uint32_t blk = tile * bpt + my_block;
+        const unsigned char* wblk = stage0 + (size_t)s * tile_bytes + (size_t)my_block * bb;
+        const uint4* wt = reinterpret_cast<const uint4*>(wblk);
+        if (work) {
+            for (uint32_t q = part; q * 4 < G; q += wpb) {
+                const uint32_t g = q * 4 + (lane >> 3);
+                if (g >= G)
+                    continue;
+                const uint4 w = wt[g * kRowBlock + r];
+                uint32_t mk[32];
+                const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        mk[t * 8 + j] = words[t] & (0x01010101u << j);
+                const uint32_t n = blk * kRowBlock + r;
+                for (uint32_t mm = 0; mm < mrows; ++mm) {
+                    const int d = group_dot(mk, act_s + (mm * G + g) * kActStride, tot_s[mm * G + g]);
+                    if (EPI == kEpiDotGroups) {
+                        if (n < a.n)
+                            store_i16_any(a.out + (size_t)(m0 + mm) * a.out_stride + ((size_t)n * G + g) * 2u,
+                                          (int16_t)d);
+                    } else {
+                        blk_d[(mm * kRowBlock + r) * G + g] = (int16_t)d;
+                    }
+                }
+            }
+        }
+        if (EPI != kEpiDotGroups) {
+            named_barrier(1, cthreads);  // every group's D of the tile is in shared memory
+            // Ordered FP32 scale-accumulate, by the first warp of each block;
+            // the scales come from the same stage.
+            const uint16_t* sc_blk = reinterpret_cast<const uint16_t*>(wblk + (size_t)G * 128u);
+            if (part == 0) {
+                for (uint32_t p = lane; p < mrows * kRowBlock; p += 32) {
+                    const uint32_t mm = p / kRowBlock, rr = p % kRowBlock;
+                    const uint32_t n = blk * kRowBlock + rr;
+                    float acc = 0.0f;
+                    if (work && n < a.n) {
+                        const uint16_t* sc = sc_blk + rr * G;
+                        const int16_t* dd = blk_d + (mm * kRowBlock + rr) * G;
+#pragma unroll 8
+                        for (uint32_t g = 0; g < G; ++g)
+                            acc = __fadd_rn(acc, __fmul_rn(h2f(sc[g]), (float)dd[g]));
+                        if (PRO != kProSliced || a.row_scale)
+                            acc = __fmul_rn(acc, rs_s[mm]);
+                        if (EPI == kEpiView) {
+                            store_f32_any(a.out + (size_t)(m0 + mm) * a.out_stride + (size_t)n * 4u, acc);
+                        } else if (EPI == kEpiResidual) {
+                            float* dst = reinterpret_cast<float*>(a.out + (size_t)(m0 + mm) * a.out_stride) + n;
+                            *dst = __fadd_rn(*dst, acc);
+                        }
+                    }
+                    if (EPI == kEpiSwiGLU)
+                        epi_s[(my_block * mrows + mm) * kRowBlock + rr] = acc;
+                }
+            }
+            if (EPI == kEpiSwiGLU) {
+                // Blocks 2k (gate rows) and 2k+1 (up rows) hold the same 8 rows.
+                named_barrier(1, cthreads);
+                if (part == 0 && (my_block & 1) == 0 && work) {
+                    for (uint32_t p = lane; p < mrows * kRowBlock; p += 32) {
+                        const uint32_t mm = p / kRowBlock, rr = p % kRowBlock;
+                        if (blk * kRowBlock + rr >= a.n)
+                            continue;
+                        const float g = epi_s[(my_block * mrows + mm) * kRowBlock + rr];
+                        const float u = epi_s[((my_block + 1) * mrows + mm) * kRowBlock + rr];
+                        const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf_cr(-g)));
+                        reinterpret_cast<float*>(a.out + (size_t)(m0 + mm) * a.out_stride)[(blk / 2) * kRowBlock + rr] =
+                            __fmul_rn(silu, u);
+                    }
+                }
+            }
+            named_barrier(1, cthreads);  // shared D/epilogue buffers and the stage are free again
+        }
+        __syncwarp();
+        if (lane == 0)
+            mbar_arrive(&empty[s]);  // this warp no longer reads the stage
+    }
+}
+
+// Launch shape for one matrix, row count and variant.
+struct GemvLaunch {
+    uint32_t blocks_per_tile, stages, tiles, grid_x;
+    size_t smem;
+    int pro, epi;
+};
+
+using GemvFn = void (*)(GemvArgs);
+
+inline GemvFn gemv_fn(int pro, int epi) {
+    if (pro == kProSliced && epi == kEpiDotGroups) return w1a8_gemv_kernel<kProSliced, kEpiDotGroups>;
+    if (pro == kProSliced && epi == kEpiView) return w1a8_gemv_kernel<kProSliced, kEpiView>;
+    if (pro == kProQuant && epi == kEpiView) return w1a8_gemv_kernel<kProQuant, kEpiView>;
+    if (pro == kProQuant && epi == kEpiResidual) return w1a8_gemv_kernel<kProQuant, kEpiResidual>;
+    if (pro == kProRmsNorm && epi == kEpiView) return w1a8_gemv_kernel<kProRmsNorm, kEpiView>;
+    if (pro == kProRmsNorm && epi == kEpiSwiGLU) return w1a8_gemv_kernel<kProRmsNorm, kEpiSwiGLU>;
+    return nullptr;
+}
+
+constexpr size_t kGemvSmemBudget = 200u * 1024u;
+
+// Blocks per tile so even small matrices spread over every SM (B = 1 gives
+// one block per CTA, its groups split over the 4 compute warps); ring depth
+// that fits the shared-memory budget; persistent grid from the occupancy of
+// that configuration. SwiGLU needs gate/up block pairs in a tile.
+// Prologues that build the activations in the CTA hold up to this many inputs.
+constexpr uint32_t kMaxPrologueK = 8192;
+
+inline GemvLaunch plan_gemv(int sm_count, uint32_t n, uint32_t groups, uint32_t m, int pro, int epi) {
+    const uint32_t nblocks = (n + kRowBlock - 1) / kRowBlock;
+    const uint32_t mrows = m < (uint32_t)kRowsPerCta ? m : (uint32_t)kRowsPerCta;
+    const uint32_t min_bpt = epi == kEpiSwiGLU ? 2u : 1u;
+    GemvLaunch c;
+    c.pro = pro;
+    c.epi = epi;
+    c.blocks_per_tile = nblocks >= 8u * sm_count ? 4u : (nblocks >= 2u * sm_count ? 2u : 1u);
+    if (c.blocks_per_tile < min_bpt)
+        c.blocks_per_tile = min_bpt;
+    c.stages = 4;
+    for (;;) {
+        c.smem = gemv_smem_plan(groups, mrows, c.blocks_per_tile, c.stages, pro, epi).total;
+        if (c.smem <= kGemvSmemBudget)
+            break;
+        if (c.stages > 2)
+            --c.stages;
+        else if (c.blocks_per_tile > min_bpt)
+            c.blocks_per_tile /= 2;
+        else
+            break;
+    }
+    c.tiles = (nblocks + c.blocks_per_tile - 1) / c.blocks_per_tile;
+    int occ = 1;
+    const GemvFn fn = gemv_fn(pro, epi);
+    // The attribute is per function, shared by every matrix's launches.
+    cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvSmemBudget);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, (const void*)fn, (int)(kComputeWarps + 1) * 32,
+                                                      c.smem) != cudaSuccess ||
+        occ < 1)
+        occ = 1;
+    const uint32_t mchunks = (m + kRowsPerCta - 1) / kRowsPerCta;
+    uint32_t slots = (uint32_t)sm_count * (uint32_t)occ;
+    slots = slots > mchunks ? slots / mchunks : 1u;
+    c.grid_x = c.tiles < slots ? c.tiles : slots;
+    return c;
+}
+
+// Launches on `s`; with pdl the launch may overlap the previous kernel of the
+// stream (the kernel waits for it before touching activations).
+inline cudaError_t launch_gemv(const GemvLaunch& c, uint32_t m, const GemvArgs& a, cudaStream_t s, bool pdl) {
+    const GemvFn fn = gemv_fn(c.pro, c.epi);
+    if (!fn)
+        return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c.grid_x, (m + kRowsPerCta - 1) / kRowsPerCta);
+    cfg.blockDim = dim3((kComputeWarps + 1) * 32);
+    cfg.dynamicSmemBytes = c.smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, fn, a);
+}
+
+}  // namespace bnn
