@@ -50,6 +50,10 @@ constexpr int kStatusBadInput = 1;  // an input row had NaN/Inf (F32) or -128 (I
 constexpr int kStatusNonFinite = 4; // a normalisation divisor was not finite
 constexpr uint32_t kBlockPad = 4;
 constexpr uint32_t kComputeWarps = 4;
+static_assert(kComputeWarps * 32 == 128 && kSumHeadWarp == 3, "exact_sumsq runs on the four compute warps");
+// Prologues that build the activations in the CTA hold up to this many inputs
+// (in registers: kMaxPrologueK / 512 float4 per compute thread).
+constexpr uint32_t kMaxPrologueK = 8192;
 
 enum Prologue : int { kProSliced = 0, kProQuant = 1, kProRmsNorm = 2 };
 enum Epilogue : int { kEpiDotGroups = 0, kEpiView = 1, kEpiResidual = 2, kEpiSwiGLU = 3 };
@@ -110,7 +114,7 @@ struct GemvArgs {
 };
 
 struct GemvSmem {
-    size_t bars, rs, act, tot, xbuf, qbuf, seg, dsm, epi, stage, total;
+    size_t bars, rs, act, tot, xbuf, seg, dsm, epi, stage, total;
 };
 
 __host__ __device__ inline GemvSmem gemv_smem_plan(uint32_t groups, uint32_t mrows, uint32_t bpt,
@@ -121,9 +125,8 @@ __host__ __device__ inline GemvSmem gemv_smem_plan(uint32_t groups, uint32_t mro
     p.act = 256;
     p.tot = p.act + (size_t)mrows * groups * kActStride * 4u;
     p.xbuf = (p.tot + (size_t)mrows * groups * 4u + 15) & ~(size_t)15;  // float4 stores
-    p.qbuf = p.xbuf + (pro != kProSliced ? (size_t)groups * kGroup * 4u : 0);  // FP32 row
-    p.seg = p.qbuf + (pro != kProSliced ? (size_t)groups * kGroup : 0);          // int8 row
-    p.dsm = p.seg + (pro == kProRmsNorm ? 32u * kSegMax * sizeof(SumSeg) + 128u : 0);
+    p.seg = p.xbuf + (pro == kProRmsNorm ? (size_t)groups * kGroup * 4u : 0);  // FP32 row
+    p.dsm = p.seg + (pro == kProRmsNorm ? kSumSmemBytes : 0);
     p.epi = p.dsm + (epi != kEpiDotGroups ? (size_t)bpt * mrows * kRowBlock * groups * 2u : 0);
     p.epi = (p.epi + 15) & ~(size_t)15;
     p.stage = p.epi + (epi == kEpiSwiGLU ? (size_t)bpt * mrows * kRowBlock * 4u : 0);
@@ -159,39 +162,6 @@ __device__ __forceinline__ int group_dot(const uint32_t (&mk)[32], const uint32_
     return (pos128 >> 6) - total;
 }
 
-// The reference's RMSNorm sum fl(...fl(fl(x0*x0) + x1*x1)...) in index order:
-// exact mode reproduces it bit for bit with warp 0 (exact_sum.cuh); fast mode
-// uses a fixed-order tree over the compute threads. Returns it to every
-// compute thread.
-static __device__ float rms_sum(const float* xs, uint32_t k, bool exact, uint32_t nthreads, float* red,
-                                SumSeg* seg, int* cnt) {
-    const uint32_t tid = threadIdx.x;
-    if (exact) {
-        if (tid < 32) {
-            const float s = exact_sumsq_warp(xs, (int)k, seg, cnt);
-            if (tid == 0)
-                red[0] = s;
-        }
-    } else {
-        float s = 0.0f;
-        for (uint32_t i = tid; i < k; i += nthreads)
-            s = __fadd_rn(s, __fmul_rn(xs[i], xs[i]));
-        for (int o = 16; o > 0; o >>= 1)
-            s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-        if ((tid & 31) == 0)
-            red[1 + (tid >> 5)] = s;
-        named_barrier(1, nthreads);
-        if (tid == 0) {
-            float t = 0.0f;
-            for (uint32_t w = 0; w < nthreads / 32; ++w)
-                t = __fadd_rn(t, red[1 + w]);
-            red[0] = t;
-        }
-    }
-    named_barrier(1, nthreads);
-    return red[0];
-}
-
 template <int PRO, int EPI>
 __global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
     griddep_launch_dependents();
@@ -211,9 +181,7 @@ __global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
     uint32_t* act_s = reinterpret_cast<uint32_t*>(sm + plan.act);
     int32_t* tot_s = reinterpret_cast<int32_t*>(sm + plan.tot);
     float* xbuf = reinterpret_cast<float*>(sm + plan.xbuf);
-    uint32_t* qbuf = reinterpret_cast<uint32_t*>(sm + plan.qbuf);
-    SumSeg* seg = reinterpret_cast<SumSeg*>(sm + plan.seg);
-    int* seg_cnt = reinterpret_cast<int*>(sm + plan.seg + 32u * kSegMax * sizeof(SumSeg));
+    unsigned char* sum_mem = sm + plan.seg;  // exact RMS sum scratch
     int16_t* dsm = reinterpret_cast<int16_t*>(sm + plan.dsm);
     float* epi_s = reinterpret_cast<float*>(sm + plan.epi);
     unsigned char* stage0 = sm + plan.stage;
@@ -269,79 +237,124 @@ __global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
             rs_s[tid] = a.row_scale ? a.row_scale[m0 + tid] : 1.0f;
         named_barrier(1, cthreads);
     } else {
+        // One warp quantises one group (32 lanes x 4 values) per pass, so the
+        // row stays in registers from its load to the sliced words.
+        constexpr uint32_t kPasses = kMaxPrologueK / (kGroup * kComputeWarps);
         const uint32_t K = G * kGroup;
         for (uint32_t mm = 0; mm < mrows; ++mm) {
             const float4* xr = reinterpret_cast<const float4*>(a.x + (size_t)(m0 + mm) * a.x_stride);
+            float4 v[kPasses];
             int bad = 0;
-            for (uint32_t i = tid; i < K / 4; i += cthreads) {
-                const float4 v = xr[i];
-                bad |= !isfinite(v.x) | !isfinite(v.y) | !isfinite(v.z) | !isfinite(v.w);
-                reinterpret_cast<float4*>(xbuf)[i] = v;
+#pragma unroll
+            for (uint32_t p = 0; p < kPasses; ++p) {
+                const uint32_t g = p * kComputeWarps + warp;
+                if (g < G) {
+                    v[p] = xr[g * 32u + lane];
+                    bad |= !isfinite(v[p].x) | !isfinite(v[p].y) | !isfinite(v[p].z) | !isfinite(v[p].w);
+                }
             }
             // A linear rejects non-finite input (ValidateF32Input, soft :294-308);
             // before RMSNorm it shows up as a non-finite divisor instead.
             if (bad && PRO == kProQuant)
                 flags[0] = 2;
-            named_barrier(1, cthreads);
             if (PRO == kProRmsNorm) {
-                const float sum = rms_sum(xbuf, K, a.exact != 0, cthreads, red, seg, seg_cnt);
-                const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)K), a.eps));
+                // The reference's RMSNorm sum fl(...fl(fl(x0*x0) + x1*x1)...) in
+                // index order (qwen3.c:361-372): exact mode reproduces it bit for
+                // bit with warp 0 (exact_sum.cuh) from a shared-memory copy of the
+                // row; fast mode sums in a fixed tree order over the compute threads.
+                if (a.exact) {
+#pragma unroll
+                    for (uint32_t p = 0; p < kPasses; ++p) {
+                        const uint32_t g = p * kComputeWarps + warp;
+                        if (g < G)
+                            reinterpret_cast<float4*>(xbuf)[g * 32u + lane] = v[p];
+                    }
+                    named_barrier(1, cthreads);
+                    const float sum = exact_sumsq(xbuf, (int)K, sum_mem, 1);
+                    if (tid == 0)
+                        red[0] = sum;
+                } else {
+                    float sum = 0.0f;
+#pragma unroll
+                    for (uint32_t p = 0; p < kPasses; ++p) {
+                        if (p * kComputeWarps + warp < G) {
+                            sum = __fadd_rn(sum, __fmul_rn(v[p].x, v[p].x));
+                            sum = __fadd_rn(sum, __fmul_rn(v[p].y, v[p].y));
+                            sum = __fadd_rn(sum, __fmul_rn(v[p].z, v[p].z));
+                            sum = __fadd_rn(sum, __fmul_rn(v[p].w, v[p].w));
+                        }
+                    }
+                    for (int o = 16; o > 0; o >>= 1)
+                        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+                    if (lane == 0)
+                        red[1 + warp] = sum;
+                    named_barrier(1, cthreads);
+                    if (tid == 0) {
+                        float t = 0.0f;
+                        for (uint32_t w = 0; w < consumers; ++w)
+                            t = __fadd_rn(t, red[1 + w]);
+                        red[0] = t;
+                    }
+                }
+                named_barrier(1, cthreads);
+                const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], (float)K), a.eps));
                 if (!isfinite(rms) || rms == 0.0f) {
                     if (tid == 0) {
                         flags[0] = 1;
                         atomicOr(a.status, kStatusNonFinite);
                     }
                 } else {
-                    for (uint32_t i = tid; i < K; i += cthreads)
-                        xbuf[i] = __fmul_rn(__fdiv_rn(xbuf[i], rms), a.gain[i]);
+                    const float4* gr = reinterpret_cast<const float4*>(a.gain);
+#pragma unroll
+                    for (uint32_t p = 0; p < kPasses; ++p) {
+                        const uint32_t g = p * kComputeWarps + warp;
+                        if (g < G) {
+                            const float4 gn = gr[g * 32u + lane];
+                            v[p].x = __fmul_rn(__fdiv_rn(v[p].x, rms), gn.x);
+                            v[p].y = __fmul_rn(__fdiv_rn(v[p].y, rms), gn.y);
+                            v[p].z = __fmul_rn(__fdiv_rn(v[p].z, rms), gn.z);
+                            v[p].w = __fmul_rn(__fdiv_rn(v[p].w, rms), gn.w);
+                        }
+                    }
                 }
-                named_barrier(1, cthreads);
             }
             float amax = 0.0f;
-            for (uint32_t i = tid; i < K; i += cthreads)
-                amax = fmaxf(amax, fabsf(xbuf[i]));
+#pragma unroll
+            for (uint32_t p = 0; p < kPasses; ++p)
+                if (p * kComputeWarps + warp < G)
+                    amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v[p].x), fabsf(v[p].y))),
+                                 fmaxf(fabsf(v[p].z), fabsf(v[p].w)));
             for (int o = 16; o > 0; o >>= 1)
                 amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
             if (lane == 0)
-                red[1 + warp] = amax;
+                red[8 + warp] = amax;
             named_barrier(1, cthreads);
-            amax = red[1];
+            amax = red[8];
             for (uint32_t w = 1; w < consumers; ++w)
-                amax = fmaxf(amax, red[1 + w]);
+                amax = fmaxf(amax, red[8 + w]);
             const float s = row_scale_from_absmax(amax);
             const RowQuantizer quant(s);
-            // Quantise four consecutive values per thread (coalesced); a warp's
-            // 32 lanes cover exactly one group per pass, so each pass's group
-            // total is one warp reduction, done for all passes together.
-            constexpr uint32_t kMaxPasses = 16;  // K <= 8192
-            int part[kMaxPasses];
-            uint32_t passes = 0;
-            for (uint32_t qi = tid; qi < K / 4; qi += cthreads, ++passes) {
-                const float4 v = reinterpret_cast<const float4*>(xbuf)[qi];
-                const int8_t q0 = quant(v.x), q1 = quant(v.y), q2 = quant(v.z), q3 = quant(v.w);
-                qbuf[qi] = (uint32_t)(uint8_t)q0 | ((uint32_t)(uint8_t)q1 << 8) | ((uint32_t)(uint8_t)q2 << 16) |
-                           ((uint32_t)(uint8_t)q3 << 24);
-                part[passes & (kMaxPasses - 1)] = (int)q0 + (int)q1 + (int)q2 + (int)q3;
-            }
+            // Lane L = 8t + 2i + h holds q[32t + 8i + 4h + b], b = 0..3, of its
+            // warp's group. A 4x4 byte transpose across the lanes that share
+            // (t, h) leaves lane L with slice word (t, j = 4h + i): the bytes
+            // q[32t + 8i' + j], i' = 0..3.
+            const uint32_t slot = (lane >> 3) * 8u + (lane & 1u) * 4u + ((lane >> 1) & 3u);
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-                for (uint32_t p = 0; p < kMaxPasses; ++p)
-                    if (p < passes)
-                        part[p] += __shfl_xor_sync(0xffffffffu, part[p], o);
-            if (lane == 0)
-                for (uint32_t p = 0; p < passes; ++p)
-                    tot_s[mm * G + p * consumers + warp] = part[p];
-            named_barrier(1, cthreads);
-            // Slice: word (t, j) of group g takes byte (j & 3) of the four
-            // int8 words holding q[32t + 8i + j], i = 0..3.
-            for (uint32_t w = tid; w < G * kWordsPerGroup; w += cthreads) {
-                const uint32_t g = w / kWordsPerGroup, tj = w % kWordsPerGroup, t = tj >> 3, j = tj & 7;
-                const uint32_t* qw = qbuf + g * 32u + 8u * t + (j >> 2);
-                const uint32_t b = j & 3u;
-                const uint32_t lo = __byte_perm(qw[0], qw[2], b | ((4u + b) << 4));
-                const uint32_t hi = __byte_perm(qw[4], qw[6], b | ((4u + b) << 4));
-                act_s[(mm * G + g) * kActStride + tj] = __byte_perm(lo, hi, 0x5410);
+            for (uint32_t p = 0; p < kPasses; ++p) {
+                const uint32_t g = p * kComputeWarps + warp;
+                if (g < G) {
+                    const int8_t q0 = quant(v[p].x), q1 = quant(v[p].y), q2 = quant(v[p].z), q3 = quant(v[p].w);
+                    uint32_t w = (uint32_t)(uint8_t)q0 | ((uint32_t)(uint8_t)q1 << 8) |
+                                 ((uint32_t)(uint8_t)q2 << 16) | ((uint32_t)(uint8_t)q3 << 24);
+                    const int total = __reduce_add_sync(0xffffffffu, (int)q0 + (int)q1 + (int)q2 + (int)q3);
+                    uint32_t o = __shfl_xor_sync(0xffffffffu, w, 4);
+                    w = (lane & 4u) ? __byte_perm(w, o, 0x3276) : __byte_perm(w, o, 0x5410);
+                    o = __shfl_xor_sync(0xffffffffu, w, 2);
+                    w = (lane & 2u) ? __byte_perm(w, o, 0x3715) : __byte_perm(w, o, 0x6240);
+                    act_s[(mm * G + g) * kActStride + slot] = w;
+                    if (lane == 0)
+                        tot_s[mm * G + g] = total;
+                }
             }
             if (tid == 0)
                 rs_s[mm] = s;
@@ -471,9 +484,6 @@ constexpr size_t kGemvSmemBudget = 200u * 1024u;
 // one block per CTA, its groups split over the 4 compute warps); ring depth
 // that fits the shared-memory budget; persistent grid from the occupancy of
 // that configuration. SwiGLU needs gate/up block pairs in a tile.
-// Prologues that build the activations in the CTA hold up to this many inputs.
-constexpr uint32_t kMaxPrologueK = 8192;
-
 inline GemvLaunch plan_gemv(int sm_count, uint32_t n, uint32_t groups, uint32_t m, int pro, int epi) {
     const uint32_t nblocks = (n + kRowBlock - 1) / kRowBlock;
     const uint32_t mrows = m < (uint32_t)kRowsPerCta ? m : (uint32_t)kRowsPerCta;
