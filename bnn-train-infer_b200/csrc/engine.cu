@@ -37,6 +37,8 @@
 
 namespace {
 
+constexpr size_t kAttnSmemBudget = 200u * 1024u;  // dynamic shared memory of one attention block
+
 thread_local std::string g_last_error;
 
 BNND_Status fail(BNND_Status st, const char* fmt, ...) {
@@ -294,12 +296,13 @@ struct bnnd_context {
     BNND_ContextParams params{};
     uint32_t rows = 1, n_ctx = 0, pos = 0;
     cudaStream_t stream = nullptr;
-    DevMem x, qkv, y, h, logits, kcache, vcache, rope_cos, rope_sin;
+    DevMem x, qkv, y, h, logits, kcache, vcache, rope_cos, rope_sin, scores;
     DevMem pos_d, tok_in, tok_next, tok_seq, hist, hist_count, status;
     DevMem mlp_a, mlp_b;
     size_t tok_seq_cap = 0;
     uint32_t hist_cap = 0;
     bnn::GemvLaunch plan_qkv{}, plan_o{}, plan_gu{}, plan_down{}, plan_head{};
+    size_t attn_smem = 0;  // dynamic shared memory of the attention kernel
     std::vector<bnn::GemvLaunch> plan_mlp;
     bool pdl = true;  // launch the W1A8 linears with programmatic dependent launch
     cudaGraphExec_t graph_logits = nullptr, graph_prefill = nullptr, graph_profile = nullptr;
@@ -555,6 +558,23 @@ void rope_tables(const bnnd_model* m, uint32_t n_ctx, std::vector<float>* cs, st
 
 // One W1A8 linear: FP32 input rows x (stride l.in), RMSNorm gains when the
 // plan's prologue normalises, output rows of `out_stride` bytes.
+
+// The attention kernel, launched like the linears (programmatic dependent
+// launch: it streams K/V tiles of earlier steps while the q|k|v projection
+// finishes).
+cudaError_t launch_attention(bnnd_context* c, const bnn::eng::AttnArgs& a) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.kv_heads, c->rows);
+    cfg.blockDim = dim3(bnn::eng::kAttnThreads);
+    cfg.dynamicSmemBytes = c->attn_smem;
+    cfg.stream = c->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = c->pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, bnn::eng::attention_kernel, a);
+}
 cudaError_t launch_linear(const bnnd_context* c, const bnn::GemvLaunch& cl, const Linear& l, const float* x,
                           const float* gain, uint32_t rows, float* out, size_t out_stride, int* status) {
     bnn::GemvArgs a = {};
@@ -595,32 +615,18 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
         // attn_norm + q|k|v projections (prologue: RMSNorm + quantise)
         ck("w1a8_gemv:qkv", launch_linear(c, c->plan_qkv, L.qkv, c->x.as<float>(), L.attn_norm.as<float>(), R,
                                           c->qkv.as<float>(), qkv_pitch, status));
-        bnn::eng::QkArgs qa;
-        qa.qkv = c->qkv.as<float>();
-        qa.q_norm = L.q_norm.as<float>();
-        qa.k_norm = L.k_norm.as<float>();
-        qa.rope_cos = c->rope_cos.as<float>();
-        qa.rope_sin = c->rope_sin.as<float>();
-        qa.pos = c->pos_d.as<uint32_t>();
-        const size_t layer_cache = (size_t)R * c->n_ctx * KV;
-        qa.kcache = c->kcache.as<float>() + (size_t)l * layer_cache;
-        qa.vcache = c->vcache.as<float>() + (size_t)l * layer_cache;
-        qa.c = C;
-        qa.kv = KV;
-        qa.hd = HD;
-        qa.heads = in.heads;
-        qa.kv_heads = in.kv_heads;
-        qa.n_ctx = c->n_ctx;
-        qa.eps = m->eps;
-        qa.exact = exact;
-        qa.status = status;
-        bnn::eng::qk_norm_rope_kernel<<<dim3(in.heads + in.kv_heads, R), HD, HD * 8, s>>>(qa);
-        ck("qk_norm_rope_kernel");
+        // q/k norm + rope + KV append + attention, one block per (KV head, row)
         bnn::eng::AttnArgs aa;
         aa.qkv = c->qkv.as<float>();
-        aa.kcache = qa.kcache;
-        aa.vcache = qa.vcache;
-        aa.pos = qa.pos;
+        aa.q_norm = L.q_norm.as<float>();
+        aa.k_norm = L.k_norm.as<float>();
+        aa.rope_cos = c->rope_cos.as<float>();
+        aa.rope_sin = c->rope_sin.as<float>();
+        aa.pos = c->pos_d.as<uint32_t>();
+        const size_t layer_cache = (size_t)R * c->n_ctx * KV;
+        aa.kcache = c->kcache.as<float>() + (size_t)l * layer_cache;
+        aa.vcache = c->vcache.as<float>() + (size_t)l * layer_cache;
+        aa.scores = c->scores.p ? c->scores.as<float>() : nullptr;
         aa.y = c->y.as<float>();
         aa.c = C;
         aa.kv = KV;
@@ -628,11 +634,11 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
         aa.heads = in.heads;
         aa.kv_heads = in.kv_heads;
         aa.n_ctx = c->n_ctx;
+        aa.eps = m->eps;
         aa.scale = 1.0f / sqrtf((float)HD);
         aa.exact = exact;
         aa.status = status;
-        bnn::eng::attention_kernel<<<dim3(in.heads, R), 256, (size_t)(HD + c->n_ctx) * 4, s>>>(aa);
-        ck("attention_kernel");
+        ck("attention_kernel", launch_attention(c, aa));
         // attn_output, x += o (prologue: quantise the attention output)
         ck("w1a8_gemv:o", launch_linear(c, c->plan_o, L.o, c->y.as<float>(), nullptr, R, c->x.as<float>(),
                                         (size_t)C * 4u, status));
@@ -723,9 +729,23 @@ BNND_Status create_llm_context(bnnd_context* c) {
     for (const bnn::GemvLaunch* p : {&c->plan_qkv, &c->plan_o, &c->plan_gu, &c->plan_down, &c->plan_head})
         if (p->smem > bnn::kGemvSmemBudget)
             return fail(BNND_ENOTSUP, "hidden/ffn width too large for the contraction kernel");
-    if ((in.head_dim + c->n_ctx) * 4u > 200u * 1024u)
-        return fail(BNND_ENOTSUP, "context too large for one attention block");
-    cudaFuncSetAttribute(bnn::eng::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    const uint32_t kv_mul = in.heads / in.kv_heads;
+    if (in.head_dim % 32 != 0 || in.head_dim > 256 || kv_mul > 16 ||
+        kv_mul * in.head_dim > bnn::eng::kAttnThreads * bnn::eng::kAttnMaxChains)
+        return fail(BNND_ENOTSUP, "attention shape (head_dim %u, %u query heads per KV head) not supported",
+                    in.head_dim, kv_mul);
+    // scores of a block's query heads in shared memory when they fit, else in
+    // a device scratch [rows][heads][n_ctx]
+    bnn::eng::AttnSmem ap = bnn::eng::attn_smem_plan(in.head_dim, kv_mul, c->n_ctx, true);
+    if (ap.total > kAttnSmemBudget) {
+        ap = bnn::eng::attn_smem_plan(in.head_dim, kv_mul, c->n_ctx, false);
+        if ((st = dev_alloc(c->scores, (size_t)R * in.heads * c->n_ctx * 4)))
+            return st;
+    }
+    c->attn_smem = ap.total;
+    CUDA_OR(cudaFuncSetAttribute(bnn::eng::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kAttnSmemBudget),
+            BNND_EIO);
     if ((st = capture_step(c, true, &c->graph_logits)) || (st = capture_step(c, false, &c->graph_prefill)))
         return st;
     return BNND_OK;

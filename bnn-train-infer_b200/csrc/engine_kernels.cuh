@@ -4,8 +4,8 @@
 // FP32 operation order (bnn-sw-v2/qwen3/qwen3.c, bnn-mlp/bnn-mlp.c), using
 // explicit round-to-nearest intrinsics so nothing is fused or reassociated:
 //   embed_kernel            qwen3_embed               qwen3.c:374-385
-//   qk_norm_rope_kernel     per-head q/k RMSNorm, RoPE, KV append  qwen3.c:418-438
-//   attention_kernel        causal softmax attention  qwen3.c:440-478
+//   attention_kernel        per-head q/k RMSNorm, RoPE, KV append and
+//                           causal softmax attention  qwen3.c:418-478
 //   argmax_kernel           greedy pick + finite check  bnn-infer-v2.c:48-54, engine.c:262-267
 //   mlp_post_kernel         post_scale/bias + ReLU    bnn-mlp.c:189-193
 // RMSNorm before a linear, the row quantisation and SwiGLU run inside the
@@ -16,6 +16,7 @@
 
 #include <cstdint>
 #include "bnn_device.cuh"
+#include "bnn_sync.cuh"
 
 namespace bnn {
 namespace eng {
@@ -88,135 +89,344 @@ __global__ void embed_kernel(const int32_t* tokens, const unsigned char* wblocks
     }
 }
 
-struct QkArgs {
-    float* qkv;            // [rows][C + 2KV]: q | k | v
-    const float* q_norm;   // [HD]
-    const float* k_norm;   // [HD]
-    const float* rope_cos; // [n_ctx][HD/2]
-    const float* rope_sin;
-    const uint32_t* pos;   // [rows]
-    float* kcache;         // this layer: [rows][n_ctx][KV]
-    float* vcache;
-    uint32_t c, kv, hd, heads, kv_heads, n_ctx;
-    float eps;
-    int exact;
-    int* status;
-};
-
-// One block per (head, row), blockDim.x == head_dim. Q heads are normalised
-// and rotated in place; K heads are normalised, rotated and appended to the
-// K cache at this row's position, together with the matching V head.
-__global__ void qk_norm_rope_kernel(QkArgs a) {
-    extern __shared__ __align__(16) unsigned char e_smem[];
-    float* v = reinterpret_cast<float*>(e_smem);
-    float* sq = v + a.hd;
-    __shared__ float red[64];
-    const uint32_t hh = blockIdx.x, row = blockIdx.y, i = threadIdx.x;
-    const bool is_q = hh < a.heads;
-    const uint32_t kvh = is_q ? 0 : hh - a.heads;
-    const size_t width = a.c + 2u * a.kv;
-    float* vec = a.qkv + (size_t)row * width + (is_q ? hh * a.hd : a.c + kvh * a.hd);
-    const float x = vec[i];
-    v[i] = x;
-    sq[i] = __fmul_rn(x, x);
-    const float sum = block_sum_ordered(sq, a.hd, a.exact != 0, red);
-    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)a.hd), a.eps));
-    if (!isfinite(rms) || rms == 0.0f) {
-        if (i == 0)
-            atomicOr(a.status, kStatusNonFinite);
-        return;
-    }
-    const float* gain = is_q ? a.q_norm : a.k_norm;
-    v[i] = __fmul_rn(__fdiv_rn(x, rms), gain[i]);
-    __syncthreads();
-    const uint32_t half = a.hd / 2, p = a.pos[row];
-    float out;
-    if (i < half) {
-        const float c = a.rope_cos[(size_t)p * half + i], s = a.rope_sin[(size_t)p * half + i];
-        out = __fsub_rn(__fmul_rn(v[i], c), __fmul_rn(v[i + half], s));
-    } else {
-        const uint32_t j = i - half;
-        const float c = a.rope_cos[(size_t)p * half + j], s = a.rope_sin[(size_t)p * half + j];
-        out = __fadd_rn(__fmul_rn(v[j], s), __fmul_rn(v[i], c));
-    }
-    if (is_q) {
-        vec[i] = out;
-    } else {
-        const size_t slot = ((size_t)row * a.n_ctx + p) * a.kv + kvh * a.hd + i;
-        a.kcache[slot] = out;
-        a.vcache[slot] = a.qkv[(size_t)row * width + a.c + a.kv + kvh * a.hd + i];
-    }
-}
+// ---- attention: q/k RMSNorm, RoPE, KV append and causal softmax attention
+// in one kernel per (KV head, row). The KV cache of a layer is laid out
+// [rows][kv_heads][n_ctx][head_dim], so the positions of one head are
+// contiguous: K and V are streamed through shared memory as tiles of
+// kAttnTile positions with 1D bulk copies (K rows padded against bank
+// conflicts), in a two-stage ring; the first K tiles are requested before
+// the kernel waits for the q|k|v projection, since the cache rows it reads
+// were written by earlier steps. The current position's k and v are used
+// straight from shared memory.
+constexpr uint32_t kAttnThreads = 256;
+constexpr uint32_t kAttnTile = 128;
+constexpr uint32_t kAttnStages = 2;
+constexpr uint32_t kAttnMaxChains = 4;  // (q head, dim) chains per thread: kv_mul * head_dim <= 1024
 
 struct AttnArgs {
-    const float* qkv;     // q part: [rows][C + 2KV]
-    const float* kcache;  // this layer: [rows][n_ctx][KV]
-    const float* vcache;
-    const uint32_t* pos;
-    float* y;             // [rows][C]
+    const float* qkv;       // [rows][C + 2KV]: q | k | v projections
+    const float* q_norm;    // [HD]
+    const float* k_norm;    // [HD]
+    const float* rope_cos;  // [n_ctx][HD/2]
+    const float* rope_sin;
+    const uint32_t* pos;    // [rows]
+    float* kcache;          // this layer: [rows][kv_heads][n_ctx][HD]
+    float* vcache;
+    float* scores;          // [rows][heads][n_ctx] when they do not fit in shared memory, else null
+    float* y;               // [rows][C]
     uint32_t c, kv, hd, heads, kv_heads, n_ctx;
-    float scale;          // 1 / sqrtf(head_dim), computed on the host as qwen3.c:404
+    float eps;
+    float scale;            // 1 / sqrtf(head_dim), computed on the host as qwen3.c:404
     int exact;
     int* status;
 };
 
-// One block per (q head, row). scores[t] = fl(dot(q, k_t)) * scale, dots
-// accumulated serially over the head dimension; softmax with expf(s - max),
-// a sequential sum over t and a division; then y_i = sum_t p_t * v_t,i,
-// sequential in t, one thread per i.
-__global__ void attention_kernel(AttnArgs a) {
-    extern __shared__ __align__(16) unsigned char e_smem[];
-    float* q = reinterpret_cast<float*>(e_smem);
-    float* sc = q + a.hd;
-    __shared__ float red[64];
-    const uint32_t h = blockIdx.x, row = blockIdx.y;
-    const uint32_t kvh = h / (a.heads / a.kv_heads);
-    const uint32_t n = a.pos[row] + 1;  // positions 0..pos inclusive
-    const size_t width = a.c + 2u * a.kv;
-    for (uint32_t i = threadIdx.x; i < a.hd; i += blockDim.x)
-        q[i] = a.qkv[(size_t)row * width + h * a.hd + i];
-    __syncthreads();
-    const float* kbase = a.kcache + (size_t)row * a.n_ctx * a.kv + kvh * a.hd;
-    const float* vbase = a.vcache + (size_t)row * a.n_ctx * a.kv + kvh * a.hd;
-    int bad = 0;
-    float mx = -INFINITY;
-    for (uint32_t t = threadIdx.x; t < n; t += blockDim.x) {
-        const float4* k4 = reinterpret_cast<const float4*>(kbase + (size_t)t * a.kv);
-        float dot = 0.0f;
-        for (uint32_t i = 0; i < a.hd / 4; ++i) {
-            const float4 kk = k4[i];
-            dot = __fadd_rn(dot, __fmul_rn(q[4 * i], kk.x));
-            dot = __fadd_rn(dot, __fmul_rn(q[4 * i + 1], kk.y));
-            dot = __fadd_rn(dot, __fmul_rn(q[4 * i + 2], kk.z));
-            dot = __fadd_rn(dot, __fmul_rn(q[4 * i + 3], kk.w));
+struct AttnSmem {
+    size_t bars, red, q, kn, vn, sc, ring, stage_bytes, total;
+};
+
+__host__ __device__ inline AttnSmem attn_smem_plan(uint32_t hd, uint32_t kv_mul, uint32_t n_ctx, bool sc_smem) {
+    AttnSmem p;
+    p.bars = 0;                                // full[kAttnStages]
+    p.red = 64;                                // 64 floats
+    p.q = p.red + 64 * 4;                      // [kv_mul][hd]
+    p.kn = p.q + (size_t)kv_mul * hd * 4;      // [hd]
+    p.vn = p.kn + (size_t)hd * 4;              // [hd]
+    p.sc = p.vn + (size_t)hd * 4;              // [kv_mul][n_ctx] when in shared memory
+    p.ring = (p.sc + (sc_smem ? (size_t)kv_mul * n_ctx * 4 : 0) + 127) & ~(size_t)127;
+    p.stage_bytes = (size_t)kAttnTile * (hd + 4) * 4;  // K rows padded by 4 floats; V tiles dense
+    p.total = p.ring + kAttnStages * p.stage_bytes;
+    return p;
+}
+
+// qwen3_rmsnorm of one head vector (HD floats in shared memory, by one warp)
+// followed by qwen3_rope (qwen3.c:418-438), in place. Returns false when the
+// divisor is not finite or zero.
+__device__ inline bool attn_norm_rope(float* v, uint32_t hd, const float* gain, const float* cs, const float* sn,
+                                      float eps, bool exact) {
+    const uint32_t lane = threadIdx.x & 31;
+    float sum = 0.0f;
+    if (exact) {
+        // the reference's serial sum, index order (loads batched ahead)
+        if (lane == 0) {
+            for (uint32_t i = 0; i < hd; i += 8) {
+                float a[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    a[j] = __fmul_rn(v[i + j], v[i + j]);
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    sum = __fadd_rn(sum, a[j]);
+            }
         }
-        const float s = __fmul_rn(dot, a.scale);
-        bad |= !isfinite(s);
-        sc[t] = s;
-        mx = fmaxf(mx, s);
+        sum = __shfl_sync(0xffffffffu, sum, 0);
+    } else {
+        for (uint32_t i = lane; i < hd; i += 32)
+            sum = __fadd_rn(sum, __fmul_rn(v[i], v[i]));
+        for (int o = 16; o > 0; o >>= 1)
+            sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
     }
-    mx = block_max(mx, red);
-    if (__syncthreads_or(bad)) {
-        if (threadIdx.x == 0)
-            atomicOr(a.status, kStatusNonFinite);
-        return;
+    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)hd), eps));
+    if (!isfinite(rms) || rms == 0.0f)
+        return false;
+    for (uint32_t i = lane; i < hd; i += 32)
+        v[i] = __fmul_rn(__fdiv_rn(v[i], rms), gain[i]);
+    __syncwarp();
+    const uint32_t half = hd / 2;
+    float out[8];  // hd <= 256
+#pragma unroll
+    for (uint32_t k = 0; k < 8; ++k) {
+        const uint32_t i = lane + 32u * k;
+        if (i < half)
+            out[k] = __fsub_rn(__fmul_rn(v[i], cs[i]), __fmul_rn(v[i + half], sn[i]));
+        else if (i < hd)
+            out[k] = __fadd_rn(__fmul_rn(v[i - half], sn[i - half]), __fmul_rn(v[i], cs[i - half]));
     }
-    for (uint32_t t = threadIdx.x; t < n; t += blockDim.x)
-        sc[t] = expf_cr(__fsub_rn(sc[t], mx));
-    const float sum = block_sum_ordered(sc, n, a.exact != 0, red);
-    if (!(sum > 0.0f) || !isfinite(sum)) {
-        if (threadIdx.x == 0)
-            atomicOr(a.status, kStatusNonFinite);
-        return;
+    __syncwarp();
+#pragma unroll
+    for (uint32_t k = 0; k < 8; ++k)
+        if (lane + 32u * k < hd)
+            v[lane + 32u * k] = out[k];
+    __syncwarp();
+    return true;
+}
+// One block of kAttnThreads per (KV head g, row); it serves the kv_mul query
+// heads g * kv_mul .. that share the KV head (qwen3.c:440-478):
+//   scores[t] = fl(dot(q, k_t)) * scale, the dot accumulated serially over
+//   the head dimension; softmax with expf(s - max), a serial sum over t and a
+//   division; y_i = sum_t p_t * v_t,i, serial in t.
+// Fast mode replaces the serial sums of the norms and the softmax by trees.
+__global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) {
+    griddep_launch_dependents();
+    extern __shared__ __align__(128) unsigned char e_smem[];
+    const uint32_t g = blockIdx.x, row = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t HD = a.hd, kv_mul = a.heads / a.kv_heads;
+    const bool sc_smem = a.scores == nullptr;
+    const AttnSmem plan = attn_smem_plan(HD, kv_mul, a.n_ctx, sc_smem);
+    uint64_t* full = reinterpret_cast<uint64_t*>(e_smem + plan.bars);
+    float* red = reinterpret_cast<float*>(e_smem + plan.red);
+    float* q_s = reinterpret_cast<float*>(e_smem + plan.q);
+    float* kn_s = reinterpret_cast<float*>(e_smem + plan.kn);
+    float* vn_s = reinterpret_cast<float*>(e_smem + plan.vn);
+    float* sc = sc_smem ? reinterpret_cast<float*>(e_smem + plan.sc)
+                        : a.scores + ((size_t)row * a.heads + (size_t)g * kv_mul) * a.n_ctx;
+    unsigned char* ring = e_smem + plan.ring;
+    int* flag = reinterpret_cast<int*>(red + 62);  // [0] abort: earlier failure, non-finite, timeout
+
+    const uint32_t pos = a.pos[row], n = pos + 1;
+    const uint32_t ntiles = (n + kAttnTile - 1) / kAttnTile, nloads = 2 * ntiles;
+    const size_t head_base = ((size_t)row * a.kv_heads + g) * a.n_ctx * HD;
+    const float* kc = a.kcache + head_base;
+    const float* vc = a.vcache + head_base;
+    const uint32_t kstride = HD + 4;
+
+    if (tid == 0) {
+        for (uint32_t s = 0; s < kAttnStages; ++s)
+            mbar_init(&full[s], 1);
+        fence_barrier_init();
+        *flag = 0;
     }
-    for (uint32_t t = threadIdx.x; t < n; t += blockDim.x)
-        sc[t] = __fdiv_rn(sc[t], sum);
     __syncthreads();
-    for (uint32_t i = threadIdx.x; i < a.hd; i += blockDim.x) {
-        float acc = 0.0f;
-        for (uint32_t t = 0; t < n; ++t)
-            acc = __fadd_rn(acc, __fmul_rn(sc[t], vbase[(size_t)t * a.kv + i]));
-        a.y[(size_t)row * a.c + h * a.hd + i] = acc;
+    // Load L (< ntiles: K tile L, rows padded; else V tile L - ntiles, dense)
+    // into stage L % kAttnStages; issued by warp 0.
+    auto issue = [&](uint32_t L) {
+        const uint32_t s = L % kAttnStages;
+        const bool is_k = L < ntiles;
+        const uint32_t t0 = (is_k ? L : L - ntiles) * kAttnTile;
+        const uint32_t rows_in = min(kAttnTile, n - t0);
+        unsigned char* dst = ring + (size_t)s * plan.stage_bytes;
+        if (lane == 0)
+            mbar_arrive_expect_tx(&full[s], rows_in * HD * 4u);
+        __syncwarp();
+        if (is_k) {
+            for (uint32_t r = lane; r < rows_in; r += 32)
+                bulk_g2s(dst + (size_t)r * kstride * 4u, kc + (size_t)(t0 + r) * HD, HD * 4u, &full[s]);
+        } else if (lane == 0) {
+            bulk_g2s(dst, vc + (size_t)t0 * HD, rows_in * HD * 4u, &full[s]);
+        }
+    };
+    if (warp == 0)
+        for (uint32_t L = 0; L < kAttnStages && L < nloads; ++L)
+            issue(L);
+
+    // ---- wait for the q|k|v projection; norm + rope of the q heads and the k head
+    griddep_wait();
+    const size_t width = a.c + 2u * a.kv;
+    const float* qkv_row = a.qkv + (size_t)row * width;
+    for (uint32_t i = tid; i < kv_mul * HD; i += kAttnThreads)
+        q_s[i] = qkv_row[(size_t)g * kv_mul * HD + i];
+    for (uint32_t i = tid; i < HD; i += kAttnThreads) {
+        kn_s[i] = qkv_row[a.c + (size_t)g * HD + i];
+        vn_s[i] = qkv_row[a.c + a.kv + (size_t)g * HD + i];
+    }
+    if (tid == 0 && *a.status != 0)
+        *flag = 1;  // an earlier kernel failed: skip the work, keep the copy protocol
+    __syncthreads();
+    const float* cs = a.rope_cos + (size_t)pos * (HD / 2);
+    const float* sn = a.rope_sin + (size_t)pos * (HD / 2);
+    if (warp <= kv_mul) {
+        float* v = warp < kv_mul ? q_s + (size_t)warp * HD : kn_s;
+        if (!attn_norm_rope(v, HD, warp < kv_mul ? a.q_norm : a.k_norm, cs, sn, a.eps, a.exact != 0) && lane == 0) {
+            *flag = 1;
+            atomicOr(a.status, kStatusNonFinite);
+        }
+    }
+    __syncthreads();
+    // append this position's k and v to the cache (read back by later steps)
+    for (uint32_t i = tid; i < HD; i += kAttnThreads) {
+        a.kcache[head_base + (size_t)pos * HD + i] = kn_s[i];
+        a.vcache[head_base + (size_t)pos * HD + i] = vn_s[i];
+    }
+
+    // ---- scores
+    int bad = 0;
+    uint32_t L = 0;
+    for (uint32_t tile = 0; tile < ntiles; ++tile, ++L) {
+        const uint32_t s = L % kAttnStages, t0 = tile * kAttnTile, rows_in = min(kAttnTile, n - t0);
+        if (!mbar_wait(&full[s], (L / kAttnStages) & 1) && lane == 0) {
+            *flag = 1;
+            atomicOr(a.status, kStatusTimeout);
+        }
+        float* kt = reinterpret_cast<float*>(ring + (size_t)s * plan.stage_bytes);
+        if (pos >= t0 && pos < t0 + rows_in)
+            for (uint32_t i = tid; i < HD; i += kAttnThreads)
+                kt[(size_t)(pos - t0) * kstride + i] = kn_s[i];
+        __syncthreads();
+        if (*flag == 0) {
+            for (uint32_t pr = tid; pr < kv_mul * kAttnTile; pr += kAttnThreads) {
+                const uint32_t h = pr / kAttnTile, tt = pr % kAttnTile;
+                if (tt >= rows_in)
+                    continue;
+                const float4* k4 = reinterpret_cast<const float4*>(kt + (size_t)tt * kstride);
+                const float4* q4 = reinterpret_cast<const float4*>(q_s + (size_t)h * HD);
+                float dot = 0.0f;
+                for (uint32_t i = 0; i < HD / 4; ++i) {
+                    const float4 kk = k4[i], qq = q4[i];
+                    dot = __fadd_rn(dot, __fmul_rn(qq.x, kk.x));
+                    dot = __fadd_rn(dot, __fmul_rn(qq.y, kk.y));
+                    dot = __fadd_rn(dot, __fmul_rn(qq.z, kk.z));
+                    dot = __fadd_rn(dot, __fmul_rn(qq.w, kk.w));
+                }
+                const float score = __fmul_rn(dot, a.scale);
+                bad |= !isfinite(score);
+                sc[(size_t)h * a.n_ctx + t0 + tt] = score;
+            }
+        }
+        fence_proxy_async();  // this thread's accesses to stage s come before the next bulk copy into it
+        __syncthreads();      // stage s is free again
+        if (warp == 0 && L + kAttnStages < nloads)
+            issue(L + kAttnStages);
+    }
+    if (__syncthreads_or(bad) && tid == 0) {
+        *flag = 1;
+        atomicOr(a.status, kStatusNonFinite);  // "attention score is not finite"
+    }
+    __syncthreads();
+
+    // ---- softmax per query head: max, expf(s - max), serial sum, division
+    const bool live = *flag == 0;
+    if (live) {
+        if (warp < kv_mul) {
+            float mx = -INFINITY;
+            for (uint32_t t = lane; t < n; t += 32)
+                mx = fmaxf(mx, sc[(size_t)warp * a.n_ctx + t]);
+            for (int o = 16; o > 0; o >>= 1)
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (lane == 0)
+                red[warp] = mx;
+        }
+        __syncthreads();
+        for (uint32_t i = tid; i < kv_mul * n; i += kAttnThreads) {
+            const uint32_t h = i / n, t = i % n;
+            float* e = &sc[(size_t)h * a.n_ctx + t];
+            *e = expf_cr(__fsub_rn(*e, red[h]));
+        }
+        __syncthreads();
+        if (warp < kv_mul) {
+            const float* e = sc + (size_t)warp * a.n_ctx;
+            float sum = 0.0f;
+            if (a.exact) {
+                if (lane == 0) {
+                    uint32_t t = 0;
+                    for (; t + 8 <= n; t += 8) {
+                        float v[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            v[j] = e[t + j];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            sum = __fadd_rn(sum, v[j]);
+                    }
+                    for (; t < n; ++t)
+                        sum = __fadd_rn(sum, e[t]);
+                }
+            } else {
+                for (uint32_t t = lane; t < n; t += 32)
+                    sum = __fadd_rn(sum, e[t]);
+                for (int o = 16; o > 0; o >>= 1)
+                    sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+            }
+            if (lane == 0) {
+                red[16 + warp] = sum;
+                if (!(sum > 0.0f) || !isfinite(sum)) {  // "attention softmax failed"
+                    *flag = 1;
+                    atomicOr(a.status, kStatusNonFinite);
+                }
+            }
+        }
+        __syncthreads();
+        if (*flag == 0)
+            for (uint32_t i = tid; i < kv_mul * n; i += kAttnThreads) {
+                const uint32_t h = i / n, t = i % n;
+                float* e = &sc[(size_t)h * a.n_ctx + t];
+                *e = __fdiv_rn(*e, red[16 + h]);
+            }
+    }
+    __syncthreads();
+
+    // ---- y = sum_t p_t * v_t, one serial chain per (query head, dim)
+    const bool live2 = *flag == 0;
+    float acc[kAttnMaxChains];
+#pragma unroll
+    for (uint32_t c = 0; c < kAttnMaxChains; ++c)
+        acc[c] = 0.0f;
+    for (uint32_t tile = 0; tile < ntiles; ++tile, ++L) {
+        const uint32_t s = L % kAttnStages, t0 = tile * kAttnTile, rows_in = min(kAttnTile, n - t0);
+        if (!mbar_wait(&full[s], (L / kAttnStages) & 1) && lane == 0) {
+            *flag = 1;
+            atomicOr(a.status, kStatusTimeout);
+        }
+        float* vt = reinterpret_cast<float*>(ring + (size_t)s * plan.stage_bytes);
+        if (pos >= t0 && pos < t0 + rows_in)
+            for (uint32_t i = tid; i < HD; i += kAttnThreads)
+                vt[(size_t)(pos - t0) * HD + i] = vn_s[i];
+        __syncthreads();
+        if (live2) {
+#pragma unroll
+            for (uint32_t c = 0; c < kAttnMaxChains; ++c) {
+                const uint32_t ch = tid + c * kAttnThreads;
+                if (ch < kv_mul * HD) {
+                    const uint32_t h = ch / HD, d = ch % HD;
+                    const float* p = sc + (size_t)h * a.n_ctx + t0;
+                    float v = acc[c];
+                    for (uint32_t tt = 0; tt < rows_in; ++tt)
+                        v = __fadd_rn(v, __fmul_rn(p[tt], vt[(size_t)tt * HD + d]));
+                    acc[c] = v;
+                }
+            }
+        }
+        fence_proxy_async();
+        __syncthreads();
+        if (warp == 0 && L + kAttnStages < nloads)
+            issue(L + kAttnStages);
+    }
+    if (live2 && *flag == 0) {
+#pragma unroll
+        for (uint32_t c = 0; c < kAttnMaxChains; ++c) {
+            const uint32_t ch = tid + c * kAttnThreads;
+            if (ch < kv_mul * HD)
+                a.y[(size_t)row * a.c + (size_t)g * kv_mul * HD + ch] = acc[c];
+        }
     }
 }
 

@@ -3,30 +3,32 @@
 // qwen3_rmsnorm (bnn-sw-v2/qwen3/qwen3.c:361-372) accumulates
 //     s_0 = 0,  s_{i+1} = fl(s_i + fl(x_i * x_i)),  i = 0..n-1
 // in index order. Run literally that is a chain of n dependent adds; this
-// file produces the identical float with the four compute warps of a CTA.
+// file produces the identical float with the 128 threads of four warps.
 //
 // Every term a_i = fl(x_i * x_i) is >= 0, so s is non-decreasing. While s_i
 // and s_{i+1} lie in one binade [2^e, 2^(e+1)), with grid spacing
 // u = 2^(e-23), the rounded add is s_i + u * RN(a_i / u), where RN is round
 // to nearest and a tie (a_i / u exactly half-way) is broken by the parity of
 // s_i. So a run of steps inside one binade with no tie adds the exact integer
-// D = sum RN(a_i / u), independent of where the run starts, and runs of the
-// same binade that follow one another add their D's.
+// D = sum RN(a_i / u), independent of where the run starts.
 //
 // Which binade each s_i is in is guessed from an approximate FP32 prefix p_i
-// of the squares. A step counts as "inside binade e" only with a relative
-// margin of 2^-12 on both sides; steps that cross a binade, start below
-// 2^-100, or hit a tie are done serially ("singles").
+// of the squares (per-thread sums and a block scan). A step counts as
+// "inside binade e" only with a relative margin of 2^-12 on both sides; steps
+// that cross a binade, start below 2^-100 or hit a tie are "singles".
 //
-// Work split: one warp sums the head [0, H) serially (the sum crosses most
-// binades early, where a_i is large relative to s_i); 96 lanes classify
-// contiguous chunks of [H, n) into runs and singles with one uniform,
-// predicated loop; the entries are compacted and consecutive runs of one
-// binade merged into an op list; one warp then walks the ops in order from
-// the head's value. A merged run is applied in one exact add only after
-// checking that s starts inside binade e and ends below 2^(e+1); otherwise
-// its elements are replayed serially. So the result never depends on the
-// margin argument, only the speed does.
+// Each thread classifies a contiguous chunk and records only where an op
+// starts: every single, and the first element of each run (a change of
+// binade). Records carry the running total of the increments RN(a_i / u)
+// before them, so a run's D is the difference of two neighbouring records;
+// a run that continues the previous thread's last run is dropped, which
+// merges the two. One warp then walks the ops 32 at a time: all lanes run
+// the same chain of adds (one add per op) and each keeps the value before
+// and after its op; each lane checks its op, and the chain restarts after
+// the first op that fails, which is replayed step by step. A single always
+// passes; a run passes when s starts inside binade e and the sum stays below
+// 2^(e+1). So the result never depends on the margin argument, only the
+// speed does.
 #pragma once
 
 #include <cstdint>
@@ -35,40 +37,53 @@
 
 namespace bnn {
 
-constexpr int kSegMax = 8;           // entries per lane before the lane goes fully serial
-constexpr int kSegSlot = kSegMax + 1;  // per-lane slot stride (one scratch entry)
-constexpr int kSegSingle = -1000;    // op: one serial step; d holds the bits of a_first
-constexpr int kSegChunk = -1001;     // op: serial steps over [first, last)
-constexpr int kRunEMin = -100;       // runs only in binades where u and 2^(23-e) are normal
+constexpr int kSumThreads = 128;       // four warps
+constexpr int kSumSlots = 16;          // records per thread before its chunk goes serial
+constexpr int kSumBatch = 8;           // elements loaded ahead per step
+constexpr int kRunEMin = -100;         // runs only in binades where u and 2^(23-e) are normal
 constexpr int kRunEMax = 125;
 constexpr uint32_t kLoMant = 1u << 11;                  // p >= 2^e * (1 + 2^-12)
 constexpr uint32_t kHiMant = (1u << 23) - (1u << 12);   // p <= 2^(e+1) * (1 - 2^-12)
-constexpr int kSumLanes = 96;        // classifying lanes: warps 0..2
-constexpr int kSumHeadWarp = 3;      // warp that sums the head serially
+constexpr int kTagSingle = 0;          // record tags: a single, a run (e + 128), a serial chunk
+constexpr int kTagChunk = 255;
 
-struct SumSeg {
-    int e;      // binade exponent of a run, or kSegSingle / kSegChunk
-    int first;  // first element index
-    int last;   // one past the last element index
-    int d;      // run: sum of RN(a_i / u); single: bits of a_first
+// One op record: key = first element | tag << 16; cum = increments before it.
+struct SumRec {
+    int key;
+    int cum;
 };
 
-// Shared memory of one sum: per-lane slots (reused for the ops), the
-// compacted list, and a few words of cross-warp state.
-constexpr int kSumSlotEntries = kSumLanes * kSegSlot;
-constexpr int kSumListEntries = kSumLanes * kSegMax;
-constexpr size_t kSumSmemBytes = (size_t)(kSumSlotEntries + kSumListEntries) * sizeof(SumSeg) + 64;
+__host__ __device__ inline int rec_first(int key) { return key & 0xffff; }
+__host__ __device__ inline int rec_tag(int key) { return (key >> 16) & 0xff; }
+
+// Shared memory of one sum: per-thread record slots (stride padded against
+// bank conflicts), the compacted op list (+ sentinel), last tags, scratch.
+constexpr int kSumSlotStride = kSumSlots + 1;
+constexpr int kSumListMax = kSumThreads * kSumSlots;
+constexpr size_t kSumSlotsOffset = 0;
+constexpr size_t kSumListOffset = kSumSlotsOffset + (size_t)kSumThreads * kSumSlotStride * sizeof(SumRec);
+constexpr size_t kSumTagsOffset = kSumListOffset + (size_t)(kSumListMax + 2) * sizeof(SumRec);
+constexpr size_t kSumMiscOffset = kSumTagsOffset + kSumThreads * sizeof(int);
+constexpr size_t kSumSmemBytes = kSumMiscOffset + 64 * sizeof(float);
 
 __host__ __device__ inline uint32_t fbits(float v) {
+#ifdef __CUDA_ARCH__
+    return __float_as_uint(v);
+#else
     uint32_t b;
     memcpy(&b, &v, sizeof b);
     return b;
+#endif
 }
 
 __host__ __device__ inline float fvalue(uint32_t b) {
+#ifdef __CUDA_ARCH__
+    return __uint_as_float(b);
+#else
     float v;
     memcpy(&v, &b, sizeof v);
     return v;
+#endif
 }
 
 __host__ __device__ inline float pow2f(int e) {
@@ -95,16 +110,9 @@ inline float mul_rn(float a, float b) {
 }
 #endif
 
-// Head length H and chunk length of the classifying lanes for n terms.
-__host__ __device__ inline int sum_head_len(int n) {
-    const int h = 32 + n / 32;
-    return n - h < kSumLanes * 4 ? n : h;  // short rows: all serial
-}
-
-__host__ __device__ inline int sum_chunk_len(int n, int h) {
-    // odd, so that the lanes' i-th elements fall in different banks
-    return ((n - h + kSumLanes - 1) / kSumLanes) | 1;
-}
+// Elements per thread: odd, so that the threads' i-th elements fall in
+// different shared-memory banks.
+__host__ __device__ inline int sum_chunk_len(int n) { return ((n + kSumThreads - 1) / kSumThreads) | 1; }
 
 // Serial sum of squares over [first, last) starting from s.
 __host__ __device__ inline float sum_serial(const float* xs, float s, int first, int last) {
@@ -113,224 +121,228 @@ __host__ __device__ inline float sum_serial(const float* xs, float s, int first,
     return s;
 }
 
-// Classifies [first, last), whose approximate prefix before `first` is p0,
-// into out[0..kSegMax): runs and singles in element order. Returns their
-// count, or -1 when more are needed (the chunk is then replayed serially).
-// One uniform loop with predicated updates, so the lanes never diverge.
-__host__ __device__ inline int sum_classify(const float* xs, int first, int last, float p0, SumSeg* out) {
-    int count = 0;
-    int run_e = kSegSingle, run_d = 0, run_first = first;
+// Approximate sum of squares of xs[first, last) (any order will do).
+__host__ __device__ inline float sum_approx(const float* xs, int first, int last) {
+    float q[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int i = first; i < last; i += kSumBatch) {
+#pragma unroll
+        for (int j = 0; j < kSumBatch; ++j) {
+            const float v = sq_rn(xs[i + j < last ? i + j : first]);
+            q[j & 3] = add_rn(q[j & 3], i + j < last ? v : 0.0f);
+        }
+    }
+    return add_rn(add_rn(q[0], q[1]), add_rn(q[2], q[3]));
+}
+
+// Classifies [first, last), whose approximate prefix before `first` is p0.
+// Records each op start into out[0..kSumSlots) (cum relative to `first`;
+// out[kSumSlots] is scratch);
+// returns the count, or -1 when more are needed. Sets *inc_total to the sum
+// of the run increments and *last_tag to the tag of the last element (-1 if
+// the range is empty). Only the prefix add, the start test and the counts are
+// chained from element to element.
+__host__ __device__ inline int sum_classify(const float* xs, int first, int last, float p0, SumRec* out,
+                                            int* inc_total, int* last_tag) {
+    int count = 0, cum = 0, prev = -1;
     float p = p0;
-    for (int i = first; i < last; ++i) {
-        const float a = sq_rn(xs[i]);
-        const float pn = add_rn(p, a);
-        const uint32_t eb = fbits(p) >> 23;  // p >= 0: the biased exponent
-        const int e = (int)eb - 127;
-        // inside binade e with the margin: p >= 2^e (1 + 2^-12) and
-        // pn <= 2^(e+1) (1 - 2^-12); false for NaN and infinity too
-        const bool in = e >= kRunEMin && e <= kRunEMax && p >= fvalue((eb << 23) | kLoMant) &&
-                        pn <= fvalue((eb << 23) | kHiMant);
-        const int ec = in ? e : 0;
-        const float v = mul_rn(a, fvalue((uint32_t)(150 - ec) << 23));  // a / u, exact
-        const float r = rintf(v);
-        const bool lin = in && fabsf(v - r) != 0.5f;
-        const int inc = lin ? (int)r : 0;
-        const bool cont = lin && e == run_e;
-        if (!cont && run_e != kSegSingle) {  // the current run ends before i
-            if (count < kSegMax)
-                out[count] = SumSeg{run_e, run_first, i, run_d};
-            ++count;
+    for (int base = first; base < last; base += kSumBatch) {
+        float a[kSumBatch];
+#pragma unroll
+        for (int j = 0; j < kSumBatch; ++j)
+            a[j] = sq_rn(xs[base + j < last ? base + j : first]);
+#pragma unroll
+        for (int j = 0; j < kSumBatch; ++j) {
+            const int i = base + j;
+            const bool valid = i < last;
+            const float pn = add_rn(p, a[j]);
+            const uint32_t eb = fbits(p) >> 23;  // p >= 0: the biased exponent
+            const int e = (int)eb - 127;
+            // inside binade e with the margin: p >= 2^e (1 + 2^-12) and
+            // pn <= 2^(e+1) (1 - 2^-12); false for NaN and infinity too
+            const bool in = e >= kRunEMin && e <= kRunEMax && p >= fvalue((eb << 23) | kLoMant) &&
+                            pn <= fvalue((eb << 23) | kHiMant);
+            const int ec = in ? e : 0;
+            const float v = mul_rn(a[j], fvalue((uint32_t)(150 - ec) << 23));  // a / u, exact
+            const float r = rintf(v);
+            const bool lin = in && fabsf(v - r) != 0.5f;
+            const int tag = lin ? e + 128 : kTagSingle;
+            const bool start = valid && (!lin || tag != prev);
+            // unconditional store (a branch here would keep the compiler from
+            // overlapping neighbouring elements): uncounted records go to the
+            // scratch slot out[kSumSlots]
+            out[start && count < kSumSlots ? count : kSumSlots] = SumRec{i | (tag << 16), cum};
+            count += start;
+            cum += valid && lin ? (int)r : 0;
+            prev = valid ? tag : prev;
+            p = valid ? pn : p;
         }
-        if (!lin) {
-            if (count < kSegMax)
-                out[count] = SumSeg{kSegSingle, i, i + 1, (int)fbits(a)};
-            ++count;
-        }
-        run_d = cont ? run_d + inc : inc;
-        run_first = cont ? run_first : i;
-        run_e = lin ? e : kSegSingle;
-        p = pn;
     }
-    if (run_e != kSegSingle) {
-        if (count < kSegMax)
-            out[count] = SumSeg{run_e, run_first, last, run_d};
-        ++count;
-    }
-    return count <= kSegMax ? count : -1;
+    *inc_total = cum;
+    *last_tag = prev;
+    return count <= kSumSlots ? count : -1;
 }
 
-// Merges consecutive runs of one binade in the compacted list into ops;
-// returns the op count. (The device does the same with one warp.)
-inline int sum_merge_host(const SumSeg* list, int count, SumSeg* ops) {
-    int g = -1;
-    for (int k = 0; k < count; ++k) {
-        const SumSeg it = list[k];
-        if (it.e >= kRunEMin && k > 0 && list[k - 1].e == it.e) {
-            ops[g].d += it.d;
-            ops[g].last = it.last;
-        } else {
-            ops[++g] = it;
+// The op that list[k] starts, applied to s on the host (the reference of
+// what the warp walk does): returns the new s.
+__host__ __device__ inline float sum_apply(const float* xs, float s, SumRec rec, SumRec next) {
+    const int tag = rec_tag(rec.key), first = rec_first(rec.key), last = rec_first(next.key);
+    if (tag == kTagSingle)
+        return add_rn(s, sq_rn(xs[first]));
+    if (tag != kTagChunk) {
+        const int e = tag - 128, d = next.cum - rec.cum;
+        if (d >= 0 && d < (1 << 24) && s >= pow2f(e) && s < pow2f(e + 1)) {
+            const float t = add_rn(s, mul_rn((float)d, pow2f(e - 23)));
+            if (t < pow2f(e + 1))
+                return t;
         }
     }
-    return g + 1;
-}
-
-// Applies the ops in order to s.
-__host__ __device__ inline float sum_walk(const float* xs, float s, const SumSeg* ops, int count) {
-#pragma unroll 4
-    for (int k = 0; k < count; ++k) {
-        const SumSeg g = ops[k];
-        if (g.e >= kRunEMin) {
-            // exact when s starts inside binade e and the sum stays below
-            // 2^(e+1): 0 <= d < 2^24 with u = 2^(e-23) normal makes d * u a
-            // float, and s and d * u are multiples of u
-            const float lo = pow2f(g.e), hi = pow2f(g.e + 1);
-            const bool dok = g.d >= 0 && g.d < (1 << 24);
-            const float t = add_rn(s, mul_rn((float)(dok ? g.d : 0), pow2f(g.e - 23)));
-            if (dok && s >= lo && s < hi && t < hi)
-                s = t;
-            else
-                s = sum_serial(xs, s, g.first, g.last);
-        } else if (g.e == kSegSingle) {
-            s = add_rn(s, fvalue((uint32_t)g.d));
-        } else {
-            s = sum_serial(xs, s, g.first, g.last);
-        }
-    }
-    return s;
+    return sum_serial(xs, s, first, last);
 }
 
 #ifdef __CUDACC__
-__device__ __forceinline__ void sum_bar(int id, int threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-// Serial sum of squares of xs[0..h), loads and squares batched ahead of the
-// dependent adds.
-__device__ __forceinline__ float sum_head(const float* xs, int h) {
-    float s = 0.0f;
-    int i = 0;
-    for (; i + 8 <= h; i += 8) {
-        float a[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            a[j] = sq_rn(xs[i + j]);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            s = add_rn(s, a[j]);
-    }
-    for (; i < h; ++i)
-        s = add_rn(s, sq_rn(xs[i]));
-    return s;
+__device__ __forceinline__ void sum_bar(int id) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kSumThreads) : "memory");
 }
 
 // Called by the 128 threads of warps 0..3 of a CTA; returns the serial sum of
-// squares of xs[0..n), n >= 1 (shared memory), to all of them. Uses named
-// barriers `bar` (128 threads) and `bar + 1` (warps 0..2) and kSumSmemBytes
-// of 16-byte aligned shared memory at `mem`.
+// squares of xs[0..n), 1 <= n <= 65535 (shared memory), to all of them.
+// Uses named barrier `bar` (128 threads) and kSumSmemBytes of 16-byte
+// aligned shared memory at `mem`.
 static __device__ __noinline__ float exact_sumsq(const float* xs, int n, unsigned char* mem, int bar) {
-    SumSeg* slots = reinterpret_cast<SumSeg*>(mem);  // per-lane slots, then the ops
-    SumSeg* list = slots + kSumSlotEntries;
-    float* xf = reinterpret_cast<float*>(list + kSumListEntries);  // [0..2] chunk sums, [3..5] head parts
-    int* xi = reinterpret_cast<int*>(xf + 6);                       // [0..2] entry counts
-    float* head_value = xf + 12;
-    float* result = xf + 13;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int h = sum_head_len(n);
-    if (warp == kSumHeadWarp) {
-        if (lane == 0)
-            *head_value = sum_head(xs, h);
-        sum_bar(bar, 128);  // head value ready
-        sum_bar(bar, 128);  // result ready
-        return *result;
+    SumRec* slots = reinterpret_cast<SumRec*>(mem + kSumSlotsOffset);
+    SumRec* list = reinterpret_cast<SumRec*>(mem + kSumListOffset);
+    int* tags = reinterpret_cast<int*>(mem + kSumTagsOffset);
+    float* misc = reinterpret_cast<float*>(mem + kSumMiscOffset);
+    float* wsum = misc;                              // [4] warp sums of the partials
+    int* wcnt = reinterpret_cast<int*>(misc + 4);    // [4] warp record counts
+    int* winc = reinterpret_cast<int*>(misc + 8);    // [4] warp increment totals
+    float* abuf = misc + 16;                         // [32] addends of a walk round
+    float* result = misc + 48;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int len = sum_chunk_len(n);
+    const int first = min(t * len, n), last = min(first + len, n);
+
+    // approximate prefix before `first`: block scan of the chunk sums
+    const float part = sum_approx(xs, first, last);
+    float incl = part;
+    for (int o = 1; o < 32; o <<= 1) {
+        const float v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o)
+            incl = add_rn(incl, v);
     }
-    int nops = 0;
-    if (h < n) {
-        const int c = sum_chunk_len(n, h);
-        const int first = min(h + tid * c, n), last = min(first + c, n);
-        float part0 = 0.0f, part1 = 0.0f, hp = 0.0f;
-        int i = first;
-        for (; i + 1 < last; i += 2) {
-            part0 = add_rn(part0, sq_rn(xs[i]));
-            part1 = add_rn(part1, sq_rn(xs[i + 1]));
-        }
-        if (i < last)
-            part0 = add_rn(part0, sq_rn(xs[i]));
-        for (int j = tid; j < h; j += kSumLanes)
-            hp = add_rn(hp, sq_rn(xs[j]));
-        float incl = add_rn(part0, part1);
-        for (int o = 1; o < 32; o <<= 1) {
-            const float t = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o)
-                incl = add_rn(incl, t);
-            hp = add_rn(hp, __shfl_xor_sync(0xffffffffu, hp, o));
-        }
-        if (lane == 31) {
-            xf[warp] = incl;
-            xf[3 + warp] = hp;
-        }
-        sum_bar(bar + 1, kSumLanes);
-        float base = add_rn(add_rn(xf[3], xf[4]), xf[5]);
-        if (warp > 0)
-            base = add_rn(base, xf[0]);
-        if (warp > 1)
-            base = add_rn(base, xf[1]);
-        float excl = __shfl_up_sync(0xffffffffu, incl, 1);
-        if (lane == 0)
-            excl = 0.0f;
-        SumSeg* mine = slots + tid * kSegSlot;
-        int cnt = sum_classify(xs, first, last, add_rn(base, excl), mine);
-        if (cnt < 0) {
-            mine[0] = SumSeg{kSegChunk, first, last, 0};
-            cnt = 1;
-        }
-        // compact the entries into the list: exclusive scan of the counts
-        int off = cnt;
-        for (int o = 1; o < 32; o <<= 1) {
-            const int t = __shfl_up_sync(0xffffffffu, off, o);
-            if (lane >= o)
-                off += t;
-        }
-        if (lane == 31)
-            xi[warp] = off;
-        sum_bar(bar + 1, kSumLanes);
-        const int total = xi[0] + xi[1] + xi[2];
-        off += (warp > 0 ? xi[0] : 0) + (warp > 1 ? xi[1] : 0) - cnt;
-        for (int k = 0; k < cnt; ++k)
-            list[off + k] = mine[k];
-        sum_bar(bar + 1, kSumLanes);  // list complete, slots free
-        if (warp == 0) {
-            // merge consecutive runs of one binade into ops (over the slots)
-            for (int r = 0; r < total; r += 32) {
-                const int k = r + lane;
-                const bool valid = k < total;
-                SumSeg it{kSegSingle, 0, 0, 0};
-                bool head = false;
-                if (valid) {
-                    it = list[k];
-                    head = !(it.e >= kRunEMin && k > 0 && list[k - 1].e == it.e);
-                }
-                const unsigned hb = __ballot_sync(0xffffffffu, head);
-                const int gid = nops + __popc(hb & ((2u << lane) - 1u)) - 1;
-                if (head)
-                    slots[gid] = it;
-                __syncwarp();
-                if (valid && !head) {
-                    atomicAdd(&slots[gid].d, it.d);
-                    atomicMax(&slots[gid].last, it.last);
-                }
-                __syncwarp();
-                nops += __popc(hb);
-            }
-        }
+    float excl = __shfl_up_sync(0xffffffffu, incl, 1);
+    if (lane == 0)
+        excl = 0.0f;
+    if (lane == 31)
+        wsum[warp] = incl;
+    sum_bar(bar);
+    for (int w = 0; w < warp; ++w)
+        excl = add_rn(excl, wsum[w]);
+
+    SumRec* mine = slots + t * kSumSlotStride;
+    int inc_total, last_tag;
+    int cnt = sum_classify(xs, first, last, excl, mine, &inc_total, &last_tag);
+    if (cnt < 0) {
+        mine[0] = SumRec{first | (kTagChunk << 16), 0};
+        cnt = 1;
+        last_tag = kTagChunk;
     }
-    sum_bar(bar, 128);  // head value ready
+    tags[t] = last_tag;
+    int iincl = inc_total;
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, iincl, o);
+        if (lane >= o)
+            iincl += v;
+    }
+    if (lane == 31)
+        winc[warp] = iincl;
+    sum_bar(bar);
+
+    // A first record that continues the previous thread's last run is
+    // dropped: the two runs become one op.
+    const int tag0 = cnt > 0 ? rec_tag(mine[0].key) : -1;
+    const bool drop = tag0 != -1 && tag0 != kTagSingle && tag0 != kTagChunk && t > 0 && tags[t - 1] == tag0;
+    const int keep = cnt - (drop ? 1 : 0);
+    int cincl = keep;
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, cincl, o);
+        if (lane >= o)
+            cincl += v;
+    }
+    if (lane == 31)
+        wcnt[warp] = cincl;
+    sum_bar(bar);
+    int coff = cincl - keep, ioff = iincl - inc_total;
+    for (int w = 0; w < warp; ++w) {
+        coff += wcnt[w];
+        ioff += winc[w];
+    }
+    const int total = wcnt[0] + wcnt[1] + wcnt[2] + wcnt[3];
+    for (int k = drop ? 1 : 0; k < cnt; ++k) {
+        SumRec r = mine[k];
+        r.cum += ioff;
+        list[coff + k - (drop ? 1 : 0)] = r;
+    }
+    if (t == 0)  // sentinel: where the last op ends, and the final total
+        list[total] = list[total + 1] = SumRec{n, winc[0] + winc[1] + winc[2] + winc[3]};
+    sum_bar(bar);
+
     if (warp == 0) {
-        const float s = sum_walk(xs, *head_value, slots, nops);
+        float s = 0.0f;
+        int k = 0;
+        while (k < total) {
+            const int idx = k + lane;
+            const bool valid = idx < total;
+            const int ci = valid ? idx : total;  // the sentinel (and the slot after it) past the end
+            const SumRec rec = list[ci], nx = list[ci + 1];
+            const int tag = rec_tag(rec.key);
+            const float a = sq_rn(xs[min(rec_first(rec.key), n - 1)]);
+            // a run is exact when s starts inside binade e and the sum stays
+            // below 2^(e+1): 0 <= d < 2^24 with u = 2^(e-23) normal makes
+            // d * u a float, and s and d * u are multiples of u
+            const int d = nx.cum - rec.cum;
+            const bool single = tag == kTagSingle;
+            const bool run = valid && !single && tag != kTagChunk && d >= 0 && d < (1 << 24);
+            const int e = run ? tag - 128 : 0;
+            const float addend = !valid ? 0.0f : single ? a : run ? mul_rn((float)d, pow2f(e - 23)) : 0.0f;
+            bool ok = !valid || single || run;  // a chunk (or a bad d) fails
+            abuf[lane] = addend;
+            __syncwarp();
+            float ad[32];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 v = reinterpret_cast<const float4*>(abuf)[q];
+                ad[4 * q] = v.x;
+                ad[4 * q + 1] = v.y;
+                ad[4 * q + 2] = v.z;
+                ad[4 * q + 3] = v.w;
+            }
+            float cur = s, before = s, after = s;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float next = add_rn(cur, ad[j]);
+                before = lane == j ? cur : before;
+                after = lane == j ? next : after;
+                cur = next;
+            }
+            if (run)
+                ok = before >= pow2f(e) && before < pow2f(e + 1) && after < pow2f(e + 1);
+            const unsigned bad = __ballot_sync(0xffffffffu, !ok);
+            if (bad == 0) {
+                s = cur;
+                k += 32;
+                continue;
+            }
+            // replay the first failing op step by step, restart after it
+            const int f = __ffs(bad) - 1;
+            s = __shfl_sync(0xffffffffu, before, f);
+            s = sum_serial(xs, s, rec_first(list[k + f].key), rec_first(list[k + f + 1].key));
+            k += f + 1;
+        }
         if (lane == 0)
             *result = s;
     }
-    sum_bar(bar, 128);  // result ready
+    sum_bar(bar);
     return *result;
 }
 #endif

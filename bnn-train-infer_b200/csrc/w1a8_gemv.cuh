@@ -50,7 +50,7 @@ constexpr int kStatusBadInput = 1;  // an input row had NaN/Inf (F32) or -128 (I
 constexpr int kStatusNonFinite = 4; // a normalisation divisor was not finite
 constexpr uint32_t kBlockPad = 4;
 constexpr uint32_t kComputeWarps = 4;
-static_assert(kComputeWarps * 32 == 128 && kSumHeadWarp == 3, "exact_sumsq runs on the four compute warps");
+static_assert(kComputeWarps * 32 == kSumThreads, "exact_sumsq runs on the four compute warps");
 // Prologues that build the activations in the CTA hold up to this many inputs
 // (in registers: kMaxPrologueK / 512 float4 per compute thread).
 constexpr uint32_t kMaxPrologueK = 8192;
