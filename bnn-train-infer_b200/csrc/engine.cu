@@ -298,6 +298,7 @@ struct bnnd_context {
     cudaStream_t stream = nullptr;
     DevMem x, qkv, y, h, logits, kcache, vcache, rope_cos, rope_sin, scores;
     DevMem pos_d, tok_in, tok_next, tok_seq, hist, hist_count, status;
+    DevMem best;  // [rows] packed greedy pick of the lm_head epilogue
     DevMem mlp_a, mlp_b;
     size_t tok_seq_cap = 0;
     uint32_t hist_cap = 0;
@@ -573,10 +574,15 @@ cudaError_t launch_attention(bnnd_context* c, const bnn::eng::AttnArgs& a) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = c->pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, bnn::eng::attention_kernel, a);
+    if (a.hd == 128)
+        return cudaLaunchKernelEx(&cfg, bnn::eng::attention_kernel<128>, a);
+    if (a.hd == 64)
+        return cudaLaunchKernelEx(&cfg, bnn::eng::attention_kernel<64>, a);
+    return cudaErrorInvalidValue;
 }
 cudaError_t launch_linear(const bnnd_context* c, const bnn::GemvLaunch& cl, const Linear& l, const float* x,
-                          const float* gain, uint32_t rows, float* out, size_t out_stride, int* status) {
+                          const float* gain, uint32_t rows, float* out, size_t out_stride, int* status,
+                          unsigned long long* best = nullptr) {
     bnn::GemvArgs a = {};
     a.wblocks = l.m->wblocks;
     a.n = l.out;
@@ -593,6 +599,7 @@ cudaError_t launch_linear(const bnnd_context* c, const bnn::GemvLaunch& cl, cons
     a.out = reinterpret_cast<unsigned char*>(out);
     a.out_stride = out_stride;
     a.status = status;
+    a.best = best;
     g_next_bytes = ((double)l.out * l.in * 0.140625 + 4.0 * l.in + 4.0 * l.out) * rows;
     return bnn::launch_gemv(cl, rows, a, c->stream, c->pdl);
 }
@@ -607,7 +614,8 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
     cudaStream_t s = c->stream;
     int* status = c->status.as<int>();
     const int exact = c->params.exact;
-    bnn::eng::embed_kernel<<<R, 256, 0, s>>>(c->tok_in.as<int32_t>(), m->lm_head.m->wblocks, C, c->x.as<float>());
+    bnn::eng::embed_kernel<<<R, 256, 0, s>>>(c->tok_in.as<int32_t>(), m->lm_head.m->wblocks, C, c->x.as<float>(),
+                                             c->best.as<unsigned long long>());
     ck("embed_kernel");
     const size_t qkv_pitch = (size_t)(C + 2 * KV) * 4u;
     for (uint32_t l = 0; l < in.n_layers; ++l) {
@@ -650,15 +658,15 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
                                            (size_t)C * 4u, status));
     }
     if (with_logits) {
+        // out_norm + lm_head; the epilogue also takes the greedy pick
         ck("w1a8_gemv:lm_head", launch_linear(c, c->plan_head, m->lm_head, c->x.as<float>(), m->out_norm.as<float>(),
-                                              R, c->logits.as<float>(), (size_t)in.n_vocab * 4u, status));
-        bnn::eng::argmax_kernel<<<R, 1024, 0, s>>>(c->logits.as<float>(), in.n_vocab, c->tok_next.as<int32_t>(),
-                                                  status);
-        ck("argmax_kernel");
+                                              R, c->logits.as<float>(), (size_t)in.n_vocab * 4u, status,
+                                              c->best.as<unsigned long long>()));
     }
     bnn::eng::step_end_kernel<<<1, 32 * ((R + 31) / 32), 0, s>>>(
-        R, c->pos_d.as<uint32_t>(), c->tok_in.as<int32_t>(), c->tok_next.as<int32_t>(), c->hist.as<int32_t>(),
-        c->hist_count.as<uint32_t>(), c->hist_cap, with_logits ? 1 : 0);
+        R, c->pos_d.as<uint32_t>(), c->tok_in.as<int32_t>(), c->tok_next.as<int32_t>(),
+        c->best.as<unsigned long long>(), c->hist.as<int32_t>(), c->hist_count.as<uint32_t>(), c->hist_cap,
+        with_logits ? 1 : 0);
     ck("step_end_kernel");
     const cudaError_t tail = cudaGetLastError();
     if (tail != cudaSuccess && ck.err == cudaSuccess)
@@ -705,7 +713,8 @@ BNND_Status create_llm_context(bnnd_context* c) {
         (st = dev_alloc(c->logits, (size_t)R * in.n_vocab * 4)) || (st = dev_alloc(c->kcache, cache)) ||
         (st = dev_alloc(c->vcache, cache)) || (st = dev_alloc(c->pos_d, (size_t)R * 4)) ||
         (st = dev_alloc(c->tok_in, (size_t)R * 4)) || (st = dev_alloc(c->tok_next, (size_t)R * 4)) ||
-        (st = dev_alloc(c->hist_count, 4)) || (st = dev_alloc(c->status, 4)))
+        (st = dev_alloc(c->hist_count, 4)) || (st = dev_alloc(c->status, 4)) ||
+        (st = dev_alloc(c->best, (size_t)R * 8)))
         return st;
     c->hist_cap = c->n_ctx;
     if ((st = dev_alloc(c->hist, (size_t)c->hist_cap * R * 4)))
@@ -730,7 +739,7 @@ BNND_Status create_llm_context(bnnd_context* c) {
         if (p->smem > bnn::kGemvSmemBudget)
             return fail(BNND_ENOTSUP, "hidden/ffn width too large for the contraction kernel");
     const uint32_t kv_mul = in.heads / in.kv_heads;
-    if (in.head_dim % 32 != 0 || in.head_dim > 256 || kv_mul > 16 ||
+    if ((in.head_dim != 64 && in.head_dim != 128) || kv_mul > 16 ||
         kv_mul * in.head_dim > bnn::eng::kAttnThreads * bnn::eng::kAttnMaxChains)
         return fail(BNND_ENOTSUP, "attention shape (head_dim %u, %u query heads per KV head) not supported",
                     in.head_dim, kv_mul);
@@ -743,7 +752,10 @@ BNND_Status create_llm_context(bnnd_context* c) {
             return st;
     }
     c->attn_smem = ap.total;
-    CUDA_OR(cudaFuncSetAttribute(bnn::eng::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    CUDA_OR(cudaFuncSetAttribute(bnn::eng::attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kAttnSmemBudget),
+            BNND_EIO);
+    CUDA_OR(cudaFuncSetAttribute(bnn::eng::attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kAttnSmemBudget),
             BNND_EIO);
     if ((st = capture_step(c, true, &c->graph_logits)) || (st = capture_step(c, false, &c->graph_prefill)))

@@ -6,10 +6,11 @@
 //   embed_kernel            qwen3_embed               qwen3.c:374-385
 //   attention_kernel        per-head q/k RMSNorm, RoPE, KV append and
 //                           causal softmax attention  qwen3.c:418-478
-//   argmax_kernel           greedy pick + finite check  bnn-infer-v2.c:48-54, engine.c:262-267
 //   mlp_post_kernel         post_scale/bias + ReLU    bnn-mlp.c:189-193
-// RMSNorm before a linear, the row quantisation and SwiGLU run inside the
-// W1A8 linears (w1a8_gemv.cuh prologues/epilogues). In exact mode every long
+// RMSNorm before a linear, the row quantisation, SwiGLU and the greedy pick
+// (bnn-infer-v2.c:48-54, engine.c:262-267: first index of the maximum, any
+// non-finite logit an error) run inside the W1A8 linears (w1a8_gemv.cuh
+// prologues/epilogues). In exact mode every long
 // sum is accumulated serially in index order, as the reference does; fast
 // mode uses a fixed-order tree instead.
 #pragma once
@@ -74,8 +75,11 @@ static __device__ float block_sum_ordered(const float* vals, uint32_t n, bool ex
 
 // qwen3_embed: x[c] = bit ? scale : -scale, read from lm_head's packed
 // blocks (token_embd and lm_head are the same tied matrix).
-__global__ void embed_kernel(const int32_t* tokens, const unsigned char* wblocks, uint32_t c, float* x) {
+__global__ void embed_kernel(const int32_t* tokens, const unsigned char* wblocks, uint32_t c, float* x,
+                             unsigned long long* best) {
     const uint32_t row = blockIdx.x;
+    if (threadIdx.x == 0)
+        best[row] = 0ull;  // the step's greedy pick starts empty
     const uint32_t tok = (uint32_t)tokens[row];
     const uint32_t groups = c / kGroup;
     const uint32_t r = tok % kRowBlock;
@@ -122,7 +126,7 @@ struct AttnArgs {
 };
 
 struct AttnSmem {
-    size_t bars, red, q, kn, vn, sc, ring, stage_bytes, total;
+    size_t bars, red, q, kn, vn, gq, gk, rc, rs, sc, ring, stage_bytes, total;
 };
 
 __host__ __device__ inline AttnSmem attn_smem_plan(uint32_t hd, uint32_t kv_mul, uint32_t n_ctx, bool sc_smem) {
@@ -132,7 +136,11 @@ __host__ __device__ inline AttnSmem attn_smem_plan(uint32_t hd, uint32_t kv_mul,
     p.q = p.red + 64 * 4;                      // [kv_mul][hd]
     p.kn = p.q + (size_t)kv_mul * hd * 4;      // [hd]
     p.vn = p.kn + (size_t)hd * 4;              // [hd]
-    p.sc = p.vn + (size_t)hd * 4;              // [kv_mul][n_ctx] when in shared memory
+    p.gq = p.vn + (size_t)hd * 4;              // q_norm gain [hd]
+    p.gk = p.gq + (size_t)hd * 4;              // k_norm gain [hd]
+    p.rc = p.gk + (size_t)hd * 4;              // cos row of this position [hd/2]
+    p.rs = p.rc + (size_t)hd * 2;              // sin row [hd/2]
+    p.sc = p.rs + (size_t)hd * 2;              // [kv_mul][n_ctx] when in shared memory
     p.ring = (p.sc + (sc_smem ? (size_t)kv_mul * n_ctx * 4 : 0) + 127) & ~(size_t)127;
     p.stage_bytes = (size_t)kAttnTile * (hd + 4) * 4;  // K rows padded by 4 floats; V tiles dense
     p.total = p.ring + kAttnStages * p.stage_bytes;
@@ -140,67 +148,77 @@ __host__ __device__ inline AttnSmem attn_smem_plan(uint32_t hd, uint32_t kv_mul,
 }
 
 // qwen3_rmsnorm of one head vector (HD floats in shared memory, by one warp)
-// followed by qwen3_rope (qwen3.c:418-438), in place. Returns false when the
-// divisor is not finite or zero.
-__device__ inline bool attn_norm_rope(float* v, uint32_t hd, const float* gain, const float* cs, const float* sn,
-                                      float eps, bool exact) {
+// followed by qwen3_rope (qwen3.c:418-438), in place; gain, cos and sin rows
+// in shared memory. Returns false when the divisor is not finite or zero.
+template <int HD>
+__device__ inline bool attn_norm_rope(float* v, const float* gain, const float* cs, const float* sn, float eps,
+                                      bool exact) {
+    constexpr int kPer = HD / 32;
     const uint32_t lane = threadIdx.x & 31;
+    float x[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k)
+        x[k] = v[lane + 32 * k];
     float sum = 0.0f;
     if (exact) {
         // the reference's serial sum, index order (loads batched ahead)
         if (lane == 0) {
-            for (uint32_t i = 0; i < hd; i += 8) {
-                float a[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
+            for (int i = 0; i < HD; i += 16) {
+                float a[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
                     a[j] = __fmul_rn(v[i + j], v[i + j]);
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
+                for (int j = 0; j < 16; ++j)
                     sum = __fadd_rn(sum, a[j]);
             }
         }
         sum = __shfl_sync(0xffffffffu, sum, 0);
     } else {
-        for (uint32_t i = lane; i < hd; i += 32)
-            sum = __fadd_rn(sum, __fmul_rn(v[i], v[i]));
+#pragma unroll
+        for (int k = 0; k < kPer; ++k)
+            sum = __fadd_rn(sum, __fmul_rn(x[k], x[k]));
         for (int o = 16; o > 0; o >>= 1)
             sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
     }
-    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)hd), eps));
+    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)HD), eps));
     if (!isfinite(rms) || rms == 0.0f)
         return false;
-    for (uint32_t i = lane; i < hd; i += 32)
-        v[i] = __fmul_rn(__fdiv_rn(v[i], rms), gain[i]);
-    __syncwarp();
-    const uint32_t half = hd / 2;
-    float out[8];  // hd <= 256
 #pragma unroll
-    for (uint32_t k = 0; k < 8; ++k) {
-        const uint32_t i = lane + 32u * k;
-        if (i < half)
-            out[k] = __fsub_rn(__fmul_rn(v[i], cs[i]), __fmul_rn(v[i + half], sn[i]));
-        else if (i < hd)
-            out[k] = __fadd_rn(__fmul_rn(v[i - half], sn[i - half]), __fmul_rn(v[i], cs[i - half]));
+    for (int k = 0; k < kPer; ++k)
+        v[lane + 32 * k] = __fmul_rn(__fdiv_rn(x[k], rms), gain[lane + 32 * k]);
+    __syncwarp();
+    constexpr int kHalf = HD / 2;
+    float out[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const int i = lane + 32 * k;
+        if (i < kHalf)
+            out[k] = __fsub_rn(__fmul_rn(v[i], cs[i]), __fmul_rn(v[i + kHalf], sn[i]));
+        else
+            out[k] = __fadd_rn(__fmul_rn(v[i - kHalf], sn[i - kHalf]), __fmul_rn(v[i], cs[i - kHalf]));
     }
     __syncwarp();
 #pragma unroll
-    for (uint32_t k = 0; k < 8; ++k)
-        if (lane + 32u * k < hd)
-            v[lane + 32u * k] = out[k];
+    for (int k = 0; k < kPer; ++k)
+        v[lane + 32 * k] = out[k];
     __syncwarp();
     return true;
 }
+
 // One block of kAttnThreads per (KV head g, row); it serves the kv_mul query
 // heads g * kv_mul .. that share the KV head (qwen3.c:440-478):
 //   scores[t] = fl(dot(q, k_t)) * scale, the dot accumulated serially over
 //   the head dimension; softmax with expf(s - max), a serial sum over t and a
 //   division; y_i = sum_t p_t * v_t,i, serial in t.
 // Fast mode replaces the serial sums of the norms and the softmax by trees.
+template <int HD>
 __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) {
     griddep_launch_dependents();
     extern __shared__ __align__(128) unsigned char e_smem[];
     const uint32_t g = blockIdx.x, row = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t HD = a.hd, kv_mul = a.heads / a.kv_heads;
+    const uint32_t kv_mul = a.heads / a.kv_heads;
     const bool sc_smem = a.scores == nullptr;
     const AttnSmem plan = attn_smem_plan(HD, kv_mul, a.n_ctx, sc_smem);
     uint64_t* full = reinterpret_cast<uint64_t*>(e_smem + plan.bars);
@@ -208,6 +226,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     float* q_s = reinterpret_cast<float*>(e_smem + plan.q);
     float* kn_s = reinterpret_cast<float*>(e_smem + plan.kn);
     float* vn_s = reinterpret_cast<float*>(e_smem + plan.vn);
+    float* gq_s = reinterpret_cast<float*>(e_smem + plan.gq);
+    float* gk_s = reinterpret_cast<float*>(e_smem + plan.gk);
+    float* rc_s = reinterpret_cast<float*>(e_smem + plan.rc);
+    float* rs_s = reinterpret_cast<float*>(e_smem + plan.rs);
     float* sc = sc_smem ? reinterpret_cast<float*>(e_smem + plan.sc)
                         : a.scores + ((size_t)row * a.heads + (size_t)g * kv_mul) * a.n_ctx;
     unsigned char* ring = e_smem + plan.ring;
@@ -218,7 +240,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     const size_t head_base = ((size_t)row * a.kv_heads + g) * a.n_ctx * HD;
     const float* kc = a.kcache + head_base;
     const float* vc = a.vcache + head_base;
-    const uint32_t kstride = HD + 4;
+    constexpr uint32_t kstride = HD + 4;
 
     if (tid == 0) {
         for (uint32_t s = 0; s < kAttnStages; ++s)
@@ -248,6 +270,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     if (warp == 0)
         for (uint32_t L = 0; L < kAttnStages && L < nloads; ++L)
             issue(L);
+    // weights and rope rows do not depend on earlier kernels either
+    for (uint32_t i = tid; i < HD; i += kAttnThreads) {
+        gq_s[i] = a.q_norm[i];
+        gk_s[i] = a.k_norm[i];
+    }
+    for (uint32_t i = tid; i < HD / 2; i += kAttnThreads) {
+        rc_s[i] = a.rope_cos[(size_t)pos * (HD / 2) + i];
+        rs_s[i] = a.rope_sin[(size_t)pos * (HD / 2) + i];
+    }
 
     // ---- wait for the q|k|v projection; norm + rope of the q heads and the k head
     griddep_wait();
@@ -262,11 +293,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     if (tid == 0 && *a.status != 0)
         *flag = 1;  // an earlier kernel failed: skip the work, keep the copy protocol
     __syncthreads();
-    const float* cs = a.rope_cos + (size_t)pos * (HD / 2);
-    const float* sn = a.rope_sin + (size_t)pos * (HD / 2);
     if (warp <= kv_mul) {
         float* v = warp < kv_mul ? q_s + (size_t)warp * HD : kn_s;
-        if (!attn_norm_rope(v, HD, warp < kv_mul ? a.q_norm : a.k_norm, cs, sn, a.eps, a.exact != 0) && lane == 0) {
+        if (!attn_norm_rope<HD>(v, warp < kv_mul ? gq_s : gk_s, rc_s, rs_s, a.eps, a.exact != 0) && lane == 0) {
             *flag = 1;
             atomicOr(a.status, kStatusNonFinite);
         }
@@ -300,6 +329,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
                 const float4* k4 = reinterpret_cast<const float4*>(kt + (size_t)tt * kstride);
                 const float4* q4 = reinterpret_cast<const float4*>(q_s + (size_t)h * HD);
                 float dot = 0.0f;
+#pragma unroll
                 for (uint32_t i = 0; i < HD / 4; ++i) {
                     const float4 kk = k4[i], qq = q4[i];
                     dot = __fadd_rn(dot, __fmul_rn(qq.x, kk.x));
@@ -409,7 +439,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
                     const uint32_t h = ch / HD, d = ch % HD;
                     const float* p = sc + (size_t)h * a.n_ctx + t0;
                     float v = acc[c];
-                    for (uint32_t tt = 0; tt < rows_in; ++tt)
+                    uint32_t tt = 0;
+                    for (; tt + 8 <= rows_in; tt += 8) {
+                        float pv[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            pv[j] = __fmul_rn(p[tt + j], vt[(size_t)(tt + j) * HD + d]);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            v = __fadd_rn(v, pv[j]);
+                    }
+                    for (; tt < rows_in; ++tt)
                         v = __fadd_rn(v, __fmul_rn(p[tt], vt[(size_t)tt * HD + d]));
                     acc[c] = v;
                 }
@@ -430,64 +470,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     }
 }
 
-// Greedy pick per row: the first index holding the maximum (strict > scan in
-// index order); any non-finite logit flags the step (BNNE_Decode's check).
-__global__ void argmax_kernel(const float* logits, uint32_t v, int32_t* out, int* status) {
-    __shared__ float bv[32];
-    __shared__ uint32_t bi[32];
-    __shared__ int bad_any;
-    const uint32_t row = blockIdx.x;
-    const float* l = logits + (size_t)row * v;
-    if (threadIdx.x == 0)
-        bad_any = 0;
-    __syncthreads();
-    float best = -INFINITY;
-    uint32_t idx = 0xffffffffu;
-    int bad = 0;
-    for (uint32_t i = threadIdx.x; i < v; i += blockDim.x) {
-        const float x = l[i];
-        bad |= !isfinite(x);
-        if (x > best || (x == best && i < idx)) {
-            best = x;
-            idx = i;
-        }
-    }
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-        const uint32_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (ob > best || (ob == best && oi < idx)) {
-            best = ob;
-            idx = oi;
-        }
-    }
-    if (bad)
-        bad_any = 1;
-    const uint32_t w = threadIdx.x >> 5;
-    if ((threadIdx.x & 31) == 0) {
-        bv[w] = best;
-        bi[w] = idx;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (uint32_t k = 1; k < (blockDim.x >> 5); ++k)
-            if (bv[k] > best || (bv[k] == best && bi[k] < idx)) {
-                best = bv[k];
-                idx = bi[k];
-            }
-        out[row] = (int32_t)(idx == 0xffffffffu ? 0 : idx);
-        if (bad_any)
-            atomicOr(status, kStatusNonFinite);
-    }
-}
-
-// End of a decode step: advance every row's position; the greedy pick
-// becomes the next input and is appended to the generation history.
-__global__ void step_end_kernel(uint32_t rows, uint32_t* pos, int32_t* tok_in, const int32_t* tok_next,
-                                int32_t* hist, uint32_t* hist_count, uint32_t hist_cap, int has_logits) {
+// End of a decode step: advance every row's position; the greedy pick (the
+// lm_head epilogue's packed key: index = ~low word) becomes the next input
+// and is appended to the generation history.
+__global__ void step_end_kernel(uint32_t rows, uint32_t* pos, int32_t* tok_in, int32_t* tok_next,
+                                const unsigned long long* best, int32_t* hist, uint32_t* hist_count,
+                                uint32_t hist_cap, int has_logits) {
     const uint32_t r = threadIdx.x;
     if (r < rows) {
         pos[r] += 1;
         if (has_logits) {
+            const unsigned long long b = best[r];
+            tok_next[r] = b ? (int32_t)(0xffffffffu - (uint32_t)(b & 0xffffffffull)) : 0;
             tok_in[r] = tok_next[r];
             const uint32_t h = *hist_count;
             if (h < hist_cap)

@@ -111,7 +111,19 @@ struct GemvArgs {
     unsigned char* out;            // first logical output row
     size_t out_stride;             // bytes between output rows
     int* status;
+    // kEpiView: when set, best[m] collects max over the row's outputs of
+    // (order-preserving bits of the value) << 32 | ~index, i.e. the greedy
+    // pick (first index of the maximum); non-finite outputs set the status
+    unsigned long long* best;
 };
+
+// 64-bit argmax key of output `n` with value y (-0 counts as +0; larger
+// values, then smaller indices, give larger keys).
+__device__ __forceinline__ unsigned long long argmax_key(float y, uint32_t n) {
+    const uint32_t u = y == 0.0f ? 0u : __float_as_uint(y);
+    const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)ord << 32) | (0xffffffffu - n);
+}
 
 struct GemvSmem {
     size_t bars, rs, act, tot, xbuf, seg, dsm, epi, stage, total;
@@ -367,6 +379,7 @@ __global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
     const bool abort = flags[0] != 0;
 
     // ---- contraction over this CTA's tiles
+    unsigned long long best0 = 0ull, best1 = 0ull;  // kEpiView argmax: outputs p = lane, lane + 32
     const uint32_t r = lane & 7;
     const uint32_t my_block = warp / wpb, part = warp % wpb;
     int16_t* blk_d = dsm + (size_t)my_block * mrows * kRowBlock * G;
@@ -426,6 +439,15 @@ __global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
                             acc = __fmul_rn(acc, rs_s[mm]);
                         if (EPI == kEpiView) {
                             store_f32_any(a.out + (size_t)(m0 + mm) * a.out_stride + (size_t)n * 4u, acc);
+                            if (a.best) {
+                                if (!isfinite(acc))
+                                    atomicOr(a.status, kStatusNonFinite);
+                                const unsigned long long key = argmax_key(acc, n);
+                                if (p < 32)
+                                    best0 = key > best0 ? key : best0;
+                                else
+                                    best1 = key > best1 ? key : best1;
+                            }
                         } else if (EPI == kEpiResidual) {
                             float* dst = reinterpret_cast<float*>(a.out + (size_t)(m0 + mm) * a.out_stride) + n;
                             *dst = __fadd_rn(*dst, acc);
@@ -456,6 +478,21 @@ __global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
         __syncwarp();
         if (lane == 0)
             mbar_arrive(&empty[s]);  // this warp no longer reads the stage
+    }
+    if (EPI == kEpiView && a.best != nullptr && part == 0) {
+        // lanes 8k..8k+7 hold outputs of one activation row: reduce, one atomic
+#pragma unroll
+        for (uint32_t k = 0; k < 2; ++k) {
+            unsigned long long b = k == 0 ? best0 : best1;
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) {
+                const unsigned long long ob = __shfl_xor_sync(0xffffffffu, b, o);
+                b = ob > b ? ob : b;
+            }
+            const uint32_t p = lane + 32u * k;
+            if ((lane & 7) == 0 && p < mrows * kRowBlock && b != 0ull)
+                atomicMax(&a.best[m0 + p / kRowBlock], b);
+        }
     }
 }
 
