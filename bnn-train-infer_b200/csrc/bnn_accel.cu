@@ -403,8 +403,11 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
                               size_t in_stride, size_t out_stride) {
     const BNN_Matrix m = job->matrix;
     const uint32_t K = m->in_features, G = m->groups, M = job->rows;
-    const size_t act_bytes = align256((size_t)M * K);
-    const size_t tot_bytes = align256((size_t)M * G * 4u);
+    // From kMmaMinRows rows the group dots run on the tensor cores
+    // (w1a8_mma.cuh); below, on the dp4a contraction (w1a8_gemv.cuh).
+    const bool mma = M >= bnn::kMmaMinRows;
+    const size_t act_bytes = align256(mma ? bnn::mma_a_bytes(M, G) : (size_t)M * K);
+    const size_t tot_bytes = mma ? 0 : align256((size_t)M * G * 4u);
     const size_t scl_bytes = align256((size_t)M * 4u);
     BNN_Status st = ensure_scratch(device, act_bytes + tot_bytes + scl_bytes);
     if (st != BNN_OK)
@@ -417,13 +420,14 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
 
     if (cudaMemsetAsync(device->d_status, 0, sizeof(int), s) != cudaSuccess)
         return BNN_EIO;
-    bnn::PrepArgs pa;
+    bnn::PrepArgs pa = {};
     pa.in = job->input.buffer->data + job->input.offset;
     pa.in_stride = in_stride;
     pa.kind = in_type == BNN_TYPE_F32 ? bnn::kInputF32 : bnn::kInputI8;
     pa.k = K;
     pa.m = M;
     pa.act = act;
+    pa.a_sw = mma ? base : nullptr;
     pa.totals = totals;
     pa.row_scale = rscale;
     pa.status = device->d_status;
@@ -435,6 +439,7 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
         bnn::PrepArgs chunk = pa;
         chunk.in = pa.in + (size_t)r0 * in_stride;
         chunk.act = act + (size_t)r0 * G * bnn::kWordsPerGroup;
+        chunk.row0 = r0;
         chunk.totals = totals + (size_t)r0 * G;
         chunk.row_scale = rscale + r0;
         chunk.m = rows;
@@ -442,6 +447,26 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
     }
 
     const int epi = job->operation == BNN_OP_DOT_GROUPS ? bnn::kEpiDotGroups : bnn::kEpiView;
+    unsigned char* out = job->output.buffer->data + job->output.offset;
+    if (mma) {
+        const uint32_t rows_per_launch = 65535u * bnn::kMmaM;
+        for (uint32_t r0 = 0; r0 < M; r0 += rows_per_launch) {
+            bnn::MmaArgs ma = {};
+            ma.wblocks = m->wblocks;
+            ma.n = m->out_features;
+            ma.groups = G;
+            ma.m = std::min<uint32_t>(M - r0, rows_per_launch);
+            ma.a_sw = base + (size_t)(r0 / bnn::kMmaM) * G * bnn::kMmaATile;
+            ma.row_scale = in_type == BNN_TYPE_F32 ? rscale + r0 : nullptr;
+            ma.out = out + (size_t)r0 * out_stride;
+            ma.out_stride = out_stride;
+            ma.epi = epi;
+            ma.status = device->d_status;
+            if (bnn::launch_mma(ma, s) != cudaSuccess)
+                return BNN_EIO;
+        }
+        return BNN_OK;
+    }
     const bnn::GemvLaunch cl = bnn::plan_gemv(device->sm_count, m->out_features, G, M, bnn::kProSliced, epi);
     const uint32_t rows_per_launch = 65535u * bnn::kRowsPerCta;
     for (uint32_t r0 = 0; r0 < M; r0 += rows_per_launch) {
@@ -457,7 +482,7 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
         ga.act = act + (size_t)r0 * G * bnn::kWordsPerGroup;
         ga.totals = totals + (size_t)r0 * G;
         ga.row_scale = in_type == BNN_TYPE_F32 ? rscale + r0 : nullptr;
-        ga.out = job->output.buffer->data + job->output.offset + (size_t)r0 * out_stride;
+        ga.out = out + (size_t)r0 * out_stride;
         ga.out_stride = out_stride;
         ga.status = device->d_status;
         if (bnn::launch_gemv(cl, rows, ga, s, false) != cudaSuccess)

@@ -89,7 +89,7 @@ extern "C" BNN_Status bnn_b200_gemm_f32_noalloc(BNN_Matrix matrix, const float* 
     // The status word keeps the previous call's verdict: clear it first.
     if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess)
         return BNN_EIO;
-    bnn::PrepArgs pa;
+    bnn::PrepArgs pa = {};
     pa.in = reinterpret_cast<const unsigned char*>(x);
     pa.in_stride = (size_t)K * 4u;
     pa.kind = bnn::kInputF32;

@@ -1,0 +1,344 @@
+// w1a8_mma.cuh - the W1A8 contraction for many activation rows on the
+// 5th-generation tensor cores (ComputeRow, soft-bnn-accelerator.c:219-276).
+//
+// With weights w in {-1, +1} and int8 activations q, the reference's group
+// dot D = 2 * pos - total (soft :251-258) is exactly sum_k w_k * q_k, an int8
+// x int8 product with an int32 sum. So a tile of 128 activation rows x 32
+// output rows runs as tcgen05.mma kind::i8 (A = q, B = +-1, both K-major,
+// 128-byte swizzle), four K=32 instructions per 128-wide group, each group
+// into its own TMEM accumulator (32 columns). Groups are processed in chunks
+// of kMmaChunk, double-buffered in TMEM (2 x 8 x 32 = 512 columns), so the
+// MMAs of one chunk overlap the epilogue of the previous one. The epilogue
+// reads D per group with tcgen05.ld and does the reference's FP32 work in
+// its order: acc = fl(acc + fl(F32(scale_g) * D_g)) for increasing g, then
+// Y = fl(acc * s) (F32 ops) or Z = acc (I8 ops); DOT_GROUPS stores (int16)D.
+//
+// Operands in shared memory:
+//   A  the prep kernel writes the quantised rows pre-tiled: block (m_tile, g)
+//      is the 16 KB 128B-swizzled K-major image of 128 rows x 128 bytes, so
+//      one 1D bulk copy per group fills a ring stage;
+//   B  the tile's four 8-row weight blocks (bits and scales of every group,
+//      w1a8_gemv.cuh layout) arrive with one bulk copy; the epilogue warps
+//      expand each chunk's bits to +-1 bytes in the swizzled layout.
+//
+// Warp roles (192 threads): warp 0 streams the copies, warp 1 owns the TMEM
+// allocation and one of its lanes issues the MMAs, warps 2-5 expand B and
+// run the epilogue (warp w reads TMEM lanes 32 * (w % 4) .. + 31, i.e. tile
+// rows). Every wait is bounded; a timeout sets the status word, and the TMEM
+// is released only after a final commit shows every issued MMA completed.
+#pragma once
+
+#include <cstdint>
+#include "bnn_device.cuh"
+#include "bnn_sync.cuh"
+#include "w1a8_gemv.cuh"
+
+namespace bnn {
+
+constexpr uint32_t kMmaM = 128;                      // activation rows per tile (TMEM lanes)
+constexpr uint32_t kMmaN = 32;                       // output rows per tile (four weight blocks)
+constexpr uint32_t kMmaChunk = 8;                    // groups per TMEM buffer
+constexpr uint32_t kMmaStages = 4;                   // A ring depth
+constexpr uint32_t kMmaATile = kMmaM * kGroup;       // 16 KB: one group of 128 rows
+constexpr uint32_t kMmaBTile = kMmaN * kGroup;       // 4 KB: one group of 32 rows as +-1 bytes
+constexpr uint32_t kMmaThreads = 192;
+constexpr uint32_t kMmaTmemCols = 2 * kMmaChunk * kMmaN;  // 512
+constexpr uint32_t kMmaMinRows = 64;                 // BNN_Execute's tensor-core threshold
+
+// Instruction descriptor: D s32, A and B signed 8-bit, both K-major, N, M.
+constexpr uint32_t kMmaIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((kMmaN >> 3) << 17) | ((kMmaM >> 4) << 24);
+
+// Byte offset of activation (row, group g, 16-byte chunk c) in the pre-tiled A.
+__host__ __device__ inline size_t mma_a_offset(uint32_t row, uint32_t g, uint32_t groups, uint32_t c) {
+    const uint32_t mt = row / kMmaM, r = row % kMmaM;
+    return ((size_t)mt * groups + g) * kMmaATile + (r / 8u) * 1024u + (r % 8u) * 128u + ((c ^ (r % 8u)) * 16u);
+}
+
+inline size_t mma_a_bytes(uint32_t rows, uint32_t groups) {
+    return (size_t)((rows + kMmaM - 1) / kMmaM) * groups * kMmaATile;
+}
+
+struct MmaArgs {
+    const unsigned char* wblocks;  // packed 8-row blocks, padded to 4 blocks
+    uint32_t n, groups, m;         // output rows, K/128, activation rows of this launch
+    const unsigned char* a_sw;     // pre-tiled int8 activations of this launch
+    const float* row_scale;        // [M], or nullptr: the I8 ops return Z unscaled
+    unsigned char* out;            // first logical output row
+    size_t out_stride;             // bytes between output rows
+    int epi;                       // kEpiView or kEpiDotGroups
+    int* status;
+};
+
+struct MmaSmem {
+    size_t a, b, w, bars, total;
+};
+
+__host__ __device__ inline MmaSmem mma_smem_plan(uint32_t groups) {
+    MmaSmem p;
+    p.a = 0;
+    p.b = p.a + (size_t)kMmaStages * kMmaATile;
+    p.w = p.b + (size_t)2 * kMmaChunk * kMmaBTile;
+    p.bars = (p.w + (size_t)4 * groups * 144u + 15) & ~(size_t)15;
+    p.total = p.bars + 256 + 1024;  // barriers and words, plus slack to 1024-align the base
+    return p;
+}
+
+// ---- tcgen05 primitives (inline PTX)
+__device__ __forceinline__ uint64_t mma_smem_desc(uint32_t saddr) {
+    // K-major, 128-byte swizzle: 8-row groups 1024 B apart (SBO), LBO 16 B
+    // (unused for this layout), descriptor version 1, layout type 2
+    const uint32_t lo = ((saddr >> 4) & 0x3fffu) | (1u << 16);
+    const uint32_t hi = (1024u >> 4) | (1u << 14) | (2u << 29);
+    return ((uint64_t)hi << 32) | lo;
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+    const uint32_t mask = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(kMmaIdesc), "r"(accumulate), "r"(mask));
+}
+
+// Arrives on `bar` once every tcgen05 operation this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Four weight bits (LSB first) as four bytes: +1 for a set bit, -1 otherwise.
+__device__ __forceinline__ uint32_t expand_signs4(uint32_t v) {
+    const uint32_t b = (v * 0x00204081u) & 0x01010101u;  // byte i = bit i
+    return (b * 0xfeu) ^ 0xffffffffu;
+}
+
+// Grid (ceil(N / 32), ceil(M / 128)); kMmaThreads threads; mma_smem_plan().total
+// bytes of dynamic shared memory.
+static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs a) {
+    extern __shared__ __align__(1024) unsigned char mma_smem_raw[];
+    // the swizzle pattern follows shared-memory address bits: 1024-align the base
+    const uint32_t raw = smem_addr(mma_smem_raw);
+    unsigned char* sm = mma_smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    const uint32_t G = a.groups;
+    const MmaSmem plan = mma_smem_plan(G);
+    unsigned char* a_ring = sm + plan.a;
+    unsigned char* b_buf = sm + plan.b;
+    const unsigned char* wtile = sm + plan.w;
+    uint64_t* wfull = reinterpret_cast<uint64_t*>(sm + plan.bars);
+    uint64_t* afull = wfull + 1;
+    uint64_t* aempty = afull + kMmaStages;
+    uint64_t* bready = aempty + kMmaStages;
+    uint64_t* dready = bready + 2;
+    uint64_t* tfree = dready + 2;
+    uint64_t* mdone = tfree + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
+
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t nt = blockIdx.x, mt = blockIdx.y;
+    const uint32_t nchunks = (G + kMmaChunk - 1) / kMmaChunk;
+    const uint32_t wbytes = 4u * G * 144u;
+
+    if (*a.status != 0)
+        return;  // an input row was rejected: no output is written
+
+    if (tid == 0) {
+        mbar_init(wfull, 1);
+        for (uint32_t s = 0; s < kMmaStages; ++s) {
+            mbar_init(&afull[s], 1);
+            mbar_init(&aempty[s], 1);
+        }
+        for (uint32_t b = 0; b < 2; ++b) {
+            mbar_init(&bready[b], 128);
+            mbar_init(&dready[b], 1);
+            mbar_init(&tfree[b], 128);
+        }
+        mbar_init(mdone, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(kMmaTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---- producer: the weight tile once, then one A block per group
+        if (lane == 0) {
+            mbar_arrive_expect_tx(wfull, wbytes);
+            bulk_g2s(sm + plan.w, a.wblocks + (size_t)nt * wbytes, wbytes, wfull);
+            uint32_t g = 0;
+            for (; g < G; ++g) {
+                const uint32_t s = g % kMmaStages;
+                if (g >= kMmaStages && !mbar_wait(&aempty[s], ((g / kMmaStages) - 1) & 1)) {
+                    atomicOr(a.status, kStatusTimeout);
+                    break;
+                }
+                mbar_arrive_expect_tx(&afull[s], kMmaATile);
+                bulk_g2s(a_ring + (size_t)s * kMmaATile, a.a_sw + ((size_t)mt * G + g) * kMmaATile, kMmaATile,
+                         &afull[s]);
+            }
+            // no copy may still be in flight when the CTA exits
+            for (uint32_t j = g > kMmaStages ? g - kMmaStages : 0; j < g; ++j)
+                if (!mbar_wait(&afull[j % kMmaStages], (j / kMmaStages) & 1))
+                    atomicOr(a.status, kStatusTimeout);
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer
+        if (lane == 0) {
+            for (uint32_t c = 0; c < nchunks; ++c) {
+                const uint32_t b = c & 1;
+                bool ok = mbar_wait(&bready[b], (c >> 1) & 1);
+                if (ok && c >= 2)
+                    ok = mbar_wait(&tfree[b], ((c >> 1) - 1) & 1);
+                if (!ok) {
+                    atomicOr(a.status, kStatusTimeout);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t g0 = c * kMmaChunk, gn = min(kMmaChunk, G - g0);
+                for (uint32_t gi = 0; gi < gn; ++gi) {
+                    const uint32_t g = g0 + gi, s = g % kMmaStages;
+                    if (!mbar_wait(&afull[s], (g / kMmaStages) & 1)) {
+                        atomicOr(a.status, kStatusTimeout);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_base = smem_addr(a_ring + (size_t)s * kMmaATile);
+                    const uint32_t b_base = smem_addr(b_buf + (size_t)(b * kMmaChunk + gi) * kMmaBTile);
+                    const uint32_t d = tmem + b * (kMmaChunk * kMmaN) + gi * kMmaN;
+#pragma unroll
+                    for (uint32_t k = 0; k < kGroup / 32; ++k)
+                        mma_i8(d, mma_smem_desc(a_base + 32u * k), mma_smem_desc(b_base + 32u * k), k);
+                    mma_commit(&aempty[s]);  // the A stage is free once these MMAs have read it
+                }
+                if (!ok)
+                    break;
+                mma_commit(&dready[b]);
+            }
+            mma_commit(mdone);  // completes when every MMA issued above has completed
+        }
+        __syncwarp();
+    } else {
+        // ---- warps 2..5: expand B chunks, then the ordered FP32 epilogue
+        const uint32_t et = tid - 64;           // 0..127
+        const uint32_t quad = warp & 3;         // TMEM lane quadrant this warp may read
+        const uint32_t row = quad * 32 + lane;  // tile row = TMEM lane
+        const uint32_t m = mt * kMmaM + row;
+        bool ok = mbar_wait(wfull, 0);
+        if (!ok)
+            atomicOr(a.status, kStatusTimeout);
+        auto expand = [&](uint32_t c) {
+            const uint32_t b = c & 1, g0 = c * kMmaChunk, gn = min(kMmaChunk, G - g0);
+            for (uint32_t p = et; p < gn * kMmaN * 8u; p += 128u) {
+                const uint32_t gi = p / (kMmaN * 8u), rest = p % (kMmaN * 8u), n = rest / 8u, j = rest % 8u;
+                const uint32_t bits = *reinterpret_cast<const uint16_t*>(wtile + (n / 8u) * G * 144u +
+                                                                         (g0 + gi) * 128u + (n % 8u) * 16u + j * 2u);
+                uint4 o;
+                o.x = expand_signs4(bits & 0xfu);
+                o.y = expand_signs4((bits >> 4) & 0xfu);
+                o.z = expand_signs4((bits >> 8) & 0xfu);
+                o.w = expand_signs4(bits >> 12);
+                *reinterpret_cast<uint4*>(b_buf + (size_t)(b * kMmaChunk + gi) * kMmaBTile + (n / 8u) * 1024u +
+                                          (n % 8u) * 128u + ((j ^ (n % 8u)) * 16u)) = o;
+            }
+            fence_proxy_async();  // the MMAs read these bytes through the async proxy
+            mbar_arrive(&bready[b]);
+        };
+        expand(0);
+        if (nchunks > 1)
+            expand(1);
+        float acc[kMmaN];
+#pragma unroll
+        for (uint32_t n = 0; n < kMmaN; ++n)
+            acc[n] = 0.0f;
+        const bool dot_groups = a.epi == kEpiDotGroups;
+        const bool live = m < a.m;
+        for (uint32_t c = 0; c < nchunks && ok; ++c) {
+            const uint32_t b = c & 1, g0 = c * kMmaChunk, gn = min(kMmaChunk, G - g0);
+            if (!mbar_wait(&dready[b], (c >> 1) & 1)) {
+                atomicOr(a.status, kStatusTimeout);
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            for (uint32_t gi = 0; gi < gn; ++gi) {
+                uint32_t d[kMmaN];
+                tmem_ld32(tmem + ((quad * 32u) << 16) + b * (kMmaChunk * kMmaN) + gi * kMmaN, d);
+                const uint32_t g = g0 + gi;
+                if (dot_groups) {
+                    if (live)
+                        for (uint32_t n = 0; n < kMmaN; ++n) {
+                            const uint32_t on = nt * kMmaN + n;
+                            if (on < a.n)
+                                store_i16_any(a.out + (size_t)m * a.out_stride + ((size_t)on * G + g) * 2u,
+                                              (int16_t)(int32_t)d[n]);
+                        }
+                } else {
+#pragma unroll
+                    for (uint32_t n = 0; n < kMmaN; ++n) {
+                        const float sc = h2f(*reinterpret_cast<const uint16_t*>(
+                            wtile + (n / 8u) * G * 144u + G * 128u + ((n % 8u) * G + g) * 2u));
+                        acc[n] = __fadd_rn(acc[n], __fmul_rn(sc, (float)(int32_t)d[n]));
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tfree[b]);
+            if (c + 2 < nchunks)
+                expand(c + 2);  // buffer b is free: the MMAs of chunk c have completed
+        }
+        if (ok && live && !dot_groups) {
+            const float s = a.row_scale ? a.row_scale[m] : 1.0f;
+            for (uint32_t n = 0; n < kMmaN; ++n) {
+                const uint32_t on = nt * kMmaN + n;
+                if (on < a.n)
+                    store_f32_any(a.out + (size_t)m * a.out_stride + (size_t)on * 4u,
+                                  a.row_scale ? __fmul_rn(acc[n], s) : acc[n]);
+            }
+        }
+    }
+
+    // ---- teardown: TMEM reads are done; free TMEM after every MMA completed
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        if (!mbar_wait(mdone, 0) && lane == 0)
+            atomicOr(a.status, kStatusTimeout);
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kMmaTmemCols));
+    }
+}
+
+// Launches the contraction of `a.m` rows (a.m <= 65535 * kMmaM) on `s`.
+inline cudaError_t launch_mma(const MmaArgs& a, cudaStream_t s) {
+    const MmaSmem p = mma_smem_plan(a.groups);
+    cudaError_t e = cudaFuncSetAttribute(w1a8_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.total);
+    if (e != cudaSuccess)
+        return e;
+    const dim3 grid((a.n + kMmaN - 1) / kMmaN, (a.m + kMmaM - 1) / kMmaM);
+    w1a8_mma_kernel<<<grid, kMmaThreads, p.total, s>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace bnn

@@ -11,6 +11,7 @@
 #include <cfloat>
 #include "bnn_device.cuh"
 #include "w1a8_gemv.cuh"
+#include "w1a8_mma.cuh"
 
 namespace bnn {
 
@@ -24,7 +25,9 @@ struct PrepArgs {
     size_t in_stride;         // bytes between rows
     int kind;                 // kInputI8 / kInputF32
     uint32_t k, m;
-    uint32_t* act;            // [M][G][32]
+    uint32_t* act;            // [M][G][32] sliced words (dp4a path), or
+    unsigned char* a_sw;      // non-null: pre-tiled rows for w1a8_mma_kernel instead
+    uint32_t row0;            // row index of this launch's first row within a_sw
     int32_t* totals;          // [M][G]
     float* row_scale;         // [M]
     int* status;
@@ -92,6 +95,17 @@ static __global__ void __launch_bounds__(kPrepThreads) w1a8_prep_kernel(PrepArgs
     __syncthreads();
 
     const uint32_t groups = a.k / kGroup;
+    if (a.a_sw) {
+        // tensor-core operand: 16-byte chunks into the 128B-swizzled row tiles
+        for (uint32_t c = tid; c < groups * 8u; c += kPrepThreads) {
+            const uint32_t g = c / 8u, j = c % 8u;
+            *reinterpret_cast<uint4*>(a.a_sw + mma_a_offset(a.row0 + m, g, groups, j)) =
+                *reinterpret_cast<const uint4*>(qs + g * kGroup + j * 16u);
+        }
+        if (tid == 0)
+            a.row_scale[m] = scale;
+        return;
+    }
     uint32_t* act = a.act + (size_t)m * groups * kWordsPerGroup;
     for (uint32_t w = tid; w < groups * kWordsPerGroup; w += kPrepThreads) {
         uint32_t g = w / kWordsPerGroup, tj = w % kWordsPerGroup;
