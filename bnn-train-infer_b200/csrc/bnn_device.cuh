@@ -89,6 +89,9 @@ __device__ __forceinline__ int8_t quantize_one(float x, float s) {
     return (int8_t)(int)r;
 }
 
+// The same, kept out of line: the rare exact path of RowQuantizer.
+static __device__ __noinline__ int8_t quantize_one_slow(float x, float s) { return quantize_one(x, s); }
+
 // Quantiser for one row with a known scale s, exactly equal to quantize_one
 // but without a division per element in the common case.
 // y = fl(x * fl(1/s)) differs from fl(x/s) by less than 2e-5 when |x/s| <= 127
@@ -107,12 +110,17 @@ struct RowQuantizer {
     __device__ __forceinline__ int8_t operator()(float x) const {
         if (!exact_only) {
             const float y = __fmul_rn(x, rcp);
-            if (fabsf(y - (floorf(y) + 0.5f)) > 3.0e-5f) {
-                float r = fminf(fmaxf(roundf(y), -127.0f), 127.0f);
-                return (int8_t)(int)r;
+            // t = fl(1.5 * 2^23 + y) holds RNE(y) as an integer (|y| < 2^22);
+            // y - RNE(y) is exact. Away from half-integers RNE equals the
+            // reference's round-half-away-from-zero.
+            const float t = __fadd_rn(y, 12582912.0f);
+            const float r = __fsub_rn(t, 12582912.0f);
+            if (fabsf(__fsub_rn(y, r)) < 0.49997f) {  // farther than 3e-5 from a half-integer
+                const int v = (int)(__float_as_uint(t) - 0x4b400000u);
+                return (int8_t)min(max(v, -127), 127);
             }
         }
-        return quantize_one(x, s);
+        return quantize_one_slow(x, s);
     }
 };
 

@@ -560,6 +560,19 @@ void rope_tables(const bnnd_model* m, uint32_t n_ctx, std::vector<float>* cs, st
 // One W1A8 linear: FP32 input rows x (stride l.in), RMSNorm gains when the
 // plan's prologue normalises, output rows of `out_stride` bytes.
 
+// Attention instantiations: head_dim 64/128 x 1/2/4/8 query heads per KV head.
+using AttnFn = void (*)(bnn::eng::AttnArgs);
+AttnFn attention_fn(uint32_t hd, uint32_t kv_mul) {
+    using namespace bnn::eng;
+#define BNN_ATTN_CASE(H, Q) \
+    if (hd == H && kv_mul == Q)  \
+        return attention_kernel<H, Q>;
+    BNN_ATTN_CASE(128, 1) BNN_ATTN_CASE(128, 2) BNN_ATTN_CASE(128, 4) BNN_ATTN_CASE(128, 8)
+    BNN_ATTN_CASE(64, 1) BNN_ATTN_CASE(64, 2) BNN_ATTN_CASE(64, 4) BNN_ATTN_CASE(64, 8)
+#undef BNN_ATTN_CASE
+    return nullptr;
+}
+
 // The attention kernel, launched like the linears (programmatic dependent
 // launch: it streams K/V tiles of earlier steps while the q|k|v projection
 // finishes).
@@ -574,11 +587,8 @@ cudaError_t launch_attention(bnnd_context* c, const bnn::eng::AttnArgs& a) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = c->pdl ? 1 : 0;
-    if (a.hd == 128)
-        return cudaLaunchKernelEx(&cfg, bnn::eng::attention_kernel<128>, a);
-    if (a.hd == 64)
-        return cudaLaunchKernelEx(&cfg, bnn::eng::attention_kernel<64>, a);
-    return cudaErrorInvalidValue;
+    const AttnFn fn = attention_fn(a.hd, a.heads / a.kv_heads);
+    return fn ? cudaLaunchKernelEx(&cfg, fn, a) : cudaErrorInvalidValue;
 }
 cudaError_t launch_linear(const bnnd_context* c, const bnn::GemvLaunch& cl, const Linear& l, const float* x,
                           const float* gain, uint32_t rows, float* out, size_t out_stride, int* status,
@@ -739,8 +749,7 @@ BNND_Status create_llm_context(bnnd_context* c) {
         if (p->smem > bnn::kGemvSmemBudget)
             return fail(BNND_ENOTSUP, "hidden/ffn width too large for the contraction kernel");
     const uint32_t kv_mul = in.heads / in.kv_heads;
-    if ((in.head_dim != 64 && in.head_dim != 128) || kv_mul > 16 ||
-        kv_mul * in.head_dim > bnn::eng::kAttnThreads * bnn::eng::kAttnMaxChains)
+    if (attention_fn(in.head_dim, kv_mul) == nullptr)
         return fail(BNND_ENOTSUP, "attention shape (head_dim %u, %u query heads per KV head) not supported",
                     in.head_dim, kv_mul);
     // scores of a block's query heads in shared memory when they fit, else in
@@ -748,14 +757,11 @@ BNND_Status create_llm_context(bnnd_context* c) {
     bnn::eng::AttnSmem ap = bnn::eng::attn_smem_plan(in.head_dim, kv_mul, c->n_ctx, true);
     if (ap.total > kAttnSmemBudget) {
         ap = bnn::eng::attn_smem_plan(in.head_dim, kv_mul, c->n_ctx, false);
-        if ((st = dev_alloc(c->scores, (size_t)R * in.heads * c->n_ctx * 4)))
+        if ((st = dev_alloc(c->scores, (size_t)R * in.heads * bnn::eng::attn_sc_stride(c->n_ctx) * 4)))
             return st;
     }
     c->attn_smem = ap.total;
-    CUDA_OR(cudaFuncSetAttribute(bnn::eng::attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)kAttnSmemBudget),
-            BNND_EIO);
-    CUDA_OR(cudaFuncSetAttribute(bnn::eng::attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    CUDA_OR(cudaFuncSetAttribute(attention_fn(in.head_dim, kv_mul), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kAttnSmemBudget),
             BNND_EIO);
     if ((st = capture_step(c, true, &c->graph_logits)) || (st = capture_step(c, false, &c->graph_prefill)))

@@ -105,7 +105,6 @@ __global__ void embed_kernel(const int32_t* tokens, const unsigned char* wblocks
 constexpr uint32_t kAttnThreads = 256;
 constexpr uint32_t kAttnTile = 128;
 constexpr uint32_t kAttnStages = 2;
-constexpr uint32_t kAttnMaxChains = 4;  // (q head, dim) chains per thread: kv_mul * head_dim <= 1024
 
 struct AttnArgs {
     const float* qkv;       // [rows][C + 2KV]: q | k | v projections
@@ -116,7 +115,7 @@ struct AttnArgs {
     const uint32_t* pos;    // [rows]
     float* kcache;          // this layer: [rows][kv_heads][n_ctx][HD]
     float* vcache;
-    float* scores;          // [rows][heads][n_ctx] when they do not fit in shared memory, else null
+    float* scores;          // [rows][heads][attn_sc_stride(n_ctx)] when they do not fit in shared memory, else null
     float* y;               // [rows][C]
     uint32_t c, kv, hd, heads, kv_heads, n_ctx;
     float eps;
@@ -124,6 +123,10 @@ struct AttnArgs {
     int exact;
     int* status;
 };
+
+// Scores of one query head occupy a row of this many floats (a multiple of
+// 4, so the V pass can read four probabilities at once).
+__host__ __device__ inline uint32_t attn_sc_stride(uint32_t n_ctx) { return (n_ctx + 3u) & ~3u; }
 
 struct AttnSmem {
     size_t bars, red, q, kn, vn, gq, gk, rc, rs, sc, ring, stage_bytes, total;
@@ -140,8 +143,8 @@ __host__ __device__ inline AttnSmem attn_smem_plan(uint32_t hd, uint32_t kv_mul,
     p.gk = p.gq + (size_t)hd * 4;              // k_norm gain [hd]
     p.rc = p.gk + (size_t)hd * 4;              // cos row of this position [hd/2]
     p.rs = p.rc + (size_t)hd * 2;              // sin row [hd/2]
-    p.sc = p.rs + (size_t)hd * 2;              // [kv_mul][n_ctx] when in shared memory
-    p.ring = (p.sc + (sc_smem ? (size_t)kv_mul * n_ctx * 4 : 0) + 127) & ~(size_t)127;
+    p.sc = p.rs + (size_t)hd * 2;              // [kv_mul][attn_sc_stride(n_ctx)] when in shared memory
+    p.ring = (p.sc + (sc_smem ? (size_t)kv_mul * attn_sc_stride(n_ctx) * 4 : 0) + 127) & ~(size_t)127;
     p.stage_bytes = (size_t)kAttnTile * (hd + 4) * 4;  // K rows padded by 4 floats; V tiles dense
     p.total = p.ring + kAttnStages * p.stage_bytes;
     return p;
@@ -213,12 +216,12 @@ __device__ inline bool attn_norm_rope(float* v, const float* gain, const float* 
 //   the head dimension; softmax with expf(s - max), a serial sum over t and a
 //   division; y_i = sum_t p_t * v_t,i, serial in t.
 // Fast mode replaces the serial sums of the norms and the softmax by trees.
-template <int HD>
+template <int HD, int KVM>
 __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) {
     griddep_launch_dependents();
     extern __shared__ __align__(128) unsigned char e_smem[];
     const uint32_t g = blockIdx.x, row = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t kv_mul = a.heads / a.kv_heads;
+    constexpr uint32_t kv_mul = KVM;  // query heads per KV head (a.heads / a.kv_heads)
     const bool sc_smem = a.scores == nullptr;
     const AttnSmem plan = attn_smem_plan(HD, kv_mul, a.n_ctx, sc_smem);
     uint64_t* full = reinterpret_cast<uint64_t*>(e_smem + plan.bars);
@@ -230,8 +233,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     float* gk_s = reinterpret_cast<float*>(e_smem + plan.gk);
     float* rc_s = reinterpret_cast<float*>(e_smem + plan.rc);
     float* rs_s = reinterpret_cast<float*>(e_smem + plan.rs);
+    const uint32_t sc_stride = attn_sc_stride(a.n_ctx);  // per-head rows of scores, float4-aligned
     float* sc = sc_smem ? reinterpret_cast<float*>(e_smem + plan.sc)
-                        : a.scores + ((size_t)row * a.heads + (size_t)g * kv_mul) * a.n_ctx;
+                        : a.scores + ((size_t)row * a.heads + (size_t)g * kv_mul) * sc_stride;
     unsigned char* ring = e_smem + plan.ring;
     int* flag = reinterpret_cast<int*>(red + 62);  // [0] abort: earlier failure, non-finite, timeout
 
@@ -339,7 +343,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
                 }
                 const float score = __fmul_rn(dot, a.scale);
                 bad |= !isfinite(score);
-                sc[(size_t)h * a.n_ctx + t0 + tt] = score;
+                sc[(size_t)h * sc_stride + t0 + tt] = score;
             }
         }
         fence_proxy_async();  // this thread's accesses to stage s come before the next bulk copy into it
@@ -359,7 +363,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
         if (warp < kv_mul) {
             float mx = -INFINITY;
             for (uint32_t t = lane; t < n; t += 32)
-                mx = fmaxf(mx, sc[(size_t)warp * a.n_ctx + t]);
+                mx = fmaxf(mx, sc[(size_t)warp * sc_stride + t]);
             for (int o = 16; o > 0; o >>= 1)
                 mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
             if (lane == 0)
@@ -368,12 +372,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
         __syncthreads();
         for (uint32_t i = tid; i < kv_mul * n; i += kAttnThreads) {
             const uint32_t h = i / n, t = i % n;
-            float* e = &sc[(size_t)h * a.n_ctx + t];
+            float* e = &sc[(size_t)h * sc_stride + t];
             *e = expf_cr(__fsub_rn(*e, red[h]));
         }
         __syncthreads();
         if (warp < kv_mul) {
-            const float* e = sc + (size_t)warp * a.n_ctx;
+            const float* e = sc + (size_t)warp * sc_stride;
             float sum = 0.0f;
             if (a.exact) {
                 if (lane == 0) {
@@ -408,18 +412,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
         if (*flag == 0)
             for (uint32_t i = tid; i < kv_mul * n; i += kAttnThreads) {
                 const uint32_t h = i / n, t = i % n;
-                float* e = &sc[(size_t)h * a.n_ctx + t];
+                float* e = &sc[(size_t)h * sc_stride + t];
                 *e = __fdiv_rn(*e, red[16 + h]);
             }
     }
     __syncthreads();
 
-    // ---- y = sum_t p_t * v_t, one serial chain per (query head, dim)
+    // ---- y = sum_t p_t * v_t, one serial chain per (query head, dim): thread
+    // d < HD runs the chains of dim d for every query head of the block, so
+    // each v element is read once; p comes four positions at a time.
     const bool live2 = *flag == 0;
-    float acc[kAttnMaxChains];
+    float acc[KVM];
 #pragma unroll
-    for (uint32_t c = 0; c < kAttnMaxChains; ++c)
-        acc[c] = 0.0f;
+    for (uint32_t h = 0; h < KVM; ++h)
+        acc[h] = 0.0f;
     for (uint32_t tile = 0; tile < ntiles; ++tile, ++L) {
         const uint32_t s = L % kAttnStages, t0 = tile * kAttnTile, rows_in = min(kAttnTile, n - t0);
         if (!mbar_wait(&full[s], (L / kAttnStages) & 1) && lane == 0) {
@@ -431,28 +437,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
             for (uint32_t i = tid; i < HD; i += kAttnThreads)
                 vt[(size_t)(pos - t0) * HD + i] = vn_s[i];
         __syncthreads();
-        if (live2) {
+        if (live2 && tid < HD) {
+            const uint32_t d = tid;
+            uint32_t tt = 0;
+            for (; tt + 4 <= rows_in; tt += 4) {
+                const float v0 = vt[(size_t)tt * HD + d], v1 = vt[(size_t)(tt + 1) * HD + d];
+                const float v2 = vt[(size_t)(tt + 2) * HD + d], v3 = vt[(size_t)(tt + 3) * HD + d];
 #pragma unroll
-            for (uint32_t c = 0; c < kAttnMaxChains; ++c) {
-                const uint32_t ch = tid + c * kAttnThreads;
-                if (ch < kv_mul * HD) {
-                    const uint32_t h = ch / HD, d = ch % HD;
-                    const float* p = sc + (size_t)h * a.n_ctx + t0;
-                    float v = acc[c];
-                    uint32_t tt = 0;
-                    for (; tt + 8 <= rows_in; tt += 8) {
-                        float pv[8];
-#pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            pv[j] = __fmul_rn(p[tt + j], vt[(size_t)(tt + j) * HD + d]);
-#pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            v = __fadd_rn(v, pv[j]);
-                    }
-                    for (; tt < rows_in; ++tt)
-                        v = __fadd_rn(v, __fmul_rn(p[tt], vt[(size_t)tt * HD + d]));
-                    acc[c] = v;
+                for (uint32_t h = 0; h < KVM; ++h) {
+                    const float4 p = *reinterpret_cast<const float4*>(sc + (size_t)h * sc_stride + t0 + tt);
+                    float v = acc[h];
+                    v = __fadd_rn(v, __fmul_rn(p.x, v0));
+                    v = __fadd_rn(v, __fmul_rn(p.y, v1));
+                    v = __fadd_rn(v, __fmul_rn(p.z, v2));
+                    v = __fadd_rn(v, __fmul_rn(p.w, v3));
+                    acc[h] = v;
                 }
+            }
+            for (; tt < rows_in; ++tt) {
+                const float v0 = vt[(size_t)tt * HD + d];
+#pragma unroll
+                for (uint32_t h = 0; h < KVM; ++h)
+                    acc[h] = __fadd_rn(acc[h], __fmul_rn(sc[(size_t)h * sc_stride + t0 + tt], v0));
             }
         }
         fence_proxy_async();
@@ -460,13 +466,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
         if (warp == 0 && L + kAttnStages < nloads)
             issue(L + kAttnStages);
     }
-    if (live2 && *flag == 0) {
+    if (live2 && *flag == 0 && tid < HD) {
 #pragma unroll
-        for (uint32_t c = 0; c < kAttnMaxChains; ++c) {
-            const uint32_t ch = tid + c * kAttnThreads;
-            if (ch < kv_mul * HD)
-                a.y[(size_t)row * a.c + (size_t)g * kv_mul * HD + ch] = acc[c];
-        }
+        for (uint32_t h = 0; h < KVM; ++h)
+            a.y[(size_t)row * a.c + ((size_t)g * kv_mul + h) * HD + tid] = acc[h];
     }
 }
 

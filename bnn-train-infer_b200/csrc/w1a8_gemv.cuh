@@ -137,7 +137,7 @@ __host__ __device__ inline GemvSmem gemv_smem_plan(uint32_t groups, uint32_t mro
     p.act = 256;
     p.tot = p.act + (size_t)mrows * groups * kActStride * 4u;
     p.xbuf = (p.tot + (size_t)mrows * groups * 4u + 15) & ~(size_t)15;  // float4 stores
-    p.seg = p.xbuf + (pro == kProRmsNorm ? (size_t)groups * kGroup * 4u : 0);  // FP32 row
+    p.seg = p.xbuf + (pro != kProSliced ? (size_t)groups * kGroup * 4u : 0);  // FP32 row
     p.dsm = p.seg + (pro == kProRmsNorm ? kSumSmemBytes : 0);
     p.epi = p.dsm + (epi != kEpiDotGroups ? (size_t)bpt * mrows * kRowBlock * groups * 2u : 0);
     p.epi = (p.epi + 15) & ~(size_t)15;
@@ -249,67 +249,50 @@ __global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
             rs_s[tid] = a.row_scale ? a.row_scale[m0 + tid] : 1.0f;
         named_barrier(1, cthreads);
     } else {
-        // One warp quantises one group (32 lanes x 4 values) per pass, so the
-        // row stays in registers from its load to the sliced words.
-        constexpr uint32_t kPasses = kMaxPrologueK / (kGroup * kComputeWarps);
+        // The row is staged in shared memory once; every later pass is a
+        // rolled loop over it (compact code: the kernels of a decode step take
+        // turns on every SM, so their instruction footprint matters).
         const uint32_t K = G * kGroup;
+        float4* xb4 = reinterpret_cast<float4*>(xbuf);
         for (uint32_t mm = 0; mm < mrows; ++mm) {
             const float4* xr = reinterpret_cast<const float4*>(a.x + (size_t)(m0 + mm) * a.x_stride);
-            float4 v[kPasses];
             int bad = 0;
-#pragma unroll
-            for (uint32_t p = 0; p < kPasses; ++p) {
-                const uint32_t g = p * kComputeWarps + warp;
-                if (g < G) {
-                    v[p] = xr[g * 32u + lane];
-                    bad |= !isfinite(v[p].x) | !isfinite(v[p].y) | !isfinite(v[p].z) | !isfinite(v[p].w);
-                }
+            float amax = 0.0f;
+#pragma unroll 4
+            for (uint32_t i = tid; i < K / 4; i += cthreads) {
+                const float4 v = xr[i];
+                bad |= !isfinite(v.x) | !isfinite(v.y) | !isfinite(v.z) | !isfinite(v.w);
+                amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
+                xb4[i] = v;
             }
             // A linear rejects non-finite input (ValidateF32Input, soft :294-308);
             // before RMSNorm it shows up as a non-finite divisor instead.
             if (bad && PRO == kProQuant)
                 flags[0] = 2;
+            named_barrier(1, cthreads);
             if (PRO == kProRmsNorm) {
                 // The reference's RMSNorm sum fl(...fl(fl(x0*x0) + x1*x1)...) in
                 // index order (qwen3.c:361-372): exact mode reproduces it bit for
-                // bit with warp 0 (exact_sum.cuh) from a shared-memory copy of the
-                // row; fast mode sums in a fixed tree order over the compute threads.
+                // bit with the four compute warps (exact_sum.cuh); fast mode sums
+                // in a fixed tree order.
+                float sum;
                 if (a.exact) {
-#pragma unroll
-                    for (uint32_t p = 0; p < kPasses; ++p) {
-                        const uint32_t g = p * kComputeWarps + warp;
-                        if (g < G)
-                            reinterpret_cast<float4*>(xbuf)[g * 32u + lane] = v[p];
-                    }
-                    named_barrier(1, cthreads);
-                    const float sum = exact_sumsq(xbuf, (int)K, sum_mem, 1);
-                    if (tid == 0)
-                        red[0] = sum;
+                    sum = exact_sumsq(xbuf, (int)K, sum_mem, 1);
                 } else {
-                    float sum = 0.0f;
-#pragma unroll
-                    for (uint32_t p = 0; p < kPasses; ++p) {
-                        if (p * kComputeWarps + warp < G) {
-                            sum = __fadd_rn(sum, __fmul_rn(v[p].x, v[p].x));
-                            sum = __fadd_rn(sum, __fmul_rn(v[p].y, v[p].y));
-                            sum = __fadd_rn(sum, __fmul_rn(v[p].z, v[p].z));
-                            sum = __fadd_rn(sum, __fmul_rn(v[p].w, v[p].w));
-                        }
-                    }
+                    float t = 0.0f;
+                    for (uint32_t i = tid; i < K; i += cthreads)
+                        t = __fadd_rn(t, __fmul_rn(xbuf[i], xbuf[i]));
                     for (int o = 16; o > 0; o >>= 1)
-                        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+                        t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
                     if (lane == 0)
-                        red[1 + warp] = sum;
+                        red[1 + warp] = t;
                     named_barrier(1, cthreads);
-                    if (tid == 0) {
-                        float t = 0.0f;
-                        for (uint32_t w = 0; w < consumers; ++w)
-                            t = __fadd_rn(t, red[1 + w]);
-                        red[0] = t;
-                    }
+                    sum = 0.0f;
+                    for (uint32_t w = 0; w < consumers; ++w)
+                        sum = __fadd_rn(sum, red[1 + w]);
                 }
-                named_barrier(1, cthreads);
-                const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], (float)K), a.eps));
+                const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)K), a.eps));
+                amax = 0.0f;
                 if (!isfinite(rms) || rms == 0.0f) {
                     if (tid == 0) {
                         flags[0] = 1;
@@ -317,25 +300,19 @@ __global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
                     }
                 } else {
                     const float4* gr = reinterpret_cast<const float4*>(a.gain);
-#pragma unroll
-                    for (uint32_t p = 0; p < kPasses; ++p) {
-                        const uint32_t g = p * kComputeWarps + warp;
-                        if (g < G) {
-                            const float4 gn = gr[g * 32u + lane];
-                            v[p].x = __fmul_rn(__fdiv_rn(v[p].x, rms), gn.x);
-                            v[p].y = __fmul_rn(__fdiv_rn(v[p].y, rms), gn.y);
-                            v[p].z = __fmul_rn(__fdiv_rn(v[p].z, rms), gn.z);
-                            v[p].w = __fmul_rn(__fdiv_rn(v[p].w, rms), gn.w);
-                        }
+#pragma unroll 2
+                    for (uint32_t i = tid; i < K / 4; i += cthreads) {
+                        float4 v = xb4[i];
+                        const float4 gn = gr[i];
+                        v.x = __fmul_rn(__fdiv_rn(v.x, rms), gn.x);
+                        v.y = __fmul_rn(__fdiv_rn(v.y, rms), gn.y);
+                        v.z = __fmul_rn(__fdiv_rn(v.z, rms), gn.z);
+                        v.w = __fmul_rn(__fdiv_rn(v.w, rms), gn.w);
+                        amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
+                        xb4[i] = v;
                     }
                 }
             }
-            float amax = 0.0f;
-#pragma unroll
-            for (uint32_t p = 0; p < kPasses; ++p)
-                if (p * kComputeWarps + warp < G)
-                    amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v[p].x), fabsf(v[p].y))),
-                                 fmaxf(fabsf(v[p].z), fabsf(v[p].w)));
             for (int o = 16; o > 0; o >>= 1)
                 amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
             if (lane == 0)
@@ -346,27 +323,25 @@ __global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
                 amax = fmaxf(amax, red[8 + w]);
             const float s = row_scale_from_absmax(amax);
             const RowQuantizer quant(s);
-            // Lane L = 8t + 2i + h holds q[32t + 8i + 4h + b], b = 0..3, of its
-            // warp's group. A 4x4 byte transpose across the lanes that share
-            // (t, h) leaves lane L with slice word (t, j = 4h + i): the bytes
-            // q[32t + 8i' + j], i' = 0..3.
+            // One warp quantises one group per pass (32 lanes x 4 values).
+            // Lane L = 8t + 2i + h holds q[32t + 8i + 4h + b], b = 0..3; a
+            // 4x4 byte transpose across the lanes that share (t, h) leaves lane
+            // L with slice word (t, j = 4h + i): the bytes q[32t + 8i' + j].
             const uint32_t slot = (lane >> 3) * 8u + (lane & 1u) * 4u + ((lane >> 1) & 3u);
-#pragma unroll
-            for (uint32_t p = 0; p < kPasses; ++p) {
-                const uint32_t g = p * kComputeWarps + warp;
-                if (g < G) {
-                    const int8_t q0 = quant(v[p].x), q1 = quant(v[p].y), q2 = quant(v[p].z), q3 = quant(v[p].w);
-                    uint32_t w = (uint32_t)(uint8_t)q0 | ((uint32_t)(uint8_t)q1 << 8) |
-                                 ((uint32_t)(uint8_t)q2 << 16) | ((uint32_t)(uint8_t)q3 << 24);
-                    const int total = __reduce_add_sync(0xffffffffu, (int)q0 + (int)q1 + (int)q2 + (int)q3);
-                    uint32_t o = __shfl_xor_sync(0xffffffffu, w, 4);
-                    w = (lane & 4u) ? __byte_perm(w, o, 0x3276) : __byte_perm(w, o, 0x5410);
-                    o = __shfl_xor_sync(0xffffffffu, w, 2);
-                    w = (lane & 2u) ? __byte_perm(w, o, 0x3715) : __byte_perm(w, o, 0x6240);
-                    act_s[(mm * G + g) * kActStride + slot] = w;
-                    if (lane == 0)
-                        tot_s[mm * G + g] = total;
-                }
+#pragma unroll 1
+            for (uint32_t g = warp; g < G; g += consumers) {
+                const float4 v = xb4[g * 32u + lane];
+                const int8_t q0 = quant(v.x), q1 = quant(v.y), q2 = quant(v.z), q3 = quant(v.w);
+                uint32_t w = (uint32_t)(uint8_t)q0 | ((uint32_t)(uint8_t)q1 << 8) | ((uint32_t)(uint8_t)q2 << 16) |
+                             ((uint32_t)(uint8_t)q3 << 24);
+                const int total = __reduce_add_sync(0xffffffffu, (int)q0 + (int)q1 + (int)q2 + (int)q3);
+                uint32_t o = __shfl_xor_sync(0xffffffffu, w, 4);
+                w = (lane & 4u) ? __byte_perm(w, o, 0x3276) : __byte_perm(w, o, 0x5410);
+                o = __shfl_xor_sync(0xffffffffu, w, 2);
+                w = (lane & 2u) ? __byte_perm(w, o, 0x3715) : __byte_perm(w, o, 0x6240);
+                act_s[(mm * G + g) * kActStride + slot] = w;
+                if (lane == 0)
+                    tot_s[mm * G + g] = total;
             }
             if (tid == 0)
                 rs_s[mm] = s;
