@@ -136,45 +136,68 @@ __host__ __device__ inline float sum_approx(const float* xs, int first, int last
 
 // Classifies [first, last), whose approximate prefix before `first` is p0.
 // Records each op start into out[0..kSumSlots) (cum relative to `first`;
-// out[kSumSlots] is scratch);
-// returns the count, or -1 when more are needed. Sets *inc_total to the sum
-// of the run increments and *last_tag to the tag of the last element (-1 if
-// the range is empty). Only the prefix add, the start test and the counts are
-// chained from element to element.
+// out[kSumSlots] is scratch); returns the count, or -1 when more are needed.
+// Sets *inc_total to the sum of the run increments and *last_tag to the tag
+// of the last element (-1 if the range is empty).
+// Written stage by stage over a batch of kSumBatch elements: only the prefix
+// adds, the start tests and the counts are chained, every other stage is
+// kSumBatch independent operations that issue back to back.
 __host__ __device__ inline int sum_classify(const float* xs, int first, int last, float p0, SumRec* out,
                                             int* inc_total, int* last_tag) {
+    constexpr float kMagic = 8388608.0f;  // 2^23: t = fl(2^23 + v) holds RNE(v) for 0 <= v < 2^23
     int count = 0, cum = 0, prev = -1;
     float p = p0;
     for (int base = first; base < last; base += kSumBatch) {
-        float a[kSumBatch];
+        float a[kSumBatch], pb[kSumBatch], pe[kSumBatch];
 #pragma unroll
         for (int j = 0; j < kSumBatch; ++j)
-            a[j] = sq_rn(xs[base + j < last ? base + j : first]);
+            a[j] = base + j < last ? sq_rn(xs[base + j < last ? base + j : first]) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < kSumBatch; ++j) {
+            pb[j] = p;
+            p = add_rn(p, a[j]);  // past the end a = +0 leaves p as is
+            pe[j] = p;
+        }
+        uint32_t eb[kSumBatch];
+#pragma unroll
+        for (int j = 0; j < kSumBatch; ++j)
+            eb[j] = fbits(pb[j]) >> 23;  // p >= 0: the biased exponent
+        bool in[kSumBatch];
+#pragma unroll
+        for (int j = 0; j < kSumBatch; ++j) {
+            // inside binade e = eb - 127 with the margin: p >= 2^e (1 + 2^-12)
+            // and pn <= 2^(e+1) (1 - 2^-12); false for NaN and infinity too
+            in[j] = eb[j] - (uint32_t)(kRunEMin + 127) <= (uint32_t)(kRunEMax - kRunEMin) &&
+                    pb[j] >= fvalue((eb[j] << 23) | kLoMant) && pe[j] <= fvalue((eb[j] << 23) | kHiMant);
+        }
+        float v[kSumBatch];
+#pragma unroll
+        for (int j = 0; j < kSumBatch; ++j)  // a / u = a * 2^(23 - e), exact; 2^(23-e) has biased exponent 277 - eb
+            v[j] = mul_rn(a[j], fvalue((in[j] ? 277u - eb[j] : 127u) << 23));
+        float t[kSumBatch];
+#pragma unroll
+        for (int j = 0; j < kSumBatch; ++j)
+            t[j] = add_rn(v[j], kMagic);
+        bool lin[kSumBatch];
+#pragma unroll
+        for (int j = 0; j < kSumBatch; ++j)
+            lin[j] = in[j] && v[j] < kMagic && fabsf(add_rn(v[j], -add_rn(t[j], -kMagic))) != 0.5f;  // not a tie
+        int inc[kSumBatch], tag[kSumBatch];
+#pragma unroll
+        for (int j = 0; j < kSumBatch; ++j) {
+            inc[j] = lin[j] ? (int)(fbits(t[j]) - 0x4b000000u) : 0;
+            tag[j] = lin[j] ? (int)eb[j] + 1 : kTagSingle;  // e + 128
+        }
 #pragma unroll
         for (int j = 0; j < kSumBatch; ++j) {
             const int i = base + j;
             const bool valid = i < last;
-            const float pn = add_rn(p, a[j]);
-            const uint32_t eb = fbits(p) >> 23;  // p >= 0: the biased exponent
-            const int e = (int)eb - 127;
-            // inside binade e with the margin: p >= 2^e (1 + 2^-12) and
-            // pn <= 2^(e+1) (1 - 2^-12); false for NaN and infinity too
-            const bool in = e >= kRunEMin && e <= kRunEMax && p >= fvalue((eb << 23) | kLoMant) &&
-                            pn <= fvalue((eb << 23) | kHiMant);
-            const int ec = in ? e : 0;
-            const float v = mul_rn(a[j], fvalue((uint32_t)(150 - ec) << 23));  // a / u, exact
-            const float r = rintf(v);
-            const bool lin = in && fabsf(v - r) != 0.5f;
-            const int tag = lin ? e + 128 : kTagSingle;
-            const bool start = valid && (!lin || tag != prev);
-            // unconditional store (a branch here would keep the compiler from
-            // overlapping neighbouring elements): uncounted records go to the
-            // scratch slot out[kSumSlots]
-            out[start && count < kSumSlots ? count : kSumSlots] = SumRec{i | (tag << 16), cum};
+            const bool start = valid && (!lin[j] || tag[j] != prev);
+            // unconditional store: uncounted records go to the scratch slot
+            out[start && count < kSumSlots ? count : kSumSlots] = SumRec{i | (tag[j] << 16), cum};
             count += start;
-            cum += valid && lin ? (int)r : 0;
-            prev = valid ? tag : prev;
-            p = valid ? pn : p;
+            cum += valid ? inc[j] : 0;
+            prev = valid ? tag[j] : prev;
         }
     }
     *inc_total = cum;
@@ -208,7 +231,7 @@ __device__ __forceinline__ void sum_bar(int id) {
 // squares of xs[0..n), 1 <= n <= 65535 (shared memory), to all of them.
 // Uses named barrier `bar` (128 threads) and kSumSmemBytes of 16-byte
 // aligned shared memory at `mem`.
-static __device__ __noinline__ float exact_sumsq(const float* xs, int n, unsigned char* mem, int bar) {
+static __device__ __forceinline__ float exact_sumsq(const float* xs, int n, unsigned char* mem, int bar) {
     SumRec* slots = reinterpret_cast<SumRec*>(mem + kSumSlotsOffset);
     SumRec* list = reinterpret_cast<SumRec*>(mem + kSumListOffset);
     int* tags = reinterpret_cast<int*>(mem + kSumTagsOffset);
