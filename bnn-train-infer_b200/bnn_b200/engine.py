@@ -26,7 +26,15 @@ class ModelInfo(ctypes.Structure):
 
 
 class ContextParams(ctypes.Structure):
-    _fields_ = [("n_ctx", c_uint32), ("n_batch", c_uint32), ("exact", c_int)]
+    _fields_ = [("n_ctx", c_uint32), ("n_batch", c_uint32), ("exact", c_int), ("comm_id", c_void_p)]
+
+
+class ShardInfo(ctypes.Structure):
+    _fields_ = [(n, c_uint32) for n in ("world", "rank", "q_begin", "q_rows", "kv_begin", "kv_rows", "c_begin",
+                                        "c_rows", "f_begin", "f_rows", "v_begin", "v_rows", "v_stride")]
+
+
+COMM_ID_BYTES = 128
 
 
 class KernelStat(ctypes.Structure):
@@ -46,6 +54,10 @@ class EngineApi:
         d = self.dll
         sig = {
             "BNND_ModelLoad": (c_int, [c_void_p, c_char_p, POINTER(c_void_p)]),
+            "BNND_ModelLoadShard": (c_int, [c_void_p, c_char_p, c_uint32, c_uint32, POINTER(c_void_p)]),
+            "BNND_ModelGetShard": (c_int, [c_void_p, POINTER(ShardInfo)]),
+            "BNND_ShardPlan": (c_int, [POINTER(ModelInfo), c_uint32, c_uint32, POINTER(ShardInfo)]),
+            "BNND_CommIdCreate": (c_int, [c_void_p]),
             "BNND_ModelFree": (None, [c_void_p]),
             "BNND_ModelGetInfo": (c_int, [c_void_p, POINTER(ModelInfo)]),
             "BNND_ContextParamsInit": (None, [POINTER(ContextParams)]),
@@ -77,16 +89,35 @@ class EngineApi:
             raise EngineError(st, self.last_error())
 
 
+def shard_plan(api: EngineApi, info: ModelInfo, world: int, rank: int) -> ShardInfo:
+    """Row ranges of `rank` when the model is column-sharded over `world` GPUs."""
+    out = ShardInfo()
+    api.check(api.ShardPlan(ctypes.byref(info), world, rank, ctypes.byref(out)))
+    return out
+
+
+def comm_id_create(api: EngineApi) -> bytes:
+    """A new NCCL unique id for BNND tensor parallelism (make it on one rank)."""
+    buf = ctypes.create_string_buffer(COMM_ID_BYTES)
+    api.check(api.CommIdCreate(buf))
+    return buf.raw
+
+
 class Model:
-    def __init__(self, device: Device, path, api: EngineApi = None):
+    """A loaded model; world > 1 loads rank `rank`'s column shard."""
+
+    def __init__(self, device: Device, path, api: EngineApi = None, world=1, rank=0):
         self.api = api or EngineApi(device.api.dll)
         self.device = device
         h = c_void_p()
-        self.api.check(self.api.ModelLoad(device.handle, str(path).encode(), ctypes.byref(h)))
+        self.api.check(self.api.ModelLoadShard(device.handle, str(path).encode(), world, rank, ctypes.byref(h)))
         self.handle = h
         info = ModelInfo()
         self.api.check(self.api.ModelGetInfo(h, ctypes.byref(info)))
         self.info = info
+        shard = ShardInfo()
+        self.api.check(self.api.ModelGetShard(h, ctypes.byref(shard)))
+        self.shard = shard
 
     def free(self):
         if self.handle:
@@ -95,10 +126,13 @@ class Model:
 
 
 class Context:
-    def __init__(self, model: Model, n_ctx=0, n_batch=1, exact=True):
+    def __init__(self, model: Model, n_ctx=0, n_batch=1, exact=True, comm_id: bytes = None):
         self.model = model
         self.api = model.api
-        p = ContextParams(n_ctx, n_batch, 1 if exact else 0)
+        p = ContextParams(n_ctx, n_batch, 1 if exact else 0, None)
+        if comm_id is not None:
+            self._comm_id = ctypes.create_string_buffer(bytes(comm_id), COMM_ID_BYTES)
+            p.comm_id = ctypes.cast(self._comm_id, c_void_p)
         h = c_void_p()
         self.api.check(self.api.ContextCreate(model.handle, ctypes.byref(p), ctypes.byref(h)))
         self.handle = h

@@ -28,6 +28,8 @@
 #include <string>
 #include <vector>
 
+#include <nccl.h>
+
 #include "bnn_b200_engine.h"
 #include "bnn_b200_ext.h"
 #include "bnn_internal.h"
@@ -174,12 +176,19 @@ struct HostW1 {
     std::vector<uint16_t> scales;
 };
 
-BNND_Status read_q1_0(const bnn::GgufFile& g, const std::string& name, uint32_t in, uint32_t out,
-                      HostW1* dst) {
+// Appends rows [row0, row0 + rows) of the [out][in] Q1_0 tensor `name` to
+// dst (all rows when rows == UINT32_MAX).
+BNND_Status read_q1_0(const bnn::GgufFile& g, const std::string& name, uint32_t in, uint32_t out_total,
+                      HostW1* dst, uint32_t row0 = 0, uint32_t rows = UINT32_MAX) {
     const bnn::GgufTensor* t = g.tensor(name);
-    if (!t || t->type != 41 || t->dims.size() != 2 || t->dims[0] != in || t->dims[1] != out ||
+    if (!t || t->type != 41 || t->dims.size() != 2 || t->dims[0] != in || t->dims[1] != out_total ||
         in % 128 != 0)
         return fail(BNND_EFORMAT, "unexpected Q1_0 tensor '%s' shape or type", name.c_str());
+    if (rows == UINT32_MAX)
+        rows = out_total - row0;
+    if (row0 > out_total || rows > out_total - row0)
+        return fail(BNND_EINVAL, "row range of '%s' outside the tensor", name.c_str());
+    const uint32_t out = rows;
     if (dst->bits.empty())
         dst->in = in;
     if (dst->in != in)
@@ -191,7 +200,7 @@ BNND_Status read_q1_0(const bnn::GgufFile& g, const std::string& name, uint32_t 
     dst->scales.resize((size_t)dst->out * groups);
     for (size_t o = 0; o < out; ++o) {
         for (size_t grp = 0; grp < groups; ++grp) {
-            const uint8_t* blk = t->data + (o * groups + grp) * 18;
+            const uint8_t* blk = t->data + ((row0 + o) * groups + grp) * 18;
             const uint16_t sc = (uint16_t)(blk[0] | (blk[1] << 8));
             if (!std::isfinite(half_bits_to_float(sc)))
                 return fail(BNND_EFORMAT, "Q1_0 scale in '%s' is not finite", name.c_str());
@@ -284,8 +293,10 @@ struct bnnd_model {
     int32_t rope_corr0 = 0, rope_corr1 = 0;
     int rope_yarn = 0;
     std::vector<std::unique_ptr<QwenLayer>> layers;
-    Linear lm_head;
+    Linear lm_head;        // this rank's lm_head rows (all of them when world == 1)
+    Linear embed;          // world > 1: the whole tied embedding, for embed_kernel
     DevMem out_norm;
+    BNND_ShardInfo shard{};  // world 1: every range is the whole matrix
     // bnn-mlp
     std::vector<std::unique_ptr<MlpLayer>> mlp;
     uint32_t mlp_max_dim = 0;
@@ -298,7 +309,11 @@ struct bnnd_context {
     cudaStream_t stream = nullptr;
     DevMem x, qkv, y, h, logits, kcache, vcache, rope_cos, rope_sin, scores;
     DevMem pos_d, tok_in, tok_next, tok_seq, hist, hist_count, status;
-    DevMem best;  // [rows] packed greedy pick of the lm_head epilogue
+    DevMem best;  // [rows] packed greedy pick of the lm_head epilogue ([world][rows] when sharded)
+    // tensor parallelism (model shard with world > 1)
+    uint32_t world = 1, rank = 0;
+    ncclComm_t comm = nullptr;
+    DevMem y_st, x_st, h_st, lg_st;  // rank-major all-gather buffers [world][rows][slice]
     DevMem mlp_a, mlp_b;
     size_t tok_seq_cap = 0;
     uint32_t hist_cap = 0;
@@ -316,12 +331,15 @@ struct bnnd_context {
     bool have_logits = false;
 
     ~bnnd_context() {
+        // graphs that hold NCCL work go before the communicator
         if (graph_logits)
             cudaGraphExecDestroy(graph_logits);
         if (graph_prefill)
             cudaGraphExecDestroy(graph_prefill);
         if (graph_profile)
             cudaGraphExecDestroy(graph_profile);
+        if (comm)
+            ncclCommDestroy(comm);
         for (cudaEvent_t e : recorder.events)
             cudaEventDestroy(e);
         if (h_status)
@@ -377,6 +395,31 @@ BNND_Status rope_params(const bnn::GgufFile& g, bnnd_model* m) {
     return BNND_OK;
 }
 
+// Row ranges of one rank's column shard (see BNND_ShardInfo).
+BNND_Status shard_plan(const BNND_ModelInfo& in, uint32_t world, uint32_t rank, BNND_ShardInfo* out) {
+    if (world == 0 || rank >= world)
+        return fail(BNND_EINVAL, "rank %u outside world %u", rank, world);
+    if (in.heads % world || in.kv_heads % world || in.hidden % (8 * world) || in.ffn % (8 * world))
+        return fail(BNND_ENOTSUP, "heads %u / kv_heads %u / hidden %u / ffn %u do not split over %u ranks",
+                    in.heads, in.kv_heads, in.hidden, in.ffn, world);
+    BNND_ShardInfo sh{};
+    sh.world = world;
+    sh.rank = rank;
+    sh.q_rows = in.heads / world * in.head_dim;
+    sh.q_begin = rank * sh.q_rows;
+    sh.kv_rows = in.kv_heads / world * in.head_dim;
+    sh.kv_begin = rank * sh.kv_rows;
+    sh.c_rows = in.hidden / world;
+    sh.c_begin = rank * sh.c_rows;
+    sh.f_rows = in.ffn / world;
+    sh.f_begin = rank * sh.f_rows;
+    sh.v_stride = ((in.n_vocab + world - 1) / world + 7) / 8 * 8;
+    sh.v_begin = std::min(rank * sh.v_stride, in.n_vocab);
+    sh.v_rows = std::min(sh.v_stride, in.n_vocab - sh.v_begin);
+    *out = sh;
+    return BNND_OK;
+}
+
 BNND_Status load_qwen3(const bnn::GgufFile& g, bnnd_model* m) {
     uint64_t L = 0, C = 0, FF = 0, H = 0, Hk = 0, kl = 0, vl = 0, ctx = 0;
     g.get_u64("qwen3.block_count", &L);
@@ -421,6 +464,13 @@ BNND_Status load_qwen3(const bnn::GgufFile& g, bnnd_model* m) {
     info.n_ctx_train = (uint32_t)ctx;
     uint64_t eos = 0;
     info.eos_token = g.get_u64("tokenizer.ggml.eos_token_id", &eos) ? (int32_t)eos : -1;
+    {
+        const uint32_t world = m->shard.world ? m->shard.world : 1, rank = m->shard.rank;
+        const BNND_Status sst = shard_plan(info, world, rank, &m->shard);
+        if (sst != BNND_OK)
+            return sst;
+    }
+    const BNND_ShardInfo& sh = m->shard;
     m->eps = eps;
     m->rope_base = base;
     BNND_Status st = rope_params(g, m);
@@ -433,7 +483,13 @@ BNND_Status load_qwen3(const bnn::GgufFile& g, bnnd_model* m) {
         HostW1 head;
         st = read_q1_0(g, "token_embd.weight", (uint32_t)C, V, &head);
         if (st == BNND_OK)
-            st = upload_w1(m->dev, head, &m->lm_head);
+            st = upload_w1(m->dev, head, sh.world > 1 ? &m->embed : &m->lm_head);
+        if (st == BNND_OK && sh.world > 1) {
+            HostW1 part;
+            st = read_q1_0(g, "token_embd.weight", (uint32_t)C, V, &part, sh.v_begin, sh.v_rows);
+            if (st == BNND_OK)
+                st = upload_w1(m->dev, part, &m->lm_head);
+        }
         if (st != BNND_OK)
             return st;
     }
@@ -447,15 +503,17 @@ BNND_Status load_qwen3(const bnn::GgufFile& g, bnnd_model* m) {
             (st = read_f32(g, p + "attn_k_norm.weight", HD, &layer->k_norm)) != BNND_OK)
             return st;
         HostW1 qkv, o, gu, down;
-        if ((st = read_q1_0(g, p + "attn_q.weight", C, C, &qkv)) != BNND_OK ||
-            (st = read_q1_0(g, p + "attn_k.weight", C, KV, &qkv)) != BNND_OK ||
-            (st = read_q1_0(g, p + "attn_v.weight", C, KV, &qkv)) != BNND_OK ||
-            (st = read_q1_0(g, p + "attn_output.weight", C, C, &o)) != BNND_OK ||
-            (st = read_q1_0(g, p + "ffn_gate.weight", C, FF, &gu)) != BNND_OK ||
-            (st = read_q1_0(g, p + "ffn_up.weight", C, FF, &gu)) != BNND_OK ||
-            (st = read_q1_0(g, p + "ffn_down.weight", FF, C, &down)) != BNND_OK)
+        // this rank's rows (all of them for world 1): whole GQA groups of
+        // q|k|v, matching gate and up ranges, o and down output ranges
+        if ((st = read_q1_0(g, p + "attn_q.weight", C, C, &qkv, sh.q_begin, sh.q_rows)) != BNND_OK ||
+            (st = read_q1_0(g, p + "attn_k.weight", C, KV, &qkv, sh.kv_begin, sh.kv_rows)) != BNND_OK ||
+            (st = read_q1_0(g, p + "attn_v.weight", C, KV, &qkv, sh.kv_begin, sh.kv_rows)) != BNND_OK ||
+            (st = read_q1_0(g, p + "attn_output.weight", C, C, &o, sh.c_begin, sh.c_rows)) != BNND_OK ||
+            (st = read_q1_0(g, p + "ffn_gate.weight", C, FF, &gu, sh.f_begin, sh.f_rows)) != BNND_OK ||
+            (st = read_q1_0(g, p + "ffn_up.weight", C, FF, &gu, sh.f_begin, sh.f_rows)) != BNND_OK ||
+            (st = read_q1_0(g, p + "ffn_down.weight", FF, C, &down, sh.c_begin, sh.c_rows)) != BNND_OK)
             return st;
-        interleave_blocks(&gu, (uint32_t)FF);
+        interleave_blocks(&gu, sh.f_rows);
         if ((st = upload_w1(m->dev, qkv, &layer->qkv)) != BNND_OK ||
             (st = upload_w1(m->dev, o, &layer->o)) != BNND_OK ||
             (st = upload_w1(m->dev, gu, &layer->gu)) != BNND_OK ||
@@ -592,7 +650,8 @@ cudaError_t launch_attention(bnnd_context* c, const bnn::eng::AttnArgs& a) {
 }
 cudaError_t launch_linear(const bnnd_context* c, const bnn::GemvLaunch& cl, const Linear& l, const float* x,
                           const float* gain, uint32_t rows, float* out, size_t out_stride, int* status,
-                          unsigned long long* best = nullptr) {
+                          unsigned long long* best = nullptr, uint32_t index_base = 0, const float* res = nullptr,
+                          size_t res_stride = 0) {
     bnn::GemvArgs a = {};
     a.wblocks = l.m->wblocks;
     a.n = l.out;
@@ -610,8 +669,24 @@ cudaError_t launch_linear(const bnnd_context* c, const bnn::GemvLaunch& cl, cons
     a.out_stride = out_stride;
     a.status = status;
     a.best = best;
+    a.index_base = index_base;
+    a.res = reinterpret_cast<const unsigned char*>(res);
+    a.res_stride = res_stride;
     g_next_bytes = ((double)l.out * l.in * 0.140625 + 4.0 * l.in + 4.0 * l.out) * rows;
     return bnn::launch_gemv(cl, rows, a, c->stream, c->pdl);
+}
+
+// All-gather of the rank-major buffer st ([world][rows][slice]; this rank's
+// part written in place) and its reordering into dst [rows][width].
+cudaError_t all_gather_rows(bnnd_context* c, float* st, uint32_t slice, float* dst, uint32_t width) {
+    const uint32_t R = c->rows;
+    const size_t count = (size_t)R * slice;
+    if (ncclAllGather(st + (size_t)c->rank * count, st, count, ncclFloat32, c->comm, c->stream) != ncclSuccess)
+        return cudaErrorUnknown;
+    const size_t total = (size_t)R * width;
+    const uint32_t blocks = (uint32_t)std::min<size_t>((total + 255) / 256, 1024);
+    bnn::eng::gather_rows_kernel<<<blocks, 256, 0, c->stream>>>(st, dst, c->world, R, slice, width, width);
+    return cudaGetLastError();
 }
 
 // Enqueues one decode step for every row (tokens already in tok_in).
@@ -620,19 +695,23 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
     LaunchCheck& ck = g_check ? *g_check : local;
     const bnnd_model* m = c->model;
     const BNND_ModelInfo& in = m->info;
-    const uint32_t C = in.hidden, F = in.ffn, HD = in.head_dim, KV = in.kv_heads * HD, R = c->rows;
+    const BNND_ShardInfo& sh = m->shard;
+    const bool tp = c->world > 1;
+    const uint32_t C = in.hidden, F = in.ffn, HD = in.head_dim, R = c->rows;
     cudaStream_t s = c->stream;
     int* status = c->status.as<int>();
     const int exact = c->params.exact;
-    bnn::eng::embed_kernel<<<R, 256, 0, s>>>(c->tok_in.as<int32_t>(), m->lm_head.m->wblocks, C, c->x.as<float>(),
-                                             c->best.as<unsigned long long>());
+    unsigned long long* best = c->best.as<unsigned long long>() + (size_t)c->rank * R;
+    float* x = c->x.as<float>();
+    bnn::eng::embed_kernel<<<R, 256, 0, s>>>(c->tok_in.as<int32_t>(), (tp ? m->embed : m->lm_head).m->wblocks, C, x,
+                                             best);
     ck("embed_kernel");
-    const size_t qkv_pitch = (size_t)(C + 2 * KV) * 4u;
+    const uint32_t qkv_width = sh.q_rows + 2 * sh.kv_rows;
     for (uint32_t l = 0; l < in.n_layers; ++l) {
         const QwenLayer& L = *m->layers[l];
-        // attn_norm + q|k|v projections (prologue: RMSNorm + quantise)
-        ck("w1a8_gemv:qkv", launch_linear(c, c->plan_qkv, L.qkv, c->x.as<float>(), L.attn_norm.as<float>(), R,
-                                          c->qkv.as<float>(), qkv_pitch, status));
+        // attn_norm + q|k|v projections of this rank's heads (prologue: RMSNorm + quantise)
+        ck("w1a8_gemv:qkv", launch_linear(c, c->plan_qkv, L.qkv, x, L.attn_norm.as<float>(), R, c->qkv.as<float>(),
+                                          (size_t)qkv_width * 4u, status));
         // q/k norm + rope + KV append + attention, one block per (KV head, row)
         bnn::eng::AttnArgs aa;
         aa.qkv = c->qkv.as<float>();
@@ -641,42 +720,79 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
         aa.rope_cos = c->rope_cos.as<float>();
         aa.rope_sin = c->rope_sin.as<float>();
         aa.pos = c->pos_d.as<uint32_t>();
-        const size_t layer_cache = (size_t)R * c->n_ctx * KV;
+        const size_t layer_cache = (size_t)R * c->n_ctx * sh.kv_rows;
         aa.kcache = c->kcache.as<float>() + (size_t)l * layer_cache;
         aa.vcache = c->vcache.as<float>() + (size_t)l * layer_cache;
         aa.scores = c->scores.p ? c->scores.as<float>() : nullptr;
-        aa.y = c->y.as<float>();
-        aa.c = C;
-        aa.kv = KV;
+        aa.y = tp ? c->y_st.as<float>() + (size_t)c->rank * R * sh.q_rows : c->y.as<float>();
+        aa.y_stride = tp ? sh.q_rows : C;
+        aa.c = sh.q_rows;
+        aa.kv = sh.kv_rows;
         aa.hd = HD;
-        aa.heads = in.heads;
-        aa.kv_heads = in.kv_heads;
+        aa.heads = in.heads / c->world;
+        aa.kv_heads = in.kv_heads / c->world;
         aa.n_ctx = c->n_ctx;
         aa.eps = m->eps;
         aa.scale = 1.0f / sqrtf((float)HD);
         aa.exact = exact;
         aa.status = status;
         ck("attention_kernel", launch_attention(c, aa));
+        if (tp)
+            ck("all_gather:y", all_gather_rows(c, c->y_st.as<float>(), sh.q_rows, c->y.as<float>(), C));
         // attn_output, x += o (prologue: quantise the attention output)
-        ck("w1a8_gemv:o", launch_linear(c, c->plan_o, L.o, c->y.as<float>(), nullptr, R, c->x.as<float>(),
-                                        (size_t)C * 4u, status));
+        if (tp) {
+            float* xs = c->x_st.as<float>() + (size_t)c->rank * R * sh.c_rows;
+            ck("w1a8_gemv:o", launch_linear(c, c->plan_o, L.o, c->y.as<float>(), nullptr, R, xs,
+                                            (size_t)sh.c_rows * 4u, status, nullptr, 0, x + sh.c_begin,
+                                            (size_t)C * 4u));
+            ck("all_gather:x", all_gather_rows(c, c->x_st.as<float>(), sh.c_rows, x, C));
+        } else {
+            ck("w1a8_gemv:o", launch_linear(c, c->plan_o, L.o, c->y.as<float>(), nullptr, R, x, (size_t)C * 4u,
+                                            status));
+        }
         // ffn_norm + gate|up + SwiGLU -> h
-        ck("w1a8_gemv:gate_up", launch_linear(c, c->plan_gu, L.gu, c->x.as<float>(), L.ffn_norm.as<float>(), R,
-                                              c->h.as<float>(), (size_t)F * 4u, status));
+        if (tp) {
+            ck("w1a8_gemv:gate_up", launch_linear(c, c->plan_gu, L.gu, x, L.ffn_norm.as<float>(), R,
+                                                  c->h_st.as<float>() + (size_t)c->rank * R * sh.f_rows,
+                                                  (size_t)sh.f_rows * 4u, status));
+            ck("all_gather:h", all_gather_rows(c, c->h_st.as<float>(), sh.f_rows, c->h.as<float>(), F));
+        } else {
+            ck("w1a8_gemv:gate_up", launch_linear(c, c->plan_gu, L.gu, x, L.ffn_norm.as<float>(), R,
+                                                  c->h.as<float>(), (size_t)F * 4u, status));
+        }
         // ffn_down, x += d (prologue: quantise h)
-        ck("w1a8_gemv:down", launch_linear(c, c->plan_down, L.down, c->h.as<float>(), nullptr, R, c->x.as<float>(),
-                                           (size_t)C * 4u, status));
+        if (tp) {
+            float* xs = c->x_st.as<float>() + (size_t)c->rank * R * sh.c_rows;
+            ck("w1a8_gemv:down", launch_linear(c, c->plan_down, L.down, c->h.as<float>(), nullptr, R, xs,
+                                               (size_t)sh.c_rows * 4u, status, nullptr, 0, x + sh.c_begin,
+                                               (size_t)C * 4u));
+            ck("all_gather:x", all_gather_rows(c, c->x_st.as<float>(), sh.c_rows, x, C));
+        } else {
+            ck("w1a8_gemv:down", launch_linear(c, c->plan_down, L.down, c->h.as<float>(), nullptr, R, x,
+                                               (size_t)C * 4u, status));
+        }
     }
     if (with_logits) {
         // out_norm + lm_head; the epilogue also takes the greedy pick
-        ck("w1a8_gemv:lm_head", launch_linear(c, c->plan_head, m->lm_head, c->x.as<float>(), m->out_norm.as<float>(),
-                                              R, c->logits.as<float>(), (size_t)in.n_vocab * 4u, status,
-                                              c->best.as<unsigned long long>()));
+        if (tp) {
+            ck("w1a8_gemv:lm_head",
+               launch_linear(c, c->plan_head, m->lm_head, x, m->out_norm.as<float>(), R,
+                             c->lg_st.as<float>() + (size_t)c->rank * R * sh.v_stride, (size_t)sh.v_stride * 4u,
+                             status, best, sh.v_begin));
+            ck("all_gather:logits",
+               all_gather_rows(c, c->lg_st.as<float>(), sh.v_stride, c->logits.as<float>(), in.n_vocab));
+            ck("all_gather:pick", ncclAllGather(best, c->best.p, R, ncclUint64, c->comm, s) == ncclSuccess
+                                      ? cudaSuccess
+                                      : cudaErrorUnknown);
+        } else {
+            ck("w1a8_gemv:lm_head", launch_linear(c, c->plan_head, m->lm_head, x, m->out_norm.as<float>(), R,
+                                                  c->logits.as<float>(), (size_t)in.n_vocab * 4u, status, best));
+        }
     }
     bnn::eng::step_end_kernel<<<1, 32 * ((R + 31) / 32), 0, s>>>(
         R, c->pos_d.as<uint32_t>(), c->tok_in.as<int32_t>(), c->tok_next.as<int32_t>(),
-        c->best.as<unsigned long long>(), c->hist.as<int32_t>(), c->hist_count.as<uint32_t>(), c->hist_cap,
-        with_logits ? 1 : 0);
+        c->best.as<unsigned long long>(), c->world, c->hist.as<int32_t>(), c->hist_count.as<uint32_t>(),
+        c->hist_cap, with_logits ? 1 : 0);
     ck("step_end_kernel");
     const cudaError_t tail = cudaGetLastError();
     if (tail != cudaSuccess && ck.err == cudaSuccess)
@@ -715,16 +831,38 @@ BNND_Status capture_step(bnnd_context* c, bool with_logits, cudaGraphExec_t* out
 BNND_Status create_llm_context(bnnd_context* c) {
     const bnnd_model* m = c->model;
     const BNND_ModelInfo& in = m->info;
-    const uint32_t C = in.hidden, F = in.ffn, KV = in.kv_heads * in.head_dim, R = c->rows;
+    const BNND_ShardInfo& sh = m->shard;
+    const uint32_t C = in.hidden, F = in.ffn, R = c->rows;
     BNND_Status st;
-    const size_t cache = (size_t)in.n_layers * R * c->n_ctx * KV * 4u;
-    if ((st = dev_alloc(c->x, (size_t)R * C * 4)) || (st = dev_alloc(c->qkv, (size_t)R * (C + 2 * KV) * 4)) ||
+    c->world = sh.world;
+    c->rank = sh.rank;
+    if (c->world > 1) {
+        // collective over the ranks: every rank creates its context
+        if (!c->params.comm_id)
+            return fail(BNND_EINVAL, "a sharded model needs comm_id in the context parameters");
+        ncclUniqueId id;
+        std::memcpy(&id, c->params.comm_id, sizeof id);
+        const ncclResult_t r = ncclCommInitRank(&c->comm, (int)c->world, id, (int)c->rank);
+        if (r != ncclSuccess) {
+            c->comm = nullptr;
+            return fail(BNND_EIO, "ncclCommInitRank: %s", ncclGetErrorString(r));
+        }
+    }
+    const uint32_t P = c->world;
+    const size_t cache = (size_t)in.n_layers * R * c->n_ctx * sh.kv_rows * 4u;
+    if ((st = dev_alloc(c->x, (size_t)R * C * 4)) ||
+        (st = dev_alloc(c->qkv, (size_t)R * (sh.q_rows + 2 * sh.kv_rows) * 4)) ||
         (st = dev_alloc(c->y, (size_t)R * C * 4)) || (st = dev_alloc(c->h, (size_t)R * F * 4)) ||
         (st = dev_alloc(c->logits, (size_t)R * in.n_vocab * 4)) || (st = dev_alloc(c->kcache, cache)) ||
         (st = dev_alloc(c->vcache, cache)) || (st = dev_alloc(c->pos_d, (size_t)R * 4)) ||
         (st = dev_alloc(c->tok_in, (size_t)R * 4)) || (st = dev_alloc(c->tok_next, (size_t)R * 4)) ||
         (st = dev_alloc(c->hist_count, 4)) || (st = dev_alloc(c->status, 4)) ||
-        (st = dev_alloc(c->best, (size_t)R * 8)))
+        (st = dev_alloc(c->best, (size_t)P * R * 8)))
+        return st;
+    if (P > 1 && ((st = dev_alloc(c->y_st, (size_t)P * R * sh.q_rows * 4)) ||
+                  (st = dev_alloc(c->x_st, (size_t)P * R * sh.c_rows * 4)) ||
+                  (st = dev_alloc(c->h_st, (size_t)P * R * sh.f_rows * 4)) ||
+                  (st = dev_alloc(c->lg_st, (size_t)P * R * sh.v_stride * 4))))
         return st;
     c->hist_cap = c->n_ctx;
     if ((st = dev_alloc(c->hist, (size_t)c->hist_cap * R * 4)))
@@ -740,11 +878,11 @@ BNND_Status create_llm_context(bnnd_context* c) {
     CUDA_OR(cudaMemset(c->hist_count.p, 0, 4), BNND_EIO);
     CUDA_OR(cudaMemset(c->status.p, 0, 4), BNND_EIO);
     const int sms = m->dev->sm_count;
-    c->plan_qkv = bnn::plan_gemv(sms, C + 2 * KV, C / 128, R, bnn::kProRmsNorm, bnn::kEpiView);
-    c->plan_o = bnn::plan_gemv(sms, C, C / 128, R, bnn::kProQuant, bnn::kEpiResidual);
-    c->plan_gu = bnn::plan_gemv(sms, 2 * F, C / 128, R, bnn::kProRmsNorm, bnn::kEpiSwiGLU);
-    c->plan_down = bnn::plan_gemv(sms, C, F / 128, R, bnn::kProQuant, bnn::kEpiResidual);
-    c->plan_head = bnn::plan_gemv(sms, in.n_vocab, C / 128, R, bnn::kProRmsNorm, bnn::kEpiView);
+    c->plan_qkv = bnn::plan_gemv(sms, sh.q_rows + 2 * sh.kv_rows, C / 128, R, bnn::kProRmsNorm, bnn::kEpiView);
+    c->plan_o = bnn::plan_gemv(sms, sh.c_rows, C / 128, R, bnn::kProQuant, bnn::kEpiResidual);
+    c->plan_gu = bnn::plan_gemv(sms, 2 * sh.f_rows, C / 128, R, bnn::kProRmsNorm, bnn::kEpiSwiGLU);
+    c->plan_down = bnn::plan_gemv(sms, sh.c_rows, F / 128, R, bnn::kProQuant, bnn::kEpiResidual);
+    c->plan_head = bnn::plan_gemv(sms, sh.v_rows, C / 128, R, bnn::kProRmsNorm, bnn::kEpiView);
     for (const bnn::GemvLaunch* p : {&c->plan_qkv, &c->plan_o, &c->plan_gu, &c->plan_down, &c->plan_head})
         if (p->smem > bnn::kGemvSmemBudget)
             return fail(BNND_ENOTSUP, "hidden/ffn width too large for the contraction kernel");
@@ -880,10 +1018,15 @@ BNND_Status decode(bnnd_context* c, const int32_t* tokens, uint32_t n, float* lo
 extern "C" {
 
 BNND_Status BNND_ModelLoad(BNN_Device device, const char* gguf_path, BNND_Model* out_model) {
+    return BNND_ModelLoadShard(device, gguf_path, 1, 0, out_model);
+}
+
+BNND_Status BNND_ModelLoadShard(BNN_Device device, const char* gguf_path, uint32_t world, uint32_t rank,
+                                BNND_Model* out_model) {
     if (out_model)
         *out_model = nullptr;
     g_last_error.clear();
-    if (!device || !gguf_path || !out_model)
+    if (!device || !gguf_path || !out_model || world == 0 || rank >= world)
         return BNND_EINVAL;
     bnn::GgufFile g;
     if (!g.open(gguf_path))
@@ -895,12 +1038,15 @@ BNND_Status BNND_ModelLoad(BNN_Device device, const char* gguf_path, BNND_Model*
     if (!m)
         return fail(BNND_ENOMEM, "out of memory");
     m->dev = device;
+    m->shard.world = 1;
     bnn::DeviceGuard guard(device->ordinal);
     BNND_Status st;
-    if (arch == "qwen3")
+    if (arch == "qwen3") {
+        m->shard.world = world;
+        m->shard.rank = rank;
         st = load_qwen3(g, m);
-    else if (arch == "bnn-mlp")
-        st = load_mlp(g, m);
+    } else if (arch == "bnn-mlp")
+        st = load_mlp(g, m);  // whole model: classification is data-parallel
     else
         st = fail(BNND_ENOTSUP, "unsupported GGUF architecture '%s'", arch.c_str());
     if (st != BNND_OK) {
@@ -925,11 +1071,39 @@ BNND_Status BNND_ModelGetInfo(BNND_Model model, BNND_ModelInfo* out_info) {
     return BNND_OK;
 }
 
+BNND_Status BNND_ShardPlan(const BNND_ModelInfo* info, uint32_t world, uint32_t rank, BNND_ShardInfo* out) {
+    g_last_error.clear();
+    if (!info || !out || info->task != BNND_TASK_LLM)
+        return BNND_EINVAL;
+    return shard_plan(*info, world, rank, out);
+}
+
+BNND_Status BNND_ModelGetShard(BNND_Model model, BNND_ShardInfo* out) {
+    if (!model || !out)
+        return BNND_EINVAL;
+    *out = model->shard;
+    return BNND_OK;
+}
+
+BNND_Status BNND_CommIdCreate(unsigned char id[BNND_COMM_ID_BYTES]) {
+    static_assert(sizeof(ncclUniqueId) == BNND_COMM_ID_BYTES, "NCCL unique id size");
+    g_last_error.clear();
+    if (!id)
+        return BNND_EINVAL;
+    ncclUniqueId u;
+    const ncclResult_t r = ncclGetUniqueId(&u);
+    if (r != ncclSuccess)
+        return fail(BNND_EIO, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+    std::memcpy(id, &u, sizeof u);
+    return BNND_OK;
+}
+
 void BNND_ContextParamsInit(BNND_ContextParams* params) {
     if (params) {
         params->n_ctx = 0;
         params->n_batch = 1;
         params->exact = 1;
+        params->comm_id = nullptr;
     }
 }
 

@@ -116,7 +116,8 @@ struct AttnArgs {
     float* kcache;          // this layer: [rows][kv_heads][n_ctx][HD]
     float* vcache;
     float* scores;          // [rows][heads][attn_sc_stride(n_ctx)] when they do not fit in shared memory, else null
-    float* y;               // [rows][C]
+    float* y;               // output rows: this block's heads at y + row * y_stride + head * HD
+    uint32_t y_stride;      // floats between output rows
     uint32_t c, kv, hd, heads, kv_heads, n_ctx;
     float eps;
     float scale;            // 1 / sqrtf(head_dim), computed on the host as qwen3.c:404
@@ -469,21 +470,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     if (live2 && *flag == 0 && tid < HD) {
 #pragma unroll
         for (uint32_t h = 0; h < KVM; ++h)
-            a.y[(size_t)row * a.c + ((size_t)g * kv_mul + h) * HD + tid] = acc[h];
+            a.y[(size_t)row * a.y_stride + ((size_t)g * kv_mul + h) * HD + tid] = acc[h];
     }
 }
 
 // End of a decode step: advance every row's position; the greedy pick (the
 // lm_head epilogue's packed key: index = ~low word) becomes the next input
 // and is appended to the generation history.
+// With column-sharded lm_head (world > 1) best holds every rank's key,
+// [world][rows], and the pick is their maximum.
 __global__ void step_end_kernel(uint32_t rows, uint32_t* pos, int32_t* tok_in, int32_t* tok_next,
-                                const unsigned long long* best, int32_t* hist, uint32_t* hist_count,
-                                uint32_t hist_cap, int has_logits) {
+                                const unsigned long long* best, uint32_t world, int32_t* hist,
+                                uint32_t* hist_count, uint32_t hist_cap, int has_logits) {
     const uint32_t r = threadIdx.x;
     if (r < rows) {
         pos[r] += 1;
         if (has_logits) {
-            const unsigned long long b = best[r];
+            unsigned long long b = best[r];
+            for (uint32_t p = 1; p < world; ++p)
+                b = best[(size_t)p * rows + r] > b ? best[(size_t)p * rows + r] : b;
             tok_next[r] = b ? (int32_t)(0xffffffffu - (uint32_t)(b & 0xffffffffull)) : 0;
             tok_in[r] = tok_next[r];
             const uint32_t h = *hist_count;
@@ -494,6 +499,18 @@ __global__ void step_end_kernel(uint32_t rows, uint32_t* pos, int32_t* tok_in, i
     __syncthreads();
     if (r == 0 && has_logits)
         *hist_count += 1;
+}
+
+// Rank-major all-gather result [world][rows][slice] -> row-major
+// [rows][width] (column p * slice + j comes from rank p), width <= world * slice.
+__global__ void gather_rows_kernel(const float* st, float* dst, uint32_t world, uint32_t rows, uint32_t slice,
+                                   uint32_t width, uint32_t dst_stride) {
+    const size_t total = (size_t)rows * width;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t r = (uint32_t)(i / width), col = (uint32_t)(i % width);
+        const uint32_t p = col / slice, j = col % slice;
+        dst[(size_t)r * dst_stride + col] = st[((size_t)p * rows + r) * slice + j];
+    }
 }
 
 // bnn-mlp post-op: y = fl(fl(post_scale * y) + post_bias), ReLU if y < 0.

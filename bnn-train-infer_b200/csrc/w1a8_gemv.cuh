@@ -112,9 +112,15 @@ struct GemvArgs {
     size_t out_stride;             // bytes between output rows
     int* status;
     // kEpiView: when set, best[m] collects max over the row's outputs of
-    // (order-preserving bits of the value) << 32 | ~index, i.e. the greedy
-    // pick (first index of the maximum); non-finite outputs set the status
+    // (order-preserving bits of the value) << 32 | ~(index_base + index),
+    // i.e. the greedy pick (first index of the maximum); non-finite outputs
+    // set the status
     unsigned long long* best;
+    uint32_t index_base;           // global index of output row 0 (a column shard's first row)
+    // kEpiResidual: out = fl(res + Y) with res rows at res (res_stride bytes
+    // apart); nullptr: in place, out = fl(out + Y)
+    const unsigned char* res;
+    size_t res_stride;
 };
 
 // 64-bit argmax key of output `n` with value y (-0 counts as +0; larger
@@ -417,7 +423,7 @@ __global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
                             if (a.best) {
                                 if (!isfinite(acc))
                                     atomicOr(a.status, kStatusNonFinite);
-                                const unsigned long long key = argmax_key(acc, n);
+                                const unsigned long long key = argmax_key(acc, a.index_base + n);
                                 if (p < 32)
                                     best0 = key > best0 ? key : best0;
                                 else
@@ -425,7 +431,10 @@ __global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
                             }
                         } else if (EPI == kEpiResidual) {
                             float* dst = reinterpret_cast<float*>(a.out + (size_t)(m0 + mm) * a.out_stride) + n;
-                            *dst = __fadd_rn(*dst, acc);
+                            const float base =
+                                a.res ? reinterpret_cast<const float*>(a.res + (size_t)(m0 + mm) * a.res_stride)[n]
+                                      : *dst;
+                            *dst = __fadd_rn(base, acc);
                         }
                     }
                     if (EPI == kEpiSwiGLU)

@@ -66,7 +66,41 @@ typedef struct {
     uint32_t n_ctx;
     uint32_t n_batch;
     int exact;
+    /* Sharded models only (BNND_ModelLoadShard with world > 1): the NCCL
+     * unique id of BNND_CommIdCreate, the same bytes on every rank; NULL
+     * otherwise. Context creation is then collective over the ranks. */
+    const unsigned char* comm_id;
 } BNND_ContextParams;
+
+/* Tensor parallelism over `world` GPUs of one node, one process per GPU.
+ * Every linear is sharded by out_features (q|k|v by whole GQA groups, so
+ * q/k-norm, RoPE, the KV cache and attention stay local to the rank's heads;
+ * gate/up by matching row ranges, so SwiGLU is local); each step all-gathers
+ * the outputs over NCCL after attention, o, SwiGLU and down, and reduces the
+ * greedy pick over the ranks' (value, index) keys. Every output element's
+ * arithmetic is unchanged, so results are bit-identical to world = 1. No
+ * counterpart in the reference (its accelerator is one device). */
+typedef struct {
+    uint32_t world, rank;
+    uint32_t q_begin, q_rows;   /* q outputs (heads * head_dim) of this rank */
+    uint32_t kv_begin, kv_rows; /* k and v outputs each (kv_heads * head_dim) */
+    uint32_t c_begin, c_rows;   /* o and down outputs (hidden) */
+    uint32_t f_begin, f_rows;   /* gate and up outputs each (ffn) */
+    uint32_t v_begin, v_rows;   /* lm_head outputs (vocabulary), clipped */
+    uint32_t v_stride;          /* lm_head rows per rank before clipping (multiple of 8) */
+} BNND_ShardInfo;
+/* Row ranges of `rank` (pure host computation, no device needed). ENOTSUP
+ * when the shape does not split (heads, kv_heads, hidden/8 and ffn/8 must
+ * be multiples of world). */
+BNND_Status BNND_ShardPlan(const BNND_ModelInfo* info, uint32_t world, uint32_t rank, BNND_ShardInfo* out);
+/* BNND_ModelLoad of rank `rank`'s shard (qwen3); a bnn-mlp model is loaded
+ * whole (classification is data-parallel). world = 1 is BNND_ModelLoad. */
+BNND_Status BNND_ModelLoadShard(BNN_Device device, const char* gguf_path, uint32_t world, uint32_t rank,
+                                BNND_Model* out_model);
+BNND_Status BNND_ModelGetShard(BNND_Model model, BNND_ShardInfo* out);
+#define BNND_COMM_ID_BYTES 128
+/* A new NCCL unique id, made once (by rank 0) and handed to every rank. */
+BNND_Status BNND_CommIdCreate(unsigned char id[BNND_COMM_ID_BYTES]);
 
 /* Replaces BNNE_ModelLoad (bnn-engine.h:95): parses the GGUF (architectures
  * "qwen3" and "bnn-mlp") and uploads every tensor to the device of `device`,
