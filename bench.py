@@ -26,6 +26,9 @@ model, and reports their aggregate tokens/s.
 
 Multi-GPU (torchrun, one rank per GPU): every rank decodes its own replica
 (independent sequences, no collective on the data path): weak scaling.
+--tp instead decodes one sequence with the model column-sharded over the
+ranks (NCCL all-gathers inside the step graph): strong scaling, value is the
+tokens/s of that one sequence.
 """
 import argparse
 import json
@@ -169,12 +172,18 @@ def run_b200(args):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    tp = args.tp and world > 1
     dist = None
+    if tp:
+        # the engine owns the data-path NCCL communicator (bootstrap root at a
+        # fixed loopback address); the process group only coordinates the host
+        os.environ.setdefault("NCCL_SOCKET_IFNAME", "lo")
+        os.environ.setdefault("NCCL_COMM_ID", f"127.0.0.1:{int(os.environ.get('MASTER_PORT', '29500')) + 1}")
     if world > 1:
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("gloo" if tp else "nccl", timeout=datetime.timedelta(seconds=600))
     torch.cuda.set_device(local)
 
     if rank == 0 or world == 1:
@@ -186,11 +195,16 @@ def run_b200(args):
     dev = accel.Device(local)
     api = engine.EngineApi(dev.api.dll)
     t0 = time.time()
-    model = engine.Model(dev, path, api)
+    model = engine.Model(dev, path, api, world=world if tp else 1, rank=rank if tp else 0)
     log(f"[rank {rank}] model loaded in {time.time() - t0:.1f}s")
     info = model.info
     prompt = prompt_ids(info.n_vocab)
-    ctx = engine.Context(model, n_ctx=CTX, n_batch=1, exact=not args.fast)
+    comm_id = None
+    if tp:
+        box = [engine.comm_id_create(api) if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        comm_id = box[0]
+    ctx = engine.Context(model, n_ctx=CTX, n_batch=1, exact=not args.fast, comm_id=comm_id)
     stream = torch.cuda.ExternalStream(ctx.stream())
     launches_per_step = ctx.step_launches()
 
@@ -206,7 +220,7 @@ def run_b200(args):
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
         if dist:
-            t = torch.tensor([ms], device="cuda")
+            t = torch.tensor([ms], device="cpu" if tp else "cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
         return ms
@@ -221,7 +235,8 @@ def run_b200(args):
     with ClockSampler(local) as clocks:
         ms = timed(lambda: api.check(gen(ctx.handle, args.steps + 1, None)))
     clk = clocks.summary()
-    value = args.steps * world / (ms / 1e3)   # first of the steps+1 ids was the warm-up's pick
+    streams = 1 if tp else world  # sequences decoded by the whole job
+    value = args.steps * streams / (ms / 1e3)   # first of the steps+1 ids was the warm-up's pick
 
     # ---- end to end through the public per-token call (host ids in/out)
     ctx.truncate(0)
@@ -237,7 +252,7 @@ def run_b200(args):
         host_tok[:] = tok
 
     ms_e2e = timed(e2e_loop)
-    e2e_value = args.steps * world / (ms_e2e / 1e3)
+    e2e_value = args.steps * streams / (ms_e2e / 1e3)
 
     # ---- roofline of the dominant kernel (instrumented replay of the same step)
     ctx.truncate(0)
@@ -279,14 +294,15 @@ def run_b200(args):
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (seeded random-init weights and prompt; no checkpoint offline)",
             "config": {"workload": WORKLOAD, "prompt_tokens": PROMPT_TOKENS, "ctx": CTX, "batch_per_gpu": 1,
                        "layers": info.n_layers, "hidden": info.hidden, "ffn": info.ffn, "vocab": info.n_vocab,
                        "numerics": "fast" if args.fast else "exact (reference operation order)",
                        "weight_bytes_per_token": int(weight_bytes),
                        "l2": "inputs larger than L2: 242 MB of weights streamed per token vs 126 MB L2",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+                       "parallelism": (f"tensor parallel x{world} (column-sharded linears, NCCL all-gather)"
+                                       if tp else f"replicas x{world}" if world > 1 else "single GPU")},
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
@@ -369,6 +385,8 @@ def main():
     ap.add_argument("--profile-steps", type=int, default=4)
     ap.add_argument("--ref-procs", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp", action="store_true",
+                    help="with --gpus N under torchrun: one sequence on a column-sharded model instead of N replicas")
     ap.add_argument("--model-cache", default=os.environ.get("BNN_MODEL_CACHE", "/tmp/bnn_b200_models"))
     args = ap.parse_args()
     if args.warmup < 3:
