@@ -20,6 +20,12 @@ cpu_baseline  the reference engine itself (bnn-sw-v2 + soft backend, compiled
           from its sources into oracle/_ref) decoding one token of the same
           model on one host core.
 
+--prefill measures BASELINE configs[3] instead: a step is one batched
+prefill of 512 seeded prompt tokens (every linear a GEMM of 512 rows on the
+tensor cores, tcgen05 kind::i8) plus the greedy pick of the next token,
+through BNND_DecodeArgmax with host ids in and out; value is prompt
+tokens/s, the roofline the int8 tensor rate of the whole prefill.
+
 --impl reference runs only the reference's CPU path: one soft-engine process
 per host core (it is single-threaded), each decoding tokens of the same
 model, and reports their aggregate tokens/s.
@@ -52,6 +58,11 @@ MODEL_SEED = 20261203  # rng_for(config index 2)
 PROMPT_SEED = 20261203 + 7
 WORKLOAD = ("configs[2]: Qwen3-1.7B-shape W1A8 greedy decode, random-init weights, "
             "32-token seeded prompt, ctx 1024, batch 1")
+PREFILL_METRIC = "qwen3_1p7b_w1a8_prefill_tokens_per_s"
+PREFILL_TOKENS = 512
+PREFILL_SEED = 20261204  # rng_for(config index 3)
+PREFILL_WORKLOAD = ("configs[3]: Qwen3-1.7B-shape W1A8 prefill of 512 seeded tokens in one pass "
+                    "(GEMM rows=512 on the tcgen05 int8 path), random-init weights, ctx 1024")
 
 
 def log(*a):
@@ -225,6 +236,16 @@ def run_b200(args):
             ms = float(t.item())
         return ms
 
+    if args.prefill:
+        out = run_prefill(args, ctx, info, timed, rank, world)
+        ctx.free()
+        model.free()
+        dev.close()
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return out
+
     # ---- device-resident value
     ctx.decode_argmax(prompt)                    # prefill (untimed)
     ctx.generate(args.warmup)                    # warm-up steps
@@ -319,6 +340,58 @@ def run_b200(args):
     return out
 
 
+def run_prefill(args, ctx, info, timed, rank, world):
+    """one batched 512-token prefill + greedy pick per step."""
+    import numpy as np
+    prompt = np.random.default_rng(PREFILL_SEED).integers(0, info.n_vocab, size=(1, PREFILL_TOKENS)).astype(np.int32)
+
+    def step():
+        ctx.truncate(0)
+        ctx.decode_argmax(prompt)
+
+    for _ in range(args.warmup):
+        step()
+
+    def loop():
+        for _ in range(args.steps):
+            step()
+
+    with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clocks:
+        ms = timed(loop)
+    clk = clocks.summary()
+    value = PREFILL_TOKENS * args.steps * world / (ms / 1e3)
+    # int8 multiply-adds (x2) of the layers' linears over every position, and
+    # of the lm_head over the last one (the pick)
+    head = float(info.hidden) * info.n_vocab
+    ops = 2.0 * PREFILL_TOKENS * (info.weight_count - head) + 2.0 * head
+    achieved = ops * args.steps / (ms / 1e3) / 1e12
+    d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else None
+    peak = 2.0 * float(d["bf16_tflops"]) if d else 2.0 * 1590.0
+    if rank != 0:
+        return None
+    return {
+        "metric": PREFILL_METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded random-init weights and prompt; no checkpoint offline)",
+        "config": {"workload": PREFILL_WORKLOAD, "prompt_tokens": PREFILL_TOKENS, "ctx": CTX,
+                   "numerics": "fast" if args.fast else "exact (reference operation order)",
+                   "l2": "inputs larger than L2: 242 MB of weights per pass vs 126 MB L2",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2),
+                     "peak": round(peak, 1), "unit": "TOPS", "frac": round(achieved / peak, 4),
+                     "peak_source": ("2 x measured dense bf16 (MEASURED_PEAKS.json): the int8 dense rate is "
+                                     "twice bf16" if d else "2 x fallback bf16"),
+                     "traffic": None,
+                     "what": "int8 ops (2 per multiply-add) of the 28 layers' linears over 512 rows and "
+                             "the lm_head over the last row / step time; attention and norms are inside "
+                             "the step time"},
+        "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": PREFILL_TOKENS * 4,
+                "d2h_bytes_per_step": 4, "call": "BNND_DecodeArgmax of the 512-token prompt, host ids in and out"},
+        "clocks": clk,
+    }
+
+
 def _ref_worker(path, n_tokens, conn):
     import ref_engine
     ref = ref_engine.RefEngine(path, n_ctx=CTX)
@@ -385,6 +458,8 @@ def main():
     ap.add_argument("--profile-steps", type=int, default=4)
     ap.add_argument("--ref-procs", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill", action="store_true",
+                    help="BASELINE configs[3]: batched 512-token prefill instead of decode")
     ap.add_argument("--tp", action="store_true",
                     help="with --gpus N under torchrun: one sequence on a column-sharded model instead of N replicas")
     ap.add_argument("--model-cache", default=os.environ.get("BNN_MODEL_CACHE", "/tmp/bnn_b200_models"))

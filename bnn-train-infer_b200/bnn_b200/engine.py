@@ -26,7 +26,8 @@ class ModelInfo(ctypes.Structure):
 
 
 class ContextParams(ctypes.Structure):
-    _fields_ = [("n_ctx", c_uint32), ("n_batch", c_uint32), ("exact", c_int), ("comm_id", c_void_p)]
+    _fields_ = [("n_ctx", c_uint32), ("n_batch", c_uint32), ("exact", c_int), ("comm_id", c_void_p),
+                ("prefill_chunk", c_uint32)]
 
 
 class ShardInfo(ctypes.Structure):
@@ -35,6 +36,8 @@ class ShardInfo(ctypes.Structure):
 
 
 COMM_ID_BYTES = 128
+PREFILL_MIN_TOKENS = 8        # BNND_PREFILL_MIN_TOKENS
+PREFILL_CHUNK_DEFAULT = 512   # BNND_PREFILL_CHUNK_DEFAULT
 
 
 class KernelStat(ctypes.Structure):
@@ -126,10 +129,13 @@ class Model:
 
 
 class Context:
-    def __init__(self, model: Model, n_ctx=0, n_batch=1, exact=True, comm_id: bytes = None):
+    def __init__(self, model: Model, n_ctx=0, n_batch=1, exact=True, comm_id: bytes = None,
+                 prefill_chunk=PREFILL_CHUNK_DEFAULT):
+        """prefill_chunk: positions per row of one batched prefill pass on the
+        tensor cores (0: one decode step per prompt token)."""
         self.model = model
         self.api = model.api
-        p = ContextParams(n_ctx, n_batch, 1 if exact else 0, None)
+        p = ContextParams(n_ctx, n_batch, 1 if exact else 0, None, prefill_chunk)
         if comm_id is not None:
             self._comm_id = ctypes.create_string_buffer(bytes(comm_id), COMM_ID_BYTES)
             p.comm_id = ctypes.cast(self._comm_id, c_void_p)

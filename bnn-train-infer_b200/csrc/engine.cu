@@ -35,7 +35,9 @@
 #include "bnn_internal.h"
 #include "engine_kernels.cuh"
 #include "gguf_reader.h"
+#include "prefill_kernels.cuh"
 #include "w1a8_gemv.cuh"
+#include "w1a8_mma.cuh"
 
 namespace {
 
@@ -329,6 +331,12 @@ struct bnnd_context {
     size_t h_tokens_cap = 0;
     int32_t* h_next = nullptr;     // pinned staging of greedy picks
     bool have_logits = false;
+    // batched prefill: activation rows = prompt positions of every row
+    DevMem pf_x, pf_qkv, pf_y, pf_h, pf_a, pf_rs, pf_scores, pf_meta;
+    uint32_t pf_rows = 0;          // activation rows the pf_* buffers hold
+    size_t pf_meta_cap = 0;        // entries of pf_meta (ids, positions, cache rows)
+    uint32_t* h_meta = nullptr;    // pinned staging of pf_meta
+    size_t h_meta_cap = 0;
 
     ~bnnd_context() {
         // graphs that hold NCCL work go before the communicator
@@ -348,6 +356,8 @@ struct bnnd_context {
             cudaFreeHost(h_tokens);
         if (h_next)
             cudaFreeHost(h_next);
+        if (h_meta)
+            cudaFreeHost(h_meta);
     }
 };
 
@@ -634,9 +644,9 @@ AttnFn attention_fn(uint32_t hd, uint32_t kv_mul) {
 // The attention kernel, launched like the linears (programmatic dependent
 // launch: it streams K/V tiles of earlier steps while the q|k|v projection
 // finishes).
-cudaError_t launch_attention(bnnd_context* c, const bnn::eng::AttnArgs& a) {
+cudaError_t launch_attention(bnnd_context* c, const bnn::eng::AttnArgs& a, uint32_t rows = 0) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.kv_heads, c->rows);
+    cfg.gridDim = dim3(a.kv_heads, rows ? rows : c->rows);
     cfg.blockDim = dim3(bnn::eng::kAttnThreads);
     cfg.dynamicSmemBytes = c->attn_smem;
     cfg.stream = c->stream;
@@ -713,7 +723,8 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
         ck("w1a8_gemv:qkv", launch_linear(c, c->plan_qkv, L.qkv, x, L.attn_norm.as<float>(), R, c->qkv.as<float>(),
                                           (size_t)qkv_width * 4u, status));
         // q/k norm + rope + KV append + attention, one block per (KV head, row)
-        bnn::eng::AttnArgs aa;
+        bnn::eng::AttnArgs aa = {};
+        aa.append = 1;
         aa.qkv = c->qkv.as<float>();
         aa.q_norm = L.q_norm.as<float>();
         aa.k_norm = L.k_norm.as<float>();
@@ -949,6 +960,227 @@ BNND_Status set_pos(bnnd_context* c, uint32_t pos) {
     return BNND_OK;
 }
 
+// ---- batched prefill (prefill_kernels.cuh): rows x positions activation rows
+
+// Prefill buffers for `rows` activation rows (grown on demand).
+BNND_Status ensure_prefill(bnnd_context* c, uint32_t rows) {
+    if (c->pf_rows >= rows)
+        return BNND_OK;
+    const BNND_ModelInfo& in = c->model->info;
+    const uint32_t C = in.hidden, F = in.ffn, QKV = in.hidden + 2 * in.kv_heads * in.head_dim;
+    c->pf_rows = 0;
+    for (DevMem* d : {&c->pf_x, &c->pf_qkv, &c->pf_y, &c->pf_h, &c->pf_a, &c->pf_rs, &c->pf_scores})
+        *d = DevMem();
+    BNND_Status st;
+    if ((st = dev_alloc(c->pf_x, (size_t)rows * C * 4)) || (st = dev_alloc(c->pf_qkv, (size_t)rows * QKV * 4)) ||
+        (st = dev_alloc(c->pf_y, (size_t)rows * C * 4)) || (st = dev_alloc(c->pf_h, (size_t)rows * F * 4)) ||
+        (st = dev_alloc(c->pf_a, bnn::mma_a_bytes(rows, std::max(C, F) / 128))) ||
+        (st = dev_alloc(c->pf_rs, (size_t)rows * 4)))
+        return st;
+    if (c->scores.p &&
+        (st = dev_alloc(c->pf_scores, (size_t)rows * in.heads * bnn::eng::attn_sc_stride(c->n_ctx) * 4)))
+        return st;
+    c->pf_rows = rows;
+    return BNND_OK;
+}
+
+// RMSNorm (gain non-null) or plain quantisation of `rows` rows of width k
+// into the pre-tiled tensor-core operand.
+cudaError_t prefill_prep(bnnd_context* c, const float* x, uint32_t k, const float* gain, uint32_t rows) {
+    bnn::eng::RowsPrepArgs a = {};
+    a.x = x;
+    a.x_stride = k;
+    a.gain = gain;
+    a.eps = c->model->eps;
+    a.exact = c->params.exact;
+    a.k = k;
+    a.m = rows;
+    a.a_sw = c->pf_a.as<unsigned char>();
+    a.row_scale = c->pf_rs.as<float>();
+    a.status = c->status.as<int>();
+    const size_t smem = bnn::eng::rows_prep_smem(k, c->params.exact != 0);
+    cudaError_t e = cudaFuncSetAttribute(bnn::eng::rows_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess)
+        return e;
+    bnn::eng::rows_prep_kernel<<<rows, bnn::eng::kRowsPrepThreads, smem, c->stream>>>(a);
+    return cudaGetLastError();
+}
+
+// The linear l over the prepared rows on the tensor cores; epi kEpiView,
+// kEpiResidual (out += Y) or kEpiSwiGLU.
+cudaError_t prefill_linear(bnnd_context* c, const Linear& l, uint32_t rows, float* out, size_t out_stride, int epi) {
+    bnn::MmaArgs a = {};
+    a.wblocks = l.m->wblocks;
+    a.n = l.out;
+    a.groups = l.in / 128;
+    a.m = rows;
+    a.a_sw = c->pf_a.as<unsigned char>();
+    a.row_scale = c->pf_rs.as<float>();
+    a.out = reinterpret_cast<unsigned char*>(out);
+    a.out_stride = out_stride;
+    a.epi = epi;
+    a.status = c->status.as<int>();
+    g_next_bytes = (double)l.out * l.in * 0.140625 + (double)rows * (l.in + 4.0 * l.out);
+    return bnn::launch_mma(a, c->stream);
+}
+
+using KvAppendFn = void (*)(bnn::eng::KvAppendArgs);
+KvAppendFn kv_append_fn(uint32_t hd) {
+    if (hd == 128)
+        return bnn::eng::kv_append_kernel<128>;
+    if (hd == 64)
+        return bnn::eng::kv_append_kernel<64>;
+    return nullptr;
+}
+
+// Every layer over `rows` activation rows: meta = [ids][positions][cache rows].
+cudaError_t enqueue_prefill_chunk(bnnd_context* c, uint32_t rows, const uint32_t* meta) {
+    LaunchCheck local;
+    LaunchCheck& ck = g_check ? *g_check : local;
+    const bnnd_model* m = c->model;
+    const BNND_ModelInfo& in = m->info;
+    const uint32_t C = in.hidden, F = in.ffn, HD = in.head_dim, KV = in.kv_heads * HD;
+    const uint32_t QKV = C + 2 * KV;
+    cudaStream_t s = c->stream;
+    int* status = c->status.as<int>();
+    const int32_t* ids = reinterpret_cast<const int32_t*>(meta);
+    const uint32_t* pos = meta + rows;
+    const uint32_t* slot = meta + 2 * (size_t)rows;
+    float* x = c->pf_x.as<float>();
+    float* qkv = c->pf_qkv.as<float>();
+    float* y = c->pf_y.as<float>();
+    float* h = c->pf_h.as<float>();
+    bnn::eng::embed_kernel<<<rows, 256, 0, s>>>(ids, m->lm_head.m->wblocks, C, x, nullptr);
+    ck("embed_kernel");
+    const KvAppendFn append = kv_append_fn(HD);
+    const size_t append_smem = bnn::eng::kv_append_smem(HD, in.kv_heads);
+    for (uint32_t l = 0; l < in.n_layers; ++l) {
+        const QwenLayer& L = *m->layers[l];
+        const size_t layer_cache = (size_t)c->rows * c->n_ctx * KV;
+        float* kc = c->kcache.as<float>() + (size_t)l * layer_cache;
+        float* vc = c->vcache.as<float>() + (size_t)l * layer_cache;
+        ck("rows_prep:qkv", prefill_prep(c, x, C, L.attn_norm.as<float>(), rows));
+        ck("w1a8_mma:qkv", prefill_linear(c, L.qkv, rows, qkv, (size_t)QKV * 4u, bnn::kEpiView));
+        bnn::eng::KvAppendArgs ka = {};
+        ka.qkv = qkv;
+        ka.k_norm = L.k_norm.as<float>();
+        ka.rope_cos = c->rope_cos.as<float>();
+        ka.rope_sin = c->rope_sin.as<float>();
+        ka.pos = pos;
+        ka.slot = slot;
+        ka.kcache = kc;
+        ka.vcache = vc;
+        ka.c = C;
+        ka.kv = KV;
+        ka.kv_heads = in.kv_heads;
+        ka.n_ctx = c->n_ctx;
+        ka.eps = m->eps;
+        ka.exact = c->params.exact;
+        ka.status = status;
+        append<<<rows, 32 * in.kv_heads, append_smem, s>>>(ka);
+        ck("kv_append_kernel");
+        bnn::eng::AttnArgs aa = {};
+        aa.append = 0;
+        aa.qkv = qkv;
+        aa.q_norm = L.q_norm.as<float>();
+        aa.k_norm = L.k_norm.as<float>();
+        aa.rope_cos = c->rope_cos.as<float>();
+        aa.rope_sin = c->rope_sin.as<float>();
+        aa.pos = pos;
+        aa.slot = slot;
+        aa.kcache = kc;
+        aa.vcache = vc;
+        aa.scores = c->pf_scores.p ? c->pf_scores.as<float>() : nullptr;
+        aa.y = y;
+        aa.y_stride = C;
+        aa.c = C;
+        aa.kv = KV;
+        aa.hd = HD;
+        aa.heads = in.heads;
+        aa.kv_heads = in.kv_heads;
+        aa.n_ctx = c->n_ctx;
+        aa.eps = m->eps;
+        aa.scale = 1.0f / sqrtf((float)HD);
+        aa.exact = c->params.exact;
+        aa.status = status;
+        ck("attention_kernel", launch_attention(c, aa, rows));
+        ck("rows_prep:o", prefill_prep(c, y, C, nullptr, rows));
+        ck("w1a8_mma:o", prefill_linear(c, L.o, rows, x, (size_t)C * 4u, bnn::kEpiResidual));
+        ck("rows_prep:gate_up", prefill_prep(c, x, C, L.ffn_norm.as<float>(), rows));
+        ck("w1a8_mma:gate_up", prefill_linear(c, L.gu, rows, h, (size_t)F * 4u, bnn::kEpiSwiGLU));
+        ck("rows_prep:down", prefill_prep(c, h, F, nullptr, rows));
+        ck("w1a8_mma:down", prefill_linear(c, L.down, rows, x, (size_t)C * 4u, bnn::kEpiResidual));
+    }
+    return ck.err;
+}
+
+// The prompt of every row through the batched prefill, then (want) the
+// decode step's out_norm + lm_head + greedy pick on each row's last position.
+BNND_Status prefill(bnnd_context* c, const int32_t* tokens, uint32_t n, bool want) {
+    const uint32_t R = c->rows, start = c->pos, chunk = std::min(n, c->params.prefill_chunk);
+    const size_t count = (size_t)R * n;
+    BNND_Status st = ensure_prefill(c, R * chunk);
+    if (st != BNND_OK)
+        return st;
+    if (c->pf_meta_cap < 3 * count) {
+        c->pf_meta = DevMem();
+        c->pf_meta_cap = 0;
+        if ((st = dev_alloc(c->pf_meta, 3 * count * 4)))
+            return st;
+        c->pf_meta_cap = 3 * count;
+    }
+    if (c->h_meta_cap < 3 * count) {
+        if (c->h_meta)
+            cudaFreeHost(c->h_meta);
+        c->h_meta = nullptr;
+        c->h_meta_cap = 0;
+        CUDA_OR(cudaMallocHost(&c->h_meta, 3 * count * 4), BNND_ENOMEM);
+        c->h_meta_cap = 3 * count;
+    }
+    // chunk j (positions j0 .. j0 + len - 1 of every row): rows r * len + i
+    uint32_t* hm = c->h_meta;
+    for (uint32_t j0 = 0; j0 < n; j0 += chunk) {
+        const uint32_t len = std::min(chunk, n - j0), P = R * len;
+        uint32_t* base = hm + 3 * (size_t)R * j0;
+        for (uint32_t r = 0; r < R; ++r)
+            for (uint32_t i = 0; i < len; ++i) {
+                const uint32_t p = r * len + i;
+                base[p] = (uint32_t)tokens[(size_t)r * n + j0 + i];
+                base[P + p] = start + j0 + i;
+                base[2 * P + p] = r;
+            }
+    }
+    cudaStream_t s = c->stream;
+    CUDA_OR(cudaMemcpyAsync(c->pf_meta.p, hm, 3 * count * 4, cudaMemcpyHostToDevice, s), BNND_EIO);
+    uint32_t last_len = 0;
+    for (uint32_t j0 = 0; j0 < n; j0 += chunk) {
+        last_len = std::min(chunk, n - j0);
+        CUDA_OR(enqueue_prefill_chunk(c, R * last_len, c->pf_meta.as<uint32_t>() + 3 * (size_t)R * j0), BNND_EIO);
+    }
+    // device positions: start + n after the call (the tail's step_end adds the last 1)
+    std::vector<uint32_t> pv(R, start + n - (want ? 1u : 0u));
+    CUDA_OR(cudaMemcpyAsync(c->pos_d.p, pv.data(), (size_t)R * 4, cudaMemcpyHostToDevice, s), BNND_EIO);
+    if (!want)
+        return BNND_OK;
+    const bnnd_model* m = c->model;
+    const uint32_t C = m->info.hidden;
+    float* x = c->x.as<float>();
+    CUDA_OR(cudaMemcpy2DAsync(x, (size_t)C * 4, c->pf_x.as<float>() + (size_t)(last_len - 1) * C,
+                              (size_t)last_len * C * 4, (size_t)C * 4, R, cudaMemcpyDeviceToDevice, s),
+            BNND_EIO);
+    unsigned long long* best = c->best.as<unsigned long long>();
+    CUDA_OR(cudaMemsetAsync(best, 0, (size_t)R * 8, s), BNND_EIO);
+    CUDA_OR(launch_linear(c, c->plan_head, m->lm_head, x, m->out_norm.as<float>(), R, c->logits.as<float>(),
+                          (size_t)m->info.n_vocab * 4u, c->status.as<int>(), best),
+            BNND_EIO);
+    bnn::eng::step_end_kernel<<<1, 32 * ((R + 31) / 32), 0, s>>>(
+        R, c->pos_d.as<uint32_t>(), c->tok_in.as<int32_t>(), c->tok_next.as<int32_t>(), best, 1,
+        c->hist.as<int32_t>(), c->hist_count.as<uint32_t>(), c->hist_cap, 1);
+    CUDA_OR(cudaGetLastError(), BNND_EIO);
+    return BNND_OK;
+}
+
 // Shared body of BNND_Decode / BNND_DecodeArgmax.
 BNND_Status decode(bnnd_context* c, const int32_t* tokens, uint32_t n, float* logits, int32_t* next) {
     g_last_error.clear();
@@ -985,9 +1217,19 @@ BNND_Status decode(bnnd_context* c, const int32_t* tokens, uint32_t n, float* lo
         for (uint32_t i = 0; i < n; ++i)
             seq[(size_t)i * c->rows + r] = tokens[(size_t)r * n + i];
     const uint32_t start = c->pos;
-    CUDA_OR(cudaMemcpyAsync(c->tok_seq.p, seq, count * 4, cudaMemcpyHostToDevice, c->stream), BNND_EIO);
     const bool want = logits || next;
-    for (uint32_t i = 0; i < n; ++i) {
+    const bool batched = c->params.prefill_chunk > 0 && n >= BNND_PREFILL_MIN_TOKENS && c->world == 1;
+    if (batched) {
+        BNND_Status pst = prefill(c, tokens, n, want);
+        if (pst != BNND_OK) {
+            cudaStreamSynchronize(c->stream);
+            set_pos(c, start);
+            return pst;
+        }
+    } else {
+        CUDA_OR(cudaMemcpyAsync(c->tok_seq.p, seq, count * 4, cudaMemcpyHostToDevice, c->stream), BNND_EIO);
+    }
+    for (uint32_t i = 0; i < (batched ? 0u : n); ++i) {
         CUDA_OR(cudaMemcpyAsync(c->tok_in.p, c->tok_seq.as<int32_t>() + (size_t)i * c->rows, c->rows * 4,
                                 cudaMemcpyDeviceToDevice, c->stream),
                 BNND_EIO);
@@ -1104,6 +1346,7 @@ void BNND_ContextParamsInit(BNND_ContextParams* params) {
         params->n_batch = 1;
         params->exact = 1;
         params->comm_id = nullptr;
+        params->prefill_chunk = BNND_PREFILL_CHUNK_DEFAULT;
     }
 }
 

@@ -65,7 +65,9 @@ struct MmaArgs {
     const float* row_scale;        // [M], or nullptr: the I8 ops return Z unscaled
     unsigned char* out;            // first logical output row
     size_t out_stride;             // bytes between output rows
-    int epi;                       // kEpiView or kEpiDotGroups
+    int epi;                       // kEpiView, kEpiDotGroups; engine prefill: kEpiResidual
+                                   // (out = fl(out + Y), 4-byte aligned F32 rows) or kEpiSwiGLU
+                                   // (gate/up interleaved by 8-row blocks, out = h rows)
     int* status;
 };
 
@@ -310,11 +312,34 @@ static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs
         }
         if (ok && live && !dot_groups) {
             const float s = a.row_scale ? a.row_scale[m] : 1.0f;
-            for (uint32_t n = 0; n < kMmaN; ++n) {
-                const uint32_t on = nt * kMmaN + n;
-                if (on < a.n)
-                    store_f32_any(a.out + (size_t)m * a.out_stride + (size_t)on * 4u,
-                                  a.row_scale ? __fmul_rn(acc[n], s) : acc[n]);
+            unsigned char* orow = a.out + (size_t)m * a.out_stride;
+            if (a.epi == kEpiSwiGLU) {
+                // weight blocks 4nt + 2j (gate rows) and 4nt + 2j + 1 (up rows)
+                // hold the same 8 FFN rows: h[(2nt + j) * 8 + r] (w1a8_gemv.cuh)
+#pragma unroll
+                for (uint32_t j = 0; j < 2; ++j)
+#pragma unroll
+                    for (uint32_t r = 0; r < kRowBlock; ++r) {
+                        if ((nt * 4u + 2u * j) * kRowBlock + r >= a.n)
+                            continue;
+                        const float g = __fmul_rn(acc[16u * j + r], s), u = __fmul_rn(acc[16u * j + 8u + r], s);
+                        const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf_cr(-g)));
+                        reinterpret_cast<float*>(orow)[(nt * 2u + j) * kRowBlock + r] = __fmul_rn(silu, u);
+                    }
+            } else {
+#pragma unroll
+                for (uint32_t n = 0; n < kMmaN; ++n) {
+                    const uint32_t on = nt * kMmaN + n;
+                    if (on >= a.n)
+                        continue;
+                    const float y = a.row_scale ? __fmul_rn(acc[n], s) : acc[n];
+                    if (a.epi == kEpiResidual) {
+                        float* dst = reinterpret_cast<float*>(orow) + on;
+                        *dst = __fadd_rn(*dst, y);  // x = fl(x + Y)
+                    } else {
+                        store_f32_any(orow + (size_t)on * 4u, y);
+                    }
+                }
             }
         }
     }

@@ -70,7 +70,15 @@ typedef struct {
      * unique id of BNND_CommIdCreate, the same bytes on every rank; NULL
      * otherwise. Context creation is then collective over the ranks. */
     const unsigned char* comm_id;
+    /* Batched prefill (llm, world = 1): a decode call of at least
+     * BNND_PREFILL_MIN_TOKENS tokens per row runs its prompt layer by layer
+     * over up to prefill_chunk positions of every row at once, each linear a
+     * GEMM on the tensor cores; results are bit-identical to one step per
+     * token. 0 = one decode step per token (the reference's BNNE_Decode). */
+    uint32_t prefill_chunk;
 } BNND_ContextParams;
+#define BNND_PREFILL_MIN_TOKENS 8
+#define BNND_PREFILL_CHUNK_DEFAULT 512
 
 /* Tensor parallelism over `world` GPUs of one node, one process per GPU.
  * Every linear is sharded by out_features (q|k|v by whole GQA groups, so
