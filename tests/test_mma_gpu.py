@@ -6,10 +6,11 @@ is pinned to the reference's golden vectors): DOT_GROUPS and the I8 ops bit
 for bit as integers, the F32 ops bit for bit as floats — the epilogue keeps
 the reference's per-group FP32 order, so no tolerance is needed.
 
-Shapes cover ragged M (partial 128-row tiles), ragged N (partial 32-row
-tiles), group counts that are not a multiple of the 8-group TMEM chunk, the
-largest K (8192), unaligned views, rejection before any output write, and the
-BNN_* threshold itself (63 rows on the dp4a path, 64 on the tensor cores).
+Shapes cover ragged M (partial 128-row tiles), ragged N (partial 128-row
+tiles, and several tiles per row), odd group counts (the TMEM chunk holds 2
+groups), the largest K (8192), unaligned views, rejection before any output
+write, and the BNN_* threshold itself (63 rows on the dp4a path, 64 on the
+tensor cores).
 """
 import numpy as np
 import pytest
@@ -42,6 +43,8 @@ def _run(dev, orc, op, bits, scales, x):
     (256, 1152, 96),     # 9 groups: one full chunk + 1
     (300, 6144, 40),     # 48 groups, 6 chunks, both TMEM buffers reused
     (96, 8192, 33),      # the largest K
+    (200, 1024, 300),    # three 128-row N tiles, the last one partial
+    (512, 2048, 640),    # full tiles only, four M tiles
 ])
 @pytest.mark.parametrize("op", [accel.OP_GEMM_F32, accel.OP_GEMM, accel.OP_DOT_GROUPS])
 def test_tensor_core_parity(b200_device, oracle_mod, m, k, n, op):
