@@ -644,9 +644,9 @@ AttnFn attention_fn(uint32_t hd, uint32_t kv_mul) {
 // The attention kernel, launched like the linears (programmatic dependent
 // launch: it streams K/V tiles of earlier steps while the q|k|v projection
 // finishes).
-cudaError_t launch_attention(bnnd_context* c, const bnn::eng::AttnArgs& a, uint32_t rows = 0) {
+cudaError_t launch_attention(bnnd_context* c, const bnn::eng::AttnArgs& a) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.kv_heads, rows ? rows : c->rows);
+    cfg.gridDim = dim3(a.kv_heads, c->rows);
     cfg.blockDim = dim3(bnn::eng::kAttnThreads);
     cfg.dynamicSmemBytes = c->attn_smem;
     cfg.stream = c->stream;
@@ -724,7 +724,6 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
                                           (size_t)qkv_width * 4u, status));
         // q/k norm + rope + KV append + attention, one block per (KV head, row)
         bnn::eng::AttnArgs aa = {};
-        aa.append = 1;
         aa.qkv = c->qkv.as<float>();
         aa.q_norm = L.q_norm.as<float>();
         aa.k_norm = L.k_norm.as<float>();
@@ -977,7 +976,10 @@ BNND_Status ensure_prefill(bnnd_context* c, uint32_t rows) {
         (st = dev_alloc(c->pf_a, bnn::mma_a_bytes(rows, std::max(C, F) / 128))) ||
         (st = dev_alloc(c->pf_rs, (size_t)rows * 4)))
         return st;
-    if (c->scores.p &&
+    // attention scores of a query tile in shared memory when the whole context fits, else here
+    const bnn::eng::PfSmem pf = bnn::eng::pf_smem_plan(in.head_dim, in.heads / in.kv_heads,
+                                                       bnn::eng::attn_sc_stride(c->n_ctx), true);
+    if (pf.total > bnn::eng::kPfSmemBudget &&
         (st = dev_alloc(c->pf_scores, (size_t)rows * in.heads * bnn::eng::attn_sc_stride(c->n_ctx) * 4)))
         return st;
     c->pf_rows = rows;
@@ -1025,6 +1027,18 @@ cudaError_t prefill_linear(bnnd_context* c, const Linear& l, uint32_t rows, floa
     return bnn::launch_mma(a, c->stream);
 }
 
+using PfAttnFn = void (*)(bnn::eng::PfAttnArgs);
+PfAttnFn prefill_attention_fn(uint32_t hd, uint32_t kv_mul) {
+    using namespace bnn::eng;
+#define BNN_PF_CASE(H, Q) \
+    if (hd == H && kv_mul == Q) \
+        return prefill_attention_kernel<H, Q>;
+    BNN_PF_CASE(128, 1) BNN_PF_CASE(128, 2) BNN_PF_CASE(128, 4) BNN_PF_CASE(128, 8)
+    BNN_PF_CASE(64, 1) BNN_PF_CASE(64, 2) BNN_PF_CASE(64, 4) BNN_PF_CASE(64, 8)
+#undef BNN_PF_CASE
+    return nullptr;
+}
+
 using KvAppendFn = void (*)(bnn::eng::KvAppendArgs);
 KvAppendFn kv_append_fn(uint32_t hd) {
     if (hd == 128)
@@ -1034,8 +1048,10 @@ KvAppendFn kv_append_fn(uint32_t hd) {
     return nullptr;
 }
 
-// Every layer over `rows` activation rows: meta = [ids][positions][cache rows].
-cudaError_t enqueue_prefill_chunk(bnnd_context* c, uint32_t rows, const uint32_t* meta) {
+// Every layer over `rows` = context rows x `len` activation rows (positions
+// pos_end - len .. pos_end - 1 of each row): meta = [ids][positions][cache rows].
+cudaError_t enqueue_prefill_chunk(bnnd_context* c, uint32_t rows, uint32_t len, uint32_t pos_end,
+                                  const uint32_t* meta) {
     LaunchCheck local;
     LaunchCheck& ck = g_check ? *g_check : local;
     const bnnd_model* m = c->model;
@@ -1055,6 +1071,23 @@ cudaError_t enqueue_prefill_chunk(bnnd_context* c, uint32_t rows, const uint32_t
     ck("embed_kernel");
     const KvAppendFn append = kv_append_fn(HD);
     const size_t append_smem = bnn::eng::kv_append_smem(HD, in.kv_heads);
+    // tiled causal attention: scores in shared memory up to this chunk's last position
+    const uint32_t kv_mul = in.heads / in.kv_heads;
+    const PfAttnFn pf_attn = prefill_attention_fn(HD, kv_mul);
+    const uint32_t sc_local = bnn::eng::attn_sc_stride(pos_end);
+    bnn::eng::PfSmem pf_plan = bnn::eng::pf_smem_plan(HD, kv_mul, sc_local, true);
+    const bool pf_global = pf_plan.total > bnn::eng::kPfSmemBudget;
+    if (pf_global)
+        pf_plan = bnn::eng::pf_smem_plan(HD, kv_mul, bnn::eng::attn_sc_stride(c->n_ctx), false);
+    if (!pf_attn || (pf_global && !c->pf_scores.p))
+        return cudaErrorInvalidValue;
+    {
+        const cudaError_t e = cudaFuncSetAttribute(pf_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)pf_plan.total);
+        if (e != cudaSuccess)
+            return e;
+    }
+    const dim3 pf_grid(in.kv_heads, (rows / len) * ((len + bnn::eng::kPfQT - 1) / bnn::eng::kPfQT));
     for (uint32_t l = 0; l < in.n_layers; ++l) {
         const QwenLayer& L = *m->layers[l];
         const size_t layer_cache = (size_t)c->rows * c->n_ctx * KV;
@@ -1080,31 +1113,31 @@ cudaError_t enqueue_prefill_chunk(bnnd_context* c, uint32_t rows, const uint32_t
         ka.status = status;
         append<<<rows, 32 * in.kv_heads, append_smem, s>>>(ka);
         ck("kv_append_kernel");
-        bnn::eng::AttnArgs aa = {};
-        aa.append = 0;
-        aa.qkv = qkv;
-        aa.q_norm = L.q_norm.as<float>();
-        aa.k_norm = L.k_norm.as<float>();
-        aa.rope_cos = c->rope_cos.as<float>();
-        aa.rope_sin = c->rope_sin.as<float>();
-        aa.pos = pos;
-        aa.slot = slot;
-        aa.kcache = kc;
-        aa.vcache = vc;
-        aa.scores = c->pf_scores.p ? c->pf_scores.as<float>() : nullptr;
-        aa.y = y;
-        aa.y_stride = C;
-        aa.c = C;
-        aa.kv = KV;
-        aa.hd = HD;
-        aa.heads = in.heads;
-        aa.kv_heads = in.kv_heads;
-        aa.n_ctx = c->n_ctx;
-        aa.eps = m->eps;
-        aa.scale = 1.0f / sqrtf((float)HD);
-        aa.exact = c->params.exact;
-        aa.status = status;
-        ck("attention_kernel", launch_attention(c, aa, rows));
+        bnn::eng::PfAttnArgs pa = {};
+        pa.qkv = qkv;
+        pa.q_norm = L.q_norm.as<float>();
+        pa.rope_cos = c->rope_cos.as<float>();
+        pa.rope_sin = c->rope_sin.as<float>();
+        pa.pos = pos;
+        pa.slot = slot;
+        pa.kcache = kc;
+        pa.vcache = vc;
+        pa.scores = pf_global ? c->pf_scores.as<float>() : nullptr;
+        pa.y = y;
+        pa.y_stride = C;
+        pa.c = C;
+        pa.kv = KV;
+        pa.heads = in.heads;
+        pa.kv_heads = in.kv_heads;
+        pa.n_ctx = c->n_ctx;
+        pa.len = len;
+        pa.sc_stride = pf_global ? bnn::eng::attn_sc_stride(c->n_ctx) : sc_local;
+        pa.eps = m->eps;
+        pa.scale = 1.0f / sqrtf((float)HD);
+        pa.exact = c->params.exact;
+        pa.status = status;
+        pf_attn<<<pf_grid, bnn::eng::kPfThreads, pf_plan.total, s>>>(pa);
+        ck("prefill_attention_kernel");
         ck("rows_prep:o", prefill_prep(c, y, C, nullptr, rows));
         ck("w1a8_mma:o", prefill_linear(c, L.o, rows, x, (size_t)C * 4u, bnn::kEpiResidual));
         ck("rows_prep:gate_up", prefill_prep(c, x, C, L.ffn_norm.as<float>(), rows));
@@ -1156,7 +1189,9 @@ BNND_Status prefill(bnnd_context* c, const int32_t* tokens, uint32_t n, bool wan
     uint32_t last_len = 0;
     for (uint32_t j0 = 0; j0 < n; j0 += chunk) {
         last_len = std::min(chunk, n - j0);
-        CUDA_OR(enqueue_prefill_chunk(c, R * last_len, c->pf_meta.as<uint32_t>() + 3 * (size_t)R * j0), BNND_EIO);
+        CUDA_OR(enqueue_prefill_chunk(c, R * last_len, last_len, start + j0 + last_len,
+                                      c->pf_meta.as<uint32_t>() + 3 * (size_t)R * j0),
+                BNND_EIO);
     }
     // device positions: start + n after the call (the tail's step_end adds the last 1)
     std::vector<uint32_t> pv(R, start + n - (want ? 1u : 0u));

@@ -114,10 +114,7 @@ struct AttnArgs {
     const float* rope_cos;  // [n_ctx][HD/2]
     const float* rope_sin;
     const uint32_t* pos;    // [rows]
-    const uint32_t* slot;   // [rows] KV cache row of each row, or null: the row itself
-    int append;             // 1: norm + rope this row's k and append k, v (decode); 0: already
-                            // in the cache (batched prefill, kv_append_kernel ran before)
-    float* kcache;          // this layer: [cache rows][kv_heads][n_ctx][HD]
+    float* kcache;          // this layer: [rows][kv_heads][n_ctx][HD]
     float* vcache;
     float* scores;          // [rows][heads][attn_sc_stride(n_ctx)] when they do not fit in shared memory, else null
     float* y;               // output rows: this block's heads at y + row * y_stride + head * HD
@@ -244,14 +241,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     unsigned char* ring = e_smem + plan.ring;
     int* flag = reinterpret_cast<int*>(red + 62);  // [0] abort: earlier failure, non-finite, timeout
 
-    // Batched prefill: this position's K/V (and every earlier one) were
-    // appended by the kernel before, so wait for it before the first copy.
-    const bool append = a.append != 0;
-    if (!append)
-        griddep_wait();
     const uint32_t pos = a.pos[row], n = pos + 1;
     const uint32_t ntiles = (n + kAttnTile - 1) / kAttnTile, nloads = 2 * ntiles;
-    const size_t head_base = ((size_t)(a.slot ? a.slot[row] : row) * a.kv_heads + g) * a.n_ctx * HD;
+    const size_t head_base = ((size_t)row * a.kv_heads + g) * a.n_ctx * HD;
     const float* kc = a.kcache + head_base;
     const float* vc = a.vcache + head_base;
     constexpr uint32_t kstride = HD + 4;
@@ -300,15 +292,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     const float* qkv_row = a.qkv + (size_t)row * width;
     for (uint32_t i = tid; i < kv_mul * HD; i += kAttnThreads)
         q_s[i] = qkv_row[(size_t)g * kv_mul * HD + i];
-    if (append)
-        for (uint32_t i = tid; i < HD; i += kAttnThreads) {
-            kn_s[i] = qkv_row[a.c + (size_t)g * HD + i];
-            vn_s[i] = qkv_row[a.c + a.kv + (size_t)g * HD + i];
-        }
+    for (uint32_t i = tid; i < HD; i += kAttnThreads) {
+        kn_s[i] = qkv_row[a.c + (size_t)g * HD + i];
+        vn_s[i] = qkv_row[a.c + a.kv + (size_t)g * HD + i];
+    }
     if (tid == 0 && *a.status != 0)
         *flag = 1;  // an earlier kernel failed: skip the work, keep the copy protocol
     __syncthreads();
-    if (warp < kv_mul || (warp == kv_mul && append)) {
+    if (warp <= kv_mul) {
         float* v = warp < kv_mul ? q_s + (size_t)warp * HD : kn_s;
         if (!attn_norm_rope<HD>(v, warp < kv_mul ? gq_s : gk_s, rc_s, rs_s, a.eps, a.exact != 0) && lane == 0) {
             *flag = 1;
@@ -317,11 +308,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     }
     __syncthreads();
     // append this position's k and v to the cache (read back by later steps)
-    if (append)
-        for (uint32_t i = tid; i < HD; i += kAttnThreads) {
-            a.kcache[head_base + (size_t)pos * HD + i] = kn_s[i];
-            a.vcache[head_base + (size_t)pos * HD + i] = vn_s[i];
-        }
+    for (uint32_t i = tid; i < HD; i += kAttnThreads) {
+        a.kcache[head_base + (size_t)pos * HD + i] = kn_s[i];
+        a.vcache[head_base + (size_t)pos * HD + i] = vn_s[i];
+    }
 
     // ---- scores
     int bad = 0;
@@ -333,7 +323,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
             atomicOr(a.status, kStatusTimeout);
         }
         float* kt = reinterpret_cast<float*>(ring + (size_t)s * plan.stage_bytes);
-        if (append && pos >= t0 && pos < t0 + rows_in)
+        if (pos >= t0 && pos < t0 + rows_in)
             for (uint32_t i = tid; i < HD; i += kAttnThreads)
                 kt[(size_t)(pos - t0) * kstride + i] = kn_s[i];
         __syncthreads();
@@ -445,7 +435,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
             atomicOr(a.status, kStatusTimeout);
         }
         float* vt = reinterpret_cast<float*>(ring + (size_t)s * plan.stage_bytes);
-        if (append && pos >= t0 && pos < t0 + rows_in)
+        if (pos >= t0 && pos < t0 + rows_in)
             for (uint32_t i = tid; i < HD; i += kAttnThreads)
                 vt[(size_t)(pos - t0) * HD + i] = vn_s[i];
         __syncthreads();

@@ -15,8 +15,9 @@
 //                      (w1a8_gemv.cuh kProRmsNorm / kProQuant)
 //   kv_append_kernel   k-norm + RoPE of every position's k heads and the
 //                      K/V cache append (qwen3.c:418-438), before attention
-//   attention_kernel   (engine_kernels.cuh) with append = 0: per position,
-//                      q-norm + RoPE and causal attention over the cache
+//   prefill_attention_kernel  per tile of positions: q-norm + RoPE and
+//                      causal attention over the cache, each K/V tile read
+//                      once for the whole tile (decode-kernel arithmetic)
 //
 // The linears' epilogues (View, residual add, SwiGLU) run inside the
 // tensor-core kernel. Greedy logits come from the decode step's lm_head on
@@ -194,6 +195,272 @@ __global__ void kv_append_kernel(KvAppendArgs a) {
     for (uint32_t i = lane; i < HD; i += 32) {
         a.kcache[base + i] = v[i];
         a.vcache[base + i] = qkv_row[a.c + a.kv + (size_t)g * HD + i];
+    }
+}
+
+// ---- causal attention over a tile of prompt positions
+//
+// One CTA per (KV head g, kPfQT consecutive positions of one row): the
+// kv_mul query heads of g at each position, every K and V tile of the cache
+// read once for all of them. Per query head the arithmetic is the decode
+// kernel's (attention_kernel): q-norm + RoPE (attn_norm_rope), each score a
+// serial FP32 dot over the head dimension times the scale, the maximum,
+// expf_cr(s - max), the sum in the same order (serial in exact mode, the
+// same lane-strided tree in fast mode), the division, and y accumulated
+// serially over the positions 0 .. pos. So outputs are bit-identical to one
+// decode step per position.
+constexpr uint32_t kPfQT = 16;        // query positions per CTA
+constexpr uint32_t kPfKT = 32;        // K/V positions per shared-memory tile
+constexpr uint32_t kPfThreads = 256;  // (query, key pair) and (query, 8 dims) per thread
+constexpr uint32_t kPfSmemBudget = 200u * 1024u;
+
+struct PfAttnArgs {
+    const float* qkv;       // [rows][c + 2kv]
+    const float* q_norm;    // [HD]
+    const float* rope_cos;  // [n_ctx][HD/2]
+    const float* rope_sin;
+    const uint32_t* pos;    // [rows]: consecutive positions within a row of the chunk
+    const uint32_t* slot;   // [rows] KV cache row
+    const float* kcache;    // this layer: [cache rows][kv_heads][n_ctx][HD]
+    const float* vcache;
+    float* scores;          // [rows][heads][sc_stride] when they do not fit in shared memory, else null
+    float* y;               // [rows][y_stride]: head h at h * HD
+    uint32_t y_stride;
+    uint32_t c, kv, heads, kv_heads, n_ctx;
+    uint32_t len;           // positions of each row in this chunk (rows = R * len)
+    uint32_t sc_stride;     // floats per score row (a multiple of 4)
+    float eps, scale;
+    int exact;
+    int* status;
+};
+
+struct PfSmem {
+    size_t q, kv, gq, rc, rs, red, sc, total;
+};
+
+__host__ __device__ inline PfSmem pf_smem_plan(uint32_t hd, uint32_t kv_mul, uint32_t sc_stride, bool sc_smem) {
+    PfSmem p;
+    p.q = 0;                                                    // [kPfQT * kv_mul][hd]
+    p.kv = p.q + (size_t)kPfQT * kv_mul * hd * 4u;              // [kPfKT][hd + 4]
+    p.gq = p.kv + (size_t)kPfKT * (hd + 4u) * 4u;               // [hd]
+    p.rc = p.gq + (size_t)hd * 4u;                              // [kPfQT][hd / 2]
+    p.rs = p.rc + (size_t)kPfQT * (hd / 2u) * 4u;
+    p.red = p.rs + (size_t)kPfQT * (hd / 2u) * 4u;              // 64 floats
+    p.sc = p.red + 64u * 4u;                                    // [kPfQT * kv_mul][sc_stride]
+    p.total = p.sc + (sc_smem ? (size_t)kPfQT * kv_mul * sc_stride * 4u : 0u);
+    return p;
+}
+
+template <int HD, int KVM>
+__global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttnArgs a) {
+    extern __shared__ __align__(16) unsigned char pf_smem[];
+    constexpr uint32_t kStride = HD + 4;  // padded K/V rows
+    const uint32_t g = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t tiles = (a.len + kPfQT - 1) / kPfQT;
+    const uint32_t r = blockIdx.y / tiles, i0 = (blockIdx.y % tiles) * kPfQT;
+    const uint32_t nq = min(kPfQT, a.len - i0);
+    const uint32_t p0 = r * a.len + i0;  // activation row of the first query
+    const bool sc_smem = a.scores == nullptr;
+    const PfSmem plan = pf_smem_plan(HD, KVM, a.sc_stride, sc_smem);
+    float* q_s = reinterpret_cast<float*>(pf_smem + plan.q);
+    float* kv_s = reinterpret_cast<float*>(pf_smem + plan.kv);
+    float* gq_s = reinterpret_cast<float*>(pf_smem + plan.gq);
+    float* rc_s = reinterpret_cast<float*>(pf_smem + plan.rc);
+    float* rs_s = reinterpret_cast<float*>(pf_smem + plan.rs);
+    float* red = reinterpret_cast<float*>(pf_smem + plan.red);
+    int* flag = reinterpret_cast<int*>(red + 63);
+    // score row of (query qi, head h): the decode layout [row][head][stride] when global
+    auto sc_row = [&](uint32_t qi, uint32_t h) -> float* {
+        return sc_smem ? reinterpret_cast<float*>(pf_smem + plan.sc) + (size_t)(qi * KVM + h) * a.sc_stride
+                       : a.scores + ((size_t)(p0 + qi) * a.heads + g * KVM + h) * a.sc_stride;
+    };
+    if (*a.status != 0)
+        return;
+    const uint32_t pos0 = a.pos[p0];
+    const uint32_t n_max = a.pos[p0 + nq - 1] + 1;  // keys of the last query
+    const size_t head_base = ((size_t)a.slot[p0] * a.kv_heads + g) * a.n_ctx * HD;
+    const float* kc = a.kcache + head_base;
+    const float* vc = a.vcache + head_base;
+    const size_t width = a.c + 2u * a.kv;
+
+    if (tid == 0)
+        *flag = 0;
+    for (uint32_t i = tid; i < HD; i += kPfThreads)
+        gq_s[i] = a.q_norm[i];
+    for (uint32_t i = tid; i < kPfQT * (HD / 2); i += kPfThreads) {
+        const uint32_t qi = i / (HD / 2), j = i % (HD / 2);
+        const uint32_t ps = qi < nq ? pos0 + qi : pos0;
+        rc_s[i] = a.rope_cos[(size_t)ps * (HD / 2) + j];
+        rs_s[i] = a.rope_sin[(size_t)ps * (HD / 2) + j];
+    }
+    for (uint32_t i = tid; i < kPfQT * KVM * HD; i += kPfThreads) {
+        const uint32_t v = i / HD, d = i % HD, qi = v / KVM, h = v % KVM;
+        q_s[i] = qi < nq ? a.qkv[(size_t)(p0 + qi) * width + (size_t)(g * KVM + h) * HD + d] : 0.0f;
+    }
+    __syncthreads();
+    for (uint32_t v = warp; v < nq * KVM; v += kPfThreads / 32) {
+        const uint32_t qi = v / KVM;
+        if (!attn_norm_rope<HD>(q_s + (size_t)v * HD, gq_s, rc_s + qi * (HD / 2), rs_s + qi * (HD / 2), a.eps,
+                                a.exact != 0) &&
+            lane == 0) {
+            *flag = 1;
+            atomicOr(a.status, kStatusNonFinite);
+        }
+    }
+    __syncthreads();
+    if (*flag)
+        return;
+
+    // ---- scores: thread (query sq, keys 2 kp, 2 kp + 1 of the tile), all KVM heads
+    const uint32_t sq = tid / 16, kp = tid % 16;
+    const uint32_t sq_n = pos0 + sq + 1;  // keys of query sq
+    int bad = 0;
+    for (uint32_t t0 = 0; t0 < n_max; t0 += kPfKT) {
+        const uint32_t rows_in = min(kPfKT, n_max - t0);
+        for (uint32_t i = tid; i < rows_in * (HD / 4); i += kPfThreads) {
+            const uint32_t tt = i / (HD / 4), c4 = i % (HD / 4);
+            reinterpret_cast<float4*>(kv_s + (size_t)tt * kStride)[c4] =
+                reinterpret_cast<const float4*>(kc + (size_t)(t0 + tt) * HD)[c4];
+        }
+        __syncthreads();
+        const uint32_t ta = t0 + 2 * kp, tb = ta + 1;
+        const bool va = sq < nq && ta < sq_n, vb = sq < nq && tb < sq_n;
+        if (va) {  // tb valid implies ta valid
+            const float4* ka = reinterpret_cast<const float4*>(kv_s + (size_t)(2 * kp) * kStride);
+            const float4* kb = reinterpret_cast<const float4*>(kv_s + (size_t)(2 * kp + 1) * kStride);
+            float da[KVM], db[KVM];
+#pragma unroll
+            for (int h = 0; h < KVM; ++h)
+                da[h] = db[h] = 0.0f;
+#pragma unroll 4
+            for (uint32_t i = 0; i < HD / 4; ++i) {
+                const float4 x = ka[i], y = vb ? kb[i] : ka[i];
+#pragma unroll
+                for (int h = 0; h < KVM; ++h) {
+                    const float4 q = reinterpret_cast<const float4*>(q_s + (size_t)(sq * KVM + h) * HD)[i];
+                    da[h] = __fadd_rn(da[h], __fmul_rn(q.x, x.x));
+                    da[h] = __fadd_rn(da[h], __fmul_rn(q.y, x.y));
+                    da[h] = __fadd_rn(da[h], __fmul_rn(q.z, x.z));
+                    da[h] = __fadd_rn(da[h], __fmul_rn(q.w, x.w));
+                    db[h] = __fadd_rn(db[h], __fmul_rn(q.x, y.x));
+                    db[h] = __fadd_rn(db[h], __fmul_rn(q.y, y.y));
+                    db[h] = __fadd_rn(db[h], __fmul_rn(q.z, y.z));
+                    db[h] = __fadd_rn(db[h], __fmul_rn(q.w, y.w));
+                }
+            }
+#pragma unroll
+            for (int h = 0; h < KVM; ++h) {
+                const float sa = __fmul_rn(da[h], a.scale);
+                bad |= !isfinite(sa);
+                sc_row(sq, h)[ta] = sa;
+                if (vb) {
+                    const float sb = __fmul_rn(db[h], a.scale);
+                    bad |= !isfinite(sb);
+                    sc_row(sq, h)[tb] = sb;
+                }
+            }
+        }
+        __syncthreads();  // the tile is free again
+    }
+    if (__syncthreads_or(bad)) {
+        if (tid == 0)
+            atomicOr(a.status, kStatusNonFinite);  // "attention score is not finite"
+        return;
+    }
+
+    // ---- softmax per (query, head) row, one warp per row
+    for (uint32_t v = warp; v < nq * KVM; v += kPfThreads / 32) {
+        const uint32_t qi = v / KVM, h = v % KVM, n = pos0 + qi + 1;
+        float* e = sc_row(qi, h);
+        float mx = -INFINITY;
+        for (uint32_t t = lane; t < n; t += 32)
+            mx = fmaxf(mx, e[t]);
+        for (int o = 16; o > 0; o >>= 1)
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        for (uint32_t t = lane; t < n; t += 32)
+            e[t] = expf_cr(__fsub_rn(e[t], mx));
+        __syncwarp();
+        float sum = 0.0f;
+        if (a.exact) {
+            if (lane == 0) {
+                uint32_t t = 0;
+                for (; t + 8 <= n; t += 8) {
+                    float w[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        w[j] = e[t + j];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        sum = __fadd_rn(sum, w[j]);
+                }
+                for (; t < n; ++t)
+                    sum = __fadd_rn(sum, e[t]);
+            }
+            sum = __shfl_sync(0xffffffffu, sum, 0);
+        } else {
+            for (uint32_t t = lane; t < n; t += 32)
+                sum = __fadd_rn(sum, e[t]);
+            for (int o = 16; o > 0; o >>= 1)
+                sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+        }
+        if (!(sum > 0.0f) || !isfinite(sum)) {  // "attention softmax failed"
+            if (lane == 0) {
+                *flag = 1;
+                atomicOr(a.status, kStatusNonFinite);
+            }
+            continue;
+        }
+        for (uint32_t t = lane; t < n; t += 32)
+            e[t] = __fdiv_rn(e[t], sum);
+    }
+    __syncthreads();
+    if (*flag)
+        return;
+
+    // ---- y: thread (query vq, dims 8 vd .. 8 vd + 7), all KVM heads; serial over t
+    const uint32_t vq = tid / 16, vd = (tid % 16) * 8;
+    const uint32_t vn = vq < nq ? pos0 + vq + 1 : 0;
+    float acc[KVM][8];
+#pragma unroll
+    for (int h = 0; h < KVM; ++h)
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            acc[h][j] = 0.0f;
+    for (uint32_t t0 = 0; t0 < n_max; t0 += kPfKT) {
+        const uint32_t rows_in = min(kPfKT, n_max - t0);
+        for (uint32_t i = tid; i < rows_in * (HD / 4); i += kPfThreads) {
+            const uint32_t tt = i / (HD / 4), c4 = i % (HD / 4);
+            reinterpret_cast<float4*>(kv_s + (size_t)tt * kStride)[c4] =
+                reinterpret_cast<const float4*>(vc + (size_t)(t0 + tt) * HD)[c4];
+        }
+        __syncthreads();
+        const uint32_t tend = vn > t0 ? min(rows_in, vn - t0) : 0;
+        for (uint32_t tt = 0; tt < tend; ++tt) {
+            const float4 v0 = reinterpret_cast<const float4*>(kv_s + (size_t)tt * kStride + vd)[0];
+            const float4 v1 = reinterpret_cast<const float4*>(kv_s + (size_t)tt * kStride + vd)[1];
+#pragma unroll
+            for (int h = 0; h < KVM; ++h) {
+                const float p = sc_row(vq, h)[t0 + tt];
+                acc[h][0] = __fadd_rn(acc[h][0], __fmul_rn(p, v0.x));
+                acc[h][1] = __fadd_rn(acc[h][1], __fmul_rn(p, v0.y));
+                acc[h][2] = __fadd_rn(acc[h][2], __fmul_rn(p, v0.z));
+                acc[h][3] = __fadd_rn(acc[h][3], __fmul_rn(p, v0.w));
+                acc[h][4] = __fadd_rn(acc[h][4], __fmul_rn(p, v1.x));
+                acc[h][5] = __fadd_rn(acc[h][5], __fmul_rn(p, v1.y));
+                acc[h][6] = __fadd_rn(acc[h][6], __fmul_rn(p, v1.z));
+                acc[h][7] = __fadd_rn(acc[h][7], __fmul_rn(p, v1.w));
+            }
+        }
+        __syncthreads();
+    }
+    if (vq < nq) {
+        float* yr = a.y + (size_t)(p0 + vq) * a.y_stride;
+#pragma unroll
+        for (int h = 0; h < KVM; ++h) {
+            float4* dst = reinterpret_cast<float4*>(yr + (size_t)(g * KVM + h) * HD + vd);
+            dst[0] = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+            dst[1] = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
+        }
     }
 }
 

@@ -23,6 +23,10 @@ SMALL = gguf.Qwen3Shape(layers=3, hidden=1024, heads=8, kv_heads=4, head_dim=128
                         vocab=3000, context=512)
 WIDE = gguf.Qwen3Shape(layers=2, hidden=2048, heads=16, kv_heads=8, head_dim=128, ffn=6144,
                        vocab=4000, context=1024)
+# four query heads per KV head, and a context long enough that a tile's
+# attention scores no longer fit in shared memory (global scratch path)
+LONG = gguf.Qwen3Shape(layers=1, hidden=512, heads=4, kv_heads=1, head_dim=128, ffn=512, vocab=700,
+                       context=2048)
 
 
 @pytest.fixture(scope="module")
@@ -32,6 +36,7 @@ def models(tmp_path_factory):
         "tiny": (gguf.qwen3_model(d / "tiny.gguf", TINY, seed=31), TINY),
         "small": (gguf.qwen3_model(d / "small.gguf", SMALL, seed=32, scale_lo=0.02, scale_hi=0.2), SMALL),
         "wide": (gguf.qwen3_model(d / "wide.gguf", WIDE, seed=33), WIDE),
+        "long": (gguf.qwen3_model(d / "long.gguf", LONG, seed=34), LONG),
     }
 
 
@@ -135,3 +140,15 @@ def test_prefill_long_prompt(b200_device, models):
     prompt = rng.integers(0, shape.vocab, size=(1, 512)).astype(np.int32)
     want = run(b200_device, path, [prompt], n_ctx=600, chunk=0, gen=4)
     same(run(b200_device, path, [prompt], n_ctx=600, gen=4), want)
+
+
+@pytest.mark.parametrize("exact", [True, False])
+def test_prefill_long_context_four_heads_per_kv(b200_device, models, exact):
+    """1400 positions, 4 query heads per KV head: the score rows of a tile
+    exceed shared memory, so the kernel keeps them in device scratch."""
+    path, shape = models["long"]
+    rng = np.random.default_rng(45)
+    prompt = rng.integers(0, shape.vocab, size=(1, 1400)).astype(np.int32)
+    want = run(b200_device, path, [prompt], n_ctx=1500, exact=exact, chunk=0, gen=4)
+    same(run(b200_device, path, [prompt], n_ctx=1500, exact=exact, chunk=2048, gen=4), want)
+    same(run(b200_device, path, [prompt], n_ctx=1500, exact=exact, chunk=300, gen=4), want)
