@@ -41,7 +41,7 @@
 
 namespace {
 
-constexpr size_t kAttnSmemBudget = 200u * 1024u;  // dynamic shared memory of one attention block
+constexpr size_t kAttnSmemBudget = 227u * 1024u;  // dynamic shared memory of one attention block (the sm_100 maximum)
 
 thread_local std::string g_last_error;
 
@@ -321,6 +321,7 @@ struct bnnd_context {
     uint32_t hist_cap = 0;
     bnn::GemvLaunch plan_qkv{}, plan_o{}, plan_gu{}, plan_down{}, plan_head{};
     size_t attn_smem = 0;  // dynamic shared memory of the attention kernel
+    uint32_t attn_resident = 0;  // positions whose whole K/V history the attention kernel holds in shared memory
     std::vector<bnn::GemvLaunch> plan_mlp;
     bool pdl = true;  // launch the W1A8 linears with programmatic dependent launch
     cudaGraphExec_t graph_logits = nullptr, graph_prefill = nullptr, graph_profile = nullptr;
@@ -746,6 +747,7 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
         aa.scale = 1.0f / sqrtf((float)HD);
         aa.exact = exact;
         aa.status = status;
+        aa.resident_max = c->attn_resident;
         ck("attention_kernel", launch_attention(c, aa));
         if (tp)
             ck("all_gather:y", all_gather_rows(c, c->y_st.as<float>(), sh.q_rows, c->y.as<float>(), C));
@@ -908,7 +910,11 @@ BNND_Status create_llm_context(bnnd_context* c) {
         if ((st = dev_alloc(c->scores, (size_t)R * in.heads * bnn::eng::attn_sc_stride(c->n_ctx) * 4)))
             return st;
     }
-    c->attn_smem = ap.total;
+    // past the ring, the rest of the budget holds whole K/V histories of up to
+    // attn_resident positions (the kernel's tile-free path)
+    c->attn_resident = std::min<uint32_t>(bnn::eng::attn_resident_rows(in.head_dim, kAttnSmemBudget - ap.ring),
+                                          c->n_ctx);
+    c->attn_smem = c->attn_resident > 0 ? kAttnSmemBudget : ap.total;
     CUDA_OR(cudaFuncSetAttribute(attention_fn(in.head_dim, kv_mul), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kAttnSmemBudget),
             BNND_EIO);

@@ -102,7 +102,9 @@ __global__ void embed_kernel(const int32_t* tokens, const unsigned char* wblocks
 // conflicts), in a two-stage ring; the first K tiles are requested before
 // the kernel waits for the q|k|v projection, since the cache rows it reads
 // were written by earlier steps. The current position's k and v are used
-// straight from shared memory.
+// straight from shared memory. While the whole history fits in shared memory
+// (n <= resident_max), K and V are instead copied whole at the start and
+// every phase spreads over all threads: no tiles, no per-tile waits.
 constexpr uint32_t kAttnThreads = 256;
 constexpr uint32_t kAttnTile = 128;
 constexpr uint32_t kAttnStages = 2;
@@ -124,6 +126,7 @@ struct AttnArgs {
     float scale;            // 1 / sqrtf(head_dim), computed on the host as qwen3.c:404
     int exact;
     int* status;
+    uint32_t resident_max;  // positions n up to which K and V are held whole in shared memory (0: never)
 };
 
 // Scores of one query head occupy a row of this many floats (a multiple of
@@ -133,6 +136,11 @@ __host__ __device__ inline uint32_t attn_sc_stride(uint32_t n_ctx) { return (n_c
 struct AttnSmem {
     size_t bars, red, q, kn, vn, gq, gk, rc, rs, sc, ring, stage_bytes, total;
 };
+
+// Positions held whole (K rows padded, V dense) in `bytes` of shared memory past the ring start.
+__host__ __device__ inline uint32_t attn_resident_rows(uint32_t hd, size_t bytes) {
+    return (uint32_t)(bytes / ((size_t)(2u * hd + 4u) * 4u));
+}
 
 __host__ __device__ inline AttnSmem attn_smem_plan(uint32_t hd, uint32_t kv_mul, uint32_t n_ctx, bool sc_smem) {
     AttnSmem p;
@@ -247,6 +255,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     const float* kc = a.kcache + head_base;
     const float* vc = a.vcache + head_base;
     constexpr uint32_t kstride = HD + 4;
+    const bool resident = n <= a.resident_max;
+    float* kres = reinterpret_cast<float*>(ring);                // [resident_max][kstride]
+    float* vres = kres + (size_t)a.resident_max * kstride;       // [resident_max][HD]
 
     if (tid == 0) {
         for (uint32_t s = 0; s < kAttnStages; ++s)
@@ -273,9 +284,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
             bulk_g2s(dst, vc + (size_t)t0 * HD, rows_in * HD * 4u, &full[s]);
         }
     };
-    if (warp == 0)
-        for (uint32_t L = 0; L < kAttnStages && L < nloads; ++L)
-            issue(L);
+    if (warp == 0) {
+        if (resident) {
+            // every earlier position of the head at once: K rows padded, V dense
+            if (lane == 0)
+                mbar_arrive_expect_tx(&full[0], pos * HD * 4u * 2u);
+            __syncwarp();
+            for (uint32_t r = lane; r < pos; r += 32)
+                bulk_g2s(kres + (size_t)r * kstride, kc + (size_t)r * HD, HD * 4u, &full[0]);
+            if (lane == 0 && pos > 0)
+                bulk_g2s(vres, vc, pos * HD * 4u, &full[0]);
+        } else {
+            for (uint32_t L = 0; L < kAttnStages && L < nloads; ++L)
+                issue(L);
+        }
+    }
     // weights and rope rows do not depend on earlier kernels either
     for (uint32_t i = tid; i < HD; i += kAttnThreads) {
         gq_s[i] = a.q_norm[i];
@@ -312,11 +335,42 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
         a.kcache[head_base + (size_t)pos * HD + i] = kn_s[i];
         a.vcache[head_base + (size_t)pos * HD + i] = vn_s[i];
     }
-
-    // ---- scores
     int bad = 0;
+    if (resident) {
+        for (uint32_t i = tid; i < HD; i += kAttnThreads) {
+            kres[(size_t)pos * kstride + i] = kn_s[i];
+            vres[(size_t)pos * HD + i] = vn_s[i];
+        }
+        if (!mbar_wait(&full[0], 0) && lane == 0) {
+            *flag = 1;
+            atomicOr(a.status, kStatusTimeout);
+        }
+        __syncthreads();
+        if (*flag == 0) {
+            // scores: every (query head, position) pair over all threads
+            for (uint32_t i = tid; i < kv_mul * n; i += kAttnThreads) {
+                const uint32_t h = i / n, t = i % n;
+                const float4* k4 = reinterpret_cast<const float4*>(kres + (size_t)t * kstride);
+                const float4* q4 = reinterpret_cast<const float4*>(q_s + (size_t)h * HD);
+                float dot = 0.0f;
+#pragma unroll
+                for (uint32_t j = 0; j < HD / 4; ++j) {
+                    const float4 kk = k4[j], qq = q4[j];
+                    dot = __fadd_rn(dot, __fmul_rn(qq.x, kk.x));
+                    dot = __fadd_rn(dot, __fmul_rn(qq.y, kk.y));
+                    dot = __fadd_rn(dot, __fmul_rn(qq.z, kk.z));
+                    dot = __fadd_rn(dot, __fmul_rn(qq.w, kk.w));
+                }
+                const float score = __fmul_rn(dot, a.scale);
+                bad |= !isfinite(score);
+                sc[(size_t)h * sc_stride + t] = score;
+            }
+        }
+    }
+
+    // ---- scores (tiled)
     uint32_t L = 0;
-    for (uint32_t tile = 0; tile < ntiles; ++tile, ++L) {
+    for (uint32_t tile = 0; tile < (resident ? 0u : ntiles); ++tile, ++L) {
         const uint32_t s = L % kAttnStages, t0 = tile * kAttnTile, rows_in = min(kAttnTile, n - t0);
         if (!mbar_wait(&full[s], (L / kAttnStages) & 1) && lane == 0) {
             *flag = 1;
@@ -428,6 +482,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
 #pragma unroll
     for (uint32_t h = 0; h < KVM; ++h)
         acc[h] = 0.0f;
+    if (resident) {
+        // y: one serial chain per (query head, dim) over all threads
+        if (live2)
+            for (uint32_t i = tid; i < kv_mul * HD; i += kAttnThreads) {
+                const uint32_t h = i / HD, d = i % HD;
+                const float* ph = sc + (size_t)h * sc_stride;
+                float v = 0.0f;
+                uint32_t t = 0;
+                for (; t + 4 <= n; t += 4) {
+                    const float4 p = *reinterpret_cast<const float4*>(ph + t);
+                    v = __fadd_rn(v, __fmul_rn(p.x, vres[(size_t)t * HD + d]));
+                    v = __fadd_rn(v, __fmul_rn(p.y, vres[(size_t)(t + 1) * HD + d]));
+                    v = __fadd_rn(v, __fmul_rn(p.z, vres[(size_t)(t + 2) * HD + d]));
+                    v = __fadd_rn(v, __fmul_rn(p.w, vres[(size_t)(t + 3) * HD + d]));
+                }
+                for (; t < n; ++t)
+                    v = __fadd_rn(v, __fmul_rn(ph[t], vres[(size_t)t * HD + d]));
+                if (*flag == 0)
+                    a.y[(size_t)row * a.y_stride + ((size_t)g * kv_mul + h) * HD + d] = v;
+            }
+        return;
+    }
     for (uint32_t tile = 0; tile < ntiles; ++tile, ++L) {
         const uint32_t s = L % kAttnStages, t0 = tile * kAttnTile, rows_in = min(kAttnTile, n - t0);
         if (!mbar_wait(&full[s], (L / kAttnStages) & 1) && lane == 0) {

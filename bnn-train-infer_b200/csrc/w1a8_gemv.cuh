@@ -29,10 +29,11 @@
 //                  (qwen3.c:491-495); the matrix stores gate and up rows in
 //                  alternating 8-row blocks
 //
-// Pipeline: persistent CTAs of 4 compute warps + 1 producer warp. The
+// Pipeline: persistent CTAs of 8 compute warps + 1 producer warp. The
 // producer starts streaming weights at once (they never depend on earlier
 // kernels), before the compute warps wait for the preceding kernel
-// (programmatic dependent launch) and build the activations. 4/B warps share
+// (programmatic dependent launch) and build the activations (the RMSNorm sum
+// on warps 0..3, every elementwise pass on all 8). 8/B warps share
 // one block, each taking a subset of its groups (the integer D's meet in
 // shared memory, so the FP32 order is unchanged); small matrices use B = 1 so
 // that every SM gets blocks. All waits are bounded.
@@ -49,8 +50,9 @@ constexpr int kRowsPerCta = 8;      // activation rows per CTA (grid y covers mo
 constexpr int kStatusBadInput = 1;  // an input row had NaN/Inf (F32) or -128 (I8)
 constexpr int kStatusNonFinite = 4; // a normalisation divisor was not finite
 constexpr uint32_t kBlockPad = 4;
-constexpr uint32_t kComputeWarps = 4;
-static_assert(kComputeWarps * 32 == kSumThreads, "exact_sumsq runs on the four compute warps");
+constexpr uint32_t kComputeWarps = 8;
+constexpr uint32_t kSumWarps = kSumThreads / 32;  // the RMSNorm sum runs on compute warps 0..3
+static_assert(kComputeWarps >= kSumWarps, "the RMSNorm sum needs four compute warps");
 // Prologues that build the activations in the CTA hold up to this many inputs
 // (in registers: kMaxPrologueK / 512 float4 per compute thread).
 constexpr uint32_t kMaxPrologueK = 8192;
@@ -140,7 +142,7 @@ __host__ __device__ inline GemvSmem gemv_smem_plan(uint32_t groups, uint32_t mro
     GemvSmem p;
     p.bars = 0;     // full[stages], empty[stages] (stages <= 8)
     p.rs = 128;     // row scales + status flags
-    p.act = 256;
+    p.act = 448;  // after the row scales, flags and 64 reduction slots
     p.tot = p.act + (size_t)mrows * groups * kActStride * 4u;
     p.xbuf = (p.tot + (size_t)mrows * groups * 4u + 15) & ~(size_t)15;  // float4 stores
     p.seg = p.xbuf + (pro != kProSliced ? (size_t)groups * kGroup * 4u : 0);  // FP32 row
@@ -181,7 +183,7 @@ __device__ __forceinline__ int group_dot(const uint32_t (&mk)[32], const uint32_
 }
 
 template <int PRO, int EPI>
-__global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__((kComputeWarps + 1) * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
     griddep_launch_dependents();
     extern __shared__ __align__(128) unsigned char sm[];
     const uint32_t G = a.groups;
@@ -195,7 +197,7 @@ __global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
     uint64_t* empty = full + a.stages;
     float* rs_s = reinterpret_cast<float*>(sm + plan.rs);          // [8] row scales
     int* flags = reinterpret_cast<int*>(sm + plan.rs + 32);        // [0] abort
-    float* red = reinterpret_cast<float*>(sm + plan.rs + 64);      // reduction slots (16)
+    float* red = reinterpret_cast<float*>(sm + plan.rs + 64);      // reduction slots (64)
     uint32_t* act_s = reinterpret_cast<uint32_t*>(sm + plan.act);
     int32_t* tot_s = reinterpret_cast<int32_t*>(sm + plan.tot);
     float* xbuf = reinterpret_cast<float*>(sm + plan.xbuf);
@@ -281,22 +283,30 @@ __global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
                 // index order (qwen3.c:361-372): exact mode reproduces it bit for
                 // bit with the four compute warps (exact_sum.cuh); fast mode sums
                 // in a fixed tree order.
-                float sum;
-                if (a.exact) {
-                    sum = exact_sumsq(xbuf, (int)K, sum_mem, 1);
-                } else {
-                    float t = 0.0f;
-                    for (uint32_t i = tid; i < K; i += cthreads)
-                        t = __fadd_rn(t, __fmul_rn(xbuf[i], xbuf[i]));
-                    for (int o = 16; o > 0; o >>= 1)
-                        t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
-                    if (lane == 0)
-                        red[1 + warp] = t;
-                    named_barrier(1, cthreads);
-                    sum = 0.0f;
-                    for (uint32_t w = 0; w < consumers; ++w)
-                        sum = __fadd_rn(sum, red[1 + w]);
+                // Both run on warps 0..3 (named barrier 2); the fast tree's
+                // order is that of 128 threads.
+                if (warp < kSumWarps) {
+                    float sum;
+                    if (a.exact) {
+                        sum = exact_sumsq(xbuf, (int)K, sum_mem, 2);
+                    } else {
+                        float t = 0.0f;
+                        for (uint32_t i = tid; i < K; i += kSumThreads)
+                            t = __fadd_rn(t, __fmul_rn(xbuf[i], xbuf[i]));
+                        for (int o = 16; o > 0; o >>= 1)
+                            t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
+                        if (lane == 0)
+                            red[16 + warp] = t;
+                        named_barrier(2, kSumThreads);
+                        sum = 0.0f;
+                        for (uint32_t w = 0; w < kSumWarps; ++w)
+                            sum = __fadd_rn(sum, red[16 + w]);
+                    }
+                    if (tid == 0)
+                        red[48] = sum;
                 }
+                named_barrier(1, cthreads);
+                const float sum = red[48];
                 const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)K), a.eps));
                 amax = 0.0f;
                 if (!isfinite(rms) || rms == 0.0f) {
@@ -322,11 +332,11 @@ __global__ void __launch_bounds__(5 * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
             for (int o = 16; o > 0; o >>= 1)
                 amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
             if (lane == 0)
-                red[8 + warp] = amax;
+                red[32 + warp] = amax;
             named_barrier(1, cthreads);
-            amax = red[8];
+            amax = red[32];
             for (uint32_t w = 1; w < consumers; ++w)
-                amax = fmaxf(amax, red[8 + w]);
+                amax = fmaxf(amax, red[32 + w]);
             const float s = row_scale_from_absmax(amax);
             const RowQuantizer quant(s);
             // One warp quantises one group per pass (32 lanes x 4 values).
