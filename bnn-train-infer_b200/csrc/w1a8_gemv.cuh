@@ -4,7 +4,7 @@
 // rows; block b is G*144 bytes:
 //     [G][8][16 B]  sign bits of row 8b+r, group g, public bit order
 //     [8][G]        binary16 scales of row 8b+r, group g
-// A tile of B = 1, 2 or 4 consecutive blocks is one contiguous range that the
+// A tile of B = 1, 2, 4 or 8 consecutive blocks is one contiguous range that the
 // producer warp streams into shared memory with a single 1D bulk copy, bits
 // and scales together. Allocations are padded to kBlockPad blocks.
 //
@@ -98,7 +98,7 @@ struct GemvArgs {
     const unsigned char* wblocks;  // packed blocks (see header)
     uint32_t n, groups, m;         // packed output rows, K/128, activation rows
     uint32_t tiles, stages;        // tiles of B blocks; shared-memory ring depth
-    uint32_t blocks_per_tile;      // B = 1, 2 or 4
+    uint32_t blocks_per_tile;      // B = 1, 2, 4 or 8
     // kProSliced
     const uint32_t* act;           // [M][G][32]
     const int32_t* totals;         // [M][G]
@@ -522,7 +522,11 @@ inline GemvLaunch plan_gemv(int sm_count, uint32_t n, uint32_t groups, uint32_t 
     GemvLaunch c;
     c.pro = pro;
     c.epi = epi;
-    c.blocks_per_tile = nblocks >= 8u * sm_count ? 4u : (nblocks >= 2u * sm_count ? 2u : 1u);
+    // one block per compute warp when there are blocks to spare (no split groups,
+    // no hand-off between warps inside a block)
+    c.blocks_per_tile = nblocks >= 16u * sm_count ? kComputeWarps
+                        : nblocks >= 8u * sm_count ? 4u
+                        : (nblocks >= 2u * sm_count ? 2u : 1u);
     if (c.blocks_per_tile < min_bpt)
         c.blocks_per_tile = min_bpt;
     c.stages = 4;
