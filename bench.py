@@ -26,6 +26,20 @@ tensor cores, tcgen05 kind::i8) plus the greedy pick of the next token,
 through BNND_DecodeArgmax with host ids in and out; value is prompt
 tokens/s, the roofline the int8 tensor rate of the whole prefill.
 
+--sweep measures BASELINE configs[1]: GEMV_F32 and DOT_GROUPS at the Qwen3
+linear shapes (K x N = 2048x2048, 2048x1024, 2048x6144, 6144x2048,
+2048x151669), rows = 1. Kernel time is CUDA events around each job on the
+device's stream with L2 flushed (a 256 MB write) before every job; GB/s is
+the algorithmic bytes (N*K*0.140625 + 4K + 4N for GEMV_F32, N*K/8 + K + 2NK/128
+for DOT_GROUPS) over that time. e2e is the full synchronous call with host
+buffers (BufferWrite, BNN_Execute, BufferRead; 2048x151669 through 19 jobs of
+at most 8192 rows, as linear.c does). value is GEMV_F32 GB/s at 2048x151669.
+
+--classify measures BASELINE configs[0]: the bnn-mlp classifier
+(896->512 relu, 512->512 relu, 512->10) over 1000 seeded samples in batches
+of 64 through BNND_Classify (each linear a 64-row GEMM_F32 on the tensor
+cores), host samples in and logits out per call; value is samples/s.
+
 --impl reference runs only the reference's CPU path: one soft-engine process
 per host core (it is single-threaded), each decoding tokens of the same
 model, and reports their aggregate tokens/s.
@@ -392,6 +406,206 @@ def run_prefill(args, ctx, info, timed, rank, world):
     }
 
 
+def run_classify(args):
+    """bnn-mlp classify, 1000 samples in batches of 64."""
+    import numpy as np
+    import torch
+    from bnn_b200 import accel, engine, gguf
+    cache = Path(args.model_cache)
+    cache.mkdir(parents=True, exist_ok=True)
+    path = cache / "bnn_mlp_seed20261201.gguf"
+    if not path.exists():
+        tmp = path.with_suffix(f".tmp{os.getpid()}")
+        gguf.bnn_mlp_model(tmp)
+        os.replace(tmp, path)
+    torch.cuda.set_device(0)
+    dev = accel.Device(0)
+    api = engine.EngineApi(dev.api.dll)
+    model = engine.Model(dev, path, api)
+    info = model.info
+    batch, n_samples = 64, 1000
+    rng = np.random.default_rng(20261201)
+    x = np.zeros((n_samples, info.input_size), dtype=np.float32)
+    x[:, :784] = rng.standard_normal((n_samples, 784)).astype(np.float32)
+    ctx = engine.Context(model, n_batch=batch)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    out = np.empty((n_samples, info.n_classes), dtype=np.float32)
+
+    def one_pass():
+        for b0 in range(0, n_samples, batch):
+            out[b0:b0 + batch] = ctx.classify(x[b0:b0 + batch])
+
+    for _ in range(args.warmup):
+        one_pass()
+    with ClockSampler(0) as clocks:
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            one_pass()
+        e1.record(stream)
+        e1.synchronize()
+        wall = time.perf_counter() - t0
+    clk = clocks.summary()
+    ms = e0.elapsed_time(e1)
+    value = n_samples * args.steps / (ms / 1e3)
+    macs = 896 * 512 + 512 * 512 + 512 * 10  # per sample
+    tops = 2.0 * macs * n_samples * args.steps / (ms / 1e3) / 1e12
+    d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else None
+    peak = 2.0 * float(d["bf16_tflops"]) if d else 2.0 * 1590.0
+    pred = out.argmax(axis=1)
+    ctx.free()
+    model.free()
+    dev.close()
+    return {
+        "metric": "bnn_mlp_classify_samples_per_s", "value": round(value, 1), "unit": "samples/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded bnn-mlp weights; 1000 N(0,1) samples of 784 values, zero-padded to 896)",
+        "config": {"workload": "configs[0]: bnn-mlp W1A8 classifier 896->512->512->10, 1000 samples, "
+                               "BNND_Classify batch 64 (16 calls per step)",
+                   "l2": "weights (0.1 MB) stay in L2; the workload is latency-bound (one step = 16 calls)",
+                   "predicted_class_histogram": np.bincount(pred, minlength=info.n_classes).tolist()},
+        "roofline": {"bound": "tensor", "achieved": round(tops, 3), "peak": round(peak, 1), "unit": "TOPS",
+                     "frac": round(tops / peak, 6),
+                     "peak_source": "2 x measured dense bf16" if d else "2 x fallback bf16", "traffic": None,
+                     "what": "2 x 726,016 int8 multiply-adds per sample / step time (host copies included)"},
+        "e2e": {"value": round(n_samples * args.steps / wall, 1), "unit": "samples/s",
+                "h2d_bytes_per_step": n_samples * info.input_size * 4, "d2h_bytes_per_step": n_samples * info.n_classes * 4,
+                "call": "BNND_Classify per batch of 64, host samples in, host logits out"},
+        "clocks": clk,
+    }
+
+
+SWEEP_SHAPES = [(2048, 2048), (2048, 1024), (2048, 6144), (6144, 2048), (2048, 151669)]  # (K, N)
+
+
+def run_sweep(args):
+    """single-op GEMV_F32 / DOT_GROUPS sweep, rows = 1."""
+    import ctypes
+    import numpy as np
+    import torch
+    from bnn_b200 import accel, synth
+    torch.cuda.set_device(0)
+    dev = accel.Device(0)
+    dll = dev.api.dll
+    dll.bnn_b200_execute_async.restype = ctypes.c_int
+    dll.bnn_b200_execute_async.argtypes = [ctypes.c_void_p, ctypes.POINTER(accel.Job)]
+    dll.bnn_b200_sync.restype = ctypes.c_int
+    dll.bnn_b200_sync.argtypes = [ctypes.c_void_p]
+    dll.bnn_b200_device_stream.restype = ctypes.c_void_p
+    dll.bnn_b200_device_stream.argtypes = [ctypes.c_void_p]
+    dll.bnn_b200_matrix_create_unbounded.restype = ctypes.c_int
+    dll.bnn_b200_matrix_create_unbounded.argtypes = [ctypes.c_void_p, ctypes.POINTER(accel.MatrixDesc),
+                                                     ctypes.POINTER(ctypes.c_void_p)]
+    stream = torch.cuda.ExternalStream(dll.bnn_b200_device_stream(dev.handle))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 2 x L2
+    hbm, hbm_kind = measured_peaks()
+    rng = synth.rng_for(1)
+    results = []
+
+    def matrix(bits, scales, k, n):
+        bits = np.ascontiguousarray(bits)
+        scales = np.ascontiguousarray(scales)
+        desc = accel.MatrixDesc(k, n, accel.GROUP, bits.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), bits.nbytes,
+                                scales.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16)), scales.size)
+        h = ctypes.c_void_p()
+        st = dll.bnn_b200_matrix_create_unbounded(dev.handle, ctypes.byref(desc), ctypes.byref(h))
+        if st != accel.OK:
+            raise accel.BnnError(st, "matrix")
+        m = accel.Matrix.__new__(accel.Matrix)
+        m.device, m.k, m.n, m.handle = dev, k, n, h
+        return m
+
+    with ClockSampler(0) as clocks:
+        for k, n in SWEEP_SHAPES:
+            bits, scales = synth.w1_matrix(rng, k, n)
+            x = synth.activations(rng, 1, k)
+            scale = float(np.abs(x).max()) / 127.0
+            q = np.clip(np.rint(x / scale), -127, 127).astype(np.int8)
+            m = matrix(bits, scales, k, n)
+            g = k // 128
+            for op, inp, out_bytes, alg in (
+                    (accel.OP_GEMV_F32, x, n * 4, n * k * 0.140625 + 4 * k + 4 * n),
+                    (accel.OP_DOT_GROUPS, q, n * g * 2, n * k / 8 + k + 2 * n * g)):
+                bi, bo = accel.Buffer(dev, inp.nbytes), accel.Buffer(dev, out_bytes)
+                bi.write(inp)
+                it, ot = accel.OP_TYPES[op]
+                job = accel.Job(operation=op, matrix=m.handle, input=accel.BufferView(bi.handle, it, 0, 0),
+                                output=accel.BufferView(bo.handle, ot, 0, 0), rows=1)
+                times = []
+                for i in range(args.warmup + args.steps):
+                    with torch.cuda.stream(stream):
+                        flush.fill_(i & 0xff)
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        e0.record(stream)
+                        if dll.bnn_b200_execute_async(dev.handle, ctypes.byref(job)) != accel.OK:
+                            raise accel.BnnError(-1, "execute_async")
+                        e1.record(stream)
+                    e1.synchronize()
+                    if i >= args.warmup:
+                        times.append(e0.elapsed_time(e1))
+                if dll.bnn_b200_sync(dev.handle) != accel.OK:
+                    raise accel.BnnError(-1, "sync")
+                us = statistics.median(times) * 1e3
+                # the public synchronous path, host buffers (N > 8192: 8192-row chunks)
+                host_out = np.empty(out_bytes, dtype=np.uint8)
+                chunks = []
+                if n <= 8192:
+                    chunks.append((m, bo, n))
+                else:
+                    for r0 in range(0, n, 8192):
+                        rn = min(8192, n - r0)
+                        mc = accel.Matrix(dev, bits[r0:r0 + rn], scales[r0:r0 + rn])
+                        chunks.append((mc, accel.Buffer(dev, out_bytes // n * rn), rn))
+                t_e2e = []
+                for i in range(max(3, args.steps // 4)):
+                    t0 = time.perf_counter()
+                    bi.write(inp)
+                    off = 0
+                    for mc, bc, rn in chunks:
+                        st = dev.execute(op, mc, bi, bc, rows=1)
+                        if st != accel.OK:
+                            raise accel.BnnError(st, "BNN_Execute")
+                        nb = out_bytes // n * rn
+                        host_out[off:off + nb] = bc.read(nb)
+                        off += nb
+                    t_e2e.append(time.perf_counter() - t0)
+                for mc, bc, rn in chunks:
+                    if mc is not m:
+                        mc.destroy()
+                        bc.free()
+                e2e_us = statistics.median(t_e2e) * 1e6
+                results.append({"op": "GEMV_F32" if op == accel.OP_GEMV_F32 else "DOT_GROUPS", "k": k, "n": n,
+                                "bytes": int(alg), "kernel_us": round(us, 2),
+                                "gbs": round(alg / (us * 1e-6) / 1e9, 1),
+                                "frac_of_hbm": round(alg / (us * 1e-6) / 1e9 / hbm, 4),
+                                "e2e_us": round(e2e_us, 1), "e2e_jobs": len(chunks)})
+                bi.free()
+                bo.free()
+            m.destroy()
+    clk = clocks.summary()
+    dev.close()
+    head = [r for r in results if r["op"] == "GEMV_F32" and r["n"] == 151669][0]
+    return {
+        "metric": "w1a8_gemv_f32_hbm_gbs", "value": head["gbs"], "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(head["kernel_us"] / 1e3, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded W1 bits, FP16 scales ~U[0.005,0.05], FP32 N(0,1) activations with 1% x20)",
+        "config": {"workload": "configs[1]: single-op GEMV_F32 / DOT_GROUPS sweep at the Qwen3-1.7B linear "
+                               "shapes, rows = 1 (value: GEMV_F32 2048x151669 as one job)",
+                   "l2": "flushed (256 MB write) before every timed job", "shapes": results},
+        "roofline": {"bound": "hbm", "achieved": head["gbs"], "peak": hbm, "unit": "GB/s",
+                     "frac": round(head["gbs"] / hbm, 4), "peak_source": hbm_kind, "traffic": None,
+                     "what": "prep + contraction of one GEMV_F32 job (kernel time), algorithmic bytes"},
+        "e2e": {"value": round(head["bytes"] / (head["e2e_us"] * 1e-6) / 1e9, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": 2048 * 4, "d2h_bytes_per_step": 151669 * 4,
+                "call": "BufferWrite + 19 x BNN_Execute (<= 8192 rows) + BufferRead, host buffers"},
+        "clocks": clk,
+    }
+
+
 def _ref_worker(path, n_tokens, conn):
     import ref_engine
     ref = ref_engine.RefEngine(path, n_ctx=CTX)
@@ -458,6 +672,10 @@ def main():
     ap.add_argument("--profile-steps", type=int, default=4)
     ap.add_argument("--ref-procs", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--classify", action="store_true",
+                    help="BASELINE configs[0]: bnn-mlp classify, batch 64 (samples/s)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="BASELINE configs[1]: single-op GEMV_F32 / DOT_GROUPS sweep (HBM GB/s)")
     ap.add_argument("--prefill", action="store_true",
                     help="BASELINE configs[3]: batched 512-token prefill instead of decode")
     ap.add_argument("--tp", action="store_true",
@@ -466,7 +684,12 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    out = run_reference(args) if args.impl == "reference" else run_b200(args)
+    if args.sweep and args.impl != "reference":
+        out = run_sweep(args)
+    elif args.classify and args.impl != "reference":
+        out = run_classify(args)
+    else:
+        out = run_reference(args) if args.impl == "reference" else run_b200(args)
     if out is not None:
         print(json.dumps(out), flush=True)
 

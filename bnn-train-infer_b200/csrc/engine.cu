@@ -38,6 +38,7 @@
 #include "prefill_kernels.cuh"
 #include "w1a8_gemv.cuh"
 #include "w1a8_mma.cuh"
+#include "w1a8_prep.cuh"
 
 namespace {
 
@@ -317,6 +318,7 @@ struct bnnd_context {
     ncclComm_t comm = nullptr;
     DevMem y_st, x_st, h_st, lg_st;  // rank-major all-gather buffers [world][rows][slice]
     DevMem mlp_a, mlp_b;
+    DevMem mlp_asw, mlp_rs;  // classify batches of kMmaMinRows+ rows: tensor-core operand, row scales
     size_t tok_seq_cap = 0;
     uint32_t hist_cap = 0;
     bnn::GemvLaunch plan_qkv{}, plan_o{}, plan_gu{}, plan_down{}, plan_head{};
@@ -931,6 +933,9 @@ BNND_Status create_mlp_context(bnnd_context* c) {
         (st = dev_alloc(c->status, 4)))
         return st;
     CUDA_OR(cudaMemset(c->status.p, 0, 4), BNND_EIO);
+    if (R >= bnn::kMmaMinRows &&
+        ((st = dev_alloc(c->mlp_asw, bnn::mma_a_bytes(R, D / 128))) || (st = dev_alloc(c->mlp_rs, (size_t)R * 4))))
+        return st;
     for (const auto& l : m->mlp) {
         c->plan_mlp.push_back(
             bnn::plan_gemv(m->dev->sm_count, l->w.out, l->w.in / 128, R, bnn::kProQuant, bnn::kEpiView));
@@ -1529,11 +1534,42 @@ BNND_Status BNND_Classify(BNND_Context c, const float* input, uint32_t n_samples
     float* cur = c->mlp_a.as<float>();
     float* nxt = c->mlp_b.as<float>();
     CUDA_OR(cudaMemcpyAsync(cur, input, inputs * 4, cudaMemcpyHostToDevice, s), BNND_EIO);
+    const bool mma = n_samples >= bnn::kMmaMinRows;  // the batch on the tensor cores (BNN_Execute's threshold)
     for (size_t i = 0; i < m->mlp.size(); ++i) {
         const MlpLayer& L = *m->mlp[i];
-        CUDA_OR(launch_linear(c, c->plan_mlp[i], L.w, cur, nullptr, n_samples, nxt, (size_t)L.w.out * 4u,
-                              c->status.as<int>()),
-                BNND_EIO);
+        if (mma) {
+            // QuantizeRow of every sample into the pre-tiled operand, then GEMM_F32
+            bnn::PrepArgs pa = {};
+            pa.in = reinterpret_cast<const unsigned char*>(cur);
+            pa.in_stride = (size_t)L.w.in * 4u;
+            pa.kind = bnn::kInputF32;
+            pa.k = L.w.in;
+            pa.m = n_samples;
+            pa.a_sw = c->mlp_asw.as<unsigned char>();
+            pa.row_scale = c->mlp_rs.as<float>();
+            pa.status = c->status.as<int>();
+            const size_t prep_smem = bnn::prep_smem_bytes(L.w.in);
+            CUDA_OR(cudaFuncSetAttribute(bnn::w1a8_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)prep_smem),
+                    BNND_EIO);
+            bnn::w1a8_prep_kernel<<<n_samples, bnn::kPrepThreads, prep_smem, s>>>(pa);
+            bnn::MmaArgs ma = {};
+            ma.wblocks = L.w.m->wblocks;
+            ma.n = L.w.out;
+            ma.groups = L.w.in / 128;
+            ma.m = n_samples;
+            ma.a_sw = c->mlp_asw.as<unsigned char>();
+            ma.row_scale = c->mlp_rs.as<float>();
+            ma.out = reinterpret_cast<unsigned char*>(nxt);
+            ma.out_stride = (size_t)L.w.out * 4u;
+            ma.epi = bnn::kEpiView;
+            ma.status = c->status.as<int>();
+            CUDA_OR(bnn::launch_mma(ma, s), BNND_EIO);
+        } else {
+            CUDA_OR(launch_linear(c, c->plan_mlp[i], L.w, cur, nullptr, n_samples, nxt, (size_t)L.w.out * 4u,
+                                  c->status.as<int>()),
+                    BNND_EIO);
+        }
         bnn::eng::mlp_post_kernel<<<64, 256, 0, s>>>(nxt, L.post_scale.as<float>(), L.post_bias.as<float>(),
                                                      L.w.out, n_samples, L.relu);
         std::swap(cur, nxt);
