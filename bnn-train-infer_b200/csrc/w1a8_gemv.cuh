@@ -183,7 +183,7 @@ __device__ __forceinline__ int group_dot(const uint32_t (&mk)[32], const uint32_
 }
 
 template <int PRO, int EPI>
-__global__ void __launch_bounds__((kComputeWarps + 1) * 32, 1) w1a8_gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__((kComputeWarps + 1) * 32, 2) w1a8_gemv_kernel(GemvArgs a) {
     griddep_launch_dependents();
     extern __shared__ __align__(128) unsigned char sm[];
     const uint32_t G = a.groups;
@@ -541,18 +541,40 @@ inline GemvLaunch plan_gemv(int sm_count, uint32_t n, uint32_t groups, uint32_t 
         else
             break;
     }
-    c.tiles = (nblocks + c.blocks_per_tile - 1) / c.blocks_per_tile;
-    int occ = 1;
     const GemvFn fn = gemv_fn(pro, epi);
     // The attribute is per function, shared by every matrix's launches.
     cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvSmemBudget);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, (const void*)fn, (int)(kComputeWarps + 1) * 32,
-                                                      c.smem) != cudaSuccess ||
-        occ < 1)
-        occ = 1;
     const uint32_t mchunks = (m + kRowsPerCta - 1) / kRowsPerCta;
-    uint32_t slots = (uint32_t)sm_count * (uint32_t)occ;
-    slots = slots > mchunks ? slots / mchunks : 1u;
+    uint32_t slots = 1;
+    // Every CTA repeats the prologue, so each should get one tile: widen the
+    // tiles (up to one block per compute warp) until they fit in one wave; a
+    // CTA with a single tile needs only two ring stages.
+    auto occupancy = [&](size_t smem) {
+        int occ = 1;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, (const void*)fn, (int)(kComputeWarps + 1) * 32,
+                                                          smem) != cudaSuccess ||
+            occ < 1)
+            occ = 1;
+        const uint32_t sl = (uint32_t)sm_count * (uint32_t)occ;
+        return sl > mchunks ? sl / mchunks : 1u;
+    };
+    for (uint32_t bpt = c.blocks_per_tile;; bpt *= 2) {
+        const uint32_t tiles = (nblocks + bpt - 1) / bpt;
+        const size_t smem2 = gemv_smem_plan(groups, mrows, bpt, 2, pro, epi).total;
+        if (smem2 > kGemvSmemBudget)
+            break;
+        const uint32_t sl = occupancy(smem2);
+        if (tiles <= sl) {
+            c.blocks_per_tile = bpt;
+            c.stages = 2;
+            c.smem = smem2;
+            break;
+        }
+        if (bpt >= kComputeWarps)
+            break;
+    }
+    c.tiles = (nblocks + c.blocks_per_tile - 1) / c.blocks_per_tile;
+    slots = occupancy(c.smem);
     c.grid_x = c.tiles < slots ? c.tiles : slots;
     return c;
 }
