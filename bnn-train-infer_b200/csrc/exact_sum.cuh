@@ -3,7 +3,7 @@
 // qwen3_rmsnorm (bnn-sw-v2/qwen3/qwen3.c:361-372) accumulates
 //     s_0 = 0,  s_{i+1} = fl(s_i + fl(x_i * x_i)),  i = 0..n-1
 // in index order. Run literally that is a chain of n dependent adds; this
-// file produces the identical float with the 128 threads of four warps.
+// file produces the identical float with the 256 threads of eight warps.
 //
 // Every term a_i = fl(x_i * x_i) is >= 0, so s is non-decreasing. While s_i
 // and s_{i+1} lie in one binade [2^e, 2^(e+1)), with grid spacing
@@ -37,8 +37,9 @@
 
 namespace bnn {
 
-constexpr int kSumThreads = 128;       // four warps
-constexpr int kSumSlots = 16;          // records per thread before its chunk goes serial
+constexpr int kSumThreads = 256;       // eight warps
+constexpr int kSumWarpsN = kSumThreads / 32;
+constexpr int kSumSlots = 8;           // records per thread before its chunk goes serial
 constexpr int kSumBatch = 8;           // elements loaded ahead per step
 constexpr int kRunEMin = -100;         // runs only in binades where u and 2^(23-e) are normal
 constexpr int kRunEMax = 125;
@@ -227,20 +228,20 @@ __device__ __forceinline__ void sum_bar(int id) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kSumThreads) : "memory");
 }
 
-// Called by the 128 threads of warps 0..3 of a CTA; returns the serial sum of
+// Called by the 256 threads of warps 0..7 of a CTA; returns the serial sum of
 // squares of xs[0..n), 1 <= n <= 65535 (shared memory), to all of them.
-// Uses named barrier `bar` (128 threads) and kSumSmemBytes of 16-byte
+// Uses named barrier `bar` (256 threads) and kSumSmemBytes of 16-byte
 // aligned shared memory at `mem`.
 static __device__ __forceinline__ float exact_sumsq(const float* xs, int n, unsigned char* mem, int bar) {
     SumRec* slots = reinterpret_cast<SumRec*>(mem + kSumSlotsOffset);
     SumRec* list = reinterpret_cast<SumRec*>(mem + kSumListOffset);
     int* tags = reinterpret_cast<int*>(mem + kSumTagsOffset);
     float* misc = reinterpret_cast<float*>(mem + kSumMiscOffset);
-    float* wsum = misc;                              // [4] warp sums of the partials
-    int* wcnt = reinterpret_cast<int*>(misc + 4);    // [4] warp record counts
-    int* winc = reinterpret_cast<int*>(misc + 8);    // [4] warp increment totals
-    float* abuf = misc + 16;                         // [32] addends of a walk round
-    float* result = misc + 48;
+    float* wsum = misc;                              // [8] warp sums of the partials
+    int* wcnt = reinterpret_cast<int*>(misc + 8);    // [8] warp record counts
+    int* winc = reinterpret_cast<int*>(misc + 16);   // [8] warp increment totals
+    float* abuf = misc + 24;                         // [32] addends of a walk round
+    float* result = misc + 56;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int len = sum_chunk_len(n);
     const int first = min(t * len, n), last = min(first + len, n);
@@ -300,14 +301,19 @@ static __device__ __forceinline__ float exact_sumsq(const float* xs, int n, unsi
         coff += wcnt[w];
         ioff += winc[w];
     }
-    const int total = wcnt[0] + wcnt[1] + wcnt[2] + wcnt[3];
+    int total = 0, inc_all = 0;
+#pragma unroll
+    for (int w = 0; w < kSumWarpsN; ++w) {
+        total += wcnt[w];
+        inc_all += winc[w];
+    }
     for (int k = drop ? 1 : 0; k < cnt; ++k) {
         SumRec r = mine[k];
         r.cum += ioff;
         list[coff + k - (drop ? 1 : 0)] = r;
     }
     if (t == 0)  // sentinel: where the last op ends, and the final total
-        list[total] = list[total + 1] = SumRec{n, winc[0] + winc[1] + winc[2] + winc[3]};
+        list[total] = list[total + 1] = SumRec{n, inc_all};
     sum_bar(bar);
 
     if (warp == 0) {

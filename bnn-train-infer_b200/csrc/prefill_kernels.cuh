@@ -33,7 +33,7 @@
 namespace bnn {
 namespace eng {
 
-constexpr uint32_t kRowsPrepThreads = kSumThreads;  // the decode prologue's four compute warps
+constexpr uint32_t kRowsPrepThreads = kSumThreads;  // the decode prologue's RMSNorm sum threads
 
 struct RowsPrepArgs {
     const float* x;      // [m][k] F32 rows, x_stride floats apart

@@ -33,7 +33,7 @@
 // producer starts streaming weights at once (they never depend on earlier
 // kernels), before the compute warps wait for the preceding kernel
 // (programmatic dependent launch) and build the activations (the RMSNorm sum
-// on warps 0..3, every elementwise pass on all 8). 8/B warps share
+// and every elementwise pass on all 8). 8/B warps share
 // one block, each taking a subset of its groups (the integer D's meet in
 // shared memory, so the FP32 order is unchanged); small matrices use B = 1 so
 // that every SM gets blocks. All waits are bounded.
@@ -51,7 +51,7 @@ constexpr int kStatusBadInput = 1;  // an input row had NaN/Inf (F32) or -128 (I
 constexpr int kStatusNonFinite = 4; // a normalisation divisor was not finite
 constexpr uint32_t kBlockPad = 4;
 constexpr uint32_t kComputeWarps = 8;
-constexpr uint32_t kSumWarps = kSumThreads / 32;  // the RMSNorm sum runs on compute warps 0..3
+constexpr uint32_t kSumWarps = kSumThreads / 32;  // the RMSNorm sum runs on compute warps 0..kSumWarps-1
 static_assert(kComputeWarps >= kSumWarps, "the RMSNorm sum needs four compute warps");
 // Prologues that build the activations in the CTA hold up to this many inputs
 // (in registers: kMaxPrologueK / 512 float4 per compute thread).
@@ -281,10 +281,10 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, 2) w1a8_gemv_kernel(
             if (PRO == kProRmsNorm) {
                 // The reference's RMSNorm sum fl(...fl(fl(x0*x0) + x1*x1)...) in
                 // index order (qwen3.c:361-372): exact mode reproduces it bit for
-                // bit with the four compute warps (exact_sum.cuh); fast mode sums
+                // bit with the compute warps (exact_sum.cuh); fast mode sums
                 // in a fixed tree order.
-                // Both run on warps 0..3 (named barrier 2); the fast tree's
-                // order is that of 128 threads.
+                // Both run on warps 0..kSumWarps-1 (named barrier 2); the fast tree.s
+                // order is that of kSumThreads threads.
                 if (warp < kSumWarps) {
                     float sum;
                     if (a.exact) {
