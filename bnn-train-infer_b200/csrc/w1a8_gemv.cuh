@@ -374,6 +374,25 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, 2) w1a8_gemv_kernel(
     const uint32_t r = lane & 7;
     const uint32_t my_block = warp / wpb, part = warp % wpb;
     int16_t* blk_d = dsm + (size_t)my_block * mrows * kRowBlock * G;
+    // With one warp per block the warps never share a tile's D or epilogue
+    // slots (SwiGLU pairs excepted: a 64-thread barrier per gate/up pair), so
+    // they run through the tiles without waiting for each other.
+    const bool solo = wpb == 1;
+    auto tile_sync = [&]() {
+        if (!solo)
+            named_barrier(1, cthreads);
+        else if (EPI == kEpiSwiGLU) {
+            // constant barrier ids 3..6 (one per pair of an 8-block tile)
+            switch (my_block >> 1) {
+                case 0: named_barrier(3, 64); break;
+                case 1: named_barrier(4, 64); break;
+                case 2: named_barrier(5, 64); break;
+                default: named_barrier(6, 64); break;
+            }
+        }
+        else
+            __syncwarp();
+    };
     uint32_t i = 0;
     for (uint32_t tile = blockIdx.x; tile < a.tiles; tile += gridDim.x, ++i) {
         const uint32_t s = i % a.stages;
@@ -411,7 +430,7 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, 2) w1a8_gemv_kernel(
             }
         }
         if (EPI != kEpiDotGroups) {
-            named_barrier(1, cthreads);  // every group's D of the tile is in shared memory
+            tile_sync();  // every group's D of the block is in shared memory
             // Ordered FP32 scale-accumulate, by the first warp of each block;
             // the scales come from the same stage.
             const uint16_t* sc_blk = reinterpret_cast<const uint16_t*>(wblk + (size_t)G * 128u);
@@ -453,7 +472,7 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, 2) w1a8_gemv_kernel(
             }
             if (EPI == kEpiSwiGLU) {
                 // Blocks 2k (gate rows) and 2k+1 (up rows) hold the same 8 rows.
-                named_barrier(1, cthreads);
+                tile_sync();
                 if (part == 0 && (my_block & 1) == 0 && work) {
                     for (uint32_t p = lane; p < mrows * kRowBlock; p += 32) {
                         const uint32_t mm = p / kRowBlock, rr = p % kRowBlock;
@@ -467,7 +486,7 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, 2) w1a8_gemv_kernel(
                     }
                 }
             }
-            named_barrier(1, cthreads);  // shared D/epilogue buffers and the stage are free again
+            tile_sync();  // shared D/epilogue buffers and the stage are free again
         }
         __syncwarp();
         if (lane == 0)
@@ -575,6 +594,21 @@ inline GemvLaunch plan_gemv(int sm_count, uint32_t n, uint32_t groups, uint32_t 
     }
     c.tiles = (nblocks + c.blocks_per_tile - 1) / c.blocks_per_tile;
     slots = occupancy(c.smem);
+    if (c.tiles > slots) {
+        // CTAs loop over several tiles (large matrices): the shallowest ring
+        // that gives the most CTAs per SM (more warps hide the dot latency;
+        // the bytes in flight per SM stay the same)
+        for (uint32_t st = 2; st < c.stages; ++st) {
+            const size_t sm2 = gemv_smem_plan(groups, mrows, c.blocks_per_tile, st, pro, epi).total;
+            const uint32_t sl = occupancy(sm2);
+            if (sl > slots) {
+                c.stages = st;
+                c.smem = sm2;
+                slots = sl;
+                break;
+            }
+        }
+    }
     c.grid_x = c.tiles < slots ? c.tiles : slots;
     return c;
 }
