@@ -403,6 +403,35 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
                               size_t in_stride, size_t out_stride) {
     const BNN_Matrix m = job->matrix;
     const uint32_t K = m->in_features, G = m->groups, M = job->rows;
+    cudaStream_t s = device->stream;
+    // F32 jobs of at most kRowsPerCta rows in 16-byte aligned rows: every
+    // contraction CTA loads, validates and quantises all of them in its
+    // prologue (kProQuant) before it writes anything, so a rejected row still
+    // leaves the output untouched and no separate prep pass is needed.
+    const unsigned char* in_ptr = job->input.buffer->data + job->input.offset;
+    if (in_type == BNN_TYPE_F32 && M <= (uint32_t)bnn::kRowsPerCta && K <= bnn::kMaxPrologueK &&
+        (reinterpret_cast<uintptr_t>(in_ptr) & 15u) == 0 && (M == 1 || in_stride % 16 == 0)) {
+        if (cudaMemsetAsync(device->d_status, 0, sizeof(int), s) != cudaSuccess)
+            return BNN_EIO;
+        const bnn::GemvLaunch cl = bnn::plan_gemv(device->sm_count, m->out_features, G, M, bnn::kProQuant,
+                                                  bnn::kEpiView);
+        bnn::GemvArgs ga = {};
+        ga.wblocks = m->wblocks;
+        ga.n = m->out_features;
+        ga.groups = G;
+        ga.m = M;
+        ga.tiles = cl.tiles;
+        ga.stages = cl.stages;
+        ga.blocks_per_tile = cl.blocks_per_tile;
+        ga.x = reinterpret_cast<const float*>(in_ptr);
+        ga.x_stride = M == 1 ? K : in_stride / 4u;
+        ga.out = job->output.buffer->data + job->output.offset;
+        ga.out_stride = out_stride;
+        ga.status = device->d_status;
+        if (bnn::launch_gemv(cl, M, ga, s, false) != cudaSuccess)
+            return BNN_EIO;
+        return BNN_OK;
+    }
     // From kMmaMinRows rows the group dots run on the tensor cores
     // (w1a8_mma.cuh); below, on the dp4a contraction (w1a8_gemv.cuh).
     const bool mma = M >= bnn::kMmaMinRows;
@@ -416,7 +445,6 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
     uint32_t* act = reinterpret_cast<uint32_t*>(base);
     int32_t* totals = reinterpret_cast<int32_t*>(base + act_bytes);
     float* rscale = reinterpret_cast<float*>(base + act_bytes + tot_bytes);
-    cudaStream_t s = device->stream;
 
     if (cudaMemsetAsync(device->d_status, 0, sizeof(int), s) != cudaSuccess)
         return BNN_EIO;
