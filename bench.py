@@ -411,15 +411,26 @@ def run_classify(args):
     import numpy as np
     import torch
     from bnn_b200 import accel, engine, gguf
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    torch.cuda.set_device(local)
+    if world > 1:
+        # data-parallel: every rank classifies its own copy of the sample set
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
     cache = Path(args.model_cache)
     cache.mkdir(parents=True, exist_ok=True)
     path = cache / "bnn_mlp_seed20261201.gguf"
-    if not path.exists():
+    if rank == 0 and not path.exists():
         tmp = path.with_suffix(f".tmp{os.getpid()}")
         gguf.bnn_mlp_model(tmp)
         os.replace(tmp, path)
-    torch.cuda.set_device(0)
-    dev = accel.Device(0)
+    if dist:
+        dist.barrier()
+    dev = accel.Device(local)
     api = engine.EngineApi(dev.api.dll)
     model = engine.Model(dev, path, api)
     info = model.info
@@ -437,7 +448,9 @@ def run_classify(args):
 
     for _ in range(args.warmup):
         one_pass()
-    with ClockSampler(0) as clocks:
+    with ClockSampler(local) as clocks:
+        if dist:
+            dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -447,31 +460,42 @@ def run_classify(args):
         e1.record(stream)
         e1.synchronize()
         wall = time.perf_counter() - t0
+        torch.cuda.synchronize()
     clk = clocks.summary()
     ms = e0.elapsed_time(e1)
-    value = n_samples * args.steps / (ms / 1e3)
+    if dist:
+        t = torch.tensor([ms, wall], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, wall = float(t[0].item()), float(t[1].item())
+    value = n_samples * args.steps * world / (ms / 1e3)
     macs = 896 * 512 + 512 * 512 + 512 * 10  # per sample
-    tops = 2.0 * macs * n_samples * args.steps / (ms / 1e3) / 1e12
+    tops = 2.0 * macs * n_samples * args.steps * world / (ms / 1e3) / 1e12
     d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else None
     peak = 2.0 * float(d["bf16_tflops"]) if d else 2.0 * 1590.0
     pred = out.argmax(axis=1)
     ctx.free()
     model.free()
     dev.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
     return {
-        "metric": "bnn_mlp_classify_samples_per_s", "value": round(value, 1), "unit": "samples/s", "n_gpus": 1,
+        "metric": "bnn_mlp_classify_samples_per_s", "value": round(value, 1), "unit": "samples/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic (seeded bnn-mlp weights; 1000 N(0,1) samples of 784 values, zero-padded to 896)",
         "config": {"workload": "configs[0]: bnn-mlp W1A8 classifier 896->512->512->10, 1000 samples, "
                                "BNND_Classify batch 64 (16 calls per step)",
                    "l2": "weights (0.1 MB) stay in L2; the workload is latency-bound (one step = 16 calls)",
+                   "parallelism": f"data-parallel x{world} (every rank its own sample set)" if world > 1 else "single GPU",
                    "predicted_class_histogram": np.bincount(pred, minlength=info.n_classes).tolist()},
         "roofline": {"bound": "tensor", "achieved": round(tops, 3), "peak": round(peak, 1), "unit": "TOPS",
                      "frac": round(tops / peak, 6),
                      "peak_source": "2 x measured dense bf16" if d else "2 x fallback bf16", "traffic": None,
                      "what": "2 x 726,016 int8 multiply-adds per sample / step time (host copies included)"},
-        "e2e": {"value": round(n_samples * args.steps / wall, 1), "unit": "samples/s",
+        "e2e": {"value": round(n_samples * args.steps * world / wall, 1), "unit": "samples/s",
                 "h2d_bytes_per_step": n_samples * info.input_size * 4, "d2h_bytes_per_step": n_samples * info.n_classes * 4,
                 "call": "BNND_Classify per batch of 64, host samples in, host logits out"},
         "clocks": clk,
