@@ -20,6 +20,11 @@ cpu_baseline  the reference engine itself (bnn-sw-v2 + soft backend, compiled
           from its sources into oracle/_ref) decoding one token of the same
           model on one host core.
 
+--config5 measures BASELINE configs[4]: 8 independent contexts (one context
+row each) with 64-token seeded prompts, greedy decode at ctx 4096; every
+linear is a GEMV of 8 rows; with --tp under torchrun the model is
+column-sharded over the ranks. value is the aggregate tokens/s.
+
 --prefill measures BASELINE configs[3] instead: a step is one batched
 prefill of 512 seeded prompt tokens (every linear a GEMM of 512 rows on the
 tensor cores, tcgen05 kind::i8) plus the greedy pick of the next token,
@@ -223,13 +228,17 @@ def run_b200(args):
     model = engine.Model(dev, path, api, world=world if tp else 1, rank=rank if tp else 0)
     log(f"[rank {rank}] model loaded in {time.time() - t0:.1f}s")
     info = model.info
-    prompt = prompt_ids(info.n_vocab)
+    batch, n_ctx, n_prompt = (8, 4096, 64) if args.config5 else (1, CTX, PROMPT_TOKENS)
+    if args.config5:
+        prompt = np.random.default_rng(20261205).integers(0, info.n_vocab, size=(batch, n_prompt)).astype(np.int32)
+    else:
+        prompt = prompt_ids(info.n_vocab)
     comm_id = None
     if tp:
         box = [engine.comm_id_create(api) if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         comm_id = box[0]
-    ctx = engine.Context(model, n_ctx=CTX, n_batch=1, exact=not args.fast, comm_id=comm_id)
+    ctx = engine.Context(model, n_ctx=n_ctx, n_batch=batch, exact=not args.fast, comm_id=comm_id)
     stream = torch.cuda.ExternalStream(ctx.stream())
     launches_per_step = ctx.step_launches()
 
@@ -263,14 +272,14 @@ def run_b200(args):
     # ---- device-resident value
     ctx.decode_argmax(prompt)                    # prefill (untimed)
     ctx.generate(args.warmup)                    # warm-up steps
-    need = PROMPT_TOKENS + args.warmup + args.steps + 2
-    if need > CTX:
-        raise SystemExit(f"prompt + warmup + steps must fit ctx {CTX}")
+    need = n_prompt + args.warmup + args.steps + 2
+    if need > n_ctx:
+        raise SystemExit(f"prompt + warmup + steps must fit ctx {n_ctx}")
     gen = api.Generate
     with ClockSampler(local) as clocks:
         ms = timed(lambda: api.check(gen(ctx.handle, args.steps + 1, None)))
     clk = clocks.summary()
-    streams = 1 if tp else world  # sequences decoded by the whole job
+    streams = batch * (1 if tp else world)  # sequences decoded by the whole job
     value = args.steps * streams / (ms / 1e3)   # first of the steps+1 ids was the warm-up's pick
 
     # ---- end to end through the public per-token call (host ids in/out)
@@ -278,7 +287,7 @@ def run_b200(args):
     nxt = ctx.decode_argmax(prompt)
     for _ in range(args.warmup):
         nxt = ctx.decode_argmax(nxt)
-    host_tok = np.empty(1, dtype=np.int32)
+    host_tok = np.empty(batch, dtype=np.int32)
 
     def e2e_loop():
         tok = nxt.copy()
@@ -295,7 +304,7 @@ def run_b200(args):
     stats, total_ms = ctx.profile(args.profile_steps)
     by_kernel = {}
     for name, (launches, kms, kbytes) in stats.items():
-        key = "w1a8_contract_kernel" if name.startswith("w1a8_gemv:") else name
+        key = "w1a8_contract_kernel" if name.startswith(("w1a8_gemv:", "w1a8_mma:")) else name
         l0, m0, b0 = by_kernel.get(key, (0, 0.0, 0.0))
         by_kernel[key] = (l0 + launches, m0 + kms, b0 + kbytes)
     dominant = max(by_kernel, key=lambda k: by_kernel[k][1])
@@ -326,12 +335,18 @@ def run_b200(args):
                                  f"reference engine + soft backend built from its sources, 1 thread: "
                                  f"{sample[1]:.2f} s"}
         weight_bytes = info.weight_count * 0.140625
+        workload = WORKLOAD
+        if args.config5:
+            workload = ("configs[4]: Qwen3-1.7B-shape W1A8, 8 independent contexts with 64-token seeded prompts, "
+                        "greedy decode at ctx 4096" + (f", column-sharded over {world} GPUs" if tp else ""))
         out = {
-            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+            "metric": METRIC + ("_8ctx" if args.config5 else ""), "value": round(value, 2), "unit": "tokens/s",
+            "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
             "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (seeded random-init weights and prompt; no checkpoint offline)",
-            "config": {"workload": WORKLOAD, "prompt_tokens": PROMPT_TOKENS, "ctx": CTX, "batch_per_gpu": 1,
+            "config": {"workload": workload, "prompt_tokens": n_prompt, "ctx": n_ctx,
+                       "batch_per_gpu": batch if not tp else batch,
                        "layers": info.n_layers, "hidden": info.hidden, "ffn": info.ffn, "vocab": info.n_vocab,
                        "numerics": "fast" if args.fast else "exact (reference operation order)",
                        "weight_bytes_per_token": int(weight_bytes),
@@ -340,8 +355,8 @@ def run_b200(args):
                                        if tp else f"replicas x{world}" if world > 1 else "single GPU")},
             "roofline": roofline,
             "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
-                    "d2h_bytes_per_step": 4, "call": "BNND_DecodeArgmax per token, host ids in and out"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * batch,
+                    "d2h_bytes_per_step": 4 * batch, "call": "BNND_DecodeArgmax per token, host ids in and out"},
             "clocks": clk,
             "gpu_launches": int(launches_per_step * (args.steps + 1)),
         }
@@ -700,6 +715,8 @@ def main():
                     help="BASELINE configs[0]: bnn-mlp classify, batch 64 (samples/s)")
     ap.add_argument("--sweep", action="store_true",
                     help="BASELINE configs[1]: single-op GEMV_F32 / DOT_GROUPS sweep (HBM GB/s)")
+    ap.add_argument("--config5", action="store_true",
+                    help="BASELINE configs[4]: 8 contexts, 64-token prompts, ctx 4096 (with --tp: sharded)")
     ap.add_argument("--prefill", action="store_true",
                     help="BASELINE configs[3]: batched 512-token prefill instead of decode")
     ap.add_argument("--tp", action="store_true",

@@ -42,6 +42,7 @@
 
 namespace {
 
+constexpr uint32_t kStepMmaRows = 4;  // decode steps with this many context rows use the tensor cores
 constexpr size_t kAttnSmemBudget = 227u * 1024u;  // dynamic shared memory of one attention block (the sm_100 maximum)
 
 thread_local std::string g_last_error;
@@ -336,6 +337,7 @@ struct bnnd_context {
     bool have_logits = false;
     // batched prefill: activation rows = prompt positions of every row
     DevMem pf_x, pf_qkv, pf_y, pf_h, pf_a, pf_rs, pf_scores, pf_meta;
+    DevMem dm_a, dm_rs;            // decode steps of kStepMmaRows+ rows: tensor-core operand, row scales
     uint32_t pf_rows = 0;          // activation rows the pf_* buffers hold
     size_t pf_meta_cap = 0;        // entries of pf_meta (ids, positions, cache rows)
     uint32_t* h_meta = nullptr;    // pinned staging of pf_meta
@@ -702,6 +704,49 @@ cudaError_t all_gather_rows(bnnd_context* c, float* st, uint32_t slice, float* d
     return cudaGetLastError();
 }
 
+// RMSNorm (gain non-null) or plain quantisation of `rows` rows of width k
+// into the pre-tiled tensor-core operand.
+cudaError_t prefill_prep(bnnd_context* c, unsigned char* a_sw, float* rs, const float* x, uint32_t k, const float* gain,
+                         uint32_t rows) {
+    bnn::eng::RowsPrepArgs a = {};
+    a.x = x;
+    a.x_stride = k;
+    a.gain = gain;
+    a.eps = c->model->eps;
+    a.exact = c->params.exact;
+    a.k = k;
+    a.m = rows;
+    a.a_sw = a_sw;
+    a.row_scale = rs;
+    a.status = c->status.as<int>();
+    const size_t smem = bnn::eng::rows_prep_smem(k, c->params.exact != 0);
+    cudaError_t e = cudaFuncSetAttribute(bnn::eng::rows_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess)
+        return e;
+    bnn::eng::rows_prep_kernel<<<rows, bnn::eng::kRowsPrepThreads, smem, c->stream>>>(a);
+    return cudaGetLastError();
+}
+
+// The linear l over the prepared rows on the tensor cores; epi kEpiView,
+// kEpiResidual (out += Y) or kEpiSwiGLU.
+cudaError_t prefill_linear(bnnd_context* c, const unsigned char* a_sw, const float* rs, const Linear& l, uint32_t rows,
+                           float* out, size_t out_stride, int epi) {
+    bnn::MmaArgs a = {};
+    a.wblocks = l.m->wblocks;
+    a.n = l.out;
+    a.groups = l.in / 128;
+    a.m = rows;
+    a.a_sw = a_sw;
+    a.row_scale = rs;
+    a.out = reinterpret_cast<unsigned char*>(out);
+    a.out_stride = out_stride;
+    a.epi = epi;
+    a.status = c->status.as<int>();
+    g_next_bytes = (double)l.out * l.in * 0.140625 + (double)rows * (l.in + 4.0 * l.out);
+    return bnn::launch_mma(a, c->stream);
+}
+
 // Enqueues one decode step for every row (tokens already in tok_in).
 cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
     LaunchCheck local;
@@ -720,11 +765,24 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
                                              best);
     ck("embed_kernel");
     const uint32_t qkv_width = sh.q_rows + 2 * sh.kv_rows;
+    // Steps of several context rows (one GPU) run their linears on the tensor
+    // cores: one row-prep CTA per row (the RMSNorm sums in parallel) and the
+    // tcgen05 GEMM, instead of a contraction whose CTAs prepare the rows one
+    // after another. Same arithmetic either way.
+    unsigned char* dm_a = c->dm_a.p ? c->dm_a.as<unsigned char>() : nullptr;
+    float* dm_rs = c->dm_rs.p ? c->dm_rs.as<float>() : nullptr;
+    const bool rows_mma = dm_a != nullptr;
     for (uint32_t l = 0; l < in.n_layers; ++l) {
         const QwenLayer& L = *m->layers[l];
         // attn_norm + q|k|v projections of this rank's heads (prologue: RMSNorm + quantise)
-        ck("w1a8_gemv:qkv", launch_linear(c, c->plan_qkv, L.qkv, x, L.attn_norm.as<float>(), R, c->qkv.as<float>(),
-                                          (size_t)qkv_width * 4u, status));
+        if (rows_mma) {
+            ck("rows_prep:qkv", prefill_prep(c, dm_a, dm_rs, x, C, L.attn_norm.as<float>(), R));
+            ck("w1a8_mma:qkv", prefill_linear(c, dm_a, dm_rs, L.qkv, R, c->qkv.as<float>(), (size_t)qkv_width * 4u,
+                                              bnn::kEpiView));
+        } else {
+            ck("w1a8_gemv:qkv", launch_linear(c, c->plan_qkv, L.qkv, x, L.attn_norm.as<float>(), R,
+                                              c->qkv.as<float>(), (size_t)qkv_width * 4u, status));
+        }
         // q/k norm + rope + KV append + attention, one block per (KV head, row)
         bnn::eng::AttnArgs aa = {};
         aa.qkv = c->qkv.as<float>();
@@ -760,6 +818,9 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
                                             (size_t)sh.c_rows * 4u, status, nullptr, 0, x + sh.c_begin,
                                             (size_t)C * 4u));
             ck("all_gather:x", all_gather_rows(c, c->x_st.as<float>(), sh.c_rows, x, C));
+        } else if (rows_mma) {
+            ck("rows_prep:o", prefill_prep(c, dm_a, dm_rs, c->y.as<float>(), C, nullptr, R));
+            ck("w1a8_mma:o", prefill_linear(c, dm_a, dm_rs, L.o, R, x, (size_t)C * 4u, bnn::kEpiResidual));
         } else {
             ck("w1a8_gemv:o", launch_linear(c, c->plan_o, L.o, c->y.as<float>(), nullptr, R, x, (size_t)C * 4u,
                                             status));
@@ -770,6 +831,10 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
                                                   c->h_st.as<float>() + (size_t)c->rank * R * sh.f_rows,
                                                   (size_t)sh.f_rows * 4u, status));
             ck("all_gather:h", all_gather_rows(c, c->h_st.as<float>(), sh.f_rows, c->h.as<float>(), F));
+        } else if (rows_mma) {
+            ck("rows_prep:gate_up", prefill_prep(c, dm_a, dm_rs, x, C, L.ffn_norm.as<float>(), R));
+            ck("w1a8_mma:gate_up", prefill_linear(c, dm_a, dm_rs, L.gu, R, c->h.as<float>(), (size_t)F * 4u,
+                                                  bnn::kEpiSwiGLU));
         } else {
             ck("w1a8_gemv:gate_up", launch_linear(c, c->plan_gu, L.gu, x, L.ffn_norm.as<float>(), R,
                                                   c->h.as<float>(), (size_t)F * 4u, status));
@@ -781,6 +846,9 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
                                                (size_t)sh.c_rows * 4u, status, nullptr, 0, x + sh.c_begin,
                                                (size_t)C * 4u));
             ck("all_gather:x", all_gather_rows(c, c->x_st.as<float>(), sh.c_rows, x, C));
+        } else if (rows_mma) {
+            ck("rows_prep:down", prefill_prep(c, dm_a, dm_rs, c->h.as<float>(), F, nullptr, R));
+            ck("w1a8_mma:down", prefill_linear(c, dm_a, dm_rs, L.down, R, x, (size_t)C * 4u, bnn::kEpiResidual));
         } else {
             ck("w1a8_gemv:down", launch_linear(c, c->plan_down, L.down, c->h.as<float>(), nullptr, R, x,
                                                (size_t)C * 4u, status));
@@ -798,6 +866,13 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
             ck("all_gather:pick", ncclAllGather(best, c->best.p, R, ncclUint64, c->comm, s) == ncclSuccess
                                       ? cudaSuccess
                                       : cudaErrorUnknown);
+        } else if (rows_mma) {
+            ck("rows_prep:lm_head", prefill_prep(c, dm_a, dm_rs, x, C, m->out_norm.as<float>(), R));
+            ck("w1a8_mma:lm_head", prefill_linear(c, dm_a, dm_rs, m->lm_head, R, c->logits.as<float>(),
+                                                  (size_t)in.n_vocab * 4u, bnn::kEpiView));
+            bnn::eng::logits_argmax_kernel<<<R, bnn::eng::kArgmaxThreads, 0, s>>>(c->logits.as<float>(), in.n_vocab,
+                                                                                best, status);
+            ck("logits_argmax_kernel");
         } else {
             ck("w1a8_gemv:lm_head", launch_linear(c, c->plan_head, m->lm_head, x, m->out_norm.as<float>(), R,
                                                   c->logits.as<float>(), (size_t)in.n_vocab * 4u, status, best));
@@ -892,6 +967,10 @@ BNND_Status create_llm_context(bnnd_context* c) {
     CUDA_OR(cudaMemset(c->hist_count.p, 0, 4), BNND_EIO);
     CUDA_OR(cudaMemset(c->status.p, 0, 4), BNND_EIO);
     const int sms = m->dev->sm_count;
+    if (R >= kStepMmaRows && P == 1 &&
+        ((st = dev_alloc(c->dm_a, bnn::mma_a_bytes(R, std::max(C, F) / 128))) ||
+         (st = dev_alloc(c->dm_rs, (size_t)R * 4))))
+        return st;
     c->plan_qkv = bnn::plan_gemv(sms, sh.q_rows + 2 * sh.kv_rows, C / 128, R, bnn::kProRmsNorm, bnn::kEpiView);
     c->plan_o = bnn::plan_gemv(sms, sh.c_rows, C / 128, R, bnn::kProQuant, bnn::kEpiResidual);
     c->plan_gu = bnn::plan_gemv(sms, 2 * sh.f_rows, C / 128, R, bnn::kProRmsNorm, bnn::kEpiSwiGLU);
@@ -997,47 +1076,6 @@ BNND_Status ensure_prefill(bnnd_context* c, uint32_t rows) {
     return BNND_OK;
 }
 
-// RMSNorm (gain non-null) or plain quantisation of `rows` rows of width k
-// into the pre-tiled tensor-core operand.
-cudaError_t prefill_prep(bnnd_context* c, const float* x, uint32_t k, const float* gain, uint32_t rows) {
-    bnn::eng::RowsPrepArgs a = {};
-    a.x = x;
-    a.x_stride = k;
-    a.gain = gain;
-    a.eps = c->model->eps;
-    a.exact = c->params.exact;
-    a.k = k;
-    a.m = rows;
-    a.a_sw = c->pf_a.as<unsigned char>();
-    a.row_scale = c->pf_rs.as<float>();
-    a.status = c->status.as<int>();
-    const size_t smem = bnn::eng::rows_prep_smem(k, c->params.exact != 0);
-    cudaError_t e = cudaFuncSetAttribute(bnn::eng::rows_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess)
-        return e;
-    bnn::eng::rows_prep_kernel<<<rows, bnn::eng::kRowsPrepThreads, smem, c->stream>>>(a);
-    return cudaGetLastError();
-}
-
-// The linear l over the prepared rows on the tensor cores; epi kEpiView,
-// kEpiResidual (out += Y) or kEpiSwiGLU.
-cudaError_t prefill_linear(bnnd_context* c, const Linear& l, uint32_t rows, float* out, size_t out_stride, int epi) {
-    bnn::MmaArgs a = {};
-    a.wblocks = l.m->wblocks;
-    a.n = l.out;
-    a.groups = l.in / 128;
-    a.m = rows;
-    a.a_sw = c->pf_a.as<unsigned char>();
-    a.row_scale = c->pf_rs.as<float>();
-    a.out = reinterpret_cast<unsigned char*>(out);
-    a.out_stride = out_stride;
-    a.epi = epi;
-    a.status = c->status.as<int>();
-    g_next_bytes = (double)l.out * l.in * 0.140625 + (double)rows * (l.in + 4.0 * l.out);
-    return bnn::launch_mma(a, c->stream);
-}
-
 using PfAttnFn = void (*)(bnn::eng::PfAttnArgs);
 PfAttnFn prefill_attention_fn(uint32_t hd, uint32_t kv_mul) {
     using namespace bnn::eng;
@@ -1075,6 +1113,8 @@ cudaError_t enqueue_prefill_chunk(bnnd_context* c, uint32_t rows, uint32_t len, 
     const uint32_t* pos = meta + rows;
     const uint32_t* slot = meta + 2 * (size_t)rows;
     float* x = c->pf_x.as<float>();
+    unsigned char* pa_sw = c->pf_a.as<unsigned char>();
+    float* pa_rs = c->pf_rs.as<float>();
     float* qkv = c->pf_qkv.as<float>();
     float* y = c->pf_y.as<float>();
     float* h = c->pf_h.as<float>();
@@ -1104,8 +1144,8 @@ cudaError_t enqueue_prefill_chunk(bnnd_context* c, uint32_t rows, uint32_t len, 
         const size_t layer_cache = (size_t)c->rows * c->n_ctx * KV;
         float* kc = c->kcache.as<float>() + (size_t)l * layer_cache;
         float* vc = c->vcache.as<float>() + (size_t)l * layer_cache;
-        ck("rows_prep:qkv", prefill_prep(c, x, C, L.attn_norm.as<float>(), rows));
-        ck("w1a8_mma:qkv", prefill_linear(c, L.qkv, rows, qkv, (size_t)QKV * 4u, bnn::kEpiView));
+        ck("rows_prep:qkv", prefill_prep(c, pa_sw, pa_rs, x, C, L.attn_norm.as<float>(), rows));
+        ck("w1a8_mma:qkv", prefill_linear(c, pa_sw, pa_rs, L.qkv, rows, qkv, (size_t)QKV * 4u, bnn::kEpiView));
         bnn::eng::KvAppendArgs ka = {};
         ka.qkv = qkv;
         ka.k_norm = L.k_norm.as<float>();
@@ -1149,12 +1189,12 @@ cudaError_t enqueue_prefill_chunk(bnnd_context* c, uint32_t rows, uint32_t len, 
         pa.status = status;
         pf_attn<<<pf_grid, bnn::eng::kPfThreads, pf_plan.total, s>>>(pa);
         ck("prefill_attention_kernel");
-        ck("rows_prep:o", prefill_prep(c, y, C, nullptr, rows));
-        ck("w1a8_mma:o", prefill_linear(c, L.o, rows, x, (size_t)C * 4u, bnn::kEpiResidual));
-        ck("rows_prep:gate_up", prefill_prep(c, x, C, L.ffn_norm.as<float>(), rows));
-        ck("w1a8_mma:gate_up", prefill_linear(c, L.gu, rows, h, (size_t)F * 4u, bnn::kEpiSwiGLU));
-        ck("rows_prep:down", prefill_prep(c, h, F, nullptr, rows));
-        ck("w1a8_mma:down", prefill_linear(c, L.down, rows, x, (size_t)C * 4u, bnn::kEpiResidual));
+        ck("rows_prep:o", prefill_prep(c, pa_sw, pa_rs, y, C, nullptr, rows));
+        ck("w1a8_mma:o", prefill_linear(c, pa_sw, pa_rs, L.o, rows, x, (size_t)C * 4u, bnn::kEpiResidual));
+        ck("rows_prep:gate_up", prefill_prep(c, pa_sw, pa_rs, x, C, L.ffn_norm.as<float>(), rows));
+        ck("w1a8_mma:gate_up", prefill_linear(c, pa_sw, pa_rs, L.gu, rows, h, (size_t)F * 4u, bnn::kEpiSwiGLU));
+        ck("rows_prep:down", prefill_prep(c, pa_sw, pa_rs, h, F, nullptr, rows));
+        ck("w1a8_mma:down", prefill_linear(c, pa_sw, pa_rs, L.down, rows, x, (size_t)C * 4u, bnn::kEpiResidual));
     }
     return ck.err;
 }

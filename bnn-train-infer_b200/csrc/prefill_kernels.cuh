@@ -464,5 +464,39 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttn
     }
 }
 
+// ---- greedy pick of full logits rows (steps whose lm_head ran on the tensor cores)
+constexpr uint32_t kArgmaxThreads = 1024;
+
+// best[row] = the largest argmax_key (largest value, lowest index on ties;
+// bnn-infer-v2.c:48-54) over logits [rows][n]; a non-finite logit sets the
+// status (engine.c:262-267). One CTA per row.
+__global__ void __launch_bounds__(kArgmaxThreads) logits_argmax_kernel(const float* logits, uint32_t n,
+                                                                      unsigned long long* best, int* status) {
+    __shared__ unsigned long long red[kArgmaxThreads / 32];
+    const uint32_t row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float* lr = logits + (size_t)row * n;
+    unsigned long long b = 0ull;
+    int bad = 0;
+    for (uint32_t i = tid; i < n; i += kArgmaxThreads) {
+        const float v = lr[i];
+        bad |= !isfinite(v);
+        const unsigned long long k = argmax_key(v, i);
+        b = k > b ? k : b;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long ob = __shfl_xor_sync(0xffffffffu, b, o);
+        b = ob > b ? ob : b;
+    }
+    if (lane == 0)
+        red[warp] = b;
+    if (__syncthreads_or(bad) && tid == 0)
+        atomicOr(status, kStatusNonFinite);
+    if (tid == 0) {
+        for (uint32_t w = 1; w < kArgmaxThreads / 32; ++w)
+            b = red[w] > b ? red[w] : b;
+        best[row] = b;
+    }
+}
+
 }  // namespace eng
 }  // namespace bnn

@@ -152,3 +152,21 @@ def test_prefill_long_context_four_heads_per_kv(b200_device, models, exact):
     want = run(b200_device, path, [prompt], n_ctx=1500, exact=exact, chunk=0, gen=4)
     same(run(b200_device, path, [prompt], n_ctx=1500, exact=exact, chunk=2048, gen=4), want)
     same(run(b200_device, path, [prompt], n_ctx=1500, exact=exact, chunk=300, gen=4), want)
+
+
+@pytest.mark.parametrize("exact", [True, False])
+def test_multi_row_steps_match_single_rows(b200_device, models, exact):
+    """Five context rows: the step's linears run on the tensor cores (one
+    row-prep CTA per row) and the greedy pick comes from full logits; every
+    row must equal a one-row context fed the same tokens."""
+    path, shape = models["small"]
+    rng = np.random.default_rng(46)
+    rows = 5
+    calls = [rng.integers(0, shape.vocab, size=(rows, 20)).astype(np.int32),
+             rng.integers(0, shape.vocab, size=(rows, 3)).astype(np.int32)]
+    got = run(b200_device, path, calls, rows=rows, n_ctx=96, exact=exact, gen=6)
+    for r in range(rows):
+        want = run(b200_device, path, [c[r:r + 1] for c in calls], n_ctx=96, exact=exact, gen=6)
+        for i, (x, y) in enumerate(zip(got[0], want[0])):
+            assert np.array_equal(bits(x[r]), bits(y[0])), f"row {r} call {i}"
+        assert np.array_equal(got[1][r], want[1][0]), f"row {r} stream"
