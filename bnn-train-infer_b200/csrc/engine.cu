@@ -42,7 +42,7 @@
 
 namespace {
 
-constexpr uint32_t kStepMmaRows = 4;  // decode steps with this many context rows use the tensor cores
+constexpr uint32_t kStepRowsPrep = 4;  // decode steps of this many context rows prepare each row in its own CTA
 constexpr size_t kAttnSmemBudget = 227u * 1024u;  // dynamic shared memory of one attention block (the sm_100 maximum)
 
 thread_local std::string g_last_error;
@@ -337,7 +337,8 @@ struct bnnd_context {
     bool have_logits = false;
     // batched prefill: activation rows = prompt positions of every row
     DevMem pf_x, pf_qkv, pf_y, pf_h, pf_a, pf_rs, pf_scores, pf_meta;
-    DevMem dm_a, dm_rs;            // decode steps of kStepMmaRows+ rows: tensor-core operand, row scales
+    DevMem dm_act, dm_tot, dm_rs;  // steps of kStepRowsPrep+ rows: sliced rows, group totals, row scales
+    bnn::GemvLaunch plan_qkv_s{}, plan_o_s{}, plan_gu_s{}, plan_down_s{}, plan_head_s{};  // their contractions
     uint32_t pf_rows = 0;          // activation rows the pf_* buffers hold
     size_t pf_meta_cap = 0;        // entries of pf_meta (ids, positions, cache rows)
     uint32_t* h_meta = nullptr;    // pinned staging of pf_meta
@@ -747,6 +748,52 @@ cudaError_t prefill_linear(bnnd_context* c, const unsigned char* a_sw, const flo
     return bnn::launch_mma(a, c->stream);
 }
 
+// Multi-row steps: RMSNorm (gain non-null) + QuantizeRow of every row in its
+// own CTA, written in the contraction's sliced layout.
+cudaError_t step_prep(bnnd_context* c, const float* x, uint32_t k, const float* gain, uint32_t rows) {
+    bnn::eng::RowsPrepArgs a = {};
+    a.x = x;
+    a.x_stride = k;
+    a.gain = gain;
+    a.eps = c->model->eps;
+    a.exact = c->params.exact;
+    a.k = k;
+    a.m = rows;
+    a.act = c->dm_act.as<uint32_t>();
+    a.totals = c->dm_tot.as<int32_t>();
+    a.row_scale = c->dm_rs.as<float>();
+    a.status = c->status.as<int>();
+    const size_t smem = bnn::eng::rows_prep_smem(k, c->params.exact != 0);
+    cudaError_t e = cudaFuncSetAttribute(bnn::eng::rows_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess)
+        return e;
+    bnn::eng::rows_prep_kernel<<<rows, bnn::eng::kRowsPrepThreads, smem, c->stream>>>(a);
+    return cudaGetLastError();
+}
+
+// The contraction over the rows step_prep prepared (kProSliced prologue).
+cudaError_t step_linear(const bnnd_context* c, const bnn::GemvLaunch& cl, const Linear& l, uint32_t rows, float* out,
+                        size_t out_stride, unsigned long long* best = nullptr) {
+    bnn::GemvArgs a = {};
+    a.wblocks = l.m->wblocks;
+    a.n = l.out;
+    a.groups = l.in / 128;
+    a.m = rows;
+    a.tiles = cl.tiles;
+    a.stages = cl.stages;
+    a.blocks_per_tile = cl.blocks_per_tile;
+    a.act = c->dm_act.as<uint32_t>();
+    a.totals = c->dm_tot.as<int32_t>();
+    a.row_scale = c->dm_rs.as<float>();
+    a.out = reinterpret_cast<unsigned char*>(out);
+    a.out_stride = out_stride;
+    a.status = c->status.as<int>();
+    a.best = best;
+    g_next_bytes = ((double)l.out * l.in * 0.140625 + 4.0 * l.in + 4.0 * l.out) * rows;
+    return bnn::launch_gemv(cl, rows, a, c->stream, c->pdl);
+}
+
 // Enqueues one decode step for every row (tokens already in tok_in).
 cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
     LaunchCheck local;
@@ -765,20 +812,17 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
                                              best);
     ck("embed_kernel");
     const uint32_t qkv_width = sh.q_rows + 2 * sh.kv_rows;
-    // Steps of several context rows (one GPU) run their linears on the tensor
-    // cores: one row-prep CTA per row (the RMSNorm sums in parallel) and the
-    // tcgen05 GEMM, instead of a contraction whose CTAs prepare the rows one
-    // after another. Same arithmetic either way.
-    unsigned char* dm_a = c->dm_a.p ? c->dm_a.as<unsigned char>() : nullptr;
-    float* dm_rs = c->dm_rs.p ? c->dm_rs.as<float>() : nullptr;
-    const bool rows_mma = dm_a != nullptr;
+    // Steps of several context rows (one GPU) prepare every row in its own
+    // CTA (the RMSNorm sums in parallel) and hand the contraction sliced rows,
+    // instead of a contraction whose every CTA prepares the rows one after
+    // another. Same arithmetic either way.
+    const bool rows_prepped = c->dm_act.p != nullptr;
     for (uint32_t l = 0; l < in.n_layers; ++l) {
         const QwenLayer& L = *m->layers[l];
         // attn_norm + q|k|v projections of this rank's heads (prologue: RMSNorm + quantise)
-        if (rows_mma) {
-            ck("rows_prep:qkv", prefill_prep(c, dm_a, dm_rs, x, C, L.attn_norm.as<float>(), R));
-            ck("w1a8_mma:qkv", prefill_linear(c, dm_a, dm_rs, L.qkv, R, c->qkv.as<float>(), (size_t)qkv_width * 4u,
-                                              bnn::kEpiView));
+        if (rows_prepped) {
+            ck("rows_prep:qkv", step_prep(c, x, C, L.attn_norm.as<float>(), R));
+            ck("w1a8_gemv:qkv", step_linear(c, c->plan_qkv_s, L.qkv, R, c->qkv.as<float>(), (size_t)qkv_width * 4u));
         } else {
             ck("w1a8_gemv:qkv", launch_linear(c, c->plan_qkv, L.qkv, x, L.attn_norm.as<float>(), R,
                                               c->qkv.as<float>(), (size_t)qkv_width * 4u, status));
@@ -818,9 +862,9 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
                                             (size_t)sh.c_rows * 4u, status, nullptr, 0, x + sh.c_begin,
                                             (size_t)C * 4u));
             ck("all_gather:x", all_gather_rows(c, c->x_st.as<float>(), sh.c_rows, x, C));
-        } else if (rows_mma) {
-            ck("rows_prep:o", prefill_prep(c, dm_a, dm_rs, c->y.as<float>(), C, nullptr, R));
-            ck("w1a8_mma:o", prefill_linear(c, dm_a, dm_rs, L.o, R, x, (size_t)C * 4u, bnn::kEpiResidual));
+        } else if (rows_prepped) {
+            ck("rows_prep:o", step_prep(c, c->y.as<float>(), C, nullptr, R));
+            ck("w1a8_gemv:o", step_linear(c, c->plan_o_s, L.o, R, x, (size_t)C * 4u));
         } else {
             ck("w1a8_gemv:o", launch_linear(c, c->plan_o, L.o, c->y.as<float>(), nullptr, R, x, (size_t)C * 4u,
                                             status));
@@ -831,10 +875,9 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
                                                   c->h_st.as<float>() + (size_t)c->rank * R * sh.f_rows,
                                                   (size_t)sh.f_rows * 4u, status));
             ck("all_gather:h", all_gather_rows(c, c->h_st.as<float>(), sh.f_rows, c->h.as<float>(), F));
-        } else if (rows_mma) {
-            ck("rows_prep:gate_up", prefill_prep(c, dm_a, dm_rs, x, C, L.ffn_norm.as<float>(), R));
-            ck("w1a8_mma:gate_up", prefill_linear(c, dm_a, dm_rs, L.gu, R, c->h.as<float>(), (size_t)F * 4u,
-                                                  bnn::kEpiSwiGLU));
+        } else if (rows_prepped) {
+            ck("rows_prep:gate_up", step_prep(c, x, C, L.ffn_norm.as<float>(), R));
+            ck("w1a8_gemv:gate_up", step_linear(c, c->plan_gu_s, L.gu, R, c->h.as<float>(), (size_t)F * 4u));
         } else {
             ck("w1a8_gemv:gate_up", launch_linear(c, c->plan_gu, L.gu, x, L.ffn_norm.as<float>(), R,
                                                   c->h.as<float>(), (size_t)F * 4u, status));
@@ -846,9 +889,9 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
                                                (size_t)sh.c_rows * 4u, status, nullptr, 0, x + sh.c_begin,
                                                (size_t)C * 4u));
             ck("all_gather:x", all_gather_rows(c, c->x_st.as<float>(), sh.c_rows, x, C));
-        } else if (rows_mma) {
-            ck("rows_prep:down", prefill_prep(c, dm_a, dm_rs, c->h.as<float>(), F, nullptr, R));
-            ck("w1a8_mma:down", prefill_linear(c, dm_a, dm_rs, L.down, R, x, (size_t)C * 4u, bnn::kEpiResidual));
+        } else if (rows_prepped) {
+            ck("rows_prep:down", step_prep(c, c->h.as<float>(), F, nullptr, R));
+            ck("w1a8_gemv:down", step_linear(c, c->plan_down_s, L.down, R, x, (size_t)C * 4u));
         } else {
             ck("w1a8_gemv:down", launch_linear(c, c->plan_down, L.down, c->h.as<float>(), nullptr, R, x,
                                                (size_t)C * 4u, status));
@@ -866,13 +909,10 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
             ck("all_gather:pick", ncclAllGather(best, c->best.p, R, ncclUint64, c->comm, s) == ncclSuccess
                                       ? cudaSuccess
                                       : cudaErrorUnknown);
-        } else if (rows_mma) {
-            ck("rows_prep:lm_head", prefill_prep(c, dm_a, dm_rs, x, C, m->out_norm.as<float>(), R));
-            ck("w1a8_mma:lm_head", prefill_linear(c, dm_a, dm_rs, m->lm_head, R, c->logits.as<float>(),
-                                                  (size_t)in.n_vocab * 4u, bnn::kEpiView));
-            bnn::eng::logits_argmax_kernel<<<R, bnn::eng::kArgmaxThreads, 0, s>>>(c->logits.as<float>(), in.n_vocab,
-                                                                                best, status);
-            ck("logits_argmax_kernel");
+        } else if (rows_prepped) {
+            ck("rows_prep:lm_head", step_prep(c, x, C, m->out_norm.as<float>(), R));
+            ck("w1a8_gemv:lm_head", step_linear(c, c->plan_head_s, m->lm_head, R, c->logits.as<float>(),
+                                                (size_t)in.n_vocab * 4u, best));
         } else {
             ck("w1a8_gemv:lm_head", launch_linear(c, c->plan_head, m->lm_head, x, m->out_norm.as<float>(), R,
                                                   c->logits.as<float>(), (size_t)in.n_vocab * 4u, status, best));
@@ -967,10 +1007,18 @@ BNND_Status create_llm_context(bnnd_context* c) {
     CUDA_OR(cudaMemset(c->hist_count.p, 0, 4), BNND_EIO);
     CUDA_OR(cudaMemset(c->status.p, 0, 4), BNND_EIO);
     const int sms = m->dev->sm_count;
-    if (R >= kStepMmaRows && P == 1 &&
-        ((st = dev_alloc(c->dm_a, bnn::mma_a_bytes(R, std::max(C, F) / 128))) ||
-         (st = dev_alloc(c->dm_rs, (size_t)R * 4))))
-        return st;
+    if (R >= kStepRowsPrep && P == 1) {
+        const uint32_t gmax = std::max(C, F) / 128;
+        if ((st = dev_alloc(c->dm_act, (size_t)R * gmax * bnn::kWordsPerGroup * 4)) ||
+            (st = dev_alloc(c->dm_tot, (size_t)R * gmax * 4)) || (st = dev_alloc(c->dm_rs, (size_t)R * 4)))
+            return st;
+        c->plan_qkv_s = bnn::plan_gemv(m->dev->sm_count, sh.q_rows + 2 * sh.kv_rows, C / 128, R, bnn::kProSliced,
+                                       bnn::kEpiView);
+        c->plan_o_s = bnn::plan_gemv(m->dev->sm_count, sh.c_rows, C / 128, R, bnn::kProSliced, bnn::kEpiResidual);
+        c->plan_gu_s = bnn::plan_gemv(m->dev->sm_count, 2 * sh.f_rows, C / 128, R, bnn::kProSliced, bnn::kEpiSwiGLU);
+        c->plan_down_s = bnn::plan_gemv(m->dev->sm_count, sh.c_rows, F / 128, R, bnn::kProSliced, bnn::kEpiResidual);
+        c->plan_head_s = bnn::plan_gemv(m->dev->sm_count, sh.v_rows, C / 128, R, bnn::kProSliced, bnn::kEpiView);
+    }
     c->plan_qkv = bnn::plan_gemv(sms, sh.q_rows + 2 * sh.kv_rows, C / 128, R, bnn::kProRmsNorm, bnn::kEpiView);
     c->plan_o = bnn::plan_gemv(sms, sh.c_rows, C / 128, R, bnn::kProQuant, bnn::kEpiResidual);
     c->plan_gu = bnn::plan_gemv(sms, 2 * sh.f_rows, C / 128, R, bnn::kProRmsNorm, bnn::kEpiSwiGLU);

@@ -42,13 +42,15 @@ struct RowsPrepArgs {
     float eps;
     int exact;           // RMSNorm sum: serial (reference order) or the decode prologue's tree
     uint32_t k, m;
-    unsigned char* a_sw; // pre-tiled int8 rows (mma_a_offset)
+    unsigned char* a_sw; // pre-tiled int8 rows (mma_a_offset), or null:
+    uint32_t* act;       //   sliced words [m][k/128][32] and
+    int32_t* totals;     //   group totals [m][k/128] for the dp4a contraction (kProSliced)
     float* row_scale;    // [m]
     int* status;
 };
 
 inline size_t rows_prep_smem(uint32_t k, bool exact) {
-    return (size_t)k * 4u + (exact ? kSumSmemBytes : 0);
+    return (size_t)k * 5u + (exact ? kSumSmemBytes : 0);  // row, its int8 codes, the sum's scratch
 }
 
 // One CTA of kRowsPrepThreads per row. A non-finite input without RMSNorm is
@@ -60,7 +62,8 @@ __global__ void __launch_bounds__(kRowsPrepThreads) rows_prep_kernel(RowsPrepArg
     __shared__ int s_flag;
     float* xb = reinterpret_cast<float*>(rp_smem);
     float4* xb4 = reinterpret_cast<float4*>(rp_smem);
-    unsigned char* sum_mem = rp_smem + (size_t)a.k * 4u;
+    int8_t* qs = reinterpret_cast<int8_t*>(rp_smem + (size_t)a.k * 4u);  // sliced mode
+    unsigned char* sum_mem = rp_smem + (size_t)a.k * 5u;
     const uint32_t row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t K = a.k, G = K / kGroup;
     constexpr uint32_t nt = kRowsPrepThreads, nw = kRowsPrepThreads / 32;
@@ -129,6 +132,29 @@ __global__ void __launch_bounds__(kRowsPrepThreads) rows_prep_kernel(RowsPrepArg
         amax = fmaxf(amax, red[8 + w]);
     const float s = row_scale_from_absmax(amax);
     const RowQuantizer quant(s);
+    if (!a.a_sw) {
+        // QuantizeRow into shared memory, then the contraction's sliced words
+        // and per-group totals (w1a8_prep_kernel's layout)
+        for (uint32_t k = tid; k < K; k += nt)
+            qs[k] = quant(xb[k]);
+        __syncthreads();
+        uint32_t* act = a.act + (size_t)row * G * kWordsPerGroup;
+        for (uint32_t w = tid; w < G * kWordsPerGroup; w += nt) {
+            const uint32_t g = w / kWordsPerGroup, tj = w % kWordsPerGroup;
+            act[w] = pack_slice(qs + g * kGroup, tj >> 3, tj & 7u);
+        }
+        for (uint32_t g = warp; g < G; g += nw) {
+            const int8_t* qg = qs + g * kGroup + lane * 4u;
+            int t = (int)qg[0] + (int)qg[1] + (int)qg[2] + (int)qg[3];
+            for (int o = 16; o > 0; o >>= 1)
+                t += __shfl_xor_sync(0xffffffffu, t, o);
+            if (lane == 0)
+                a.totals[(size_t)row * G + g] = t;
+        }
+        if (tid == 0)
+            a.row_scale[row] = s;
+        return;
+    }
     // 16 quantised values (one swizzled 16-byte chunk) per thread and pass
     for (uint32_t c = tid; c < G * 8u; c += nt) {
         const float4* src = xb4 + (size_t)c * 4u;
@@ -461,40 +487,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttn
             dst[0] = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
             dst[1] = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
         }
-    }
-}
-
-// ---- greedy pick of full logits rows (steps whose lm_head ran on the tensor cores)
-constexpr uint32_t kArgmaxThreads = 1024;
-
-// best[row] = the largest argmax_key (largest value, lowest index on ties;
-// bnn-infer-v2.c:48-54) over logits [rows][n]; a non-finite logit sets the
-// status (engine.c:262-267). One CTA per row.
-__global__ void __launch_bounds__(kArgmaxThreads) logits_argmax_kernel(const float* logits, uint32_t n,
-                                                                      unsigned long long* best, int* status) {
-    __shared__ unsigned long long red[kArgmaxThreads / 32];
-    const uint32_t row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const float* lr = logits + (size_t)row * n;
-    unsigned long long b = 0ull;
-    int bad = 0;
-    for (uint32_t i = tid; i < n; i += kArgmaxThreads) {
-        const float v = lr[i];
-        bad |= !isfinite(v);
-        const unsigned long long k = argmax_key(v, i);
-        b = k > b ? k : b;
-    }
-    for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long ob = __shfl_xor_sync(0xffffffffu, b, o);
-        b = ob > b ? ob : b;
-    }
-    if (lane == 0)
-        red[warp] = b;
-    if (__syncthreads_or(bad) && tid == 0)
-        atomicOr(status, kStatusNonFinite);
-    if (tid == 0) {
-        for (uint32_t w = 1; w < kArgmaxThreads / 32; ++w)
-            b = red[w] > b ? red[w] : b;
-        best[row] = b;
     }
 }
 

@@ -521,6 +521,8 @@ using GemvFn = void (*)(GemvArgs);
 inline GemvFn gemv_fn(int pro, int epi) {
     if (pro == kProSliced && epi == kEpiDotGroups) return w1a8_gemv_kernel<kProSliced, kEpiDotGroups>;
     if (pro == kProSliced && epi == kEpiView) return w1a8_gemv_kernel<kProSliced, kEpiView>;
+    if (pro == kProSliced && epi == kEpiResidual) return w1a8_gemv_kernel<kProSliced, kEpiResidual>;
+    if (pro == kProSliced && epi == kEpiSwiGLU) return w1a8_gemv_kernel<kProSliced, kEpiSwiGLU>;
     if (pro == kProQuant && epi == kEpiView) return w1a8_gemv_kernel<kProQuant, kEpiView>;
     if (pro == kProQuant && epi == kEpiResidual) return w1a8_gemv_kernel<kProQuant, kEpiResidual>;
     if (pro == kProRmsNorm && epi == kEpiView) return w1a8_gemv_kernel<kProRmsNorm, kEpiView>;

@@ -156,9 +156,9 @@ def test_prefill_long_context_four_heads_per_kv(b200_device, models, exact):
 
 @pytest.mark.parametrize("exact", [True, False])
 def test_multi_row_steps_match_single_rows(b200_device, models, exact):
-    """Five context rows: the step's linears run on the tensor cores (one
-    row-prep CTA per row) and the greedy pick comes from full logits; every
-    row must equal a one-row context fed the same tokens."""
+    """Five context rows: every row is prepared (RMSNorm, quantisation) in
+    its own CTA and the contraction reads the sliced rows; every row must
+    equal a one-row context fed the same tokens."""
     path, shape = models["small"]
     rng = np.random.default_rng(46)
     rows = 5
