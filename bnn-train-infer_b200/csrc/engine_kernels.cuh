@@ -105,7 +105,7 @@ __global__ void embed_kernel(const int32_t* tokens, const unsigned char* wblocks
 // straight from shared memory. While the whole history fits in shared memory
 // (n <= resident_max), K and V are instead copied whole at the start and
 // every phase spreads over all threads: no tiles, no per-tile waits.
-constexpr uint32_t kAttnThreads = 256;
+constexpr uint32_t kAttnThreads = 512;
 constexpr uint32_t kAttnTile = 128;
 constexpr uint32_t kAttnStages = 2;
 
@@ -437,17 +437,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
             float sum = 0.0f;
             if (a.exact) {
                 if (lane == 0) {
-                    uint32_t t = 0;
-                    for (; t + 8 <= n; t += 8) {
-                        float v[8];
-#pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            v[j] = e[t + j];
-#pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            sum = __fadd_rn(sum, v[j]);
+                    // serial in index order; the next four terms load while
+                    // the current four are added (rows are float4-aligned)
+                    const float4* e4 = reinterpret_cast<const float4*>(e);
+                    const uint32_t n4 = n / 4;
+                    float4 cur = n4 ? e4[0] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    for (uint32_t b = 0; b < n4; ++b) {
+                        const float4 nx = b + 1 < n4 ? e4[b + 1] : cur;
+                        sum = __fadd_rn(sum, cur.x);
+                        sum = __fadd_rn(sum, cur.y);
+                        sum = __fadd_rn(sum, cur.z);
+                        sum = __fadd_rn(sum, cur.w);
+                        cur = nx;
                     }
-                    for (; t < n; ++t)
+                    for (uint32_t t = n4 * 4; t < n; ++t)
                         sum = __fadd_rn(sum, e[t]);
                 }
             } else {
@@ -490,12 +493,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
                 const float* ph = sc + (size_t)h * sc_stride;
                 float v = 0.0f;
                 uint32_t t = 0;
-                for (; t + 4 <= n; t += 4) {
-                    const float4 p = *reinterpret_cast<const float4*>(ph + t);
-                    v = __fadd_rn(v, __fmul_rn(p.x, vres[(size_t)t * HD + d]));
-                    v = __fadd_rn(v, __fmul_rn(p.y, vres[(size_t)(t + 1) * HD + d]));
-                    v = __fadd_rn(v, __fmul_rn(p.z, vres[(size_t)(t + 2) * HD + d]));
-                    v = __fadd_rn(v, __fmul_rn(p.w, vres[(size_t)(t + 3) * HD + d]));
+                for (; t + 8 <= n; t += 8) {
+                    // products of eight positions first (independent), then
+                    // the serial chain of adds
+                    const float4 p0 = *reinterpret_cast<const float4*>(ph + t);
+                    const float4 p1 = *reinterpret_cast<const float4*>(ph + t + 4);
+                    float w[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        w[j] = vres[(size_t)(t + j) * HD + d];
+                    const float pr[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        w[j] = __fmul_rn(pr[j], w[j]);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        v = __fadd_rn(v, w[j]);
                 }
                 for (; t < n; ++t)
                     v = __fadd_rn(v, __fmul_rn(ph[t], vres[(size_t)t * HD + d]));
