@@ -774,7 +774,8 @@ cudaError_t step_prep(bnnd_context* c, const float* x, uint32_t k, const float* 
 
 // The contraction over the rows step_prep prepared (kProSliced prologue).
 cudaError_t step_linear(const bnnd_context* c, const bnn::GemvLaunch& cl, const Linear& l, uint32_t rows, float* out,
-                        size_t out_stride, unsigned long long* best = nullptr) {
+                        size_t out_stride, unsigned long long* best = nullptr, uint32_t index_base = 0,
+                        const float* res = nullptr, size_t res_stride = 0) {
     bnn::GemvArgs a = {};
     a.wblocks = l.m->wblocks;
     a.n = l.out;
@@ -790,6 +791,9 @@ cudaError_t step_linear(const bnnd_context* c, const bnn::GemvLaunch& cl, const 
     a.out_stride = out_stride;
     a.status = c->status.as<int>();
     a.best = best;
+    a.index_base = index_base;
+    a.res = reinterpret_cast<const unsigned char*>(res);
+    a.res_stride = res_stride;
     g_next_bytes = ((double)l.out * l.in * 0.140625 + 4.0 * l.in + 4.0 * l.out) * rows;
     return bnn::launch_gemv(cl, rows, a, c->stream, c->pdl);
 }
@@ -817,16 +821,24 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
     // instead of a contraction whose every CTA prepares the rows one after
     // another. Same arithmetic either way.
     const bool rows_prepped = c->dm_act.p != nullptr;
+    // One linear: row prep + sliced contraction, or the contraction with the
+    // RMSNorm/quantise prologue in every CTA.
+    auto lin = [&](const char* prep_name, const char* name, const bnn::GemvLaunch& plan,
+                   const bnn::GemvLaunch& plan_s, const Linear& l, const float* xin, uint32_t k, const float* gain,
+                   float* out, size_t out_stride, unsigned long long* bst = nullptr, uint32_t ib = 0,
+                   const float* res = nullptr, size_t res_stride = 0) {
+        if (rows_prepped) {
+            ck(prep_name, step_prep(c, xin, k, gain, R));
+            ck(name, step_linear(c, plan_s, l, R, out, out_stride, bst, ib, res, res_stride));
+        } else {
+            ck(name, launch_linear(c, plan, l, xin, gain, R, out, out_stride, status, bst, ib, res, res_stride));
+        }
+    };
     for (uint32_t l = 0; l < in.n_layers; ++l) {
         const QwenLayer& L = *m->layers[l];
         // attn_norm + q|k|v projections of this rank's heads (prologue: RMSNorm + quantise)
-        if (rows_prepped) {
-            ck("rows_prep:qkv", step_prep(c, x, C, L.attn_norm.as<float>(), R));
-            ck("w1a8_gemv:qkv", step_linear(c, c->plan_qkv_s, L.qkv, R, c->qkv.as<float>(), (size_t)qkv_width * 4u));
-        } else {
-            ck("w1a8_gemv:qkv", launch_linear(c, c->plan_qkv, L.qkv, x, L.attn_norm.as<float>(), R,
-                                              c->qkv.as<float>(), (size_t)qkv_width * 4u, status));
-        }
+        lin("rows_prep:qkv", "w1a8_gemv:qkv", c->plan_qkv, c->plan_qkv_s, L.qkv, x, C, L.attn_norm.as<float>(),
+            c->qkv.as<float>(), (size_t)qkv_width * 4u);
         // q/k norm + rope + KV append + attention, one block per (KV head, row)
         bnn::eng::AttnArgs aa = {};
         aa.qkv = c->qkv.as<float>();
@@ -858,64 +870,47 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
         // attn_output, x += o (prologue: quantise the attention output)
         if (tp) {
             float* xs = c->x_st.as<float>() + (size_t)c->rank * R * sh.c_rows;
-            ck("w1a8_gemv:o", launch_linear(c, c->plan_o, L.o, c->y.as<float>(), nullptr, R, xs,
-                                            (size_t)sh.c_rows * 4u, status, nullptr, 0, x + sh.c_begin,
-                                            (size_t)C * 4u));
+            lin("rows_prep:o", "w1a8_gemv:o", c->plan_o, c->plan_o_s, L.o, c->y.as<float>(), C, nullptr, xs,
+                (size_t)sh.c_rows * 4u, nullptr, 0, x + sh.c_begin, (size_t)C * 4u);
             ck("all_gather:x", all_gather_rows(c, c->x_st.as<float>(), sh.c_rows, x, C));
-        } else if (rows_prepped) {
-            ck("rows_prep:o", step_prep(c, c->y.as<float>(), C, nullptr, R));
-            ck("w1a8_gemv:o", step_linear(c, c->plan_o_s, L.o, R, x, (size_t)C * 4u));
         } else {
-            ck("w1a8_gemv:o", launch_linear(c, c->plan_o, L.o, c->y.as<float>(), nullptr, R, x, (size_t)C * 4u,
-                                            status));
+            lin("rows_prep:o", "w1a8_gemv:o", c->plan_o, c->plan_o_s, L.o, c->y.as<float>(), C, nullptr, x,
+                (size_t)C * 4u);
         }
         // ffn_norm + gate|up + SwiGLU -> h
         if (tp) {
-            ck("w1a8_gemv:gate_up", launch_linear(c, c->plan_gu, L.gu, x, L.ffn_norm.as<float>(), R,
-                                                  c->h_st.as<float>() + (size_t)c->rank * R * sh.f_rows,
-                                                  (size_t)sh.f_rows * 4u, status));
+            lin("rows_prep:gate_up", "w1a8_gemv:gate_up", c->plan_gu, c->plan_gu_s, L.gu, x, C,
+                L.ffn_norm.as<float>(), c->h_st.as<float>() + (size_t)c->rank * R * sh.f_rows, (size_t)sh.f_rows * 4u);
             ck("all_gather:h", all_gather_rows(c, c->h_st.as<float>(), sh.f_rows, c->h.as<float>(), F));
-        } else if (rows_prepped) {
-            ck("rows_prep:gate_up", step_prep(c, x, C, L.ffn_norm.as<float>(), R));
-            ck("w1a8_gemv:gate_up", step_linear(c, c->plan_gu_s, L.gu, R, c->h.as<float>(), (size_t)F * 4u));
         } else {
-            ck("w1a8_gemv:gate_up", launch_linear(c, c->plan_gu, L.gu, x, L.ffn_norm.as<float>(), R,
-                                                  c->h.as<float>(), (size_t)F * 4u, status));
+            lin("rows_prep:gate_up", "w1a8_gemv:gate_up", c->plan_gu, c->plan_gu_s, L.gu, x, C,
+                L.ffn_norm.as<float>(), c->h.as<float>(), (size_t)F * 4u);
         }
         // ffn_down, x += d (prologue: quantise h)
         if (tp) {
             float* xs = c->x_st.as<float>() + (size_t)c->rank * R * sh.c_rows;
-            ck("w1a8_gemv:down", launch_linear(c, c->plan_down, L.down, c->h.as<float>(), nullptr, R, xs,
-                                               (size_t)sh.c_rows * 4u, status, nullptr, 0, x + sh.c_begin,
-                                               (size_t)C * 4u));
+            lin("rows_prep:down", "w1a8_gemv:down", c->plan_down, c->plan_down_s, L.down, c->h.as<float>(), F, nullptr,
+                xs, (size_t)sh.c_rows * 4u, nullptr, 0, x + sh.c_begin, (size_t)C * 4u);
             ck("all_gather:x", all_gather_rows(c, c->x_st.as<float>(), sh.c_rows, x, C));
-        } else if (rows_prepped) {
-            ck("rows_prep:down", step_prep(c, c->h.as<float>(), F, nullptr, R));
-            ck("w1a8_gemv:down", step_linear(c, c->plan_down_s, L.down, R, x, (size_t)C * 4u));
         } else {
-            ck("w1a8_gemv:down", launch_linear(c, c->plan_down, L.down, c->h.as<float>(), nullptr, R, x,
-                                               (size_t)C * 4u, status));
+            lin("rows_prep:down", "w1a8_gemv:down", c->plan_down, c->plan_down_s, L.down, c->h.as<float>(), F, nullptr,
+                x, (size_t)C * 4u);
         }
     }
     if (with_logits) {
         // out_norm + lm_head; the epilogue also takes the greedy pick
         if (tp) {
-            ck("w1a8_gemv:lm_head",
-               launch_linear(c, c->plan_head, m->lm_head, x, m->out_norm.as<float>(), R,
-                             c->lg_st.as<float>() + (size_t)c->rank * R * sh.v_stride, (size_t)sh.v_stride * 4u,
-                             status, best, sh.v_begin));
+            lin("rows_prep:lm_head", "w1a8_gemv:lm_head", c->plan_head, c->plan_head_s, m->lm_head, x, C,
+                m->out_norm.as<float>(), c->lg_st.as<float>() + (size_t)c->rank * R * sh.v_stride,
+                (size_t)sh.v_stride * 4u, best, sh.v_begin);
             ck("all_gather:logits",
                all_gather_rows(c, c->lg_st.as<float>(), sh.v_stride, c->logits.as<float>(), in.n_vocab));
             ck("all_gather:pick", ncclAllGather(best, c->best.p, R, ncclUint64, c->comm, s) == ncclSuccess
                                       ? cudaSuccess
                                       : cudaErrorUnknown);
-        } else if (rows_prepped) {
-            ck("rows_prep:lm_head", step_prep(c, x, C, m->out_norm.as<float>(), R));
-            ck("w1a8_gemv:lm_head", step_linear(c, c->plan_head_s, m->lm_head, R, c->logits.as<float>(),
-                                                (size_t)in.n_vocab * 4u, best));
         } else {
-            ck("w1a8_gemv:lm_head", launch_linear(c, c->plan_head, m->lm_head, x, m->out_norm.as<float>(), R,
-                                                  c->logits.as<float>(), (size_t)in.n_vocab * 4u, status, best));
+            lin("rows_prep:lm_head", "w1a8_gemv:lm_head", c->plan_head, c->plan_head_s, m->lm_head, x, C,
+                m->out_norm.as<float>(), c->logits.as<float>(), (size_t)in.n_vocab * 4u, best);
         }
     }
     bnn::eng::step_end_kernel<<<1, 32 * ((R + 31) / 32), 0, s>>>(
@@ -1007,7 +1002,7 @@ BNND_Status create_llm_context(bnnd_context* c) {
     CUDA_OR(cudaMemset(c->hist_count.p, 0, 4), BNND_EIO);
     CUDA_OR(cudaMemset(c->status.p, 0, 4), BNND_EIO);
     const int sms = m->dev->sm_count;
-    if (R >= kStepRowsPrep && P == 1) {
+    if (R >= kStepRowsPrep) {
         const uint32_t gmax = std::max(C, F) / 128;
         if ((st = dev_alloc(c->dm_act, (size_t)R * gmax * bnn::kWordsPerGroup * 4)) ||
             (st = dev_alloc(c->dm_tot, (size_t)R * gmax * 4)) || (st = dev_alloc(c->dm_rs, (size_t)R * 4)))

@@ -44,7 +44,7 @@ def main():
     box = [engine.comm_id_create(api) if rank == 0 else None]
     dist.broadcast_object_list(box, src=0)
     rng = np.random.default_rng(5)
-    for rows in (1, 3):
+    for rows in (1, 3, 5):  # 5: every row prepared in its own CTA (sliced contraction)
         prompt = rng.integers(0, SHAPE.vocab, size=(rows, 12), dtype=np.int32)
         model = engine.Model(dev, path, api, world=world, rank=rank)
         ctx = engine.Context(model, n_ctx=256, n_batch=rows, comm_id=box[0])
