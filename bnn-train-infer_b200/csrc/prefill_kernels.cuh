@@ -237,8 +237,9 @@ __global__ void kv_append_kernel(KvAppendArgs a) {
 // decode step per position.
 constexpr uint32_t kPfQT = 16;        // query positions per CTA
 constexpr uint32_t kPfKT = 32;        // K/V positions per shared-memory tile
-constexpr uint32_t kPfThreads = 256;  // (query, key pair) and (query, 8 dims) per thread
+constexpr uint32_t kPfThreads = 512;  // (query, key) and (query, 4 dims) per thread
 constexpr uint32_t kPfSmemBudget = 200u * 1024u;
+static_assert(kPfThreads == kPfQT * kPfKT && kPfThreads == kPfQT * 32, "thread maps of the score and V phases");
 
 struct PfAttnArgs {
     const float* qkv;       // [rows][c + 2kv]
@@ -267,8 +268,8 @@ struct PfSmem {
 __host__ __device__ inline PfSmem pf_smem_plan(uint32_t hd, uint32_t kv_mul, uint32_t sc_stride, bool sc_smem) {
     PfSmem p;
     p.q = 0;                                                    // [kPfQT * kv_mul][hd]
-    p.kv = p.q + (size_t)kPfQT * kv_mul * hd * 4u;              // [kPfKT][hd + 4]
-    p.gq = p.kv + (size_t)kPfKT * (hd + 4u) * 4u;               // [hd]
+    p.kv = p.q + (size_t)kPfQT * kv_mul * hd * 4u;              // [2][kPfKT][hd + 4] (double-buffered)
+    p.gq = p.kv + (size_t)2 * kPfKT * (hd + 4u) * 4u;           // [hd]
     p.rc = p.gq + (size_t)hd * 4u;                              // [kPfQT][hd / 2]
     p.rs = p.rc + (size_t)kPfQT * (hd / 2u) * 4u;
     p.red = p.rs + (size_t)kPfQT * (hd / 2u) * 4u;              // 64 floats
@@ -283,7 +284,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttn
     constexpr uint32_t kStride = HD + 4;  // padded K/V rows
     const uint32_t g = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t tiles = (a.len + kPfQT - 1) / kPfQT;
-    const uint32_t r = blockIdx.y / tiles, i0 = (blockIdx.y % tiles) * kPfQT;
+    // the last positions (most keys) first: the longest CTAs start in the first wave
+    const uint32_t r = blockIdx.y / tiles, i0 = (tiles - 1 - blockIdx.y % tiles) * kPfQT;
     const uint32_t nq = min(kPfQT, a.len - i0);
     const uint32_t p0 = r * a.len + i0;  // activation row of the first query
     const bool sc_smem = a.scores == nullptr;
@@ -337,30 +339,52 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttn
     if (*flag)
         return;
 
-    // ---- scores: thread (query sq, keys 2 kp, 2 kp + 1 of the tile), all KVM heads
-    const uint32_t sq = tid / 16, kp = tid % 16;
+    // K/V tiles are double-buffered: this thread's share of tile t + 1 is
+    // loaded into registers while tile t is in use, then stored to the
+    // other buffer
+    constexpr uint32_t kPer = (kPfKT * (HD / 4) + kPfThreads - 1) / kPfThreads;  // float4 per thread and tile
+    float4 pre[kPer];
+    auto tile_load = [&](const float* src, uint32_t t0) {
+        const uint32_t rows_in = min(kPfKT, n_max - t0);
+#pragma unroll
+        for (uint32_t j = 0; j < kPer; ++j) {
+            const uint32_t i = tid + j * kPfThreads;
+            if (i < rows_in * (HD / 4))
+                pre[j] = reinterpret_cast<const float4*>(src + (size_t)(t0 + i / (HD / 4)) * HD)[i % (HD / 4)];
+        }
+    };
+    auto tile_store = [&](float* dst, uint32_t t0) {
+        const uint32_t rows_in = min(kPfKT, n_max - t0);
+#pragma unroll
+        for (uint32_t j = 0; j < kPer; ++j) {
+            const uint32_t i = tid + j * kPfThreads;
+            if (i < rows_in * (HD / 4))
+                reinterpret_cast<float4*>(dst + (size_t)(i / (HD / 4)) * kStride)[i % (HD / 4)] = pre[j];
+        }
+    };
+    auto kvb = [&](uint32_t b) { return kv_s + (b ? (size_t)kPfKT * kStride : (size_t)0); };
+
+    // ---- scores: thread (query sq, key kp of the tile), all KVM heads
+    const uint32_t sq = tid / kPfKT, kp = tid % kPfKT;
     const uint32_t sq_n = pos0 + sq + 1;  // keys of query sq
     int bad = 0;
-    for (uint32_t t0 = 0; t0 < n_max; t0 += kPfKT) {
-        const uint32_t rows_in = min(kPfKT, n_max - t0);
-        for (uint32_t i = tid; i < rows_in * (HD / 4); i += kPfThreads) {
-            const uint32_t tt = i / (HD / 4), c4 = i % (HD / 4);
-            reinterpret_cast<float4*>(kv_s + (size_t)tt * kStride)[c4] =
-                reinterpret_cast<const float4*>(kc + (size_t)(t0 + tt) * HD)[c4];
-        }
-        __syncthreads();
-        const uint32_t ta = t0 + 2 * kp, tb = ta + 1;
-        const bool va = sq < nq && ta < sq_n, vb = sq < nq && tb < sq_n;
-        if (va) {  // tb valid implies ta valid
-            const float4* ka = reinterpret_cast<const float4*>(kv_s + (size_t)(2 * kp) * kStride);
-            const float4* kb = reinterpret_cast<const float4*>(kv_s + (size_t)(2 * kp + 1) * kStride);
-            float da[KVM], db[KVM];
+    tile_load(kc, 0);
+    tile_store(kvb(0), 0);
+    __syncthreads();
+    for (uint32_t t0 = 0, buf = 0; t0 < n_max; t0 += kPfKT, buf ^= 1) {
+        const bool more = t0 + kPfKT < n_max;
+        if (more)
+            tile_load(kc, t0 + kPfKT);
+        const uint32_t ta = t0 + kp;
+        if (sq < nq && ta < sq_n) {
+            const float4* ka = reinterpret_cast<const float4*>(kvb(buf) + (size_t)kp * kStride);
+            float da[KVM];
 #pragma unroll
             for (int h = 0; h < KVM; ++h)
-                da[h] = db[h] = 0.0f;
+                da[h] = 0.0f;
 #pragma unroll 4
             for (uint32_t i = 0; i < HD / 4; ++i) {
-                const float4 x = ka[i], y = vb ? kb[i] : ka[i];
+                const float4 x = ka[i];
 #pragma unroll
                 for (int h = 0; h < KVM; ++h) {
                     const float4 q = reinterpret_cast<const float4*>(q_s + (size_t)(sq * KVM + h) * HD)[i];
@@ -368,10 +392,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttn
                     da[h] = __fadd_rn(da[h], __fmul_rn(q.y, x.y));
                     da[h] = __fadd_rn(da[h], __fmul_rn(q.z, x.z));
                     da[h] = __fadd_rn(da[h], __fmul_rn(q.w, x.w));
-                    db[h] = __fadd_rn(db[h], __fmul_rn(q.x, y.x));
-                    db[h] = __fadd_rn(db[h], __fmul_rn(q.y, y.y));
-                    db[h] = __fadd_rn(db[h], __fmul_rn(q.z, y.z));
-                    db[h] = __fadd_rn(db[h], __fmul_rn(q.w, y.w));
                 }
             }
 #pragma unroll
@@ -379,14 +399,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttn
                 const float sa = __fmul_rn(da[h], a.scale);
                 bad |= !isfinite(sa);
                 sc_row(sq, h)[ta] = sa;
-                if (vb) {
-                    const float sb = __fmul_rn(db[h], a.scale);
-                    bad |= !isfinite(sb);
-                    sc_row(sq, h)[tb] = sb;
-                }
             }
         }
-        __syncthreads();  // the tile is free again
+        if (more)
+            tile_store(kvb(buf ^ 1), t0 + kPfKT);
+        __syncthreads();  // the next tile is in place; this one is free again
     }
     if (__syncthreads_or(bad)) {
         if (tid == 0)
@@ -443,50 +460,50 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttn
     if (*flag)
         return;
 
-    // ---- y: thread (query vq, dims 8 vd .. 8 vd + 7), all KVM heads; serial over t
-    const uint32_t vq = tid / 16, vd = (tid % 16) * 8;
+    // ---- y: thread (query vq, dims DV vd .. DV vd + DV - 1), all KVM heads; serial over t
+    constexpr int DV = HD / 32;
+    const uint32_t vq = tid / 32, vd = (tid % 32) * DV;
     const uint32_t vn = vq < nq ? pos0 + vq + 1 : 0;
-    float acc[KVM][8];
+    float acc[KVM][DV];
 #pragma unroll
     for (int h = 0; h < KVM; ++h)
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < DV; ++j)
             acc[h][j] = 0.0f;
-    for (uint32_t t0 = 0; t0 < n_max; t0 += kPfKT) {
+    tile_load(vc, 0);
+    tile_store(kvb(0), 0);
+    __syncthreads();
+    for (uint32_t t0 = 0, buf = 0; t0 < n_max; t0 += kPfKT, buf ^= 1) {
         const uint32_t rows_in = min(kPfKT, n_max - t0);
-        for (uint32_t i = tid; i < rows_in * (HD / 4); i += kPfThreads) {
-            const uint32_t tt = i / (HD / 4), c4 = i % (HD / 4);
-            reinterpret_cast<float4*>(kv_s + (size_t)tt * kStride)[c4] =
-                reinterpret_cast<const float4*>(vc + (size_t)(t0 + tt) * HD)[c4];
-        }
-        __syncthreads();
+        const bool more = t0 + kPfKT < n_max;
+        if (more)
+            tile_load(vc, t0 + kPfKT);
+        const float* vt = kvb(buf);
         const uint32_t tend = vn > t0 ? min(rows_in, vn - t0) : 0;
         for (uint32_t tt = 0; tt < tend; ++tt) {
-            const float4 v0 = reinterpret_cast<const float4*>(kv_s + (size_t)tt * kStride + vd)[0];
-            const float4 v1 = reinterpret_cast<const float4*>(kv_s + (size_t)tt * kStride + vd)[1];
+            float v[DV];
+#pragma unroll
+            for (int j = 0; j < DV; ++j)
+                v[j] = vt[(size_t)tt * kStride + vd + j];
 #pragma unroll
             for (int h = 0; h < KVM; ++h) {
                 const float p = sc_row(vq, h)[t0 + tt];
-                acc[h][0] = __fadd_rn(acc[h][0], __fmul_rn(p, v0.x));
-                acc[h][1] = __fadd_rn(acc[h][1], __fmul_rn(p, v0.y));
-                acc[h][2] = __fadd_rn(acc[h][2], __fmul_rn(p, v0.z));
-                acc[h][3] = __fadd_rn(acc[h][3], __fmul_rn(p, v0.w));
-                acc[h][4] = __fadd_rn(acc[h][4], __fmul_rn(p, v1.x));
-                acc[h][5] = __fadd_rn(acc[h][5], __fmul_rn(p, v1.y));
-                acc[h][6] = __fadd_rn(acc[h][6], __fmul_rn(p, v1.z));
-                acc[h][7] = __fadd_rn(acc[h][7], __fmul_rn(p, v1.w));
+#pragma unroll
+                for (int j = 0; j < DV; ++j)
+                    acc[h][j] = __fadd_rn(acc[h][j], __fmul_rn(p, v[j]));
             }
         }
+        if (more)
+            tile_store(kvb(buf ^ 1), t0 + kPfKT);
         __syncthreads();
     }
     if (vq < nq) {
         float* yr = a.y + (size_t)(p0 + vq) * a.y_stride;
 #pragma unroll
-        for (int h = 0; h < KVM; ++h) {
-            float4* dst = reinterpret_cast<float4*>(yr + (size_t)(g * KVM + h) * HD + vd);
-            dst[0] = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-            dst[1] = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
-        }
+        for (int h = 0; h < KVM; ++h)
+#pragma unroll
+            for (int j = 0; j < DV; ++j)
+                yr[(size_t)(g * KVM + h) * HD + vd + j] = acc[h][j];
     }
 }
 
