@@ -3,11 +3,11 @@
 //
 // With weights w in {-1, +1} and int8 activations q, the reference's group
 // dot D = 2 * pos - total (soft :251-258) is exactly sum_k w_k * q_k, an int8
-// x int8 product with an int32 sum. So a tile of 128 activation rows x 128
-// output rows runs as tcgen05.mma kind::i8 (A = q, B = +-1, both K-major,
+// x int8 product with an int32 sum. So a tile of 128 activation rows x NT
+// (128, or 64 when 128-wide tiles would leave SMs idle) output rows runs as tcgen05.mma kind::i8 (A = q, B = +-1, both K-major,
 // 128-byte swizzle), four K=32 instructions per 128-wide group, each group
-// into its own TMEM accumulator (128 columns). Groups are processed in chunks
-// of kMmaChunk, double-buffered in TMEM (2 x 2 x 128 = 512 columns), so the
+// into its own TMEM accumulator (NT columns). Groups are processed in chunks
+// of kMmaChunk, double-buffered in TMEM (2 x 2 x NT columns), so the
 // MMAs of one chunk overlap the epilogue of the previous one. The epilogue
 // reads D per group with tcgen05.ld and does the reference's FP32 work in
 // its order: acc = fl(acc + fl(F32(scale_g) * D_g)) for increasing g, then
@@ -41,21 +41,21 @@
 namespace bnn {
 
 constexpr uint32_t kMmaM = 128;                      // activation rows per tile (TMEM lanes)
-constexpr uint32_t kMmaN = 128;                      // output rows per tile (16 weight blocks)
+constexpr uint32_t kMmaN = 128;                      // output rows per tile, wide form (16 weight blocks)
+constexpr uint32_t kMmaNarrow = 64;                  // narrow form, for matrices that give few wide tiles
 constexpr uint32_t kMmaChunk = 2;                    // groups per TMEM buffer
 constexpr uint32_t kMmaStages = 4;                   // A ring depth
 constexpr uint32_t kMmaATile = kMmaM * kGroup;       // 16 KB: one group of 128 rows
-constexpr uint32_t kMmaBTile = kMmaN * kGroup;       // 16 KB: one group of 128 rows as +-1 bytes
 constexpr uint32_t kMmaEpiWarps = 8;                 // two per TMEM lane quadrant
 constexpr uint32_t kMmaThreads = 64 + kMmaEpiWarps * 32;
 constexpr uint32_t kMmaEpiThreads = kMmaEpiWarps * 32;
-constexpr uint32_t kMmaCols = kMmaN / (kMmaEpiWarps / 4);  // columns per epilogue thread (64)
-constexpr uint32_t kMmaTmemCols = 2 * kMmaChunk * kMmaN;   // 512
 constexpr uint32_t kMmaMinRows = 64;                 // BNN_Execute's tensor-core threshold
-static_assert(kMmaChunk * kMmaN == kMmaEpiThreads, "one B row-group per epilogue thread and chunk");
+static_assert(kMmaChunk * kMmaN == kMmaEpiThreads, "at most one B row-group per epilogue thread and chunk");
 
 // Instruction descriptor: D s32, A and B signed 8-bit, both K-major, N, M.
-constexpr uint32_t kMmaIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((kMmaN >> 3) << 17) | ((kMmaM >> 4) << 24);
+__host__ __device__ constexpr uint32_t mma_idesc(uint32_t n) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((kMmaM >> 4) << 24);
+}
 
 // Byte offset of activation (row, group g, 16-byte chunk c) in the pre-tiled A.
 __host__ __device__ inline size_t mma_a_offset(uint32_t row, uint32_t g, uint32_t groups, uint32_t c) {
@@ -84,12 +84,12 @@ struct MmaSmem {
     size_t a, b, sf, bars, total;
 };
 
-__host__ __device__ inline MmaSmem mma_smem_plan(uint32_t /*groups*/) {
+__host__ __device__ inline MmaSmem mma_smem_plan(uint32_t nt) {
     MmaSmem p;
     p.a = 0;
     p.b = p.a + (size_t)kMmaStages * kMmaATile;
-    p.sf = p.b + (size_t)2 * kMmaChunk * kMmaBTile;         // FP32 scales [2][kMmaChunk][kMmaN]
-    p.bars = p.sf + (size_t)2 * kMmaChunk * kMmaN * 4u;
+    p.sf = p.b + (size_t)2 * kMmaChunk * nt * kGroup;       // FP32 scales [2][kMmaChunk][nt]
+    p.bars = p.sf + (size_t)2 * kMmaChunk * nt * 4u;
     p.total = p.bars + 256 + 1024;  // barriers and words, plus slack to 1024-align the base
     return p;
 }
@@ -103,12 +103,12 @@ __device__ __forceinline__ uint64_t mma_smem_desc(uint32_t saddr) {
     return ((uint64_t)hi << 32) | lo;
 }
 
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate, uint32_t idesc) {
     const uint32_t mask = 0;
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(kMmaIdesc), "r"(accumulate), "r"(mask));
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(mask));
 }
 
 // Arrives on `bar` once every tcgen05 operation this thread issued so far has completed.
@@ -158,18 +158,24 @@ __device__ __forceinline__ uint32_t expand_signs4(uint32_t v) {
     return (b * 0xfeu) ^ 0xffffffffu;
 }
 
-// Grid (ceil(N / 128), ceil(M / 128)); kMmaThreads threads; mma_smem_plan().total
+// Grid (ceil(N / NT), ceil(M / 128)); kMmaThreads threads; mma_smem_plan(NT).total
 // bytes of dynamic shared memory.
+template <uint32_t NT>
 static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs a) {
+    constexpr uint32_t kMmaBTile = NT * kGroup;             // one group of NT rows as +-1 bytes
+    constexpr uint32_t kMmaCols = NT / (kMmaEpiWarps / 4);  // columns per epilogue thread
+    constexpr uint32_t kMmaTmemCols = 2 * kMmaChunk * NT;   // 512 or 256
+    constexpr uint32_t kFetchThreads = kMmaChunk * NT;      // one B row-group each per chunk
+    constexpr uint32_t kIdesc = mma_idesc(NT);
     extern __shared__ __align__(1024) unsigned char mma_smem_raw[];
     // the swizzle pattern follows shared-memory address bits: 1024-align the base
     const uint32_t raw = smem_addr(mma_smem_raw);
     unsigned char* sm = mma_smem_raw + (((raw + 1023u) & ~1023u) - raw);
     const uint32_t G = a.groups;
-    const MmaSmem plan = mma_smem_plan(G);
+    const MmaSmem plan = mma_smem_plan(NT);
     unsigned char* a_ring = sm + plan.a;
     unsigned char* b_buf = sm + plan.b;
-    float* sf = reinterpret_cast<float*>(sm + plan.sf);  // [2][kMmaChunk][kMmaN]
+    float* sf = reinterpret_cast<float*>(sm + plan.sf);  // [2][kMmaChunk][NT]
     uint64_t* afull = reinterpret_cast<uint64_t*>(sm + plan.bars);
     uint64_t* aempty = afull + kMmaStages;
     uint64_t* bready = aempty + kMmaStages;
@@ -252,10 +258,10 @@ static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs
                     tc_fence_after();
                     const uint32_t a_base = smem_addr(a_ring + (size_t)s * kMmaATile);
                     const uint32_t b_base = smem_addr(b_buf + (size_t)(b * kMmaChunk + gi) * kMmaBTile);
-                    const uint32_t d = tmem + (b * kMmaChunk + gi) * kMmaN;
+                    const uint32_t d = tmem + (b * kMmaChunk + gi) * NT;
 #pragma unroll
                     for (uint32_t k = 0; k < kGroup / 32; ++k)
-                        mma_i8(d, mma_smem_desc(a_base + 32u * k), mma_smem_desc(b_base + 32u * k), k);
+                        mma_i8(d, mma_smem_desc(a_base + 32u * k), mma_smem_desc(b_base + 32u * k), k, kIdesc);
                     mma_commit(&aempty[s]);  // the A stage is free once these MMAs have read it
                 }
                 if (!ok)
@@ -269,7 +275,7 @@ static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs
         // ---- warps 2..9: fetch + expand B chunks, then the ordered FP32 epilogue
         const uint32_t et = tid - 64;                    // 0..255
         const uint32_t quad = warp & 3;                  // TMEM lane quadrant this warp may read
-        const uint32_t half = (warp - 2) >> 2;           // which 64 of the tile's columns
+        const uint32_t half = (warp - 2) >> 2;           // which half of the tile's columns
         const uint32_t row = quad * 32 + lane;           // tile row = TMEM lane
         const uint32_t m = mt * kMmaM + row;
         const uint32_t col0 = half * kMmaCols;           // first tile column of this thread
@@ -277,8 +283,9 @@ static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs
         const bool live = m < a.m;
         // B fetch of one chunk: thread et owns (group gi = et / 128, tile row n = et % 128):
         // 16 bytes of sign bits, and the scale of that row and group
-        const uint32_t fgi = et / kMmaN, fn = et % kMmaN;
-        const uint32_t fblk = nt * (kMmaN / kRowBlock) + fn / kRowBlock, fr = fn % kRowBlock;
+        const bool fetcher = et < kFetchThreads;        // the others only arrive on bready
+        const uint32_t fgi = fetcher ? et / NT : 0, fn = et % NT;
+        const uint32_t fblk = nt * (NT / kRowBlock) + fn / kRowBlock, fr = fn % kRowBlock;
         const unsigned char* fbase = a.wblocks + (size_t)fblk * G * 144u;
         uint4 fbits = make_uint4(0u, 0u, 0u, 0u);
         uint16_t fscale = 0;
@@ -286,13 +293,17 @@ static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs
             const uint32_t g = c * kMmaChunk + fgi;
             fbits = make_uint4(0u, 0u, 0u, 0u);
             fscale = 0;
-            if (fblk < nblocks && g < G) {
+            if (fetcher && fblk < nblocks && g < G) {
                 fbits = *reinterpret_cast<const uint4*>(fbase + (size_t)g * 128u + fr * 16u);
                 fscale = *reinterpret_cast<const uint16_t*>(fbase + (size_t)G * 128u + ((size_t)fr * G + g) * 2u);
             }
         };
         auto expand = [&](uint32_t c) {
             const uint32_t b = c & 1;
+            if (!fetcher) {
+                mbar_arrive(&bready[b]);
+                return;
+            }
             unsigned char* dst =
                 b_buf + (size_t)(b * kMmaChunk + fgi) * kMmaBTile + (fn / 8u) * 1024u + (fn % 8u) * 128u;
             const uint32_t w[4] = {fbits.x, fbits.y, fbits.z, fbits.w};
@@ -306,7 +317,7 @@ static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs
                 o.w = expand_signs4(bits >> 12);
                 *reinterpret_cast<uint4*>(dst + ((j ^ (fn % 8u)) * 16u)) = o;
             }
-            sf[(b * kMmaChunk + fgi) * kMmaN + fn] = h2f(fscale);
+            sf[(b * kMmaChunk + fgi) * NT + fn] = h2f(fscale);
             fence_proxy_async();  // the MMAs read these bytes through the async proxy
             mbar_arrive(&bready[b]);
         };
@@ -333,22 +344,23 @@ static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs
             tc_fence_after();
             for (uint32_t gi = 0; gi < gn && ok; ++gi) {
                 uint32_t d[kMmaCols];
-                const uint32_t taddr = tmem + ((quad * 32u) << 16) + (b * kMmaChunk + gi) * kMmaN + col0;
-                tmem_ld32(taddr, d);
-                tmem_ld32(taddr + 32u, d + 32);
+                const uint32_t taddr = tmem + ((quad * 32u) << 16) + (b * kMmaChunk + gi) * NT + col0;
+#pragma unroll
+                for (uint32_t q = 0; q < kMmaCols / 32; ++q)
+                    tmem_ld32(taddr + 32u * q, d + 32 * q);
                 tmem_wait();
                 const uint32_t g = g0 + gi;
                 if (dot_groups) {
                     if (live)
 #pragma unroll
                         for (uint32_t j = 0; j < kMmaCols; ++j) {
-                            const uint32_t on = nt * kMmaN + col0 + j;
+                            const uint32_t on = nt * NT + col0 + j;
                             if (on < a.n)
                                 store_i16_any(a.out + (size_t)m * a.out_stride + ((size_t)on * G + g) * 2u,
                                               (int16_t)(int32_t)d[j]);
                         }
                 } else {
-                    const float4* sc4 = reinterpret_cast<const float4*>(sf + (b * kMmaChunk + gi) * kMmaN + col0);
+                    const float4* sc4 = reinterpret_cast<const float4*>(sf + (b * kMmaChunk + gi) * NT + col0);
 #pragma unroll
                     for (uint32_t q = 0; q < kMmaCols / 4; ++q) {
                         const float4 sc = sc4[q];
@@ -383,7 +395,7 @@ static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs
                 y[2 * j + 1] = f2_hi(v);
             }
             unsigned char* orow = a.out + (size_t)m * a.out_stride;
-            const uint32_t n0 = nt * kMmaN + col0;
+            const uint32_t n0 = nt * NT + col0;
             if (a.epi == kEpiSwiGLU) {
                 // weight blocks 2k (gate rows) and 2k + 1 (up rows) hold the same
                 // 8 FFN rows: h[k * 8 + r] (w1a8_gemv.cuh)
@@ -428,14 +440,29 @@ static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs
     }
 }
 
-// Launches the contraction of `a.m` rows (a.m <= 65535 * kMmaM) on `s`.
+// Launches the contraction of `a.m` rows (a.m <= 65535 * kMmaM) on `s`:
+// 128-wide tiles, or 64-wide when the wide grid would leave SMs idle.
 inline cudaError_t launch_mma(const MmaArgs& a, cudaStream_t s) {
-    const MmaSmem p = mma_smem_plan(a.groups);
-    cudaError_t e = cudaFuncSetAttribute(w1a8_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.total);
+    static int sms = 0;
+    if (sms == 0) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+            sms = 148;
+    }
+    const uint32_t mtiles = (a.m + kMmaM - 1) / kMmaM;
+    const bool narrow = (size_t)((a.n + kMmaN - 1) / kMmaN) * mtiles < (size_t)sms;
+    const uint32_t nt = narrow ? kMmaNarrow : kMmaN;
+    const MmaSmem p = mma_smem_plan(nt);
+    const void* fn = narrow ? (const void*)w1a8_mma_kernel<kMmaNarrow> : (const void*)w1a8_mma_kernel<kMmaN>;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.total);
     if (e != cudaSuccess)
         return e;
-    const dim3 grid((a.n + kMmaN - 1) / kMmaN, (a.m + kMmaM - 1) / kMmaM);
-    w1a8_mma_kernel<<<grid, kMmaThreads, p.total, s>>>(a);
+    const dim3 grid((a.n + nt - 1) / nt, mtiles);
+    if (narrow)
+        w1a8_mma_kernel<kMmaNarrow><<<grid, kMmaThreads, p.total, s>>>(a);
+    else
+        w1a8_mma_kernel<kMmaN><<<grid, kMmaThreads, p.total, s>>>(a);
     return cudaGetLastError();
 }
 
