@@ -270,6 +270,43 @@ static BNN_Status bnn_b200_matrix_create_limited(BNN_Device device, const BNN_Ma
     return BNN_OK;
 }
 
+BNN_Status bnn_b200_matrix_alloc(BNN_Device device, uint32_t in_features, uint32_t out_features,
+                                 BNN_Matrix* out_matrix) {
+    if (out_matrix == nullptr)
+        return BNN_EINVAL;
+    *out_matrix = nullptr;
+    if (device == nullptr || in_features == 0 || in_features % kGroupSize != 0 || out_features == 0)
+        return BNN_EINVAL;
+    bnn::DeviceGuard guard(device->ordinal);
+    if (!guard.ok())
+        return BNN_EIO;
+    auto* m = new (std::nothrow) bnn_accel_matrix();
+    if (!m)
+        return BNN_ENOMEM;
+    const uint32_t groups = in_features / kGroupSize;
+    size_t nblocks = (out_features + bnn::kRowBlock - 1) / bnn::kRowBlock;
+    nblocks = (nblocks + bnn::kBlockPad - 1) / bnn::kBlockPad * bnn::kBlockPad;
+    const size_t packed_bytes = nblocks * bnn::block_bytes(groups);
+    if (cudaMalloc(&m->wblocks, packed_bytes) != cudaSuccess) {
+        cudaGetLastError();
+        delete m;
+        return BNN_ENOMEM;
+    }
+    if (cudaMemsetAsync(m->wblocks, 0, packed_bytes, device->stream) != cudaSuccess ||
+        cudaStreamSynchronize(device->stream) != cudaSuccess) {
+        cudaFree(m->wblocks);
+        delete m;
+        return BNN_EIO;
+    }
+    m->owner = device;
+    m->in_features = in_features;
+    m->out_features = out_features;
+    m->groups = groups;
+    ++device->matrix_count;
+    *out_matrix = m;
+    return BNN_OK;
+}
+
 BNN_Status BNN_MatrixCreate(BNN_Device device, const BNN_MatrixDesc* desc, BNN_Matrix* out_matrix) {
     return bnn_b200_matrix_create_limited(device, desc, out_matrix, kMaxFeatures);
 }

@@ -34,6 +34,12 @@ struct bnn_accel_buffer {
     unsigned char* data;      // device memory
 };
 
+// A matrix of in x out features whose packed blocks are zero (every bit -1,
+// every scale +0); the caller fills them on the device (the engine's Q1_0
+// loader). Counts towards the device's matrices like BNN_MatrixCreate.
+extern "C" BNN_Status bnn_b200_matrix_alloc(BNN_Device device, uint32_t in_features, uint32_t out_features,
+                                            BNN_Matrix* out_matrix);
+
 namespace bnn {
 
 // Makes `ordinal` current for the lifetime of the guard, restoring the

@@ -173,79 +173,6 @@ struct Linear {
     ~Linear() { BNN_MatrixDestroy(m); }
 };
 
-// Host staging for one (possibly row-concatenated) W1 matrix.
-struct HostW1 {
-    uint32_t in = 0, out = 0;
-    std::vector<uint8_t> bits;
-    std::vector<uint16_t> scales;
-};
-
-// Appends rows [row0, row0 + rows) of the [out][in] Q1_0 tensor `name` to
-// dst (all rows when rows == UINT32_MAX).
-BNND_Status read_q1_0(const bnn::GgufFile& g, const std::string& name, uint32_t in, uint32_t out_total,
-                      HostW1* dst, uint32_t row0 = 0, uint32_t rows = UINT32_MAX) {
-    const bnn::GgufTensor* t = g.tensor(name);
-    if (!t || t->type != 41 || t->dims.size() != 2 || t->dims[0] != in || t->dims[1] != out_total ||
-        in % 128 != 0)
-        return fail(BNND_EFORMAT, "unexpected Q1_0 tensor '%s' shape or type", name.c_str());
-    if (rows == UINT32_MAX)
-        rows = out_total - row0;
-    if (row0 > out_total || rows > out_total - row0)
-        return fail(BNND_EINVAL, "row range of '%s' outside the tensor", name.c_str());
-    const uint32_t out = rows;
-    if (dst->bits.empty())
-        dst->in = in;
-    if (dst->in != in)
-        return fail(BNND_EFORMAT, "tensor '%s' input width differs", name.c_str());
-    const size_t groups = in / 128, row_bytes = in / 8;
-    const size_t r0 = dst->out;
-    dst->out += out;
-    dst->bits.resize((size_t)dst->out * row_bytes);
-    dst->scales.resize((size_t)dst->out * groups);
-    for (size_t o = 0; o < out; ++o) {
-        for (size_t grp = 0; grp < groups; ++grp) {
-            const uint8_t* blk = t->data + ((row0 + o) * groups + grp) * 18;
-            const uint16_t sc = (uint16_t)(blk[0] | (blk[1] << 8));
-            if (!std::isfinite(half_bits_to_float(sc)))
-                return fail(BNND_EFORMAT, "Q1_0 scale in '%s' is not finite", name.c_str());
-            dst->scales[(r0 + o) * groups + grp] = sc;
-            std::memcpy(&dst->bits[(r0 + o) * row_bytes + grp * 16], blk + 2, 16);
-        }
-    }
-    return BNND_OK;
-}
-
-// Reorders a [gate(F); up(F)] row stack into alternating 8-row blocks
-// (gate 0-7, up 0-7, gate 8-15, ...) for the SwiGLU epilogue, which pairs
-// block 2p (gate) with block 2p+1 (up). Row order does not change any output.
-void interleave_blocks(HostW1* h, uint32_t f) {
-    const size_t rb = h->in / 8, sg = h->in / 128;
-    std::vector<uint8_t> bits(h->bits.size());
-    std::vector<uint16_t> scales(h->scales.size());
-    for (uint32_t row = 0; row < 2 * f; ++row) {
-        const uint32_t up = row >= f, r = up ? row - f : row;
-        const size_t dst = (size_t)(r / 8) * 16 + (up ? 8 : 0) + r % 8;
-        std::memcpy(&bits[dst * rb], &h->bits[(size_t)row * rb], rb);
-        std::memcpy(&scales[dst * sg], &h->scales[(size_t)row * sg], sg * 2);
-    }
-    h->bits.swap(bits);
-    h->scales.swap(scales);
-}
-
-BNND_Status upload_w1(BNN_Device dev, const HostW1& h, Linear* l) {
-    BNN_MatrixDesc d;
-    d.in_features = h.in;
-    d.out_features = h.out;
-    d.group_size = 128;
-    d.weight_bits = h.bits.data();
-    d.weight_bytes = h.bits.size();
-    d.scale_fp16 = h.scales.data();
-    d.scale_count = h.scales.size();
-    l->in = h.in;
-    l->out = h.out;
-    return from_accel(bnn_b200_matrix_create_unbounded(dev, &d, &l->m), "matrix upload");
-}
-
 BNND_Status read_f32(const bnn::GgufFile& g, const std::string& name, size_t count, DevMem* dst,
                      std::vector<float>* host = nullptr) {
     const bnn::GgufTensor* t = g.tensor(name);
@@ -436,6 +363,63 @@ BNND_Status shard_plan(const BNND_ModelInfo& in, uint32_t world, uint32_t rank, 
     return BNND_OK;
 }
 
+// ---- GGUF -> device loader: Q1_0 tensors are uploaded as they are in the
+// file and repacked into the contraction's layout by q1_0_pack_kernel.
+struct DeviceLoader {
+    BNN_Device dev = nullptr;
+    DevMem stage, bad;  // raw Q1_0 rows of one tensor; the scale check word
+    size_t cap = 0;
+};
+
+BNND_Status w1_alloc(DeviceLoader* ld, uint32_t in, uint32_t out, Linear* l) {
+    l->in = in;
+    l->out = out;
+    return from_accel(bnn_b200_matrix_alloc(ld->dev, in, out, &l->m), "matrix allocation");
+}
+
+// Rows row0 .. row0 + rows - 1 of Q1_0 tensor `name` ([out_total][in]) into
+// l's rows from dst_row0 (half < 0), or interleaved as gate (half 0) or up
+// (half 1) blocks.
+BNND_Status w1_add(DeviceLoader* ld, const bnn::GgufFile& g, const std::string& name, uint32_t in,
+                   uint32_t out_total, Linear* l, uint32_t dst_row0, int half, uint32_t row0 = 0,
+                   uint32_t rows = UINT32_MAX) {
+    const bnn::GgufTensor* t = g.tensor(name);
+    if (!t || t->type != 41 || t->dims.size() != 2 || t->dims[0] != in || t->dims[1] != out_total ||
+        in % 128 != 0 || l->in != in)
+        return fail(BNND_EFORMAT, "unexpected Q1_0 tensor '%s' shape or type", name.c_str());
+    if (rows == UINT32_MAX)
+        rows = out_total - row0;
+    if (row0 > out_total || rows > out_total - row0)
+        return fail(BNND_EINVAL, "row range of '%s' outside the tensor", name.c_str());
+    const uint32_t groups = in / 128;
+    const size_t bytes = (size_t)rows * groups * 18u;
+    BNND_Status st;
+    if (ld->cap < bytes) {
+        ld->stage = DevMem();
+        ld->cap = 0;
+        if ((st = dev_alloc(ld->stage, bytes)))
+            return st;
+        ld->cap = bytes;
+    }
+    if (!ld->bad.p && (st = dev_alloc(ld->bad, 4)))
+        return st;
+    const cudaStream_t s = ld->dev->stream;
+    CUDA_OR(cudaMemsetAsync(ld->bad.p, 0, 4, s), BNND_EIO);
+    CUDA_OR(cudaMemcpyAsync(ld->stage.p, t->data + (size_t)row0 * groups * 18u, bytes, cudaMemcpyHostToDevice, s),
+            BNND_EIO);
+    const size_t units = (size_t)rows * groups;
+    const unsigned grid = (unsigned)std::min<size_t>((units + 255) / 256, 148u * 16u);
+    bnn::eng::q1_0_pack_kernel<<<grid, 256, 0, s>>>(ld->stage.as<uint8_t>(), rows, groups, dst_row0, half,
+                                                   l->m->wblocks, ld->bad.as<int>());
+    int bad = 0;
+    CUDA_OR(cudaGetLastError(), BNND_EIO);
+    CUDA_OR(cudaMemcpyAsync(&bad, ld->bad.p, 4, cudaMemcpyDeviceToHost, s), BNND_EIO);
+    CUDA_OR(cudaStreamSynchronize(s), BNND_EIO);
+    if (bad)
+        return fail(BNND_EFORMAT, "Q1_0 scale in '%s' is not finite", name.c_str());
+    return BNND_OK;
+}
+
 BNND_Status load_qwen3(const bnn::GgufFile& g, bnnd_model* m) {
     uint64_t L = 0, C = 0, FF = 0, H = 0, Hk = 0, kl = 0, vl = 0, ctx = 0;
     g.get_u64("qwen3.block_count", &L);
@@ -495,18 +479,17 @@ BNND_Status load_qwen3(const bnn::GgufFile& g, bnnd_model* m) {
     st = read_f32(g, "output_norm.weight", C, &m->out_norm);
     if (st != BNND_OK)
         return st;
+    DeviceLoader ld;
+    ld.dev = m->dev;
     {
-        HostW1 head;
-        st = read_q1_0(g, "token_embd.weight", (uint32_t)C, V, &head);
-        if (st == BNND_OK)
-            st = upload_w1(m->dev, head, sh.world > 1 ? &m->embed : &m->lm_head);
-        if (st == BNND_OK && sh.world > 1) {
-            HostW1 part;
-            st = read_q1_0(g, "token_embd.weight", (uint32_t)C, V, &part, sh.v_begin, sh.v_rows);
-            if (st == BNND_OK)
-                st = upload_w1(m->dev, part, &m->lm_head);
-        }
-        if (st != BNND_OK)
+        Linear* full = sh.world > 1 ? &m->embed : &m->lm_head;
+        if ((st = w1_alloc(&ld, (uint32_t)C, V, full)) != BNND_OK ||
+            (st = w1_add(&ld, g, "token_embd.weight", (uint32_t)C, V, full, 0, -1)) != BNND_OK)
+            return st;
+        if (sh.world > 1 &&
+            ((st = w1_alloc(&ld, (uint32_t)C, sh.v_rows, &m->lm_head)) != BNND_OK ||
+             (st = w1_add(&ld, g, "token_embd.weight", (uint32_t)C, V, &m->lm_head, 0, -1, sh.v_begin, sh.v_rows)) !=
+                 BNND_OK))
             return st;
     }
     uint64_t weights = (uint64_t)C * V;
@@ -518,22 +501,25 @@ BNND_Status load_qwen3(const bnn::GgufFile& g, bnnd_model* m) {
             (st = read_f32(g, p + "attn_q_norm.weight", HD, &layer->q_norm)) != BNND_OK ||
             (st = read_f32(g, p + "attn_k_norm.weight", HD, &layer->k_norm)) != BNND_OK)
             return st;
-        HostW1 qkv, o, gu, down;
         // this rank's rows (all of them for world 1): whole GQA groups of
-        // q|k|v, matching gate and up ranges, o and down output ranges
-        if ((st = read_q1_0(g, p + "attn_q.weight", C, C, &qkv, sh.q_begin, sh.q_rows)) != BNND_OK ||
-            (st = read_q1_0(g, p + "attn_k.weight", C, KV, &qkv, sh.kv_begin, sh.kv_rows)) != BNND_OK ||
-            (st = read_q1_0(g, p + "attn_v.weight", C, KV, &qkv, sh.kv_begin, sh.kv_rows)) != BNND_OK ||
-            (st = read_q1_0(g, p + "attn_output.weight", C, C, &o, sh.c_begin, sh.c_rows)) != BNND_OK ||
-            (st = read_q1_0(g, p + "ffn_gate.weight", C, FF, &gu, sh.f_begin, sh.f_rows)) != BNND_OK ||
-            (st = read_q1_0(g, p + "ffn_up.weight", C, FF, &gu, sh.f_begin, sh.f_rows)) != BNND_OK ||
-            (st = read_q1_0(g, p + "ffn_down.weight", FF, C, &down, sh.c_begin, sh.c_rows)) != BNND_OK)
-            return st;
-        interleave_blocks(&gu, sh.f_rows);
-        if ((st = upload_w1(m->dev, qkv, &layer->qkv)) != BNND_OK ||
-            (st = upload_w1(m->dev, o, &layer->o)) != BNND_OK ||
-            (st = upload_w1(m->dev, gu, &layer->gu)) != BNND_OK ||
-            (st = upload_w1(m->dev, down, &layer->down)) != BNND_OK)
+        // q|k|v, matching gate and up ranges (interleaved by 8-row blocks for
+        // the SwiGLU epilogue), o and down output ranges
+        const uint32_t Cq = sh.q_rows, Ck = sh.kv_rows;
+        if ((st = w1_alloc(&ld, C, Cq + 2 * Ck, &layer->qkv)) != BNND_OK ||
+            (st = w1_add(&ld, g, p + "attn_q.weight", C, C, &layer->qkv, 0, -1, sh.q_begin, Cq)) != BNND_OK ||
+            (st = w1_add(&ld, g, p + "attn_k.weight", C, KV, &layer->qkv, Cq, -1, sh.kv_begin, Ck)) != BNND_OK ||
+            (st = w1_add(&ld, g, p + "attn_v.weight", C, KV, &layer->qkv, Cq + Ck, -1, sh.kv_begin, Ck)) !=
+                BNND_OK ||
+            (st = w1_alloc(&ld, C, sh.c_rows, &layer->o)) != BNND_OK ||
+            (st = w1_add(&ld, g, p + "attn_output.weight", C, C, &layer->o, 0, -1, sh.c_begin, sh.c_rows)) !=
+                BNND_OK ||
+            (st = w1_alloc(&ld, C, 2 * sh.f_rows, &layer->gu)) != BNND_OK ||
+            (st = w1_add(&ld, g, p + "ffn_gate.weight", C, FF, &layer->gu, 0, 0, sh.f_begin, sh.f_rows)) !=
+                BNND_OK ||
+            (st = w1_add(&ld, g, p + "ffn_up.weight", C, FF, &layer->gu, 0, 1, sh.f_begin, sh.f_rows)) != BNND_OK ||
+            (st = w1_alloc(&ld, FF, sh.c_rows, &layer->down)) != BNND_OK ||
+            (st = w1_add(&ld, g, p + "ffn_down.weight", FF, C, &layer->down, 0, -1, sh.c_begin, sh.c_rows)) !=
+                BNND_OK)
             return st;
         weights += (uint64_t)C * (C + 2 * KV) + (uint64_t)C * C + 3ull * C * FF;
         m->layers.push_back(std::move(layer));
@@ -543,6 +529,8 @@ BNND_Status load_qwen3(const bnn::GgufFile& g, bnnd_model* m) {
 }
 
 BNND_Status load_mlp(const bnn::GgufFile& g, bnnd_model* m) {
+    DeviceLoader ld;
+    ld.dev = m->dev;
     uint64_t blocks = 0, in = 0, classes = 0, pixels = 0;
     float stdv = 1.0f;
     g.get_u64("bnn-mlp.block_count", &blocks);
@@ -572,10 +560,11 @@ BNND_Status load_mlp(const bnn::GgufFile& g, bnnd_model* m) {
         if (lin != expected)
             return fail(BNND_EFORMAT, "layer %u input width %u does not match previous output %u", i, lin,
                         expected);
-        HostW1 w;
-        BNND_Status st = read_q1_0(g, p + "weight", lin, lout, &w);
+        if (lin % 128 != 0)
+            return fail(BNND_EFORMAT, "unexpected Q1_0 tensor '%sweight' shape or type", p.c_str());
+        BNND_Status st = w1_alloc(&ld, lin, lout, &layer->w);
         if (st == BNND_OK)
-            st = upload_w1(m->dev, w, &layer->w);
+            st = w1_add(&ld, g, p + "weight", lin, lout, &layer->w, 0, -1);
         if (st == BNND_OK)
             st = read_f32(g, p + "post_scale", lout, &layer->post_scale);
         if (st == BNND_OK)

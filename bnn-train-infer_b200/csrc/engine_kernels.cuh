@@ -564,6 +564,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     }
 }
 
+// GGUF Q1_0 rows straight into the contraction's packed blocks (loader).
+// A Q1_0 block is 18 bytes per 128 weights: the binary16 scale
+// (little-endian) then 16 sign bytes in the public bit order
+// (linear.c:26-62). Source row o of the slice goes to matrix row
+// dst_row0 + o, or with half >= 0 to the interleaved gate/up position
+// (o / 8) * 16 + half * 8 + o % 8. A non-finite scale sets *bad.
+__global__ void q1_0_pack_kernel(const uint8_t* raw, uint32_t rows, uint32_t groups, uint32_t dst_row0, int half,
+                                 unsigned char* wblocks, int* bad) {
+    const size_t total = (size_t)rows * groups;
+    const size_t bb = (size_t)groups * 144u;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t o = (uint32_t)(i / groups), g = (uint32_t)(i % groups);
+        const uint8_t* src = raw + i * 18u;
+        const uint32_t row = half < 0 ? dst_row0 + o : (o / 8u) * 16u + (uint32_t)half * 8u + o % 8u;
+        const uint32_t blk = row / kRowBlock, r = row % kRowBlock;
+        const uint16_t sc = (uint16_t)(src[0] | (src[1] << 8));
+        if ((sc & 0x7c00u) == 0x7c00u)
+            atomicOr(bad, 1);
+        uint32_t w[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+            w[t] = (uint32_t)src[2 + 4 * t] | ((uint32_t)src[3 + 4 * t] << 8) | ((uint32_t)src[4 + 4 * t] << 16) |
+                   ((uint32_t)src[5 + 4 * t] << 24);
+        unsigned char* b = wblocks + (size_t)blk * bb;
+        *reinterpret_cast<uint4*>(b + ((size_t)g * kRowBlock + r) * 16u) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint16_t*>(b + (size_t)groups * 128u + ((size_t)r * groups + g) * 2u) = sc;
+    }
+}
+
 // End of a decode step: advance every row's position; the greedy pick (the
 // lm_head epilogue's packed key: index = ~low word) becomes the next input
 // and is appended to the generation history.
