@@ -442,9 +442,32 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, 2) w1a8_gemv_kernel(
                     if (work && n < a.n) {
                         const uint16_t* sc = sc_blk + rr * G;
                         const int16_t* dd = blk_d + (mm * kRowBlock + rr) * G;
+                        if ((G & 7u) == 0) {
+                            // eight groups per pair of 16-byte loads; D (|D| <= 16256)
+                            // to float exactly through the 1.5 * 2^23 bias
+                            for (uint32_t g0 = 0; g0 < G; g0 += 8) {
+                                const uint4 sv = *reinterpret_cast<const uint4*>(sc + g0);
+                                const uint4 dv = *reinterpret_cast<const uint4*>(dd + g0);
+                                const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+                                const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
+                                float p[8];
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) {
+                                    const int d0 = (int)(int16_t)(dw[j] & 0xffffu), d1 = (int)(int16_t)(dw[j] >> 16);
+                                    const float f0 = __fsub_rn(__int_as_float(0x4b400000 + d0), 12582912.0f);
+                                    const float f1 = __fsub_rn(__int_as_float(0x4b400000 + d1), 12582912.0f);
+                                    p[2 * j] = __fmul_rn(h2f((uint16_t)(sw[j] & 0xffffu)), f0);
+                                    p[2 * j + 1] = __fmul_rn(h2f((uint16_t)(sw[j] >> 16)), f1);
+                                }
+#pragma unroll
+                                for (int j = 0; j < 8; ++j)
+                                    acc = __fadd_rn(acc, p[j]);
+                            }
+                        } else {
 #pragma unroll 8
-                        for (uint32_t g = 0; g < G; ++g)
-                            acc = __fadd_rn(acc, __fmul_rn(h2f(sc[g]), (float)dd[g]));
+                            for (uint32_t g = 0; g < G; ++g)
+                                acc = __fadd_rn(acc, __fmul_rn(h2f(sc[g]), (float)dd[g]));
+                        }
                         if (PRO != kProSliced || a.row_scale)
                             acc = __fmul_rn(acc, rs_s[mm]);
                         if (EPI == kEpiView) {
