@@ -540,6 +540,7 @@ def run_sweep(args):
                                                      ctypes.POINTER(ctypes.c_void_p)]
     stream = torch.cuda.ExternalStream(dll.bnn_b200_device_stream(dev.handle))
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 2 x L2
+    flush_sink = torch.empty((), dtype=torch.uint8, device="cuda")
     hbm, hbm_kind = measured_peaks()
     rng = synth.rng_for(1)
     results = []
@@ -576,7 +577,10 @@ def run_sweep(args):
                 times = []
                 for i in range(args.warmup + args.steps):
                     with torch.cuda.stream(stream):
+                        # L2 flush: write a buffer twice the L2, then read it, so the
+                        # flush's dirty lines are written back before the timed job
                         flush.fill_(i & 0xff)
+                        flush_sink.copy_(flush.max())
                         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                         e0.record(stream)
                         if dll.bnn_b200_execute_async(dev.handle, ctypes.byref(job)) != accel.OK:
@@ -634,7 +638,7 @@ def run_sweep(args):
         "data": "synthetic (seeded W1 bits, FP16 scales ~U[0.005,0.05], FP32 N(0,1) activations with 1% x20)",
         "config": {"workload": "configs[1]: single-op GEMV_F32 / DOT_GROUPS sweep at the Qwen3-1.7B linear "
                                "shapes, rows = 1 (value: GEMV_F32 2048x151669 as one job)",
-                   "l2": "flushed (256 MB write) before every timed job", "shapes": results},
+                   "l2": "flushed before every timed job (256 MB written, then read back, so no dirty flush lines are written back inside the timed job)", "shapes": results},
         "roofline": {"bound": "hbm", "achieved": head["gbs"], "peak": hbm, "unit": "GB/s",
                      "frac": round(head["gbs"] / hbm, 4), "peak_source": hbm_kind, "traffic": None,
                      "what": "prep + contraction of one GEMV_F32 job (kernel time), algorithmic bytes"},

@@ -1,8 +1,8 @@
 // bnn_sync.cuh - mbarrier and bulk-copy (TMA 1D) helpers with bounded waits.
 //
-// Every wait here gives up after a bounded number of polls and reports it,
-// so a logic error can never leave a GPU spinning forever: the caller sets
-// an error bit that the host maps to BNN_ETIMEOUT.
+// Every wait here gives up after a bounded time (and a bounded number of
+// polls) and reports it, so a logic error can never leave a GPU spinning
+// forever: the caller sets an error bit that the host maps to BNN_ETIMEOUT.
 #pragma once
 
 #include <cstdint>
@@ -10,8 +10,20 @@
 namespace bnn {
 
 constexpr int kStatusTimeout = 2;
-// ~ seconds of polling at worst; a healthy wait completes in microseconds.
+// A healthy wait completes in microseconds; a wait gives up after one second
+// of device time (or this many polls, whichever comes first).
 constexpr uint32_t kWaitPollLimit = 1u << 26;
+constexpr uint64_t kWaitNsLimit = 1000000000ull;
+// Suspend-time hint of a blocking poll: a waiting warp sleeps until the phase
+// completes (or this many ns pass) instead of re-issuing the poll, so waiting
+// producer/consumer warps leave the issue slots to the warps doing the work.
+constexpr uint32_t kSuspendHintNs = 20000u;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -51,11 +63,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete; false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kWaitPollLimit; ++i)
-        if (mbar_try_wait(bar, parity))
+    if (mbar_try_wait(bar, parity))
+        return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 0; i < kWaitPollLimit; ++i) {
+        if (mbar_try_wait_suspend(bar, parity))
             return true;
+        if (globaltimer_ns() - t0 > kWaitNsLimit)
+            return false;
+    }
     return false;
 }
 

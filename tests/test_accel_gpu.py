@@ -220,3 +220,50 @@ def test_extremes_and_special_scales(b200_device, oracle_mod):
         want, _, _ = oracle_mod.gemm_f32(bits, scales, x)
         got = accel.run_op(b200_device, accel.OP_GEMM_F32, bits, scales, x)
         assert bits_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def _unbounded_matrix(device, bits, scales):
+    """A matrix past the reference's 8192-row cap (bnn_b200_matrix_create_unbounded,
+    how the device engine holds lm_head): its contraction runs several rounds of
+    tiles per CTA."""
+    import ctypes
+    dll = device.api.dll
+    fn = dll.bnn_b200_matrix_create_unbounded
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p, ctypes.POINTER(accel.MatrixDesc), ctypes.POINTER(ctypes.c_void_p)]
+    n, kb = bits.shape
+    desc = accel.MatrixDesc(kb * 8, n, accel.GROUP, bits.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)),
+                            bits.nbytes, scales.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16)), scales.size)
+    h = ctypes.c_void_p()
+    assert fn(device.handle, ctypes.byref(desc), ctypes.byref(h)) == accel.OK
+    m = accel.Matrix.__new__(accel.Matrix)
+    m.device, m.k, m.n, m.handle = device, kb * 8, n, h
+    return m
+
+
+def test_multi_round_tiles(b200_device, oracle_mod):
+    """4741 blocks of 8 rows on 2 x 148 CTAs of 8-block tiles: each CTA loops
+    over two or three tiles through its shared-memory ring (the last tile
+    partly past the matrix). GEMV_F32 and DOT_GROUPS stay bit-exact."""
+    rng = synth.rng_for(9, salt=1)
+    k, n = 256, 8 * 4741 - 3
+    bits, scales = synth.w1_matrix(rng, k, n)
+    bits, scales = np.ascontiguousarray(bits), np.ascontiguousarray(scales)
+    x = synth.activations(rng, 1, k)
+    want, q, _ = oracle_mod.gemm_f32(bits, scales, x)
+    m = _unbounded_matrix(b200_device, bits, scales)
+    bi, bq, bo, bd = (accel.Buffer(b200_device, k * 4), accel.Buffer(b200_device, k),
+                      accel.Buffer(b200_device, n * 4), accel.Buffer(b200_device, n * (k // 128) * 2))
+    try:
+        bi.write(np.ascontiguousarray(x[0], dtype=np.float32))
+        assert b200_device.execute(accel.OP_GEMV_F32, m, bi, bo, rows=1) == accel.OK
+        got = bo.read(n * 4).view(np.float32)
+        assert bits_equal(got.view(np.uint32), want[0].view(np.uint32))
+        bq.write(np.ascontiguousarray(q[0], dtype=np.int8))
+        assert b200_device.execute(accel.OP_DOT_GROUPS, m, bq, bd, rows=1) == accel.OK
+        d = bd.read(n * (k // 128) * 2).view(np.int16).reshape(1, -1)
+        assert np.array_equal(d, oracle_mod.dot_groups(bits, scales, q).reshape(1, -1))
+    finally:
+        for b in (bi, bq, bo, bd):
+            b.free()
+        m.destroy()

@@ -222,3 +222,27 @@ def test_dropin_reference_tools_match(oracle_mod, models, tmp_path):
         assert r.returncode == 0, r.stderr
         outs.append(out.read_bytes())
     assert outs[0] == outs[1]
+
+
+# a 40000-row lm_head (5000 blocks: 625 8-block tiles on 296 CTAs) runs more
+# than one round of tiles per CTA through the shared-memory ring
+ROUNDS = gguf.Qwen3Shape(layers=1, hidden=256, heads=2, kv_heads=1, head_dim=128, ffn=512, vocab=40000,
+                         context=64)
+
+
+def test_multi_round_lm_head_logits(b200_device, ref_engine_mod, tmp_path):
+    path = gguf.qwen3_model(tmp_path / "rounds.gguf", ROUNDS, seed=14)
+    rng = np.random.default_rng(6)
+    ids = rng.integers(0, ROUNDS.vocab, size=5).astype(np.int32)
+    ref = ref_engine_mod.RefEngine(path, n_ctx=32)
+    m = engine.Model(b200_device, path)
+    ctx = engine.Context(m, n_ctx=32)
+    try:
+        for i, t in enumerate(ids):
+            want = ref.decode([t])
+            got = ctx.decode([t])[0]
+            assert np.array_equal(bits(got), bits(want)), f"position {i}"
+    finally:
+        ctx.free()
+        m.free()
+        ref.close()
