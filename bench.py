@@ -165,15 +165,16 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def ncu_traffic():
+def ncu_traffic(metric):
     """Per-launch DRAM bytes of the contraction kernel from the committed ncu
-    summary (profiles/roofline_traffic.json), if one matches this workload."""
+    summary (profiles/roofline_traffic.json), if one matches this workload's
+    metric (None otherwise)."""
     p = ROOT / "profiles" / "roofline_traffic.json"
     if not p.exists():
         return None
     try:
         d = json.loads(p.read_text())
-        return d.get(METRIC)
+        return d.get(metric)
     except (ValueError, OSError):
         return None
 
@@ -311,7 +312,7 @@ def run_b200(args):
     launches, kms, kbytes = by_kernel["w1a8_contract_kernel"]
     peak, peak_kind = measured_peaks()
     achieved = kbytes / (kms / 1e3) / 1e9
-    traffic = ncu_traffic()
+    traffic = ncu_traffic(METRIC + ("_8ctx" if args.config5 else ""))
     roofline = {
         "kernel": "w1a8_contract_kernel", "dominant_kernel": dominant, "bound": "hbm",
         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -518,6 +519,8 @@ def run_classify(args):
 
 
 SWEEP_SHAPES = [(2048, 2048), (2048, 1024), (2048, 6144), (6144, 2048), (2048, 151669)]  # (K, N)
+SWEEP_STREAM = 8            # device copies of a large matrix for the job-stream timing
+L2_BYTES = 126 << 20        # B200 L2
 
 
 def run_sweep(args):
@@ -558,8 +561,12 @@ def run_sweep(args):
         m.device, m.k, m.n, m.handle = dev, k, n, h
         return m
 
+    shapes = SWEEP_SHAPES
+    if args.sweep_shape:
+        k_, n_ = (int(v) for v in args.sweep_shape.lower().split("x"))
+        shapes = [(k_, n_)]
     with ClockSampler(0) as clocks:
-        for k, n in SWEEP_SHAPES:
+        for k, n in shapes:
             bits, scales = synth.w1_matrix(rng, k, n)
             x = synth.activations(rng, 1, k)
             scale = float(np.abs(x).max()) / 127.0
@@ -592,6 +599,35 @@ def run_sweep(args):
                 if dll.bnn_b200_sync(dev.handle) != accel.OK:
                     raise accel.BnnError(-1, "sync")
                 us = statistics.median(times) * 1e3
+                # Matrices larger than L2 / 3 are also timed as a stream of jobs: the
+                # job runs on SWEEP_STREAM device copies of the matrix in turn (together
+                # more than twice the L2, so every job reads its weights from HBM), all
+                # jobs between one pair of events, per-job time = elapsed / jobs. This
+                # leaves out the launch latency and the 2 us event granularity that a
+                # single timed job carries.
+                stream_us = None
+                wbytes = n * k * 0.140625
+                if wbytes * SWEEP_STREAM > 2 * L2_BYTES:
+                    copies = [m] + [matrix(bits, scales, k, n) for _ in range(SWEEP_STREAM - 1)]
+                    sjobs = [accel.Job(operation=op, matrix=mc.handle, input=job.input, output=job.output, rows=1)
+                             for mc in copies]
+                    st_times = []
+                    for i in range(args.warmup + args.steps):
+                        with torch.cuda.stream(stream):
+                            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                            e0.record(stream)
+                            for sj in sjobs:
+                                if dll.bnn_b200_execute_async(dev.handle, ctypes.byref(sj)) != accel.OK:
+                                    raise accel.BnnError(-1, "execute_async")
+                            e1.record(stream)
+                        e1.synchronize()
+                        if i >= args.warmup:
+                            st_times.append(e0.elapsed_time(e1) / len(sjobs))
+                    if dll.bnn_b200_sync(dev.handle) != accel.OK:
+                        raise accel.BnnError(-1, "sync")
+                    stream_us = statistics.median(st_times) * 1e3
+                    for mc in copies[1:]:
+                        mc.destroy()
                 # the public synchronous path, host buffers (N > 8192: 8192-row chunks)
                 host_out = np.empty(out_bytes, dtype=np.uint8)
                 chunks = []
@@ -625,22 +661,34 @@ def run_sweep(args):
                                 "gbs": round(alg / (us * 1e-6) / 1e9, 1),
                                 "frac_of_hbm": round(alg / (us * 1e-6) / 1e9 / hbm, 4),
                                 "e2e_us": round(e2e_us, 1), "e2e_jobs": len(chunks)})
+                if stream_us is not None:
+                    results[-1].update({"stream_kernel_us": round(stream_us, 2),
+                                        "stream_gbs": round(alg / (stream_us * 1e-6) / 1e9, 1),
+                                        "stream_frac_of_hbm": round(alg / (stream_us * 1e-6) / 1e9 / hbm, 4)})
                 bi.free()
                 bo.free()
             m.destroy()
     clk = clocks.summary()
     dev.close()
-    head = [r for r in results if r["op"] == "GEMV_F32" and r["n"] == 151669][0]
+    head = [r for r in results if r["op"] == "GEMV_F32" and r["n"] == shapes[-1][1]][0]
+    head_gbs = head.get("stream_gbs", head["gbs"])
+    head_us = head.get("stream_kernel_us", head["kernel_us"])
     return {
-        "metric": "w1a8_gemv_f32_hbm_gbs", "value": head["gbs"], "unit": "GB/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(head["kernel_us"] / 1e3, 5),
+        "metric": "w1a8_gemv_f32_hbm_gbs", "value": head_gbs, "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(head_us / 1e3, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic (seeded W1 bits, FP16 scales ~U[0.005,0.05], FP32 N(0,1) activations with 1% x20)",
-        "config": {"workload": "configs[1]: single-op GEMV_F32 / DOT_GROUPS sweep at the Qwen3-1.7B linear "
-                               "shapes, rows = 1 (value: GEMV_F32 2048x151669 as one job)",
-                   "l2": "flushed before every timed job (256 MB written, then read back, so no dirty flush lines are written back inside the timed job)", "shapes": results},
-        "roofline": {"bound": "hbm", "achieved": head["gbs"], "peak": hbm, "unit": "GB/s",
-                     "frac": round(head["gbs"] / hbm, 4), "peak_source": hbm_kind, "traffic": None,
+        "config": {"workload": ("one shape of " if args.sweep_shape else "") +
+                               "configs[1]: single-op GEMV_F32 / DOT_GROUPS sweep at the Qwen3-1.7B linear "
+                               "shapes, rows = 1 (value: GEMV_F32 2048x151669 as one job, timed in a stream "
+                               "of jobs over 8 device copies of the matrix; kernel_us/gbs: one job after an "
+                               "L2 flush, launch latency included)",
+                   "l2": "kernel_us: flushed before every timed job (256 MB written, then read back, so no dirty "
+                         "flush lines are written back inside the timed job); stream_kernel_us: inputs larger "
+                         "than L2 (8 copies x 44 MB, each job's weights last touched 7 jobs earlier)",
+                   "shapes": results},
+        "roofline": {"bound": "hbm", "achieved": head_gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": round(head_gbs / hbm, 4), "peak_source": hbm_kind, "traffic": None,
                      "what": "prep + contraction of one GEMV_F32 job (kernel time), algorithmic bytes"},
         "e2e": {"value": round(head["bytes"] / (head["e2e_us"] * 1e-6) / 1e9, 1), "unit": "GB/s",
                 "h2d_bytes_per_step": 2048 * 4, "d2h_bytes_per_step": 151669 * 4,
@@ -719,6 +767,8 @@ def main():
                     help="BASELINE configs[0]: bnn-mlp classify, batch 64 (samples/s)")
     ap.add_argument("--sweep", action="store_true",
                     help="BASELINE configs[1]: single-op GEMV_F32 / DOT_GROUPS sweep (HBM GB/s)")
+    ap.add_argument("--sweep-shape", default=None,
+                    help="with --sweep: one KxN shape only (e.g. 2048x151669, for profiling)")
     ap.add_argument("--config5", action="store_true",
                     help="BASELINE configs[4]: 8 contexts, 64-token prompts, ctx 4096 (with --tp: sharded)")
     ap.add_argument("--prefill", action="store_true",
