@@ -837,7 +837,7 @@ cudaError_t enqueue_step(bnnd_context* c, bool with_logits) {
         aa.rope_sin = c->rope_sin.as<float>();
         aa.pos = c->pos_d.as<uint32_t>();
         const size_t layer_cache = (size_t)R * c->n_ctx * sh.kv_rows;
-        aa.kcache = c->kcache.as<float>() + (size_t)l * layer_cache;
+        aa.kcache = c->kcache.as<float>() + (size_t)l * (layer_cache / HD * bnn::eng::kcache_row(HD));
         aa.vcache = c->vcache.as<float>() + (size_t)l * layer_cache;
         aa.scores = c->scores.p ? c->scores.as<float>() : nullptr;
         aa.y = tp ? c->y_st.as<float>() + (size_t)c->rank * R * sh.q_rows : c->y.as<float>();
@@ -962,11 +962,13 @@ BNND_Status create_llm_context(bnnd_context* c) {
         }
     }
     const uint32_t P = c->world;
+    // V: [layers][rows][kv heads][n_ctx][HD]; K the same with kcache_row(HD) floats a position
     const size_t cache = (size_t)in.n_layers * R * c->n_ctx * sh.kv_rows * 4u;
+    const size_t kcache = cache / in.head_dim * bnn::eng::kcache_row(in.head_dim);
     if ((st = dev_alloc(c->x, (size_t)R * C * 4)) ||
         (st = dev_alloc(c->qkv, (size_t)R * (sh.q_rows + 2 * sh.kv_rows) * 4)) ||
         (st = dev_alloc(c->y, (size_t)R * C * 4)) || (st = dev_alloc(c->h, (size_t)R * F * 4)) ||
-        (st = dev_alloc(c->logits, (size_t)R * in.n_vocab * 4)) || (st = dev_alloc(c->kcache, cache)) ||
+        (st = dev_alloc(c->logits, (size_t)R * in.n_vocab * 4)) || (st = dev_alloc(c->kcache, kcache)) ||
         (st = dev_alloc(c->vcache, cache)) || (st = dev_alloc(c->pos_d, (size_t)R * 4)) ||
         (st = dev_alloc(c->tok_in, (size_t)R * 4)) || (st = dev_alloc(c->tok_next, (size_t)R * 4)) ||
         (st = dev_alloc(c->hist_count, 4)) || (st = dev_alloc(c->status, 4)) ||
@@ -1174,7 +1176,7 @@ cudaError_t enqueue_prefill_chunk(bnnd_context* c, uint32_t rows, uint32_t len, 
     for (uint32_t l = 0; l < in.n_layers; ++l) {
         const QwenLayer& L = *m->layers[l];
         const size_t layer_cache = (size_t)c->rows * c->n_ctx * KV;
-        float* kc = c->kcache.as<float>() + (size_t)l * layer_cache;
+        float* kc = c->kcache.as<float>() + (size_t)l * (layer_cache / HD * bnn::eng::kcache_row(HD));
         float* vc = c->vcache.as<float>() + (size_t)l * layer_cache;
         ck("rows_prep:qkv", prefill_prep(c, pa_sw, pa_rs, x, C, L.attn_norm.as<float>(), rows));
         ck("w1a8_mma:qkv", prefill_linear(c, pa_sw, pa_rs, L.qkv, rows, qkv, (size_t)QKV * 4u, bnn::kEpiView));

@@ -116,8 +116,8 @@ struct AttnArgs {
     const float* rope_cos;  // [n_ctx][HD/2]
     const float* rope_sin;
     const uint32_t* pos;    // [rows]
-    float* kcache;          // this layer: [rows][kv_heads][n_ctx][HD]
-    float* vcache;
+    float* kcache;          // this layer: [rows][kv_heads][n_ctx][kcache_row(HD)]
+    float* vcache;          // this layer: [rows][kv_heads][n_ctx][HD]
     float* scores;          // [rows][heads][attn_sc_stride(n_ctx)] when they do not fit in shared memory, else null
     float* y;               // output rows: this block's heads at y + row * y_stride + head * HD
     uint32_t y_stride;      // floats between output rows
@@ -128,6 +128,11 @@ struct AttnArgs {
     int* status;
     uint32_t resident_max;  // positions n up to which K and V are held whole in shared memory (0: never)
 };
+
+// Floats per K-cache position: the head vector and 4 floats of padding, so a
+// run of positions copied into shared memory with one bulk copy already has
+// the bank-spread row stride the score loops read (padding never read).
+__host__ __device__ constexpr uint32_t kcache_row(uint32_t hd) { return hd + 4u; }
 
 // Scores of one query head occupy a row of this many floats (a multiple of
 // 4, so the V pass can read four probabilities at once).
@@ -251,10 +256,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
 
     const uint32_t pos = a.pos[row], n = pos + 1;
     const uint32_t ntiles = (n + kAttnTile - 1) / kAttnTile, nloads = 2 * ntiles;
+    constexpr uint32_t kstride = kcache_row(HD);  // K rows in the cache and in shared memory
     const size_t head_base = ((size_t)row * a.kv_heads + g) * a.n_ctx * HD;
-    const float* kc = a.kcache + head_base;
+    const size_t khead_base = ((size_t)row * a.kv_heads + g) * a.n_ctx * kstride;
+    const float* kc = a.kcache + khead_base;
     const float* vc = a.vcache + head_base;
-    constexpr uint32_t kstride = HD + 4;
     const bool resident = n <= a.resident_max;
     float* kres = reinterpret_cast<float*>(ring);                // [resident_max][kstride]
     float* vres = kres + (size_t)a.resident_max * kstride;       // [resident_max][HD]
@@ -274,26 +280,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
         const uint32_t t0 = (is_k ? L : L - ntiles) * kAttnTile;
         const uint32_t rows_in = min(kAttnTile, n - t0);
         unsigned char* dst = ring + (size_t)s * plan.stage_bytes;
-        if (lane == 0)
-            mbar_arrive_expect_tx(&full[s], rows_in * HD * 4u);
-        __syncwarp();
-        if (is_k) {
-            for (uint32_t r = lane; r < rows_in; r += 32)
-                bulk_g2s(dst + (size_t)r * kstride * 4u, kc + (size_t)(t0 + r) * HD, HD * 4u, &full[s]);
-        } else if (lane == 0) {
-            bulk_g2s(dst, vc + (size_t)t0 * HD, rows_in * HD * 4u, &full[s]);
+        if (lane == 0) {
+            // K tile: padded rows, V tile: dense rows; one bulk copy each
+            const uint32_t bytes = rows_in * (is_k ? kstride : (uint32_t)HD) * 4u;
+            mbar_arrive_expect_tx(&full[s], bytes);
+            bulk_g2s(dst, is_k ? kc + (size_t)t0 * kstride : vc + (size_t)t0 * HD, bytes, &full[s]);
         }
+        __syncwarp();
     };
     if (warp == 0) {
         if (resident) {
             // every earlier position of the head at once: K rows padded, V dense
-            if (lane == 0)
-                mbar_arrive_expect_tx(&full[0], pos * HD * 4u * 2u);
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&full[0], pos * (kstride + HD) * 4u);
+                if (pos > 0) {
+                    bulk_g2s(kres, kc, pos * kstride * 4u, &full[0]);
+                    bulk_g2s(vres, vc, pos * HD * 4u, &full[0]);
+                }
+            }
             __syncwarp();
-            for (uint32_t r = lane; r < pos; r += 32)
-                bulk_g2s(kres + (size_t)r * kstride, kc + (size_t)r * HD, HD * 4u, &full[0]);
-            if (lane == 0 && pos > 0)
-                bulk_g2s(vres, vc, pos * HD * 4u, &full[0]);
         } else {
             for (uint32_t L = 0; L < kAttnStages && L < nloads; ++L)
                 issue(L);
@@ -332,7 +337,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     __syncthreads();
     // append this position's k and v to the cache (read back by later steps)
     for (uint32_t i = tid; i < HD; i += kAttnThreads) {
-        a.kcache[head_base + (size_t)pos * HD + i] = kn_s[i];
+        a.kcache[khead_base + (size_t)pos * kstride + i] = kn_s[i];
         a.vcache[head_base + (size_t)pos * HD + i] = vn_s[i];
     }
     int bad = 0;

@@ -178,7 +178,7 @@ struct KvAppendArgs {
     const float* rope_sin;
     const uint32_t* pos;    // [rows]
     const uint32_t* slot;   // [rows] KV cache row
-    float* kcache;          // this layer: [cache rows][kv_heads][n_ctx][HD]
+    float* kcache;          // this layer: [cache rows][kv_heads][n_ctx][kcache_row(HD)]
     float* vcache;
     uint32_t c, kv, kv_heads, n_ctx;
     float eps;
@@ -217,10 +217,10 @@ __global__ void kv_append_kernel(KvAppendArgs a) {
     if (!attn_norm_rope<HD>(v, gk, rc, rs, a.eps, a.exact != 0) && lane == 0)
         atomicOr(a.status, kStatusNonFinite);
     __syncwarp();
-    const size_t base = (((size_t)a.slot[row] * a.kv_heads + g) * a.n_ctx + pos) * HD;
+    const size_t cell = ((size_t)a.slot[row] * a.kv_heads + g) * a.n_ctx + pos;
     for (uint32_t i = lane; i < HD; i += 32) {
-        a.kcache[base + i] = v[i];
-        a.vcache[base + i] = qkv_row[a.c + a.kv + (size_t)g * HD + i];
+        a.kcache[cell * kcache_row(HD) + i] = v[i];
+        a.vcache[cell * HD + i] = qkv_row[a.c + a.kv + (size_t)g * HD + i];
     }
 }
 
@@ -248,7 +248,7 @@ struct PfAttnArgs {
     const float* rope_sin;
     const uint32_t* pos;    // [rows]: consecutive positions within a row of the chunk
     const uint32_t* slot;   // [rows] KV cache row
-    const float* kcache;    // this layer: [cache rows][kv_heads][n_ctx][HD]
+    const float* kcache;    // this layer: [cache rows][kv_heads][n_ctx][kcache_row(HD)]
     const float* vcache;
     float* scores;          // [rows][heads][sc_stride] when they do not fit in shared memory, else null
     float* y;               // [rows][y_stride]: head h at h * HD
@@ -306,9 +306,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttn
         return;
     const uint32_t pos0 = a.pos[p0];
     const uint32_t n_max = a.pos[p0 + nq - 1] + 1;  // keys of the last query
-    const size_t head_base = ((size_t)a.slot[p0] * a.kv_heads + g) * a.n_ctx * HD;
-    const float* kc = a.kcache + head_base;
-    const float* vc = a.vcache + head_base;
+    const size_t head_cells = ((size_t)a.slot[p0] * a.kv_heads + g) * a.n_ctx;
+    const float* kc = a.kcache + head_cells * kcache_row(HD);  // padded K rows
+    const float* vc = a.vcache + head_cells * HD;
     const size_t width = a.c + 2u * a.kv;
 
     if (tid == 0)
@@ -344,13 +344,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttn
     // other buffer
     constexpr uint32_t kPer = (kPfKT * (HD / 4) + kPfThreads - 1) / kPfThreads;  // float4 per thread and tile
     float4 pre[kPer];
-    auto tile_load = [&](const float* src, uint32_t t0) {
+    auto tile_load = [&](const float* src, uint32_t src_row, uint32_t t0) {
         const uint32_t rows_in = min(kPfKT, n_max - t0);
 #pragma unroll
         for (uint32_t j = 0; j < kPer; ++j) {
             const uint32_t i = tid + j * kPfThreads;
             if (i < rows_in * (HD / 4))
-                pre[j] = reinterpret_cast<const float4*>(src + (size_t)(t0 + i / (HD / 4)) * HD)[i % (HD / 4)];
+                pre[j] = reinterpret_cast<const float4*>(src + (size_t)(t0 + i / (HD / 4)) * src_row)[i % (HD / 4)];
         }
     };
     auto tile_store = [&](float* dst, uint32_t t0) {
@@ -368,13 +368,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttn
     const uint32_t sq = tid / kPfKT, kp = tid % kPfKT;
     const uint32_t sq_n = pos0 + sq + 1;  // keys of query sq
     int bad = 0;
-    tile_load(kc, 0);
+    tile_load(kc, kcache_row(HD), 0);
     tile_store(kvb(0), 0);
     __syncthreads();
     for (uint32_t t0 = 0, buf = 0; t0 < n_max; t0 += kPfKT, buf ^= 1) {
         const bool more = t0 + kPfKT < n_max;
         if (more)
-            tile_load(kc, t0 + kPfKT);
+            tile_load(kc, kcache_row(HD), t0 + kPfKT);
         const uint32_t ta = t0 + kp;
         if (sq < nq && ta < sq_n) {
             const float4* ka = reinterpret_cast<const float4*>(kvb(buf) + (size_t)kp * kStride);
@@ -470,14 +470,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttn
 #pragma unroll
         for (int j = 0; j < DV; ++j)
             acc[h][j] = 0.0f;
-    tile_load(vc, 0);
+    tile_load(vc, HD, 0);
     tile_store(kvb(0), 0);
     __syncthreads();
     for (uint32_t t0 = 0, buf = 0; t0 < n_max; t0 += kPfKT, buf ^= 1) {
         const uint32_t rows_in = min(kPfKT, n_max - t0);
         const bool more = t0 + kPfKT < n_max;
         if (more)
-            tile_load(vc, t0 + kPfKT);
+            tile_load(vc, HD, t0 + kPfKT);
         const float* vt = kvb(buf);
         const uint32_t tend = vn > t0 ? min(rows_in, vn - t0) : 0;
         for (uint32_t tt = 0; tt < tend; ++tt) {
