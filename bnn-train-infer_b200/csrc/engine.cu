@@ -625,11 +625,11 @@ void rope_tables(const bnnd_model* m, uint32_t n_ctx, std::vector<float>* cs, st
 
 // Attention instantiations: head_dim 64/128 x 1/2/4/8 query heads per KV head.
 using AttnFn = void (*)(bnn::eng::AttnArgs);
-AttnFn attention_fn(uint32_t hd, uint32_t kv_mul) {
+AttnFn attention_fn(uint32_t hd, uint32_t kv_mul, bool sc_smem) {
     using namespace bnn::eng;
 #define BNN_ATTN_CASE(H, Q) \
     if (hd == H && kv_mul == Q)  \
-        return attention_kernel<H, Q>;
+        return sc_smem ? attention_kernel<H, Q, true> : attention_kernel<H, Q, false>;
     BNN_ATTN_CASE(128, 1) BNN_ATTN_CASE(128, 2) BNN_ATTN_CASE(128, 4) BNN_ATTN_CASE(128, 8)
     BNN_ATTN_CASE(64, 1) BNN_ATTN_CASE(64, 2) BNN_ATTN_CASE(64, 4) BNN_ATTN_CASE(64, 8)
 #undef BNN_ATTN_CASE
@@ -650,7 +650,7 @@ cudaError_t launch_attention(bnnd_context* c, const bnn::eng::AttnArgs& a) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = c->pdl ? 1 : 0;
-    const AttnFn fn = attention_fn(a.hd, a.heads / a.kv_heads);
+    const AttnFn fn = attention_fn(a.hd, a.heads / a.kv_heads, a.scores == nullptr);
     return fn ? cudaLaunchKernelEx(&cfg, fn, a) : cudaErrorInvalidValue;
 }
 cudaError_t launch_linear(const bnnd_context* c, const bnn::GemvLaunch& cl, const Linear& l, const float* x,
@@ -1014,7 +1014,7 @@ BNND_Status create_llm_context(bnnd_context* c) {
         if (p->smem > bnn::kGemvSmemBudget)
             return fail(BNND_ENOTSUP, "hidden/ffn width too large for the contraction kernel");
     const uint32_t kv_mul = in.heads / in.kv_heads;
-    if (attention_fn(in.head_dim, kv_mul) == nullptr)
+    if (attention_fn(in.head_dim, kv_mul, true) == nullptr)
         return fail(BNND_ENOTSUP, "attention shape (head_dim %u, %u query heads per KV head) not supported",
                     in.head_dim, kv_mul);
     // scores of a block's query heads in shared memory when they fit, else in
@@ -1030,7 +1030,8 @@ BNND_Status create_llm_context(bnnd_context* c) {
     c->attn_resident = std::min<uint32_t>(bnn::eng::attn_resident_rows(in.head_dim, kAttnSmemBudget - ap.ring),
                                           c->n_ctx);
     c->attn_smem = c->attn_resident > 0 ? kAttnSmemBudget : ap.total;
-    CUDA_OR(cudaFuncSetAttribute(attention_fn(in.head_dim, kv_mul), cudaFuncAttributeMaxDynamicSharedMemorySize,
+    CUDA_OR(cudaFuncSetAttribute(attention_fn(in.head_dim, kv_mul, c->scores.p == nullptr),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kAttnSmemBudget),
             BNND_EIO);
     if ((st = capture_step(c, true, &c->graph_logits)) || (st = capture_step(c, false, &c->graph_prefill)))
@@ -1111,11 +1112,11 @@ BNND_Status ensure_prefill(bnnd_context* c, uint32_t rows) {
 }
 
 using PfAttnFn = void (*)(bnn::eng::PfAttnArgs);
-PfAttnFn prefill_attention_fn(uint32_t hd, uint32_t kv_mul) {
+PfAttnFn prefill_attention_fn(uint32_t hd, uint32_t kv_mul, bool sc_smem) {
     using namespace bnn::eng;
 #define BNN_PF_CASE(H, Q) \
     if (hd == H && kv_mul == Q) \
-        return prefill_attention_kernel<H, Q>;
+        return sc_smem ? prefill_attention_kernel<H, Q, true> : prefill_attention_kernel<H, Q, false>;
     BNN_PF_CASE(128, 1) BNN_PF_CASE(128, 2) BNN_PF_CASE(128, 4) BNN_PF_CASE(128, 8)
     BNN_PF_CASE(64, 1) BNN_PF_CASE(64, 2) BNN_PF_CASE(64, 4) BNN_PF_CASE(64, 8)
 #undef BNN_PF_CASE
@@ -1158,12 +1159,12 @@ cudaError_t enqueue_prefill_chunk(bnnd_context* c, uint32_t rows, uint32_t len, 
     const size_t append_smem = bnn::eng::kv_append_smem(HD, in.kv_heads);
     // tiled causal attention: scores in shared memory up to this chunk's last position
     const uint32_t kv_mul = in.heads / in.kv_heads;
-    const PfAttnFn pf_attn = prefill_attention_fn(HD, kv_mul);
     const uint32_t sc_local = bnn::eng::attn_sc_stride(pos_end);
     bnn::eng::PfSmem pf_plan = bnn::eng::pf_smem_plan(HD, kv_mul, sc_local, true);
     const bool pf_global = pf_plan.total > bnn::eng::kPfSmemBudget;
     if (pf_global)
         pf_plan = bnn::eng::pf_smem_plan(HD, kv_mul, bnn::eng::attn_sc_stride(c->n_ctx), false);
+    const PfAttnFn pf_attn = prefill_attention_fn(HD, kv_mul, !pf_global);
     if (!pf_attn || (pf_global && !c->pf_scores.p))
         return cudaErrorInvalidValue;
     {

@@ -231,13 +231,16 @@ __device__ inline bool attn_norm_rope(float* v, const float* gain, const float* 
 //   the head dimension; softmax with expf(s - max), a serial sum over t and a
 //   division; y_i = sum_t p_t * v_t,i, serial in t.
 // Fast mode replaces the serial sums of the norms and the softmax by trees.
-template <int HD, int KVM>
+// SCS: the scores live in shared memory (a.scores null); a compile-time
+// choice, so every score access is a shared-memory access (a pointer that
+// may be either costs a serial softmax sum more than twice the cycles).
+template <int HD, int KVM, bool SCS>
 __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) {
     griddep_launch_dependents();
     extern __shared__ __align__(128) unsigned char e_smem[];
     const uint32_t g = blockIdx.x, row = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr uint32_t kv_mul = KVM;  // query heads per KV head (a.heads / a.kv_heads)
-    const bool sc_smem = a.scores == nullptr;
+    constexpr bool sc_smem = SCS;
     const AttnSmem plan = attn_smem_plan(HD, kv_mul, a.n_ctx, sc_smem);
     uint64_t* full = reinterpret_cast<uint64_t*>(e_smem + plan.bars);
     float* red = reinterpret_cast<float*>(e_smem + plan.red);

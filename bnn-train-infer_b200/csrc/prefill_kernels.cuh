@@ -278,7 +278,9 @@ __host__ __device__ inline PfSmem pf_smem_plan(uint32_t hd, uint32_t kv_mul, uin
     return p;
 }
 
-template <int HD, int KVM>
+// SCS: a tile's scores live in shared memory (a.scores null), fixed at compile
+// time so that score accesses are shared-memory accesses.
+template <int HD, int KVM, bool SCS>
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttnArgs a) {
     extern __shared__ __align__(16) unsigned char pf_smem[];
     constexpr uint32_t kStride = HD + 4;  // padded K/V rows
@@ -288,7 +290,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttn
     const uint32_t r = blockIdx.y / tiles, i0 = (tiles - 1 - blockIdx.y % tiles) * kPfQT;
     const uint32_t nq = min(kPfQT, a.len - i0);
     const uint32_t p0 = r * a.len + i0;  // activation row of the first query
-    const bool sc_smem = a.scores == nullptr;
+    constexpr bool sc_smem = SCS;
     const PfSmem plan = pf_smem_plan(HD, KVM, a.sc_stride, sc_smem);
     float* q_s = reinterpret_cast<float*>(pf_smem + plan.q);
     float* kv_s = reinterpret_cast<float*>(pf_smem + plan.kv);
