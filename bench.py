@@ -185,10 +185,12 @@ def cpu_baseline_sample(path, prompt):
     import ref_engine
     if not ref_engine.available():
         return None
+    import numpy as np
+    first = np.asarray(prompt).reshape(-1)[:1]  # one token (configs[4] passes [rows][prompt])
     ref = ref_engine.RefEngine(path, n_ctx=CTX)
     try:
         t0 = time.perf_counter()
-        ref.decode(prompt[:1])
+        ref.decode(first)
         dt = time.perf_counter() - t0
     finally:
         ref.close()
