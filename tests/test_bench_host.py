@@ -1,0 +1,49 @@
+"""Host-side pieces of bench.py (no GPU): the roofline denominators and the
+committed ncu traffic figure, and the reference CPU baseline sample (one
+token through the reference engine, whatever the shape of the prompt)."""
+import json
+import tempfile
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import bench
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def test_measured_peaks_from_driver_file():
+    p = ROOT / "MEASURED_PEAKS.json"
+    hbm, kind = bench.measured_peaks()
+    if p.exists():
+        assert kind == "measured"
+        assert hbm == float(json.loads(p.read_text())["hbm_gbs"])
+    else:
+        assert (hbm, kind) == (6650.0, "fallback")
+
+
+def test_ncu_traffic_keyed_by_metric():
+    d = json.loads((ROOT / "profiles" / "roofline_traffic.json").read_text())
+    assert bench.ncu_traffic(bench.METRIC) == d[bench.METRIC]
+    # one batch-1 decode launch per contraction: within 5 % of its algorithmic bytes
+    assert abs(d[bench.METRIC] / 2178287 - 1.0) < 0.05
+    # no capture of the 8-context workload is committed: no traffic figure for it
+    assert bench.ncu_traffic(bench.METRIC + "_8ctx") is None
+
+
+def test_cpu_baseline_sample_is_one_token():
+    import ref_engine
+    if not ref_engine.available():
+        pytest.skip("reference engine library not built (make -C oracle ref-soft)")
+    from bnn_b200 import gguf
+    shape = gguf.Qwen3Shape(layers=1, hidden=256, heads=2, kv_heads=1, head_dim=128, ffn=512, vocab=300,
+                            context=bench.CTX)
+    with tempfile.TemporaryDirectory() as d:
+        path = gguf.qwen3_model(Path(d) / "m.gguf", shape, seed=3)
+        for prompt in (np.arange(32, dtype=np.int32), np.zeros((8, 64), dtype=np.int32)):
+            rate, seconds = bench.cpu_baseline_sample(path, prompt)
+            assert rate == pytest.approx(1.0 / seconds)
+            # a 1-layer, 256-wide step takes milliseconds; a whole prompt row
+            # (64 steps) would take tens of times longer
+            assert seconds < 0.5
