@@ -4,9 +4,12 @@
 Workload: random-init Qwen3-1.7B architecture
 (28 layers, hidden 2048, 16 q / 8 kv heads of 128, SwiGLU 6144, vocab 151669,
 tied Q1_0 embedding/lm_head, RMSNorm gains ~N(1, 0.02), rope theta 1e6), a
-32-token seeded prompt, greedy decode at ctx 1024, batch 1. A step is one
-decoded token: one pass of the device-resident engine over the whole model
-(241.9 MB of Q1_0 weights streamed from HBM per token, larger than L2).
+32-token seeded prompt, 128 greedy steps at ctx 1024, batch 1. A step is
+one decoded token: one pass of the device-resident engine over the whole
+model (241.9 MB of Q1_0 weights streamed from HBM per token, larger than
+L2). The K timed steps repeat the 128-step generation: each repeat rewinds
+the context to the end of the (cached) prompt and feeds the prompt's first
+pick, so every timed step decodes at a position of the configured workload.
 
 value     tokens/s of BNND_Generate with everything resident on the device,
           timed with CUDA events on the engine's stream (max over ranks).
@@ -21,7 +24,7 @@ cpu_baseline  the reference engine itself (bnn-sw-v2 + soft backend, compiled
           model on one host core.
 
 --config5 measures BASELINE configs[4]: 8 independent contexts (one context
-row each) with 64-token seeded prompts, greedy decode at ctx 4096; every
+row each) with 64-token seeded prompts, 256 greedy steps at ctx 4096; every
 linear is a GEMV of 8 rows; with --tp under torchrun the model is
 column-sharded over the ranks. value is the aggregate tokens/s.
 
@@ -34,7 +37,9 @@ tokens/s, the roofline the int8 tensor rate of the whole prefill.
 --sweep measures BASELINE configs[1]: GEMV_F32 and DOT_GROUPS at the Qwen3
 linear shapes (K x N = 2048x2048, 2048x1024, 2048x6144, 6144x2048,
 2048x151669), rows = 1. Kernel time is CUDA events around each job on the
-device's stream with L2 flushed (a 256 MB write) before every job; GB/s is
+device's stream with L2 flushed (a 256 MB write, read back) before every job
+and, for 2048x151669, also as a stream of jobs over 8 device copies of the
+matrix (the value); GB/s is
 the algorithmic bytes (N*K*0.140625 + 4K + 4N for GEMV_F32, N*K/8 + K + 2NK/128
 for DOT_GROUPS) over that time. e2e is the full synchronous call with host
 buffers (BufferWrite, BNN_Execute, BufferRead; 2048x151669 through 19 jobs of
@@ -73,10 +78,12 @@ sys.path[:0] = [str(ROOT / "bnn-train-infer_b200"), str(ROOT / "oracle")]
 METRIC = "qwen3_1p7b_w1a8_decode_tokens_per_s"
 PROMPT_TOKENS = 32
 CTX = 1024
+GEN_STEPS = 128          # configs[2]: greedy steps after the prompt
+GEN_STEPS_8CTX = 256     # configs[4]
 MODEL_SEED = 20261203  # rng_for(config index 2)
 PROMPT_SEED = 20261203 + 7
 WORKLOAD = ("configs[2]: Qwen3-1.7B-shape W1A8 greedy decode, random-init weights, "
-            "32-token seeded prompt, ctx 1024, batch 1")
+            "32-token seeded prompt, 128 greedy steps, ctx 1024, batch 1")
 PREFILL_METRIC = "qwen3_1p7b_w1a8_prefill_tokens_per_s"
 PREFILL_TOKENS = 512
 PREFILL_SEED = 20261204  # rng_for(config index 3)
@@ -86,6 +93,39 @@ PREFILL_WORKLOAD = ("configs[3]: Qwen3-1.7B-shape W1A8 prefill of 512 seeded tok
 
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
+
+
+def run_generations(ctx, generate, first, n_prompt, gen_steps, total):
+    """Decodes `total` steps as repeats of the configured greedy generation.
+    Each repeat rewinds to the end of the prompt (whose K/V stay cached),
+    feeds the prompt's first pick and decodes up to `gen_steps` steps, i.e.
+    positions n_prompt .. n_prompt + gen_steps - 1 of the real greedy stream,
+    so every timed step is a step of the configured workload at its position.
+    generate(s) runs s - 1 further steps after a decode with logits (the
+    first of its s ids is the pick that decode made)."""
+    done = 0
+    while done < total:
+        s = min(gen_steps, total - done)
+        ctx.truncate(n_prompt)
+        ctx.decode_argmax(first)  # the step at position n_prompt
+        if s > 1:
+            generate(s)
+        done += s
+    return done
+
+
+def run_generations_per_token(ctx, first, n_prompt, gen_steps, total):
+    """run_generations through the per-token public call (host ids in and
+    out every step); returns the last ids."""
+    done, tok = 0, first
+    while done < total:
+        s = min(gen_steps, total - done)
+        ctx.truncate(n_prompt)
+        tok = first
+        for _ in range(s):
+            tok = ctx.decode_argmax(tok)
+        done += s
+    return tok
 
 
 def model_path(cache):
@@ -272,31 +312,31 @@ def run_b200(args):
             dist.destroy_process_group()
         return out
 
-    # ---- device-resident value
-    ctx.decode_argmax(prompt)                    # prefill (untimed)
-    ctx.generate(args.warmup)                    # warm-up steps
-    need = n_prompt + args.warmup + args.steps + 2
-    if need > n_ctx:
-        raise SystemExit(f"prompt + warmup + steps must fit ctx {n_ctx}")
+    # ---- device-resident value: the K timed steps repeat the configured
+    # greedy generation after the prompt (positions n_prompt ..
+    # n_prompt + gen_steps - 1), K / gen_steps times
+    first = ctx.decode_argmax(prompt)            # prefill (untimed); the prompt's first pick
+    gen_steps = GEN_STEPS_8CTX if args.config5 else GEN_STEPS
+    if n_prompt + gen_steps + 1 > n_ctx:
+        raise SystemExit(f"prompt + {gen_steps} steps must fit ctx {n_ctx}")
     gen = api.Generate
+
+    def generate(s):
+        api.check(gen(ctx.handle, s, None))
+
+    run_generations(ctx, generate, first, n_prompt, gen_steps, args.warmup)  # warm-up steps
     with ClockSampler(local) as clocks:
-        ms = timed(lambda: api.check(gen(ctx.handle, args.steps + 1, None)))
+        ms = timed(lambda: run_generations(ctx, generate, first, n_prompt, gen_steps, args.steps))
     clk = clocks.summary()
     streams = batch * (1 if tp else world)  # sequences decoded by the whole job
-    value = args.steps * streams / (ms / 1e3)   # first of the steps+1 ids was the warm-up's pick
+    value = args.steps * streams / (ms / 1e3)
 
     # ---- end to end through the public per-token call (host ids in/out)
-    ctx.truncate(0)
-    nxt = ctx.decode_argmax(prompt)
-    for _ in range(args.warmup):
-        nxt = ctx.decode_argmax(nxt)
+    run_generations_per_token(ctx, first, n_prompt, gen_steps, args.warmup)
     host_tok = np.empty(batch, dtype=np.int32)
 
     def e2e_loop():
-        tok = nxt.copy()
-        for _ in range(args.steps):
-            tok = ctx.decode_argmax(tok)
-        host_tok[:] = tok
+        host_tok[:] = run_generations_per_token(ctx, first, n_prompt, gen_steps, args.steps)
 
     ms_e2e = timed(e2e_loop)
     e2e_value = args.steps * streams / (ms_e2e / 1e3)
@@ -341,7 +381,7 @@ def run_b200(args):
         workload = WORKLOAD
         if args.config5:
             workload = ("configs[4]: Qwen3-1.7B-shape W1A8, 8 independent contexts with 64-token seeded prompts, "
-                        "greedy decode at ctx 4096" + (f", column-sharded over {world} GPUs" if tp else ""))
+                        "256 greedy steps at ctx 4096" + (f", column-sharded over {world} GPUs" if tp else ""))
         out = {
             "metric": METRIC + ("_8ctx" if args.config5 else ""), "value": round(value, 2), "unit": "tokens/s",
             "n_gpus": world,
@@ -349,6 +389,10 @@ def run_b200(args):
             "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (seeded random-init weights and prompt; no checkpoint offline)",
             "config": {"workload": workload, "prompt_tokens": n_prompt, "ctx": n_ctx,
+                       "greedy_steps": gen_steps,
+                       "timed": (f"{args.steps} decode steps as repeats of the {gen_steps}-step greedy generation "
+                                 f"after the prompt (positions {n_prompt}..{n_prompt + gen_steps - 1}; each repeat "
+                                 f"rewinds to the cached prompt and feeds its first pick)"),
                        "batch_per_gpu": batch if not tp else batch,
                        "layers": info.n_layers, "hidden": info.hidden, "ffn": info.ffn, "vocab": info.n_vocab,
                        "numerics": "fast" if args.fast else "exact (reference operation order)",
@@ -361,7 +405,7 @@ def run_b200(args):
             "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * batch,
                     "d2h_bytes_per_step": 4 * batch, "call": "BNND_DecodeArgmax per token, host ids in and out"},
             "clocks": clk,
-            "gpu_launches": int(launches_per_step * (args.steps + 1)),
+            "gpu_launches": int(launches_per_step * args.steps),
         }
     ctx.free()
     model.free()

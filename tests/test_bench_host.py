@@ -47,3 +47,45 @@ def test_cpu_baseline_sample_is_one_token():
             # a 1-layer, 256-wide step takes milliseconds; a whole prompt row
             # (64 steps) would take tens of times longer
             assert seconds < 0.5
+
+
+class _FakeContext:
+    """Positions and the logits flag as the engine keeps them (BNND_Decode*,
+    BNND_Generate, BNND_ContextTruncate), recording the position of every
+    decoded step."""
+
+    def __init__(self, n_prompt, n_ctx):
+        self.pos, self.n_ctx, self.have_logits, self.steps = n_prompt, n_ctx, True, []
+
+    def truncate(self, pos):
+        assert pos <= self.pos
+        self.pos, self.have_logits = pos, False
+
+    def decode_argmax(self, tok):
+        assert self.pos + 1 <= self.n_ctx
+        self.steps.append(self.pos)
+        self.pos += 1
+        self.have_logits = True
+        return np.asarray(tok) + 1
+
+    def generate(self, s):
+        assert self.have_logits and s >= 1 and self.pos + s - 1 <= self.n_ctx
+        self.steps.extend(range(self.pos, self.pos + s - 1))
+        self.pos += s - 1
+
+
+@pytest.mark.parametrize("total", [0, 1, 5, 128, 129, 256, 300])
+def test_timed_steps_repeat_the_configured_generation(total):
+    n_prompt, gen_steps = bench.PROMPT_TOKENS, bench.GEN_STEPS
+    first = np.array([7], dtype=np.int32)
+    for per_token in (False, True):
+        ctx = _FakeContext(n_prompt, bench.CTX)
+        if per_token:
+            bench.run_generations_per_token(ctx, first, n_prompt, gen_steps, total)
+        else:
+            assert bench.run_generations(ctx, ctx.generate, first, n_prompt, gen_steps, total) == total
+        assert len(ctx.steps) == total
+        # every step at a position of the configured generation, in repeats
+        # that each start right after the prompt
+        want = [n_prompt + i % gen_steps for i in range(total)]
+        assert ctx.steps == want
