@@ -1,8 +1,8 @@
 #!/usr/bin/env python3
 """Regenerate the committed golden fixtures from the reference tree.
 
-Run once in a container where the reference is mounted (default
-/root/reference); the outputs are committed so the GPU box never needs it.
+Run once where a checkout of the reference is available (--ref); the
+outputs are committed, so the machines that run the tests never need it.
 
 Outputs
   rtl_case.npz   the reference's fixed W1A8 regression case
