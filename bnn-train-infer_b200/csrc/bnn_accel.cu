@@ -141,6 +141,7 @@ BNN_Status BNN_DeviceOpen(uint32_t device_index, BNN_Device* out_device) {
     if (!d)
         return BNN_ENOMEM;
     d->ordinal = ordinal;
+    bnn_noalloc_forget(ordinal);
     if (cudaDeviceGetAttribute(&d->sm_count, cudaDevAttrMultiProcessorCount, ordinal) != cudaSuccess) {
         delete d;
         return BNN_EIO;
@@ -527,7 +528,7 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
             ma.out_stride = out_stride;
             ma.epi = epi;
             ma.status = device->d_status;
-            if (bnn::launch_mma(ma, s) != cudaSuccess)
+            if (bnn::launch_mma(ma, device->sm_count, s) != cudaSuccess)
                 return BNN_EIO;
         }
         return BNN_OK;

@@ -40,6 +40,10 @@ struct bnn_accel_buffer {
 extern "C" BNN_Status bnn_b200_matrix_alloc(BNN_Device device, uint32_t in_features, uint32_t out_features,
                                             BNN_Matrix* out_matrix);
 
+// Drops the allocation-free GEMM's cached per-device set-up (bnn_noalloc.cu);
+// BNN_DeviceOpen calls it so a re-created device context is set up afresh.
+void bnn_noalloc_forget(int ordinal);
+
 namespace bnn {
 
 // Makes `ordinal` current for the lifetime of the guard, restoring the

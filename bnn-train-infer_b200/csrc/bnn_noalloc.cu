@@ -17,6 +17,7 @@
 // Every call uses the same array, so calls that overlap on the GPU (from two
 // host threads, or two devices' handles of the same GPU used concurrently)
 // race on it; like all BNN_* calls on a device, callers must serialise them.
+// Each call is synchronous: it waits for its own kernels before returning.
 #include <cfenv>
 #include <cstring>
 #include <mutex>
@@ -43,15 +44,20 @@ constexpr int kMaxDevices = 64;
 std::mutex g_setup_mutex;
 void* g_scratch_addr[kMaxDevices] = {};
 
-// Device address of the scratch on `ordinal` (the current device). Looked up
-// once per device, on the first call that runs there.
-BNN_Status scratch_address(int ordinal, unsigned char** out) {
+// Per-device set-up, run by the first call on `ordinal` (the current device):
+// the scratch's device address (cudaGetSymbolAddress) and the prep kernel's
+// shared-memory limit, both checked. BNN_DeviceOpen forgets the entry
+// (bnn_noalloc_forget), so a process that reset the device and opened a new
+// handle looks the address up again instead of using a stale one.
+BNN_Status scratch_setup(int ordinal, unsigned char** out) {
     if (ordinal < 0 || ordinal >= kMaxDevices)
         return BNN_ENOTSUP;
     std::lock_guard<std::mutex> lock(g_setup_mutex);
     if (!g_scratch_addr[ordinal]) {
         void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr ||
+            cudaFuncSetAttribute(bnn::w1a8_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)bnn::prep_smem_bytes(kNoAllocMaxK)) != cudaSuccess) {
             cudaGetLastError();
             return BNN_EIO;
         }
@@ -62,6 +68,13 @@ BNN_Status scratch_address(int ordinal, unsigned char** out) {
 }
 
 }  // namespace
+
+void bnn_noalloc_forget(int ordinal) {
+    if (ordinal < 0 || ordinal >= kMaxDevices)
+        return;
+    std::lock_guard<std::mutex> lock(g_setup_mutex);
+    g_scratch_addr[ordinal] = nullptr;
+}
 
 extern "C" BNN_Status bnn_b200_gemm_f32_noalloc(BNN_Matrix matrix, const float* x, uint32_t rows, float* y) {
     if (matrix == nullptr || x == nullptr || y == nullptr || rows == 0)
@@ -75,7 +88,7 @@ extern "C" BNN_Status bnn_b200_gemm_f32_noalloc(BNN_Matrix matrix, const float* 
     if (!guard.ok())
         return BNN_EIO;
     unsigned char* scratch = nullptr;
-    BNN_Status st = scratch_address(device->ordinal, &scratch);
+    BNN_Status st = scratch_setup(device->ordinal, &scratch);
     if (st != BNN_OK)
         return st;
 
@@ -99,9 +112,11 @@ extern "C" BNN_Status bnn_b200_gemm_f32_noalloc(BNN_Matrix matrix, const float* 
     pa.totals = totals;
     pa.row_scale = rscale;
     pa.status = status;
-    cudaFuncSetAttribute(bnn::w1a8_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)bnn::prep_smem_bytes(kNoAllocMaxK));
     bnn::w1a8_prep_kernel<<<rows, bnn::kPrepThreads, bnn::prep_smem_bytes(K), s>>>(pa);
+    // A prep that did not launch would leave the previous call's rows in the
+    // shared scratch: stop before the contraction reads them.
+    if (cudaGetLastError() != cudaSuccess)
+        return BNN_EIO;
 
     const bnn::GemvLaunch cl =
         bnn::plan_gemv(device->sm_count, matrix->out_features, G, rows, bnn::kProSliced, bnn::kEpiView);
@@ -119,8 +134,11 @@ extern "C" BNN_Status bnn_b200_gemm_f32_noalloc(BNN_Matrix matrix, const float* 
     ga.out = reinterpret_cast<unsigned char*>(y);
     ga.out_stride = (size_t)matrix->out_features * 4u;
     ga.status = status;
-    if (bnn::launch_gemv(cl, rows, ga, s, false) != cudaSuccess)
+    if (bnn::launch_gemv(cl, rows, ga, s, false) != cudaSuccess) {
+        cudaGetLastError();
+        cudaStreamSynchronize(s);  // the prep may still run: leave nothing in flight
         return BNN_EIO;
+    }
     int verdict = 0;
     if (cudaMemcpyAsync(&verdict, status, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
         cudaStreamSynchronize(s) != cudaSuccess) {

@@ -734,7 +734,7 @@ cudaError_t prefill_linear(bnnd_context* c, const unsigned char* a_sw, const flo
     a.epi = epi;
     a.status = c->status.as<int>();
     g_next_bytes = (double)l.out * l.in * 0.140625 + (double)rows * (l.in + 4.0 * l.out);
-    return bnn::launch_mma(a, c->stream);
+    return bnn::launch_mma(a, c->model->dev->sm_count, c->stream);
 }
 
 // Multi-row steps: RMSNorm (gain non-null) + QuantizeRow of every row in its
@@ -1639,7 +1639,7 @@ BNND_Status BNND_Classify(BNND_Context c, const float* input, uint32_t n_samples
             ma.out_stride = (size_t)L.w.out * 4u;
             ma.epi = bnn::kEpiView;
             ma.status = c->status.as<int>();
-            CUDA_OR(bnn::launch_mma(ma, s), BNND_EIO);
+            CUDA_OR(bnn::launch_mma(ma, m->dev->sm_count, s), BNND_EIO);
         } else {
             CUDA_OR(launch_linear(c, c->plan_mlp[i], L.w, cur, nullptr, n_samples, nxt, (size_t)L.w.out * 4u,
                                   c->status.as<int>()),

@@ -441,15 +441,9 @@ static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs
 }
 
 // Launches the contraction of `a.m` rows (a.m <= 65535 * kMmaM) on `s`:
-// 128-wide tiles, or 64-wide when the wide grid would leave SMs idle.
-inline cudaError_t launch_mma(const MmaArgs& a, cudaStream_t s) {
-    static int sms = 0;
-    if (sms == 0) {
-        int dev = 0;
-        if (cudaGetDevice(&dev) != cudaSuccess ||
-            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
-            sms = 148;
-    }
+// 128-wide tiles, or 64-wide when the wide grid would leave SMs idle on a
+// device of `sms` streaming multiprocessors.
+inline cudaError_t launch_mma(const MmaArgs& a, int sms, cudaStream_t s) {
     const uint32_t mtiles = (a.m + kMmaM - 1) / kMmaM;
     const bool narrow = (size_t)((a.n + kMmaN - 1) / kMmaN) * mtiles < (size_t)sms;
     const uint32_t nt = narrow ? kMmaNarrow : kMmaN;

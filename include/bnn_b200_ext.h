@@ -58,10 +58,15 @@ void* bnn_b200_buffer_device_ptr(BNN_Buffer buffer);
  * NaN/Inf input (y untouched), BNN_ENOTSUP when the FP rounding mode is not
  * to-nearest, BNN_EIO on a CUDA failure.
  *
- * The first call on a device looks up the scratch's device address there
- * (cudaGetSymbolAddress); make that first call before any stream capture.
- * All calls share the one scratch array and it keeps the last call's
- * contents: calls that overlap on the GPU race and must be serialised. */
+ * The first call on a device (after each BNN_DeviceOpen there) looks up the
+ * scratch's device address (cudaGetSymbolAddress) and sets the prep kernel's
+ * shared-memory limit; make that first call before any stream capture. Every
+ * call is synchronous: it waits for its own kernels on the device's stream
+ * before it returns. After cudaDeviceReset every handle of that device is
+ * dead; open a new device handle (which also renews this set-up) before the
+ * next call. All calls share the one scratch array and it keeps the last
+ * call's contents: calls that overlap on the GPU race and must be
+ * serialised. */
 BNN_Status bnn_b200_gemm_f32_noalloc(BNN_Matrix matrix, const float* x, uint32_t rows, float* y);
 
 #ifdef __cplusplus

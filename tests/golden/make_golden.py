@@ -25,6 +25,7 @@ The memory image stores the weights as 18-byte Q1_0 records ordered
 addresses in meta.json (gen_model_case.py:47-53, 222-239 in the reference).
 """
 import argparse
+import os
 import base64
 import json
 from pathlib import Path
@@ -83,7 +84,9 @@ def q1_0_block(ref):
 def main():
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--ref", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--ref", type=Path,
+                    default=Path(os.environ.get("BNN_REFERENCE") or HERE.parents[2] / "reference"),
+                    help="reference checkout (default: $BNN_REFERENCE, else 'reference' beside the repo root)")
     args = ap.parse_args()
     rtl_case(args.ref)
     q1_0_block(args.ref)

@@ -9,6 +9,7 @@ shared fixed scratch array. This file is collected last on purpose.
 import ctypes
 
 import numpy as np
+import oracle
 import pytest
 
 from bnn_b200 import accel, synth
@@ -44,6 +45,10 @@ def test_noalloc_matches_execute_twice(k, n, rows):
             assert st == accel.OK, f"call {call}: status {st}"
             got = bo.read().view(np.float32).reshape(rows, n)
             assert got.tobytes() == want.tobytes(), f"call {call} differs from BNN_Execute"
+            # and straight against the CPU restatement of the soft backend
+            ref, _, _ = oracle.gemm_f32(bits, scales, x)
+            assert got.tobytes() == np.ascontiguousarray(ref, dtype=np.float32).tobytes(), \
+                f"call {call} differs from the oracle"
     finally:
         bi.free()
         bo.free()
