@@ -68,6 +68,7 @@ class EngineApi:
             "BNND_ContextFree": (None, [c_void_p]),
             "BNND_Decode": (c_int, [c_void_p, c_void_p, c_uint32, c_void_p]),
             "BNND_DecodeArgmax": (c_int, [c_void_p, c_void_p, c_uint32, c_void_p]),
+            "BNND_DecodeLogitsAll": (c_int, [c_void_p, c_void_p, c_uint32, c_void_p]),
             "BNND_Generate": (c_int, [c_void_p, c_uint32, c_void_p]),
             "BNND_ContextPos": (c_uint32, [c_void_p]),
             "BNND_ContextTruncate": (c_int, [c_void_p, c_uint32]),
@@ -156,6 +157,13 @@ class Context:
         st = self.api.Decode(self.handle, t.ctypes.data, t.shape[1],
                              out.ctypes.data if out is not None else None)
         self.api.check(st)
+        return out
+
+    def decode_logits_all(self, tokens):
+        """One-row context: feeds tokens [n]; returns the logits of every position [n][V]."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32).reshape(-1))
+        out = np.empty((t.size, self.model.info.n_vocab), dtype=np.float32)
+        self.api.check(self.api.DecodeLogitsAll(self.handle, t.ctypes.data, t.size, out.ctypes.data))
         return out
 
     def decode_argmax(self, tokens):

@@ -607,6 +607,24 @@ BNN_Status bnn_b200_sync(BNN_Device device) {
     return st ? BNN_ERANGE : BNN_OK;
 }
 
+BNN_Status bnn_b200_test_wait_limit(BNN_Device device, uint64_t limit_ns, int starve_producer) {
+    if (device == nullptr)
+        return BNN_EINVAL;
+    bnn::DeviceGuard guard(device->ordinal);
+    if (!guard.ok())
+        return BNN_EIO;
+    const unsigned long long limit = limit_ns ? (unsigned long long)limit_ns : bnn::kWaitNsLimit;
+    const int starve = starve_producer ? 1 : 0;
+    // no job of this handle may run while the limits change
+    if (cudaStreamSynchronize(device->stream) != cudaSuccess ||
+        cudaMemcpyToSymbol(bnn::g_wait_ns_limit, &limit, sizeof limit) != cudaSuccess ||
+        cudaMemcpyToSymbol(bnn::g_test_starve_producer, &starve, sizeof starve) != cudaSuccess) {
+        cudaGetLastError();
+        return BNN_EIO;
+    }
+    return BNN_OK;
+}
+
 void* bnn_b200_device_stream(BNN_Device device) {
     return device ? static_cast<void*>(device->stream) : nullptr;
 }

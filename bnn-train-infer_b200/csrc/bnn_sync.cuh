@@ -19,6 +19,11 @@ constexpr uint64_t kWaitNsLimit = 1000000000ull;
 // producer/consumer warps leave the issue slots to the warps doing the work.
 constexpr uint32_t kSuspendHintNs = 20000u;
 
+// The limit a wait applies, in ns. Each translation unit holds its own copy,
+// kWaitNsLimit unless a test lowers the copy that BNN_Execute's kernels read
+// (bnn_b200_test_wait_limit) to make a wait run out within milliseconds.
+static __device__ unsigned long long g_wait_ns_limit = kWaitNsLimit;
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -78,10 +83,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity))
         return true;
     const uint64_t t0 = globaltimer_ns();
+    const uint64_t limit = *reinterpret_cast<volatile unsigned long long*>(&g_wait_ns_limit);
     for (uint32_t i = 0; i < kWaitPollLimit; ++i) {
         if (mbar_try_wait_suspend(bar, parity))
             return true;
-        if (globaltimer_ns() - t0 > kWaitNsLimit)
+        if (globaltimer_ns() - t0 > limit)
             return false;
     }
     return false;

@@ -265,6 +265,7 @@ struct bnnd_context {
     // batched prefill: activation rows = prompt positions of every row
     DevMem pf_x, pf_qkv, pf_y, pf_h, pf_a, pf_rs, pf_scores, pf_meta;
     DevMem dm_act, dm_tot, dm_rs;  // steps of kStepRowsPrep+ rows: sliced rows, group totals, row scales
+    DevMem lg_pos;                 // BNND_DecodeLogitsAll: one position's logits
     bnn::GemvLaunch plan_qkv_s{}, plan_o_s{}, plan_gu_s{}, plan_down_s{}, plan_head_s{};  // their contractions
     uint32_t pf_rows = 0;          // activation rows the pf_* buffers hold
     size_t pf_meta_cap = 0;        // entries of pf_meta (ids, positions, cache rows)
@@ -1236,7 +1237,10 @@ cudaError_t enqueue_prefill_chunk(bnnd_context* c, uint32_t rows, uint32_t len, 
 
 // The prompt of every row through the batched prefill, then (want) the
 // decode step's out_norm + lm_head + greedy pick on each row's last position.
-BNND_Status prefill(bnnd_context* c, const int32_t* tokens, uint32_t n, bool want) {
+// all (one-row contexts only): every position's logits, [n][n_vocab] on the
+// host, each from the prefill's final hidden row through out_norm + lm_head
+// (the decode step's own kernel and plan).
+BNND_Status prefill(bnnd_context* c, const int32_t* tokens, uint32_t n, bool want, float* all = nullptr) {
     const uint32_t R = c->rows, start = c->pos, chunk = std::min(n, c->params.prefill_chunk);
     const size_t count = (size_t)R * n;
     BNND_Status st = ensure_prefill(c, R * chunk);
@@ -1273,11 +1277,24 @@ BNND_Status prefill(bnnd_context* c, const int32_t* tokens, uint32_t n, bool wan
     cudaStream_t s = c->stream;
     CUDA_OR(cudaMemcpyAsync(c->pf_meta.p, hm, 3 * count * 4, cudaMemcpyHostToDevice, s), BNND_EIO);
     uint32_t last_len = 0;
+    const bnnd_model* md = c->model;
+    const size_t V = md->info.n_vocab;
+    if (all && !c->lg_pos.p && (st = dev_alloc(c->lg_pos, V * 4)))
+        return st;
     for (uint32_t j0 = 0; j0 < n; j0 += chunk) {
         last_len = std::min(chunk, n - j0);
         CUDA_OR(enqueue_prefill_chunk(c, R * last_len, last_len, start + j0 + last_len,
                                       c->pf_meta.as<uint32_t>() + 3 * (size_t)R * j0),
                 BNND_EIO);
+        for (uint32_t i = 0; all && i < last_len; ++i) {
+            const float* xi = c->pf_x.as<float>() + (size_t)i * md->info.hidden;
+            CUDA_OR(launch_linear(c, c->plan_head, md->lm_head, xi, md->out_norm.as<float>(), 1, c->lg_pos.as<float>(),
+                                  V * 4u, c->status.as<int>()),
+                    BNND_EIO);
+            CUDA_OR(cudaMemcpyAsync(all + (size_t)(j0 + i) * V, c->lg_pos.p, V * 4, cudaMemcpyDeviceToHost,
+                                    c->stream),
+                    BNND_EIO);
+        }
     }
     // device positions: start + n after the call (the tail's step_end adds the last 1)
     std::vector<uint32_t> pv(R, start + n - (want ? 1u : 0u));
@@ -1303,7 +1320,8 @@ BNND_Status prefill(bnnd_context* c, const int32_t* tokens, uint32_t n, bool wan
 }
 
 // Shared body of BNND_Decode / BNND_DecodeArgmax.
-BNND_Status decode(bnnd_context* c, const int32_t* tokens, uint32_t n, float* logits, int32_t* next) {
+BNND_Status decode(bnnd_context* c, const int32_t* tokens, uint32_t n, float* logits, int32_t* next,
+                   float* all = nullptr) {
     g_last_error.clear();
     if (!c || !tokens || n == 0)
         return BNND_EINVAL;
@@ -1338,10 +1356,10 @@ BNND_Status decode(bnnd_context* c, const int32_t* tokens, uint32_t n, float* lo
         for (uint32_t i = 0; i < n; ++i)
             seq[(size_t)i * c->rows + r] = tokens[(size_t)r * n + i];
     const uint32_t start = c->pos;
-    const bool want = logits || next;
+    const bool want = logits || next || all;
     const bool batched = c->params.prefill_chunk > 0 && n >= BNND_PREFILL_MIN_TOKENS && c->world == 1;
     if (batched) {
-        BNND_Status pst = prefill(c, tokens, n, want);
+        BNND_Status pst = prefill(c, tokens, n, want, all);
         if (pst != BNND_OK) {
             cudaStreamSynchronize(c->stream);
             set_pos(c, start);
@@ -1355,7 +1373,11 @@ BNND_Status decode(bnnd_context* c, const int32_t* tokens, uint32_t n, float* lo
                                 cudaMemcpyDeviceToDevice, c->stream),
                 BNND_EIO);
         const bool last = i + 1 == n;
-        CUDA_OR(cudaGraphLaunch(last && want ? c->graph_logits : c->graph_prefill, c->stream), BNND_EIO);
+        CUDA_OR(cudaGraphLaunch((last && want) || all ? c->graph_logits : c->graph_prefill, c->stream), BNND_EIO);
+        if (all)
+            CUDA_OR(cudaMemcpyAsync(all + (size_t)i * m->info.n_vocab, c->logits.p, (size_t)m->info.n_vocab * 4,
+                                    cudaMemcpyDeviceToHost, c->stream),
+                    BNND_EIO);
     }
     if (logits)
         CUDA_OR(cudaMemcpyAsync(logits, c->logits.p, (size_t)c->rows * m->info.n_vocab * 4,
@@ -1520,6 +1542,15 @@ void BNND_ContextFree(BNND_Context ctx) {
 
 BNND_Status BNND_Decode(BNND_Context ctx, const int32_t* tokens, uint32_t n_tokens, float* logits) {
     return decode(ctx, tokens, n_tokens, logits, nullptr);
+}
+
+BNND_Status BNND_DecodeLogitsAll(BNND_Context ctx, const int32_t* tokens, uint32_t n_tokens, float* logits_all) {
+    g_last_error.clear();
+    if (!ctx || !logits_all)
+        return BNND_EINVAL;
+    if (ctx->rows != 1 || ctx->world != 1)
+        return fail(BNND_ENOTSUP, "per-position logits need a one-row, single-GPU context");
+    return decode(ctx, tokens, n_tokens, nullptr, nullptr, logits_all);
 }
 
 BNND_Status BNND_DecodeArgmax(BNND_Context ctx, const int32_t* tokens, uint32_t n_tokens,

@@ -57,6 +57,11 @@ static_assert(kComputeWarps >= kSumWarps, "the RMSNorm sum needs four compute wa
 // (in registers: kMaxPrologueK / 512 float4 per compute thread).
 constexpr uint32_t kMaxPrologueK = 8192;
 
+// Test hook (bnn_b200_test_wait_limit): when set, the producer warps of this
+// translation unit's contraction kernels issue no copies and arrive on no
+// barrier, so every consumer wait for a weight tile runs out.
+static __device__ int g_test_starve_producer = 0;
+
 enum Prologue : int { kProSliced = 0, kProQuant = 1, kProRmsNorm = 2 };
 enum Epilogue : int { kEpiDotGroups = 0, kEpiView = 1, kEpiResidual = 2, kEpiSwiGLU = 3 };
 
@@ -220,7 +225,7 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, 2) w1a8_gemv_kernel(
     __syncthreads();
 
     if (warp == consumers) {  // producer warp: weights never depend on earlier kernels
-        if (lane == 0) {
+        if (lane == 0 && !*reinterpret_cast<volatile int*>(&g_test_starve_producer)) {
             uint32_t i = 0;
             for (uint32_t tile = blockIdx.x; tile < a.tiles; tile += gridDim.x, ++i) {
                 const uint32_t s = i % a.stages;

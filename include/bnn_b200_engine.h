@@ -132,6 +132,13 @@ BNND_Status BNND_Decode(BNND_Context ctx, const int32_t* tokens, uint32_t n_toke
 BNND_Status BNND_DecodeArgmax(BNND_Context ctx, const int32_t* tokens, uint32_t n_tokens,
                               int32_t* next_tokens);
 
+/* BNND_Decode that returns the logits of every fed position, logits_all
+ * [n_tokens][n_vocab], as tools/precision/dump-logits.c collects them with
+ * one BNNE_Decode per token (dump-logits.c:295-306); a prompt of
+ * BNND_PREFILL_MIN_TOKENS or more still runs as one batched prefill. One-row
+ * (n_batch 1), single-GPU contexts; BNND_ENOTSUP otherwise. */
+BNND_Status BNND_DecodeLogitsAll(BNND_Context ctx, const int32_t* tokens, uint32_t n_tokens, float* logits_all);
+
 /* Greedy generation entirely on the device: feeds each row's last argmax
  * back as input for `steps` steps (one CUDA graph launch per step) and writes
  * the generated ids to out_tokens [n_batch][steps] (host) when non-NULL.

@@ -40,6 +40,16 @@ int bnn_b200_device_ordinal(BNN_Device device);
  * pointers to their own kernels). */
 void* bnn_b200_buffer_device_ptr(BNN_Buffer buffer);
 
+/* Test hook for the bounded device waits (BNN_ETIMEOUT, bnn-accelerator.h:25-26,
+ * 202). No counterpart in the reference. Sets the limit after which a wait
+ * inside BNN_Execute's kernels gives up (limit_ns; 0 restores the default of
+ * one second) and, when starve_producer is non-zero, makes the contraction's
+ * copy warps issue nothing, so the next GEMV/GEMV_F32/small-GEMM job's waits
+ * for weight tiles run out and it returns BNN_ETIMEOUT without touching its
+ * output. Affects every device in the process; waits for this handle's
+ * stream first. Call with (0, 0) to return to normal operation. */
+BNN_Status bnn_b200_test_wait_limit(BNN_Device device, uint64_t limit_ns, int starve_producer);
+
 /* GEMM_F32 that allocates nothing. No counterpart in the reference.
  *
  * For callers that cannot let a library allocate device memory while they

@@ -13,6 +13,9 @@ from pathlib import Path
 import numpy as np
 
 LIB = Path(__file__).resolve().parent / "_ref" / "libbnn_engine_soft.so"
+# The same engine sources over oracle/bnn_fast_backend.c (multi-threaded,
+# bit-identical to soft): for checks at the full Qwen3-1.7B shape.
+FAST_LIB = Path(__file__).resolve().parent / "_ref" / "libbnn_engine_fast.so"
 
 
 class BnneModelInfo(ctypes.Structure):  # bnn-engine.h:52-68
@@ -26,17 +29,16 @@ class BnneContextParams(ctypes.Structure):  # bnn-engine.h:70-74
     _fields_ = [("n_ctx", c_uint32), ("n_batch", c_uint32), ("enable_stats", c_int)]
 
 
-_dll = None
+_dlls = {}
 
 
-def available():
-    return LIB.exists()
+def available(fast=False):
+    return (FAST_LIB if fast else LIB).exists()
 
 
-def dll():
-    global _dll
-    if _dll is None:
-        d = ctypes.CDLL(str(LIB))
+def dll(fast=False):
+    if fast not in _dlls:
+        d = ctypes.CDLL(str(FAST_LIB if fast else LIB))
         d.BNN_DeviceOpen.argtypes = [c_uint32, POINTER(c_void_p)]
         d.BNN_DeviceClose.argtypes = [c_void_p]
         d.BNNE_ModelLoad.argtypes = [c_void_p, c_char_p, POINTER(c_void_p)]
@@ -49,15 +51,16 @@ def dll():
         d.BNNE_Classify.argtypes = [c_void_p, c_void_p, c_uint32, c_void_p]
         d.BNNE_ContextTruncate.argtypes = [c_void_p, c_uint32]
         d.BNNE_LastError.restype = c_char_p
-        _dll = d
-    return _dll
+        _dlls[fast] = d
+    return _dlls[fast]
 
 
 class RefEngine:
-    """One soft device + one model + one context of the reference engine."""
+    """One device + one model + one context of the reference engine: over
+    the soft backend, or (fast=True) over the multi-threaded CPU backend."""
 
-    def __init__(self, path, n_ctx=0, n_batch=0):
-        d = dll()
+    def __init__(self, path, n_ctx=0, n_batch=0, fast=False):
+        self._d = d = dll(fast)
         self.dev, self.model, self.ctx = c_void_p(), c_void_p(), c_void_p()
         assert d.BNN_DeviceOpen(0, ctypes.byref(self.dev)) == 0
         st = d.BNNE_ModelLoad(self.dev, str(path).encode(), ctypes.byref(self.model))
@@ -75,9 +78,9 @@ class RefEngine:
     def decode(self, tokens, want_logits=True):
         t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32).reshape(-1))
         out = np.empty(self.info.n_vocab, dtype=np.float32) if want_logits else None
-        st = dll().BNNE_Decode(self.ctx, t.ctypes.data, t.size, out.ctypes.data if out is not None else None)
+        st = self._d.BNNE_Decode(self.ctx, t.ctypes.data, t.size, out.ctypes.data if out is not None else None)
         if st != 0:
-            raise RuntimeError(f"BNNE_Decode: {st} {dll().BNNE_LastError()}")
+            raise RuntimeError(f"BNNE_Decode: {st} {self._d.BNNE_LastError()}")
         return out
 
     def greedy(self, prompt, steps):
@@ -93,16 +96,16 @@ class RefEngine:
     def classify(self, x):
         x = np.ascontiguousarray(x, dtype=np.float32)
         out = np.empty((x.shape[0], self.info.n_classes), dtype=np.float32)
-        st = dll().BNNE_Classify(self.ctx, x.ctypes.data, x.shape[0], out.ctypes.data)
+        st = self._d.BNNE_Classify(self.ctx, x.ctypes.data, x.shape[0], out.ctypes.data)
         if st != 0:
-            raise RuntimeError(f"BNNE_Classify: {st} {dll().BNNE_LastError()}")
+            raise RuntimeError(f"BNNE_Classify: {st} {self._d.BNNE_LastError()}")
         return out
 
     def truncate(self, pos):
-        assert dll().BNNE_ContextTruncate(self.ctx, pos) == 0
+        assert self._d.BNNE_ContextTruncate(self.ctx, pos) == 0
 
     def close(self):
-        d = dll()
+        d = self._d
         d.BNNE_ContextFree(self.ctx)
         d.BNNE_ModelFree(self.model)
         d.BNN_DeviceClose(self.dev)

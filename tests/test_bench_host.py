@@ -89,3 +89,25 @@ def test_timed_steps_repeat_the_configured_generation(total):
         # that each start right after the prompt
         want = [n_prompt + i % gen_steps for i in range(total)]
         assert ctx.steps == want
+
+
+def test_reference_arm_times_configured_positions(monkeypatch, tmp_path):
+    """--impl reference on a 1-layer model: the forked copies decode from the
+    end of the prompt, steps x ms_per_step is the slowest copy's time, and the
+    config block is the device arm's."""
+    import argparse
+    import ref_engine
+    if not ref_engine.available():
+        pytest.skip("reference engine library not built (make -C oracle ref-soft)")
+    from bnn_b200 import gguf
+    shape = gguf.Qwen3Shape(layers=1, hidden=256, heads=2, kv_heads=1, head_dim=128, ffn=512, vocab=300,
+                            context=bench.CTX)
+    path = gguf.qwen3_model(tmp_path / "m.gguf", shape, seed=3)
+    monkeypatch.setattr(bench, "model_path", lambda cache: path)
+    args = argparse.Namespace(steps=6, ref_procs=3, model_cache=str(tmp_path))
+    out = bench.run_reference(args)
+    assert out["impl"] == "reference" and out["steps"] == 6
+    assert out["value"] == pytest.approx(out["steps"] / (out["steps"] * out["ms_per_step"] / 1e3), rel=1e-2)
+    assert out["config"] == bench.decode_config(bench.gguf_shape(), bench.GEN_STEPS, bench.PROMPT_TOKENS,
+                                                bench.CTX, 1, bench.WORKLOAD)
+    assert f"positions {bench.PROMPT_TOKENS}..{bench.PROMPT_TOKENS + 1}" in out["cpu_baseline"]["sample"]
