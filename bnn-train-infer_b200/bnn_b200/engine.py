@@ -78,6 +78,7 @@ class EngineApi:
             "BNND_ContextProfile": (c_int, [c_void_p, c_uint32, c_void_p, c_uint32, POINTER(c_uint32),
                                             POINTER(ctypes.c_double)]),
             "BNND_StepLaunches": (c_uint32, [c_void_p]),
+            "BNND_StepKernelPositions": (c_uint32, [c_void_p]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(d, name)
@@ -191,6 +192,10 @@ class Context:
 
     def step_launches(self):
         return self.api.StepLaunches(self.handle)
+
+    def step_kernel_positions(self):
+        """Positions below which a decode step is one persistent kernel (0: never)."""
+        return self.api.StepKernelPositions(self.handle)
 
     def profile(self, steps):
         """Per-kernel device time over `steps` instrumented greedy steps:

@@ -19,7 +19,9 @@
 // row quantisation run inside each linear's prologue; the W1A8 linears are
 // launched with programmatic dependent launch so their weight streaming
 // overlaps the preceding kernel.
+#include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -33,6 +35,7 @@
 #include "bnn_b200_engine.h"
 #include "bnn_b200_ext.h"
 #include "bnn_internal.h"
+#include "decode_step.cuh"
 #include "engine_kernels.cuh"
 #include "gguf_reader.h"
 #include "prefill_kernels.cuh"
@@ -266,6 +269,11 @@ struct bnnd_context {
     DevMem pf_x, pf_qkv, pf_y, pf_h, pf_a, pf_rs, pf_scores, pf_meta;
     DevMem dm_act, dm_tot, dm_rs;  // steps of kStepRowsPrep+ rows: sliced rows, group totals, row scales
     DevMem lg_pos;                 // BNND_DecodeLogitsAll: one position's logits
+    // persistent step kernel (decode_step.cuh): one launch per decode step
+    DevMem st_sync, st_sched, st_sched_len, st_layers;
+    bnn::step::StepArgs st_args{};
+    uint32_t st_positions = 0;     // steps at positions below this use it (0: never)
+    cudaGraphExec_t graph_step = nullptr;
     bnn::GemvLaunch plan_qkv_s{}, plan_o_s{}, plan_gu_s{}, plan_down_s{}, plan_head_s{};  // their contractions
     uint32_t pf_rows = 0;          // activation rows the pf_* buffers hold
     size_t pf_meta_cap = 0;        // entries of pf_meta (ids, positions, cache rows)
@@ -280,6 +288,8 @@ struct bnnd_context {
             cudaGraphExecDestroy(graph_prefill);
         if (graph_profile)
             cudaGraphExecDestroy(graph_profile);
+        if (graph_step)
+            cudaGraphExecDestroy(graph_step);
         if (comm)
             ncclCommDestroy(comm);
         for (cudaEvent_t e : recorder.events)
@@ -942,6 +952,168 @@ BNND_Status capture_step(bnnd_context* c, bool with_logits, cudaGraphExec_t* out
     return BNND_OK;
 }
 
+// The persistent step kernel for one-row, single-GPU, exact-mode contexts
+// with 128-wide heads (decode_step.cuh). Leaves c->graph_step null, and the
+// per-kernel step graph in charge, when the shape or the device does not
+// allow it or BNN_STEP_KERNEL=0; failures here are not errors.
+void setup_step_kernel(bnnd_context* c) {
+    namespace st = bnn::step;
+    const bnnd_model* m = c->model;
+    const BNND_ModelInfo& in = m->info;
+    const char* env = std::getenv("BNN_STEP_KERNEL");
+    if (env && env[0] == '0')
+        return;
+    const int sms = m->dev->sm_count;
+    int coop = 0;
+    if (c->rows != 1 || c->world != 1 || !c->params.exact || in.head_dim != st::kHD || in.hidden % 128 ||
+        in.ffn % 128 || in.heads % in.kv_heads || (int)in.heads + 1 >= sms ||
+        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->dev->ordinal) != cudaSuccess || !coop) {
+        cudaGetLastError();
+        return;
+    }
+    const uint32_t C = in.hidden, F = in.ffn, L = in.n_layers, HD = in.head_dim;
+    const uint32_t n_attn = in.heads, n_gemv = (uint32_t)sms - n_attn;
+    const uint32_t qkv_rows = C + 2 * in.kv_heads * HD;
+    const uint32_t GC = C / 128, GF = F / 128;
+    auto ceil_div = [](uint32_t a, uint32_t b) { return (a + b - 1) / b; };
+    // the integer-D buffer holds the largest copy's blocks x 8 rows x groups
+    const uint32_t nb_v = ceil_div(in.n_vocab, 8);
+    uint32_t dsm_units = std::max({ceil_div(qkv_rows / 8, n_gemv) * GC, ceil_div(C / 8, n_gemv) * GF,
+                                   2 * ceil_div(F / 8, n_gemv) * GC,
+                                   std::min(st::kLmChunkBlocks, ceil_div(nb_v, n_gemv)) * GC});
+    const uint32_t dsm_bytes = dsm_units * 8u * 2u;
+    const st::GemvPlan gp = st::gemv_plan(C, F, dsm_bytes);
+    if (gp.ring >= st::kSmemBudget)
+        return;
+    const uint32_t ring = (uint32_t)((st::kSmemBudget - gp.ring) & ~(size_t)127);
+    st::ScheduleShape shape{L, C, F, qkv_rows, in.n_vocab, n_gemv, ring};
+    std::vector<st::LayerSrc> srcs(L);
+    for (uint32_t l = 0; l < L; ++l) {
+        const QwenLayer& Q = *m->layers[l];
+        srcs[l] = st::LayerSrc{(uint64_t)(uintptr_t)Q.qkv.m->wblocks, (uint64_t)(uintptr_t)Q.o.m->wblocks,
+                               (uint64_t)(uintptr_t)Q.gu.m->wblocks, (uint64_t)(uintptr_t)Q.down.m->wblocks,
+                               (uint64_t)(uintptr_t)Q.attn_norm.p, (uint64_t)(uintptr_t)Q.ffn_norm.p};
+    }
+    std::vector<std::vector<st::Copy>> scheds(n_gemv);
+    uint32_t stride = 1;
+    for (uint32_t j = 0; j < n_gemv; ++j) {
+        if (!st::build_schedule(shape, srcs, (uint64_t)(uintptr_t)m->lm_head.m->wblocks,
+                                (uint64_t)(uintptr_t)m->out_norm.p, j, &scheds[j]))
+            return;
+        stride = std::max<uint32_t>(stride, (uint32_t)scheds[j].size());
+    }
+    std::vector<st::Copy> flat((size_t)n_gemv * stride);
+    std::vector<uint32_t> lens(n_gemv);
+    for (uint32_t j = 0; j < n_gemv; ++j) {
+        std::copy(scheds[j].begin(), scheds[j].end(), flat.begin() + (size_t)j * stride);
+        lens[j] = (uint32_t)scheds[j].size();
+    }
+    const BNND_ShardInfo& sh = m->shard;
+    const size_t layer_cache = (size_t)c->n_ctx * sh.kv_rows;
+    std::vector<st::LayerPtrs> lp(L);
+    for (uint32_t l = 0; l < L; ++l) {
+        const QwenLayer& Q = *m->layers[l];
+        lp[l] = st::LayerPtrs{Q.q_norm.as<float>(), Q.k_norm.as<float>(),
+                              c->kcache.as<float>() + (size_t)l * (layer_cache / HD * bnn::eng::kcache_row(HD)),
+                              c->vcache.as<float>() + (size_t)l * layer_cache};
+    }
+    const uint32_t n_ctr = L * st::kCtrPerLayer + 1;
+    if (dev_alloc(c->st_sync, (size_t)n_ctr * 4) || dev_alloc(c->st_sched, flat.size() * sizeof(st::Copy)) ||
+        dev_alloc(c->st_sched_len, lens.size() * 4) || dev_alloc(c->st_layers, lp.size() * sizeof(st::LayerPtrs)) ||
+        cudaMemset(c->st_sync.p, 0, (size_t)n_ctr * 4) != cudaSuccess ||
+        cudaMemset(c->best.p, 0, 8) != cudaSuccess ||
+        cudaMemcpy(c->st_sched.p, flat.data(), flat.size() * sizeof(st::Copy), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(c->st_sched_len.p, lens.data(), lens.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(c->st_layers.p, lp.data(), lp.size() * sizeof(st::LayerPtrs), cudaMemcpyHostToDevice) !=
+            cudaSuccess) {
+        cudaGetLastError();
+        g_last_error.clear();
+        return;
+    }
+    st::StepArgs& a = c->st_args;
+    a.layers = c->st_layers.as<st::LayerPtrs>();
+    a.n_layers = L;
+    a.C = C;
+    a.F = F;
+    a.V = in.n_vocab;
+    a.qkv_rows = qkv_rows;
+    a.heads = in.heads;
+    a.kv_heads = in.kv_heads;
+    a.n_ctx = c->n_ctx;
+    a.n_attn = n_attn;
+    a.n_gemv = n_gemv;
+    a.sched = c->st_sched.as<st::Copy>();
+    a.sched_len = c->st_sched_len.as<uint32_t>();
+    a.sched_stride = stride;
+    a.ring_bytes = ring;
+    a.dsm_bytes = dsm_bytes;
+    a.kv_resident = std::min<uint32_t>(st::attn_resident_max(), c->n_ctx);
+    a.lm_head = m->lm_head.m->wblocks;
+    a.tok_in = c->tok_in.as<int32_t>();
+    a.pos = c->pos_d.as<uint32_t>();
+    a.tok_next = c->tok_next.as<int32_t>();
+    a.hist = c->hist.as<int32_t>();
+    a.hist_count = c->hist_count.as<uint32_t>();
+    a.hist_cap = c->hist_cap;
+    a.x = c->x.as<float>();
+    a.qkv = c->qkv.as<float>();
+    a.y = c->y.as<float>();
+    a.h = c->h.as<float>();
+    a.logits = c->logits.as<float>();
+    a.best = c->best.as<unsigned long long>();
+    a.rope_cos = c->rope_cos.as<float>();
+    a.rope_sin = c->rope_sin.as<float>();
+    a.sync = c->st_sync.as<uint32_t>();
+    a.status = c->status.as<int>();
+    a.eps = m->eps;
+    a.scale = 1.0f / sqrtf((float)HD);
+    int occ = 0;
+    if (cudaFuncSetAttribute(st::decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)st::kSmemBudget) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, st::decode_step_kernel, st::kThreads, st::kSmemBudget) !=
+            cudaSuccess ||
+        occ < 1) {
+        cudaGetLastError();
+        return;
+    }
+    // one cooperative launch per step, captured once
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        return;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((uint32_t)sms);
+    cfg.blockDim = dim3(st::kThreads);
+    cfg.dynamicSmemBytes = st::kSmemBudget;
+    cfg.stream = c->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e1 = cudaLaunchKernelEx(&cfg, st::decode_step_kernel, a);
+    const cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t e3 = (e1 == cudaSuccess && e2 == cudaSuccess) ? cudaGraphInstantiate(&exec, graph, 0) : e1;
+    if (graph)
+        cudaGraphDestroy(graph);
+    if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess) {
+        cudaGetLastError();
+        return;
+    }
+    c->graph_step = exec;
+    c->st_positions = a.kv_resident;
+}
+
+// The graph of the decode step at position `pos` (with logits / the greedy
+// pick when want): the persistent step kernel while the K/V history fits it.
+cudaGraphExec_t step_graph(const bnnd_context* c, uint32_t pos, bool want) {
+    if (!want)
+        return c->graph_prefill;
+    return c->graph_step && pos < c->st_positions ? c->graph_step : c->graph_logits;
+}
+
 BNND_Status create_llm_context(bnnd_context* c) {
     const bnnd_model* m = c->model;
     const BNND_ModelInfo& in = m->info;
@@ -1037,6 +1209,7 @@ BNND_Status create_llm_context(bnnd_context* c) {
             BNND_EIO);
     if ((st = capture_step(c, true, &c->graph_logits)) || (st = capture_step(c, false, &c->graph_prefill)))
         return st;
+    setup_step_kernel(c);
     return BNND_OK;
 }
 
@@ -1373,7 +1546,7 @@ BNND_Status decode(bnnd_context* c, const int32_t* tokens, uint32_t n, float* lo
                                 cudaMemcpyDeviceToDevice, c->stream),
                 BNND_EIO);
         const bool last = i + 1 == n;
-        CUDA_OR(cudaGraphLaunch((last && want) || all ? c->graph_logits : c->graph_prefill, c->stream), BNND_EIO);
+        CUDA_OR(cudaGraphLaunch(step_graph(c, start + i, (last && want) || all), c->stream), BNND_EIO);
         if (all)
             CUDA_OR(cudaMemcpyAsync(all + (size_t)i * m->info.n_vocab, c->logits.p, (size_t)m->info.n_vocab * 4,
                                     cudaMemcpyDeviceToHost, c->stream),
@@ -1584,7 +1757,7 @@ BNND_Status BNND_Generate(BNND_Context c, uint32_t steps, int32_t* out_tokens) {
     const uint32_t one = 1;
     CUDA_OR(cudaMemcpyAsync(c->hist_count.p, &one, 4, cudaMemcpyHostToDevice, c->stream), BNND_EIO);
     for (uint32_t i = 1; i < steps; ++i)
-        CUDA_OR(cudaGraphLaunch(c->graph_logits, c->stream), BNND_EIO);
+        CUDA_OR(cudaGraphLaunch(step_graph(c, start + i - 1, true), c->stream), BNND_EIO);
     if (out_tokens)
         CUDA_OR(cudaMemcpyAsync(out_tokens, c->hist.p, (size_t)steps * c->rows * 4, cudaMemcpyDeviceToHost,
                                 c->stream),
@@ -1763,6 +1936,8 @@ BNND_Status BNND_ContextProfile(BNND_Context c, uint32_t steps, BNND_KernelStat*
 }
 
 uint32_t BNND_StepLaunches(BNND_Context ctx) { return ctx ? ctx->step_launches : 0; }
+
+uint32_t BNND_StepKernelPositions(BNND_Context ctx) { return ctx && ctx->graph_step ? ctx->st_positions : 0; }
 
 const char* BNND_LastError(void) { return g_last_error.c_str(); }
 

@@ -174,8 +174,17 @@ typedef struct {
 BNND_Status BNND_ContextProfile(BNND_Context ctx, uint32_t steps, BNND_KernelStat* stats,
                                 uint32_t capacity, uint32_t* count, double* total_ms);
 
-/* Number of kernel launches in one decode step with logits. */
+/* Number of kernel launches in one decode step with logits (the per-kernel
+ * step graph). */
 uint32_t BNND_StepLaunches(BNND_Context ctx);
+
+/* Decode steps with logits at positions below the returned value run as ONE
+ * persistent kernel launch (one-row, single-GPU, exact-mode contexts with
+ * 128-wide heads; the whole K/V history of a head must fit one SM's shared
+ * memory); later positions, and other contexts (return 0), use the
+ * per-kernel step graph. Both give the same bits. Setting the environment
+ * variable BNN_STEP_KERNEL=0 before BNND_ContextCreate turns it off. */
+uint32_t BNND_StepKernelPositions(BNND_Context ctx);
 
 /* The CUDA stream the context's work runs on (cudaStream_t as void*). */
 void* BNND_ContextStream(BNND_Context ctx);
