@@ -79,6 +79,7 @@ class EngineApi:
                                             POINTER(ctypes.c_double)]),
             "BNND_StepLaunches": (c_uint32, [c_void_p]),
             "BNND_StepKernelPositions": (c_uint32, [c_void_p]),
+            "BNND_StepKernelTrace": (c_int, [c_void_p, c_void_p, ctypes.c_size_t, POINTER(ctypes.c_size_t)]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(d, name)
@@ -192,6 +193,15 @@ class Context:
 
     def step_launches(self):
         return self.api.StepLaunches(self.handle)
+
+    def step_kernel_trace(self):
+        """One greedy step through the step kernel with phase stamps:
+        uint64 [SMs][n_layers + 1][16] (ns, 0 = no such phase)."""
+        cnt = ctypes.c_size_t()
+        n = int(self.model.info.n_layers + 1) * 16 * 1024  # room for up to 1024 SMs
+        out = np.zeros(n, dtype=np.uint64)
+        self.api.check(self.api.StepKernelTrace(self.handle, out.ctypes.data, n, ctypes.byref(cnt)))
+        return out[:cnt.value].reshape(-1, self.model.info.n_layers + 1, 16)
 
     def step_kernel_positions(self):
         """Positions below which a decode step is one persistent kernel (0: never)."""

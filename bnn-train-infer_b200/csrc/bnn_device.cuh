@@ -124,6 +124,31 @@ struct RowQuantizer {
     }
 };
 
+// x / d correctly rounded, given rd = RN(1/d) (one reciprocal per divisor):
+// q = RN(x * rd) is within an ulp of x / d, so r = x - q d is exact by FMA,
+// and q1 = RN(q + r rd) is Markstein's corrected quotient (P. Markstein,
+// "IA-64 and Elementary Functions", 2000). q1 is then PROVED correct here:
+// its own remainder r1 = x - q1 d (exact by FMA whenever q1 is faithful) must
+// be below half the spacing of floats around q1, times |d| (a quarter ulp at
+// a power of two, where the spacing below halves); binary division has no
+// exact ties. Operands outside [2^-40, 2^40] (divisor) or quotients outside
+// [2^-60, 2^60], where those scalings could leave the normal range, and any
+// failed proof take __fdiv_rn. The result always equals __fdiv_rn(x, d).
+__device__ __forceinline__ float div_cr(float x, float d, float rd) {
+    const float q = __fmul_rn(x, rd);
+    const float r = __fmaf_rn(-q, d, x);
+    const float q1 = __fmaf_rn(r, rd, q);
+    const float r1 = __fmaf_rn(-q1, d, x);
+    const uint32_t qb = __float_as_uint(q1);
+    const uint32_t eq = (qb >> 23) & 0xffu;
+    const uint32_t ed = (__float_as_uint(d) >> 23) & 0xffu;
+    const uint32_t down = (qb & 0x7fffffu) == 0 ? 1u : 0u;  // a power of two: the spacing below is half
+    const float bound = __fmul_rn(fabsf(d), __uint_as_float((eq - 24u - down) << 23));
+    if (eq >= 127u - 60u && eq <= 127u + 60u && ed >= 127u - 40u && ed <= 127u + 40u && fabsf(r1) < bound)
+        return q1;
+    return __fdiv_rn(x, d);
+}
+
 // Correctly rounded binary32 exp: the double-precision exp rounded once to
 // float. (glibc's expf, which the reference links, is faithfully but not
 // correctly rounded: it differs from this on about 0.004% of inputs.)

@@ -12,8 +12,10 @@
 //     (and the RMSNorm gains) through a shared-memory ring from the first
 //     instruction on - weights never depend on activations, so the ring runs
 //     up to ~3 layers ahead and every contraction finds its rows on chip.
-// Phases of a layer, each a dataflow wait on a counter that the producing
-// CTAs increment after writing (release / acquire at GPU scope):
+// Phases of a layer, each a dataflow hand-off: the producing CTAs write their
+// rows as 8-byte (value, generation) pairs and the consumers poll the rows
+// themselves until every pair carries the phase's generation (no flag, no
+// fence: one L2 round trip once the last row lands):
 //   A  x ready      -> RMSNorm + quantise (every CTA, the full row) -> q|k|v rows
 //   B  q|k|v ready  -> attention (attention CTAs) -> y
 //   C  y ready      -> quantise y -> o rows, x += o   (rows the CTA owns)
@@ -44,12 +46,24 @@ constexpr uint32_t kWarps = 16;                     // compute warps of a CTA
 constexpr uint32_t kCThreads = kWarps * 32;         // 512
 constexpr uint32_t kThreads = kCThreads + 32;       // + the producer warp
 constexpr uint32_t kBarCompute = 1;                 // named barrier of the compute warps
-constexpr uint32_t kBarSum = 2;                     // warps 0..7: the exact RMS sum
+constexpr uint32_t kBarSum = 2;                     // the exact RMS sum (all compute warps)
 constexpr uint32_t kHD = 128;                       // head_dim of the step kernel
 constexpr size_t kSmemBudget = 226u * 1024u;  // dynamic; the static exit flag takes the rest of 227 KB
 
-// Counters of one layer (and the step's exit ticket after the last layer).
-enum : uint32_t { kCtrQkv = 0, kCtrY = 1, kCtrXo = 2, kCtrH = 3, kCtrXd = 4, kCtrPerLayer = 5 };
+// Hand-offs of one layer. The generation a writer stamps on its pairs is
+// epoch * 256 + layer * 5 + phase (at most 51 layers), never the all-ones
+// pattern the buffers are cleared to.
+enum : uint32_t { kPhQkv = 0, kPhY = 1, kPhXo = 2, kPhH = 3, kPhXd = 4, kPhPerLayer = 5 };
+constexpr uint32_t kMaxStepLayers = 51;
+
+__device__ __forceinline__ uint32_t hand_gen(uint32_t epoch, uint32_t l, uint32_t ph) {
+    return epoch * 256u + l * kPhPerLayer + ph;
+}
+
+// One value of a hand-off row, with its generation (8-byte stores are single-copy atomic).
+__device__ __forceinline__ void put_tagged(unsigned long long* dst, float v, uint32_t gen) {
+    __stcg(dst, ((unsigned long long)gen << 32) | __float_as_uint(v));
+}
 
 struct LayerPtrs {
     const float* q_norm;   // [HD]
@@ -76,18 +90,39 @@ struct StepArgs {
     int32_t* hist;
     uint32_t* hist_count;
     uint32_t hist_cap;
-    float *x, *qkv, *y, *h, *logits;
+    float* logits;
     unsigned long long* best;
     const float* rope_cos;          // [n_ctx][HD/2]
     const float* rope_sin;
-    uint32_t* sync;                 // [n_layers * kCtrPerLayer + 1] counters, zero at step start
+    // hand-off rows as (value, generation) pairs: a reader polls the data
+    // itself, each 8-byte pair valid once it carries the phase's generation
+    unsigned long long *xt, *qkvt, *yt, *ht;
+    uint32_t* epoch;                // step generation (advanced by the step's last CTA)
+    uint32_t* sync;                 // [1]: the exit ticket, zero at step start
     int* status;
     float eps, scale;
+    unsigned long long* trace;      // null, or [gridDim.x][n_layers + 1][kTraceSlots] %globaltimer stamps
 };
 
+constexpr uint32_t kTraceSlots = 16;
+
+__device__ __forceinline__ unsigned long long* trace_slot(const StepArgs& a, uint32_t l, uint32_t k) {
+    return a.trace ? a.trace + ((size_t)blockIdx.x * (a.n_layers + 1) + l) * kTraceSlots + k : nullptr;
+}
+
+// Phase timestamp `k` of layer record `l` of this CTA (thread 0), when tracing.
+__device__ __forceinline__ void stamp(const StepArgs& a, uint32_t l, uint32_t k) {
+    if (a.trace != nullptr && threadIdx.x == 0)
+        a.trace[((size_t)blockIdx.x * (a.n_layers + 1) + l) * kTraceSlots + k] = globaltimer_ns();
+}
+
 // ---- shared memory plans (one dynamic size; the two roles lay it out apart)
+constexpr uint32_t kOwnRowsMax = 64;  // residual rows a contraction CTA owns (8 blocks)
+
+constexpr uint32_t kSchedMax = 1024;  // copies per step a contraction CTA may stream
+
 struct GemvPlan {
-    size_t bars, red, xs, sum, act, tot, dsm, ring, total;
+    size_t bars, red, xown, offs, xs, sum, act, tot, dsm, ring, total;
 };
 
 __host__ __device__ inline GemvPlan gemv_plan(uint32_t C, uint32_t F, uint32_t dsm_bytes) {
@@ -95,9 +130,11 @@ __host__ __device__ inline GemvPlan gemv_plan(uint32_t C, uint32_t F, uint32_t d
     const uint32_t kmax = C > F ? C : F;
     p.bars = 0;                                                   // full[kSlots], empty[kSlots]
     p.red = 2 * kSlots * 8;                                       // 64 floats + flags
-    p.xs = (p.red + 64 * 4 + 64 + 15) & ~(size_t)15;              // FP32 row [kmax]
+    p.xown = p.red + 64 * 4 + 64;                                 // the CTA's residual rows [kOwnRowsMax]
+    p.offs = p.xown + kOwnRowsMax * 4;                            // ring offsets of the copies [kSchedMax]
+    p.xs = (p.offs + kSchedMax * 4 + 15) & ~(size_t)15;           // FP32 row [kmax]
     p.sum = (p.xs + (size_t)kmax * 4 + 15) & ~(size_t)15;         // exact RMS sum scratch
-    p.act = (p.sum + kSumSmemBytes + 15) & ~(size_t)15;           // sliced words [G][kActStride]
+    p.act = (p.sum + kWideSmemBytes + 15) & ~(size_t)15;          // sliced words [G][kActStride]
     p.tot = p.act + (size_t)(kmax / kGroup) * kActStride * 4;     // group totals [G]
     p.dsm = (p.tot + (size_t)(kmax / kGroup) * 4 + 15) & ~(size_t)15;  // int16 D of one copy
     p.ring = (p.dsm + dsm_bytes + 127) & ~(size_t)127;
@@ -146,49 +183,86 @@ __device__ __forceinline__ int status_now(const int* status) {
     return *reinterpret_cast<const volatile int*>(status);
 }
 
-// By the compute warps: every write of the CTA before this call is visible
-// to a CTA that saw the counter reach its target.
-__device__ __forceinline__ void arrive(uint32_t* ctr) {
+// By the compute warps: loads the K values of hand-off row `src` into xs
+// once every pair carries `gen` (bounded; gives up at once when the status
+// word is set). Each thread keeps all of its 16-byte loads in flight and
+// reissues only the pairs not yet written. Returns, to all threads, whether
+// the CTA should do its work; *amax_out and *bad_out (any non-finite value)
+// cover the whole row.
+__device__ __noinline__ bool poll_row(const unsigned long long* src, uint32_t K, uint32_t gen, float* xs, int* status,
+                                      int* flag, float* red, float* amax_out, int* bad_out) {
+    constexpr uint32_t kMine = 16;  // 16-byte chunks per thread at most (K <= 16384)
+    const uint32_t tid = threadIdx.x, chunks = K / 2;
+    const ulonglong2* s2 = reinterpret_cast<const ulonglong2*>(src);
+    if (tid == 0)
+        *flag = 1;
     named_barrier(kBarCompute, kCThreads);
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(ctr, 1u);
-    }
-}
-
-// By the compute warps: waits until *ctr >= target (bounded; gives up at
-// once when the status word is set). Returns false when the CTA should skip
-// its work.
-__device__ __forceinline__ bool wait_count(const uint32_t* ctr, uint32_t target, int* status, int* flag) {
-    if (threadIdx.x == 0) {
-        int ok = 1;
-        if (ld_acquire(ctr) < target) {
-            const uint64_t t0 = globaltimer_ns();
-            const uint64_t limit = *reinterpret_cast<volatile unsigned long long*>(&g_wait_ns_limit);
-            for (uint32_t i = 0;; ++i) {
-                if (ld_acquire(ctr) >= target)
-                    break;
-                if (status_now(status) != 0) {
-                    ok = 0;
-                    break;
-                }
-                if ((i & 63u) == 63u && globaltimer_ns() - t0 > limit) {
+    uint32_t pending = 0;
+    float amax = 0.0f;
+    int bad = 0;
+    auto take = [&](uint32_t i, ulonglong2 v) {
+        const uint32_t c = tid + i * kCThreads;
+        const bool ok0 = (uint32_t)(v.x >> 32) == gen, ok1 = (uint32_t)(v.y >> 32) == gen;
+        if (ok0 && ok1) {
+            const float f0 = __uint_as_float((uint32_t)v.x), f1 = __uint_as_float((uint32_t)v.y);
+            bad |= !isfinite(f0) | !isfinite(f1);
+            amax = fmaxf(amax, fmaxf(fabsf(f0), fabsf(f1)));
+            reinterpret_cast<float2*>(xs)[c] = make_float2(f0, f1);
+        } else {
+            pending |= 1u << i;
+        }
+    };
+#pragma unroll
+    for (uint32_t i = 0; i < kMine; ++i)
+        if (tid + i * kCThreads < chunks)
+            take(i, __ldcg(s2 + tid + i * kCThreads));
+    if (pending) {
+        const uint64_t t0 = globaltimer_ns();
+        const uint64_t limit = *reinterpret_cast<volatile unsigned long long*>(&g_wait_ns_limit);
+        for (uint32_t round = 0; pending; ++round) {
+            __nanosleep(64);
+            const uint32_t was = pending;
+            pending = 0;
+#pragma unroll
+            for (uint32_t i = 0; i < kMine; ++i)
+                if (was & (1u << i))
+                    take(i, __ldcg(s2 + tid + i * kCThreads));
+            if (pending && (round & 15u) == 15u &&
+                (status_now(status) != 0 || globaltimer_ns() - t0 > limit)) {
+                if (status_now(status) == 0)
                     atomicOr(status, kStatusTimeout);
-                    ok = 0;
-                    break;
-                }
+                *flag = 0;
+                break;
             }
         }
-        *flag = ok && status_now(status) == 0;
+    }
+    for (int o = 16; o > 0; o >>= 1)
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    bad = __reduce_or_sync(0xffffffffu, bad);
+    if ((tid & 31) == 0) {
+        red[32 + (tid >> 5)] = amax;
+        if (bad)
+            red[49] = 1.0f;
     }
     named_barrier(kBarCompute, kCThreads);
-    return *reinterpret_cast<volatile int*>(flag) != 0;
+    float m = red[32];
+    for (uint32_t w = 1; w < kWarps; ++w)
+        m = fmaxf(m, red[32 + w]);
+    *amax_out = m;
+    *bad_out = red[49] != 0.0f;
+    const bool live = *reinterpret_cast<volatile int*>(flag) != 0;
+    named_barrier(kBarCompute, kCThreads);  // red and flag are reused next
+    if (tid == 0)
+        red[49] = 0.0f;
+    return live;
 }
 
-// ---- the contraction pieces
+// ---- the contraction pieces (the larger ones kept out of line: a contraction
+// CTA runs phases A, C, D and E every layer, and one shared copy of each
+// piece stays in the instruction cache where inlined copies evict each other)
 // Integer D of every (block, row, group) of a copy of nb blocks at w into
 // dsm [b][row][g]: one warp per (block, group quad), as w1a8_gemv_kernel.
-__device__ __forceinline__ void copy_dots(const unsigned char* w, uint32_t nb, uint32_t G, const uint32_t* act_s,
+__device__ __noinline__ void copy_dots(const unsigned char* w, uint32_t nb, uint32_t G, const uint32_t* act_s,
                                           const int32_t* tot_s, int16_t* dsm) {
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, r = lane & 7;
     const uint32_t quads = (G + 3) / 4, items = nb * quads;
@@ -254,7 +328,7 @@ __device__ __forceinline__ float compute_max(float v, float* red) {
 
 // QuantizeRow of the K floats in xs (absmax given) into the sliced words and
 // group totals (the layout and lane transposes of w1a8_gemv_kernel).
-__device__ __forceinline__ float quantize_slice(const float* xs, uint32_t K, float amax, uint32_t* act_s,
+__device__ __noinline__ float quantize_slice(const float* xs, uint32_t K, float amax, uint32_t* act_s,
                                                 int32_t* tot_s) {
     const float s = row_scale_from_absmax(amax);
     const RowQuantizer quant(s);
@@ -281,52 +355,36 @@ __device__ __forceinline__ float quantize_slice(const float* xs, uint32_t K, flo
     return s;
 }
 
-// Loads K floats of a row written by other CTAs (L2, not L1) into xs.
-// Returns the absmax; *bad set for a non-finite value.
-__device__ __forceinline__ float load_row(const float* src, uint32_t K, float* xs, int* bad) {
-    float amax = 0.0f;
-    int b = 0;
-    const float4* s4 = reinterpret_cast<const float4*>(src);
-    float4* x4 = reinterpret_cast<float4*>(xs);
-    for (uint32_t i = threadIdx.x; i < K / 4; i += kCThreads) {
-        const float4 v = __ldcg(s4 + i);
-        b |= !isfinite(v.x) | !isfinite(v.y) | !isfinite(v.z) | !isfinite(v.w);
-        amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
-        x4[i] = v;
-    }
-    *bad = b;
-    return amax;
-}
-
 // RMSNorm (qwen3.c:361-372, the reference's serial sum) of the K floats in
 // xs with `gain`, in place, then QuantizeRow. Returns false (status set)
 // when the divisor is not finite or zero.
-__device__ __forceinline__ bool rms_quantize(float* xs, const float* gain, uint32_t K, float eps,
+__device__ __noinline__ bool rms_quantize(float* xs, const float* gain, uint32_t K, float eps,
                                              unsigned char* sum_mem, float* red, uint32_t* act_s, int32_t* tot_s,
-                                             float* s_out, int* status) {
+                                             float* s_out, int* status, unsigned long long* trace_at = nullptr) {
     named_barrier(kBarCompute, kCThreads);  // xs complete
-    if (threadIdx.x < (uint32_t)kSumThreads) {
-        const float sum = exact_sumsq(xs, (int)K, sum_mem, kBarSum);
-        if (threadIdx.x == 0)
-            red[48] = sum;
-    }
+    const float sum = exact_sumsq_wide(xs, (int)K, sum_mem, kBarSum);
+    if (threadIdx.x == 0)
+        red[48] = sum;
     named_barrier(kBarCompute, kCThreads);
+    if (trace_at != nullptr && threadIdx.x == 0)
+        *trace_at = globaltimer_ns();
     const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(red[48], (float)K), eps));
     if (!isfinite(rms) || rms == 0.0f) {
         if (threadIdx.x == 0)
             atomicOr(status, kStatusNonFinite);
         return false;
     }
+    const float rr = __frcp_rn(rms);
     float amax = 0.0f;
     float4* xb4 = reinterpret_cast<float4*>(xs);
     const float4* gr = reinterpret_cast<const float4*>(gain);
     for (uint32_t i = threadIdx.x; i < K / 4; i += kCThreads) {
         float4 v = xb4[i];
         const float4 gn = gr[i];
-        v.x = __fmul_rn(__fdiv_rn(v.x, rms), gn.x);
-        v.y = __fmul_rn(__fdiv_rn(v.y, rms), gn.y);
-        v.z = __fmul_rn(__fdiv_rn(v.z, rms), gn.z);
-        v.w = __fmul_rn(__fdiv_rn(v.w, rms), gn.w);
+        v.x = __fmul_rn(div_cr(v.x, rms, rr), gn.x);
+        v.y = __fmul_rn(div_cr(v.y, rms, rr), gn.y);
+        v.z = __fmul_rn(div_cr(v.z, rms, rr), gn.z);
+        v.w = __fmul_rn(div_cr(v.w, rms, rr), gn.w);
         amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
         xb4[i] = v;
     }
@@ -369,9 +427,10 @@ __device__ __forceinline__ void finish_step(const StepArgs& a, uint32_t pos) {
             a.hist[hc] = tok;
         *a.hist_count = hc + 1;
         *a.best = 0ull;
+        // the next step stamps new generations; the exit ticket starts again
+        *a.epoch = (*a.epoch + 1u) & 0xffffffu;
+        a.sync[0] = 0u;
     }
-    for (uint32_t i = threadIdx.x; i < a.n_layers * kCtrPerLayer + 1; i += kCThreads)
-        a.sync[i] = 0u;
 }
 
 // By the compute warps after the CTA's last phase: true in the CTA that
@@ -400,6 +459,7 @@ __device__ __forceinline__ void attention_role(const StepArgs& a, unsigned char*
     float *kres = reinterpret_cast<float*>(sm + p.kres), *vres = reinterpret_cast<float*>(sm + p.vres);
     constexpr uint32_t HD = kHD, kstride = eng::kcache_row(kHD);
     const uint32_t L = a.n_layers, hq = blockIdx.x, kv_mul = a.heads / a.kv_heads, g = hq / kv_mul, n = pos + 1;
+    const uint32_t epoch = *a.epoch;
     const size_t khead = (size_t)g * a.n_ctx * kstride, vhead = (size_t)g * a.n_ctx * HD;
     if (tid == 0) {
         mbar_init(kvbar, 1);
@@ -433,14 +493,37 @@ __device__ __forceinline__ void attention_role(const StepArgs& a, unsigned char*
             gq_s[i] = Lp.q_norm[i];
             gk_s[i] = Lp.k_norm[i];
         }
-        bool live = wait_count(a.sync + (size_t)l * kCtrPerLayer + kCtrQkv, a.n_gemv, a.status, flag);
-        if (tid < HD) {
-            q_s[tid] = __ldcg(a.qkv + (size_t)hq * HD + tid);
-            k_s[tid] = __ldcg(a.qkv + a.C + (size_t)g * HD + tid);
-            v_s[tid] = __ldcg(a.qkv + a.C + (size_t)a.kv_heads * HD + (size_t)g * HD + tid);
-        }
+        // q (this head), k and v (its KV head) as they are written: threads
+        // 0..63, 64..127, 128..191 each poll one 16-byte chunk (two pairs)
         if (tid == 0)
             *flag = 0;
+        named_barrier(kBarCompute, kCThreads);
+        if (tid < 3 * HD / 2) {
+            const uint32_t part = tid / (HD / 2), c = tid % (HD / 2);
+            const size_t base = part == 0 ? (size_t)hq * HD
+                                          : a.C + (size_t)(part - 1) * a.kv_heads * HD + (size_t)g * HD;
+            const ulonglong2* src = reinterpret_cast<const ulonglong2*>(a.qkvt + base) + c;
+            float* dst = part == 0 ? q_s : part == 1 ? k_s : v_s;
+            const uint32_t want = hand_gen(epoch, l, kPhQkv);
+            ulonglong2 v = __ldcg(src);
+            const uint64_t t0 = globaltimer_ns();
+            const uint64_t limit = *reinterpret_cast<volatile unsigned long long*>(&g_wait_ns_limit);
+            for (uint32_t round = 0; (uint32_t)(v.x >> 32) != want || (uint32_t)(v.y >> 32) != want; ++round) {
+                if ((round & 15u) == 15u && (status_now(a.status) != 0 || globaltimer_ns() - t0 > limit)) {
+                    if (status_now(a.status) == 0)
+                        atomicOr(a.status, kStatusTimeout);
+                    *flag = 1;
+                    break;
+                }
+                __nanosleep(64);
+                v = __ldcg(src);
+            }
+            dst[2 * c] = __uint_as_float((uint32_t)v.x);
+            dst[2 * c + 1] = __uint_as_float((uint32_t)v.y);
+        }
+        named_barrier(kBarCompute, kCThreads);
+        bool live = *reinterpret_cast<volatile int*>(flag) == 0;
+        stamp(a, l, 0);
         named_barrier(kBarCompute, kCThreads);
         if (live && warp < 2) {
             if (!eng::attn_norm_rope<HD>(warp == 0 ? q_s : k_s, warp == 0 ? gq_s : gk_s, rc_s, rs_s, a.eps, true) &&
@@ -451,6 +534,7 @@ __device__ __forceinline__ void attention_role(const StepArgs& a, unsigned char*
         }
         named_barrier(kBarCompute, kCThreads);
         live = live && *reinterpret_cast<volatile int*>(flag) == 0;
+        stamp(a, l, 1);
         // append this position's k and v (the first query head of the KV head writes)
         if (live && hq % kv_mul == 0 && tid < HD) {
             Lp.kcache[khead + (size_t)pos * kstride + tid] = k_s[tid];
@@ -461,6 +545,7 @@ __device__ __forceinline__ void attention_role(const StepArgs& a, unsigned char*
                 atomicOr(a.status, kStatusTimeout);
             live = false;
         }
+        stamp(a, l, 2);
         // scores: one position per thread, each dot serial over the head dimension
         int bad = 0;
         if (live) {
@@ -488,6 +573,7 @@ __device__ __forceinline__ void attention_role(const StepArgs& a, unsigned char*
         }
         named_barrier(kBarCompute, kCThreads);
         live = live && *reinterpret_cast<volatile int*>(flag) == 0;
+        stamp(a, l, 3);
         // softmax: max, expf(s - max), serial sum, division
         float mx = -INFINITY;
         if (live)
@@ -522,10 +608,13 @@ __device__ __forceinline__ void attention_role(const StepArgs& a, unsigned char*
         }
         named_barrier(kBarCompute, kCThreads);
         live = live && *reinterpret_cast<volatile int*>(flag) == 0;
-        if (live)
+        if (live) {
+            const float sum = red[16], rs = __frcp_rn(sum);
             for (uint32_t t = tid; t < n; t += kCThreads)
-                sc[t] = __fdiv_rn(sc[t], red[16]);
+                sc[t] = div_cr(sc[t], sum, rs);
+        }
         named_barrier(kBarCompute, kCThreads);
+        stamp(a, l, 4);
         // y_d = sum_t p_t * v_t,d: one serial chain per dimension
         if (live && tid < HD) {
             const uint32_t d = tid;
@@ -549,14 +638,14 @@ __device__ __forceinline__ void attention_role(const StepArgs& a, unsigned char*
             for (; t < pos; ++t)
                 v = __fadd_rn(v, __fmul_rn(sc[t], vres[(size_t)t * HD + d]));
             v = __fadd_rn(v, __fmul_rn(sc[pos], v_s[d]));
-            a.y[(size_t)hq * HD + d] = v;
+            put_tagged(a.yt + (size_t)hq * HD + d, v, hand_gen(epoch, l, kPhY));
         }
         // the history buffers are free again: the next layer's copies start
         fence_proxy_async();
         named_barrier(kBarCompute, kCThreads);
         if (l + 1 < L)
             prefetch(l + 1);
-        arrive(a.sync + (size_t)l * kCtrPerLayer + kCtrY);
+        stamp(a, l, 5);
     }
 }
 
@@ -571,8 +660,8 @@ __device__ __forceinline__ void contraction_role(const StepArgs& a, unsigned cha
     float* red = reinterpret_cast<float*>(sm + p.red);
     int* flag = reinterpret_cast<int*>(sm + p.red + 64 * 4);
     volatile int* stopped_at = reinterpret_cast<volatile int*>(sm + p.red + 64 * 4 + 4);
-    int* badf = reinterpret_cast<int*>(sm + p.red + 64 * 4 + 8);
     float* xs = reinterpret_cast<float*>(sm + p.xs);
+    float* xown = reinterpret_cast<float*>(sm + p.xown);  // x rows [8 o0, 8 o1), kept here between phases
     unsigned char* sum_mem = sm + p.sum;
     uint32_t* act_s = reinterpret_cast<uint32_t*>(sm + p.act);
     int32_t* tot_s = reinterpret_cast<int32_t*>(sm + p.tot);
@@ -581,6 +670,7 @@ __device__ __forceinline__ void contraction_role(const StepArgs& a, unsigned cha
     const Copy* sched = a.sched + (size_t)j * a.sched_stride;
     const uint32_t nsched = a.sched_len[j];
 
+    uint32_t* offs = reinterpret_cast<uint32_t*>(sm + p.offs);
     if (tid == 0) {
         for (uint32_t s = 0; s < kSlots; ++s) {
             mbar_init(&full[s], 1);
@@ -589,6 +679,10 @@ __device__ __forceinline__ void contraction_role(const StepArgs& a, unsigned cha
         fence_barrier_init();
         *stopped_at = 0x7fffffff;
     }
+    // the ring offset of every copy, read once (the consumers need it on the
+    // critical path; a global load there costs an L2 round trip)
+    for (uint32_t i = tid; i < nsched; i += kThreads)
+        offs[i] = sched[i].ring_off;
     __syncthreads();
     if (warp == kWarps) {
         // copy warp: the whole step's weight rows and gains, in consumption order
@@ -620,7 +714,7 @@ __device__ __forceinline__ void contraction_role(const StepArgs& a, unsigned cha
     auto take = [&]() -> const unsigned char* {
         if (!take_copy(full, ci, stopped_at) && lane == 0)
             atomicOr(a.status, kStatusTimeout);
-        return ring + sched[ci].ring_off;
+        return ring + offs[ci];
     };
     auto release = [&]() {
         named_barrier(kBarCompute, kCThreads);
@@ -628,20 +722,17 @@ __device__ __forceinline__ void contraction_role(const StepArgs& a, unsigned cha
             mbar_arrive(&empty[ci % kSlots]);
         ++ci;
     };
-    auto ctr = [&](uint32_t l, uint32_t k) { return a.sync + (size_t)l * kCtrPerLayer + k; };
-    // QuantizeRow of a row of K floats that other CTAs wrote (y or h)
-    auto quant_prologue = [&](const float* src, uint32_t K, bool live, float* s) -> bool {
-        if (tid == 0)
-            *badf = 0;
-        named_barrier(kBarCompute, kCThreads);
-        int bad = 0;
-        float amax = live ? load_row(src, K, xs, &bad) : 0.0f;
-        if (bad)
-            *badf = 1;  // a linear rejects non-finite input (ValidateF32Input, soft :294-308)
-        amax = compute_max(amax, red);
-        const bool ok = live && *reinterpret_cast<volatile int*>(badf) == 0;
-        if (live && !ok && tid == 0)
+    const uint32_t epoch = *a.epoch;
+    auto gen = [&](uint32_t l, uint32_t ph) { return hand_gen(epoch, l, ph); };
+    // QuantizeRow of a hand-off row of K floats that other CTAs wrote (y or h)
+    auto quant_prologue = [&](const unsigned long long* src, uint32_t K, uint32_t g, float* s) -> bool {
+        float amax;
+        int bad;
+        const bool live = poll_row(src, K, g, xs, a.status, flag, red, &amax, &bad);
+        // a linear rejects non-finite input (ValidateF32Input, soft :294-308)
+        if (live && bad && tid == 0)
             atomicOr(a.status, kStatusBadInput);
+        const bool ok = live && !bad;
         if (ok)
             *s = quantize_slice(xs, K, amax, act_s, tot_s);
         return ok;
@@ -663,7 +754,9 @@ __device__ __forceinline__ void contraction_role(const StepArgs& a, unsigned cha
 
     // qwen3_embed (qwen3.c:374-385): the token's row of the tied lm_head
     // blocks; the full row stays in xs for layer 0's RMSNorm, the rows this
-    // CTA owns go to x
+    // CTA owns stay in xown for the residual adds
+    if (tid == 0)
+        red[49] = 0.0f;
     if (q1 > q0 || o1 > o0) {
         const uint32_t tok = (uint32_t)a.tok_in[0];
         const unsigned char* blk = a.lm_head + (size_t)(tok / kRowBlock) * GC * 144u;
@@ -677,113 +770,126 @@ __device__ __forceinline__ void contraction_role(const StepArgs& a, unsigned cha
         }
         named_barrier(kBarCompute, kCThreads);
         for (uint32_t k = o0 * kRowBlock + tid; k < o1 * kRowBlock; k += kCThreads)
-            a.x[k] = xs[k];
+            xown[k - o0 * kRowBlock] = xs[k];
     }
+    if (tid == 0)
+        *flag = status_now(a.status) == 0;
+    named_barrier(kBarCompute, kCThreads);
+    const bool live0 = *reinterpret_cast<volatile int*>(flag) != 0;
 
     for (uint32_t l = 0; l < L; ++l) {
         // ---- A: attn_norm + q|k|v rows
+        stamp(a, l, 0);
         if (q1 > q0) {
-            bool live;
-            if (l == 0) {
-                if (tid == 0)
-                    *flag = status_now(a.status) == 0;
-                named_barrier(kBarCompute, kCThreads);
-                live = *reinterpret_cast<volatile int*>(flag) != 0;
-            } else {
-                live = wait_count(ctr(l - 1, kCtrXd), a.n_gemv, a.status, flag);
+            bool live = live0;
+            if (l > 0) {
+                float amax;
                 int bad;
-                if (live)
-                    load_row(a.x, C, xs, &bad);
+                live = poll_row(a.xt, C, gen(l - 1, kPhXd), xs, a.status, flag, red, &amax, &bad);
             }
+            stamp(a, l, 1);
             const float* gain = reinterpret_cast<const float*>(take());
-            live = live && rms_quantize(xs, gain, C, a.eps, sum_mem, red, act_s, tot_s, &s, a.status);
+            live = live && rms_quantize(xs, gain, C, a.eps, sum_mem, red, act_s, tot_s, &s, a.status,
+                                        trace_slot(a, l, 13));
             release();
+            stamp(a, l, 2);
             const unsigned char* w = take();
             const uint32_t nb = q1 - q0;
             if (live) {
                 copy_dots(w, nb, GC, act_s, tot_s, dsm);
                 named_barrier(kBarCompute, kCThreads);
+                const uint32_t g = gen(l, kPhQkv);
                 for (uint32_t q = tid; q < nb * kRowBlock; q += kCThreads) {
                     const uint32_t n = q0 * kRowBlock + q;
                     if (n < a.qkv_rows)
-                        a.qkv[n] = __fmul_rn(acc_of(w, GC, q / kRowBlock, q % kRowBlock), s);
+                        put_tagged(a.qkvt + n, __fmul_rn(acc_of(w, GC, q / kRowBlock, q % kRowBlock), s), g);
                 }
             }
             release();
         }
-        arrive(ctr(l, kCtrQkv));
+        stamp(a, l, 3);
         // ---- C: o rows, x += o
         if (o1 > o0) {
-            bool live = wait_count(ctr(l, kCtrY), a.n_attn, a.status, flag);
-            live = quant_prologue(a.y, C, live, &s);
+            bool live = quant_prologue(a.yt, C, gen(l, kPhY), &s);
+            stamp(a, l, 4);
+            stamp(a, l, 5);
             const unsigned char* w = take();
             const uint32_t nb = o1 - o0;
             if (live) {
                 copy_dots(w, nb, GC, act_s, tot_s, dsm);
                 named_barrier(kBarCompute, kCThreads);
+                const uint32_t g = gen(l, kPhXo);
                 for (uint32_t q = tid; q < nb * kRowBlock; q += kCThreads) {
-                    const uint32_t n = o0 * kRowBlock + q;
                     const float y = __fmul_rn(acc_of(w, GC, q / kRowBlock, q % kRowBlock), s);
-                    a.x[n] = __fadd_rn(__ldcg(a.x + n), y);
+                    const float xn = __fadd_rn(xown[q], y);
+                    xown[q] = xn;
+                    put_tagged(a.xt + o0 * kRowBlock + q, xn, g);
                 }
             }
             release();
         }
-        arrive(ctr(l, kCtrXo));
+        stamp(a, l, 6);
         // ---- D: ffn_norm + gate|up pairs + SwiGLU
         if (p1 > p0) {
-            bool live = wait_count(ctr(l, kCtrXo), a.n_gemv, a.status, flag);
+            float amax;
             int bad;
-            if (live)
-                load_row(a.x, C, xs, &bad);
+            bool live = poll_row(a.xt, C, gen(l, kPhXo), xs, a.status, flag, red, &amax, &bad);
+            stamp(a, l, 7);
             const float* gain = reinterpret_cast<const float*>(take());
-            live = live && rms_quantize(xs, gain, C, a.eps, sum_mem, red, act_s, tot_s, &s, a.status);
+            live = live && rms_quantize(xs, gain, C, a.eps, sum_mem, red, act_s, tot_s, &s, a.status,
+                                        trace_slot(a, l, 14));
             release();
+            stamp(a, l, 8);
             const unsigned char* w = take();
             const uint32_t np = p1 - p0;
             if (live) {
                 copy_dots(w, 2 * np, GC, act_s, tot_s, dsm);
                 named_barrier(kBarCompute, kCThreads);
+                const uint32_t g = gen(l, kPhH);
                 for (uint32_t q = tid; q < np * kRowBlock; q += kCThreads) {
                     const uint32_t k = q / kRowBlock, r = q % kRowBlock;
                     const float gt = __fmul_rn(acc_of(w, GC, 2 * k, r), s);
                     const float up = __fmul_rn(acc_of(w, GC, 2 * k + 1, r), s);
                     const float silu = __fdiv_rn(gt, __fadd_rn(1.0f, expf_cr(-gt)));
-                    a.h[(size_t)(p0 + k) * kRowBlock + r] = __fmul_rn(silu, up);
+                    put_tagged(a.ht + (size_t)(p0 + k) * kRowBlock + r, __fmul_rn(silu, up), g);
                 }
             }
             release();
         }
-        arrive(ctr(l, kCtrH));
+        stamp(a, l, 9);
         // ---- E: down rows, x += d
         if (o1 > o0) {
-            bool live = wait_count(ctr(l, kCtrH), a.n_gemv, a.status, flag);
-            live = quant_prologue(a.h, F, live, &s);
+            bool live = quant_prologue(a.ht, F, gen(l, kPhH), &s);
+            stamp(a, l, 10);
+            stamp(a, l, 11);
             const unsigned char* w = take();
             const uint32_t nb = o1 - o0;
             if (live) {
                 copy_dots(w, nb, GF, act_s, tot_s, dsm);
                 named_barrier(kBarCompute, kCThreads);
+                const uint32_t g = gen(l, kPhXd);
                 for (uint32_t q = tid; q < nb * kRowBlock; q += kCThreads) {
-                    const uint32_t n = o0 * kRowBlock + q;
                     const float d = __fmul_rn(acc_of(w, GF, q / kRowBlock, q % kRowBlock), s);
-                    a.x[n] = __fadd_rn(__ldcg(a.x + n), d);
+                    const float xn = __fadd_rn(xown[q], d);
+                    xown[q] = xn;
+                    put_tagged(a.xt + o0 * kRowBlock + q, xn, g);
                 }
             }
             release();
         }
-        arrive(ctr(l, kCtrXd));
+        stamp(a, l, 12);
     }
 
     // ---- out_norm + lm_head + greedy pick (bnn-infer-v2.c:48-54: first maximum)
     if (v1 > v0) {
-        bool live = wait_count(ctr(L - 1, kCtrXd), a.n_gemv, a.status, flag);
+        float amax;
         int bad;
-        if (live)
-            load_row(a.x, C, xs, &bad);
+        bool live = poll_row(a.xt, C, gen(L - 1, kPhXd), xs, a.status, flag, red, &amax, &bad);
+        stamp(a, L, 0);
         const float* gain = reinterpret_cast<const float*>(take());
         live = live && rms_quantize(xs, gain, C, a.eps, sum_mem, red, act_s, tot_s, &s, a.status);
         release();
+        stamp(a, L, 1);
         unsigned long long best = 0ull;
         int nonfinite = 0;
         for (uint32_t b0 = v0; b0 < v1; b0 += kLmChunkBlocks) {
@@ -805,6 +911,7 @@ __device__ __forceinline__ void contraction_role(const StepArgs& a, unsigned cha
             }
             release();
         }
+        stamp(a, L, 2);
         if (nonfinite)
             atomicOr(a.status, kStatusNonFinite);
         for (int o = 16; o > 0; o >>= 1) {
@@ -816,9 +923,12 @@ __device__ __forceinline__ void contraction_role(const StepArgs& a, unsigned cha
     }
 }
 
+static_assert(kCThreads == (uint32_t)kWideThreads, "the exact RMS sum runs on every compute thread");
+
 __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(StepArgs a) {
     extern __shared__ __align__(128) unsigned char sm[];
     const uint32_t pos = *a.pos;
+    stamp(a, a.n_layers, 15);
     if (blockIdx.x < a.n_attn) {
         if (threadIdx.x >= kCThreads)
             return;  // no copy warp in this role
@@ -829,8 +939,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(StepArgs a) {
             return;  // the copy warp has left
     }
     __shared__ int exit_flag;
-    if (exit_ticket(a.sync + (size_t)a.n_layers * kCtrPerLayer, &exit_flag))
+    if (exit_ticket(a.sync, &exit_flag)) {
         finish_step(a, pos);
+        stamp(a, a.n_layers, 14);
+    }
 }
 
 }  // namespace step

@@ -270,7 +270,7 @@ struct bnnd_context {
     DevMem dm_act, dm_tot, dm_rs;  // steps of kStepRowsPrep+ rows: sliced rows, group totals, row scales
     DevMem lg_pos;                 // BNND_DecodeLogitsAll: one position's logits
     // persistent step kernel (decode_step.cuh): one launch per decode step
-    DevMem st_sync, st_sched, st_sched_len, st_layers;
+    DevMem st_sync, st_sched, st_sched_len, st_layers, st_xt, st_qkvt, st_yt, st_ht;
     bnn::step::StepArgs st_args{};
     uint32_t st_positions = 0;     // steps at positions below this use it (0: never)
     cudaGraphExec_t graph_step = nullptr;
@@ -952,6 +952,21 @@ BNND_Status capture_step(bnnd_context* c, bool with_logits, cudaGraphExec_t* out
     return BNND_OK;
 }
 
+// One cooperative launch of the step kernel (one CTA per SM) on the context's stream.
+cudaError_t launch_step_kernel(bnnd_context* c, const bnn::step::StepArgs& a) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.n_attn + a.n_gemv);
+    cfg.blockDim = dim3(bnn::step::kThreads);
+    cfg.dynamicSmemBytes = bnn::step::kSmemBudget;
+    cfg.stream = c->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, bnn::step::decode_step_kernel, a);
+}
+
 // The persistent step kernel for one-row, single-GPU, exact-mode contexts
 // with 128-wide heads (decode_step.cuh). Leaves c->graph_step null, and the
 // per-kernel step graph in charge, when the shape or the device does not
@@ -963,12 +978,20 @@ void setup_step_kernel(bnnd_context* c) {
     const char* env = std::getenv("BNN_STEP_KERNEL");
     if (env && env[0] == '0')
         return;
+    const bool say = std::getenv("BNN_STEP_KERNEL_DEBUG") != nullptr;
+    auto why = [&](const char* what) {
+        if (say)
+            std::fprintf(stderr, "step kernel off: %s (%s)\n", what, cudaGetErrorString(cudaGetLastError()));
+        cudaGetLastError();
+    };
     const int sms = m->dev->sm_count;
     int coop = 0;
     if (c->rows != 1 || c->world != 1 || !c->params.exact || in.head_dim != st::kHD || in.hidden % 128 ||
         in.ffn % 128 || in.heads % in.kv_heads || (int)in.heads + 1 >= sms ||
+        (in.hidden / 8 + (sms - in.heads) - 1) / (sms - in.heads) * 8 > st::kOwnRowsMax ||
+        in.hidden > 16384 || in.ffn > 16384 ||
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->dev->ordinal) != cudaSuccess || !coop) {
-        cudaGetLastError();
+        why("shape or device");
         return;
     }
     const uint32_t C = in.hidden, F = in.ffn, L = in.n_layers, HD = in.head_dim;
@@ -983,8 +1006,10 @@ void setup_step_kernel(bnnd_context* c) {
                                    std::min(st::kLmChunkBlocks, ceil_div(nb_v, n_gemv)) * GC});
     const uint32_t dsm_bytes = dsm_units * 8u * 2u;
     const st::GemvPlan gp = st::gemv_plan(C, F, dsm_bytes);
-    if (gp.ring >= st::kSmemBudget)
+    if (gp.ring >= st::kSmemBudget) {
+        why("shared memory");
         return;
+    }
     const uint32_t ring = (uint32_t)((st::kSmemBudget - gp.ring) & ~(size_t)127);
     st::ScheduleShape shape{L, C, F, qkv_rows, in.n_vocab, n_gemv, ring};
     std::vector<st::LayerSrc> srcs(L);
@@ -998,9 +1023,15 @@ void setup_step_kernel(bnnd_context* c) {
     uint32_t stride = 1;
     for (uint32_t j = 0; j < n_gemv; ++j) {
         if (!st::build_schedule(shape, srcs, (uint64_t)(uintptr_t)m->lm_head.m->wblocks,
-                                (uint64_t)(uintptr_t)m->out_norm.p, j, &scheds[j]))
+                                (uint64_t)(uintptr_t)m->out_norm.p, j, &scheds[j])) {
+            why("schedule");
             return;
+        }
         stride = std::max<uint32_t>(stride, (uint32_t)scheds[j].size());
+    }
+    if (stride > st::kSchedMax) {
+        why("too many copies per step");
+        return;
     }
     std::vector<st::Copy> flat((size_t)n_gemv * stride);
     std::vector<uint32_t> lens(n_gemv);
@@ -1017,16 +1048,31 @@ void setup_step_kernel(bnnd_context* c) {
                               c->kcache.as<float>() + (size_t)l * (layer_cache / HD * bnn::eng::kcache_row(HD)),
                               c->vcache.as<float>() + (size_t)l * layer_cache};
     }
-    const uint32_t n_ctr = L * st::kCtrPerLayer + 1;
-    if (dev_alloc(c->st_sync, (size_t)n_ctr * 4) || dev_alloc(c->st_sched, flat.size() * sizeof(st::Copy)) ||
+    const uint32_t sync_init[2] = {0u, 1u};  // exit ticket, step generation
+    if (L > st::kMaxStepLayers) {
+        why("too many layers");
+        return;
+    }
+    // hand-off rows as (value, generation) pairs, cleared to a generation no step stamps
+    if (dev_alloc(c->st_xt, (size_t)C * 8) || dev_alloc(c->st_qkvt, (size_t)qkv_rows * 8) ||
+        dev_alloc(c->st_yt, (size_t)C * 8) || dev_alloc(c->st_ht, (size_t)F * 8) ||
+        cudaMemset(c->st_xt.p, 0xff, (size_t)C * 8) != cudaSuccess ||
+        cudaMemset(c->st_qkvt.p, 0xff, (size_t)qkv_rows * 8) != cudaSuccess ||
+        cudaMemset(c->st_yt.p, 0xff, (size_t)C * 8) != cudaSuccess ||
+        cudaMemset(c->st_ht.p, 0xff, (size_t)F * 8) != cudaSuccess) {
+        why("allocation");
+        g_last_error.clear();
+        return;
+    }
+    if (dev_alloc(c->st_sync, sizeof sync_init) || dev_alloc(c->st_sched, flat.size() * sizeof(st::Copy)) ||
         dev_alloc(c->st_sched_len, lens.size() * 4) || dev_alloc(c->st_layers, lp.size() * sizeof(st::LayerPtrs)) ||
-        cudaMemset(c->st_sync.p, 0, (size_t)n_ctr * 4) != cudaSuccess ||
+        cudaMemcpy(c->st_sync.p, sync_init, sizeof sync_init, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemset(c->best.p, 0, 8) != cudaSuccess ||
         cudaMemcpy(c->st_sched.p, flat.data(), flat.size() * sizeof(st::Copy), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(c->st_sched_len.p, lens.data(), lens.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(c->st_layers.p, lp.data(), lp.size() * sizeof(st::LayerPtrs), cudaMemcpyHostToDevice) !=
             cudaSuccess) {
-        cudaGetLastError();
+        why("allocation");
         g_last_error.clear();
         return;
     }
@@ -1055,15 +1101,16 @@ void setup_step_kernel(bnnd_context* c) {
     a.hist = c->hist.as<int32_t>();
     a.hist_count = c->hist_count.as<uint32_t>();
     a.hist_cap = c->hist_cap;
-    a.x = c->x.as<float>();
-    a.qkv = c->qkv.as<float>();
-    a.y = c->y.as<float>();
-    a.h = c->h.as<float>();
     a.logits = c->logits.as<float>();
     a.best = c->best.as<unsigned long long>();
     a.rope_cos = c->rope_cos.as<float>();
     a.rope_sin = c->rope_sin.as<float>();
     a.sync = c->st_sync.as<uint32_t>();
+    a.epoch = c->st_sync.as<uint32_t>() + 1;
+    a.xt = c->st_xt.as<unsigned long long>();
+    a.qkvt = c->st_qkvt.as<unsigned long long>();
+    a.yt = c->st_yt.as<unsigned long long>();
+    a.ht = c->st_ht.as<unsigned long long>();
     a.status = c->status.as<int>();
     a.eps = m->eps;
     a.scale = 1.0f / sqrtf((float)HD);
@@ -1073,45 +1120,41 @@ void setup_step_kernel(bnnd_context* c) {
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, st::decode_step_kernel, st::kThreads, st::kSmemBudget) !=
             cudaSuccess ||
         occ < 1) {
-        cudaGetLastError();
+        why("occupancy");
         return;
     }
-    // one cooperative launch per step, captured once
+    // one cooperative launch per step, captured once; where capturing it is
+    // refused (some profilers), the kernel is launched directly instead
+    c->st_positions = a.kv_resident;
     cudaGraph_t graph = nullptr;
     if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
-        cudaGetLastError();
+        why("capture");
         return;
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((uint32_t)sms);
-    cfg.blockDim = dim3(st::kThreads);
-    cfg.dynamicSmemBytes = st::kSmemBudget;
-    cfg.stream = c->stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const cudaError_t e1 = cudaLaunchKernelEx(&cfg, st::decode_step_kernel, a);
+    const cudaError_t e1 = launch_step_kernel(c, a);
     const cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
     cudaGraphExec_t exec = nullptr;
     const cudaError_t e3 = (e1 == cudaSuccess && e2 == cudaSuccess) ? cudaGraphInstantiate(&exec, graph, 0) : e1;
     if (graph)
         cudaGraphDestroy(graph);
-    if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess) {
-        cudaGetLastError();
-        return;
-    }
-    c->graph_step = exec;
-    c->st_positions = a.kv_resident;
+    if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess)
+        why("graph (direct launches instead)");
+    else
+        c->graph_step = exec;
+    if (say)
+        std::fprintf(stderr, "step kernel on below position %u (%s)\n", c->st_positions,
+                     c->graph_step ? "graph" : "direct launches");
 }
 
-// The graph of the decode step at position `pos` (with logits / the greedy
-// pick when want): the persistent step kernel while the K/V history fits it.
-cudaGraphExec_t step_graph(const bnnd_context* c, uint32_t pos, bool want) {
+// Enqueues the decode step at position `pos` (with logits and the greedy
+// pick when want): the persistent step kernel while the K/V history fits
+// it, else the per-kernel step graph.
+cudaError_t run_step(bnnd_context* c, uint32_t pos, bool want) {
     if (!want)
-        return c->graph_prefill;
-    return c->graph_step && pos < c->st_positions ? c->graph_step : c->graph_logits;
+        return cudaGraphLaunch(c->graph_prefill, c->stream);
+    if (c->st_positions && pos < c->st_positions)
+        return c->graph_step ? cudaGraphLaunch(c->graph_step, c->stream) : launch_step_kernel(c, c->st_args);
+    return cudaGraphLaunch(c->graph_logits, c->stream);
 }
 
 BNND_Status create_llm_context(bnnd_context* c) {
@@ -1546,7 +1589,7 @@ BNND_Status decode(bnnd_context* c, const int32_t* tokens, uint32_t n, float* lo
                                 cudaMemcpyDeviceToDevice, c->stream),
                 BNND_EIO);
         const bool last = i + 1 == n;
-        CUDA_OR(cudaGraphLaunch(step_graph(c, start + i, (last && want) || all), c->stream), BNND_EIO);
+        CUDA_OR(run_step(c, start + i, (last && want) || all), BNND_EIO);
         if (all)
             CUDA_OR(cudaMemcpyAsync(all + (size_t)i * m->info.n_vocab, c->logits.p, (size_t)m->info.n_vocab * 4,
                                     cudaMemcpyDeviceToHost, c->stream),
@@ -1757,7 +1800,7 @@ BNND_Status BNND_Generate(BNND_Context c, uint32_t steps, int32_t* out_tokens) {
     const uint32_t one = 1;
     CUDA_OR(cudaMemcpyAsync(c->hist_count.p, &one, 4, cudaMemcpyHostToDevice, c->stream), BNND_EIO);
     for (uint32_t i = 1; i < steps; ++i)
-        CUDA_OR(cudaGraphLaunch(step_graph(c, start + i - 1, true), c->stream), BNND_EIO);
+        CUDA_OR(run_step(c, start + i - 1, true), BNND_EIO);
     if (out_tokens)
         CUDA_OR(cudaMemcpyAsync(out_tokens, c->hist.p, (size_t)steps * c->rows * 4, cudaMemcpyDeviceToHost,
                                 c->stream),
@@ -1937,7 +1980,40 @@ BNND_Status BNND_ContextProfile(BNND_Context c, uint32_t steps, BNND_KernelStat*
 
 uint32_t BNND_StepLaunches(BNND_Context ctx) { return ctx ? ctx->step_launches : 0; }
 
-uint32_t BNND_StepKernelPositions(BNND_Context ctx) { return ctx && ctx->graph_step ? ctx->st_positions : 0; }
+uint32_t BNND_StepKernelPositions(BNND_Context ctx) { return ctx ? ctx->st_positions : 0; }
+
+BNND_Status BNND_StepKernelTrace(BNND_Context c, uint64_t* stamps, size_t capacity, size_t* count) {
+    g_last_error.clear();
+    if (!c || !stamps || !count)
+        return BNND_EINVAL;
+    if (!c->st_positions || c->pos >= c->st_positions || c->pos >= c->n_ctx)
+        return fail(BNND_ENOTSUP, "the step kernel does not serve this context or position");
+    if (!c->have_logits)
+        return fail(BNND_EINVAL, "a step trace needs a preceding decode with logits");
+    const uint32_t grid = (uint32_t)c->model->dev->sm_count;
+    const size_t words = (size_t)grid * (c->st_args.n_layers + 1) * bnn::step::kTraceSlots;
+    *count = words;
+    if (capacity < words)
+        return fail(BNND_ERANGE, "trace needs %zu entries", words);
+    bnn::DeviceGuard guard(c->model->dev->ordinal);
+    DevMem tr;
+    BNND_Status st = dev_alloc(tr, words * 8);
+    if (st != BNND_OK)
+        return st;
+    CUDA_OR(cudaMemsetAsync(tr.p, 0, words * 8, c->stream), BNND_EIO);
+    bnn::step::StepArgs a = c->st_args;
+    a.trace = tr.as<unsigned long long>();
+    CUDA_OR(launch_step_kernel(c, a), BNND_EIO);
+    CUDA_OR(cudaMemcpyAsync(stamps, tr.p, words * 8, cudaMemcpyDeviceToHost, c->stream), BNND_EIO);
+    const uint32_t start = c->pos;
+    st = finish(c, "BNND_StepKernelTrace");
+    if (st != BNND_OK) {
+        set_pos(c, start);
+        return st;
+    }
+    c->pos = start + 1;
+    return BNND_OK;
+}
 
 const char* BNND_LastError(void) { return g_last_error.c_str(); }
 

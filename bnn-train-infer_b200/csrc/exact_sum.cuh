@@ -223,6 +223,38 @@ __host__ __device__ inline float sum_apply(const float* xs, float s, SumRec rec,
     return sum_serial(xs, s, first, last);
 }
 
+// ---- the wide form: 512 threads (16 warps), 4 consecutive elements per
+// thread, rows of up to 2048 elements per pass (longer rows in passes of
+// 2048 from the exact sum so far). One approximate block scan, one
+// classification pass per element (sum_classify's rules), one block scan of
+// (op count, increment sum) and one list write, then the same walk. A run
+// never continues across a warp boundary (the first element of every warp
+// starts an op), so no thread needs its neighbour warp's tags: that costs at
+// most 15 extra ops, each checked like any other.
+constexpr int kWideThreads = 512;
+constexpr int kWideWarps = kWideThreads / 32;
+constexpr int kWidePer = 4;
+constexpr int kWideChunk = kWideThreads * kWidePer;
+constexpr size_t kWideAddOffset = 256;    // [32] addends of a walk round
+constexpr size_t kWideListOffset = 384;
+constexpr size_t kWideSmemBytes = kWideListOffset + (size_t)(kWideChunk + 2) * sizeof(SumRec);
+
+// One element's op tag (kTagSingle, or e + 128 for a run in binade e) and its
+// increment RN(a / 2^(e-23)), given the approximate sum pb before it; the
+// same tests as sum_classify.
+__host__ __device__ inline void sum_classify_one(float a, float pb, int* tag, uint32_t* inc) {
+    constexpr float kMagic = 8388608.0f;
+    const float pe = add_rn(pb, a);
+    const uint32_t eb = fbits(pb) >> 23;
+    const bool in = eb - (uint32_t)(kRunEMin + 127) <= (uint32_t)(kRunEMax - kRunEMin) &&
+                    pb >= fvalue((eb << 23) | kLoMant) && pe <= fvalue((eb << 23) | kHiMant);
+    const float v = mul_rn(a, fvalue((in ? 277u - eb : 127u) << 23));
+    const float t = add_rn(v, kMagic);
+    const bool lin = in && v < kMagic && fabsf(add_rn(v, -add_rn(t, -kMagic))) != 0.5f;
+    *inc = lin ? fbits(t) - 0x4b000000u : 0u;
+    *tag = lin ? (int)eb + 1 : kTagSingle;
+}
+
 #ifdef __CUDACC__
 __device__ __forceinline__ void sum_bar(int id) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kSumThreads) : "memory");
@@ -373,6 +405,176 @@ static __device__ __forceinline__ float exact_sumsq(const float* xs, int n, unsi
     }
     sum_bar(bar);
     return *result;
+}
+
+__device__ __forceinline__ void wide_bar(int id) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kWideThreads) : "memory");
+}
+
+// Called by the 512 threads of warps 0..15; returns the serial sum of squares
+// of xs[0..n) (shared memory, n >= 1) to all of them. Uses named barrier
+// `bar` and kWideSmemBytes of 16-byte aligned shared memory at `mem`.
+static __device__ __forceinline__ float exact_sumsq_wide(const float* xs, int n, unsigned char* mem, int bar) {
+    float* wt = reinterpret_cast<float*>(mem);             // [16] warp totals of the approximate sums
+    int* wc = reinterpret_cast<int*>(mem + 64);            // [16] warp op counts
+    uint32_t* wk = reinterpret_cast<uint32_t*>(mem + 128); // [16] warp increment sums (mod 2^32)
+    float* result = reinterpret_cast<float*>(mem + 192);
+    float* abuf = reinterpret_cast<float*>(mem + kWideAddOffset);
+    SumRec* list = reinterpret_cast<SumRec*>(mem + kWideListOffset);
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    float s0 = 0.0f;  // the exact sum before this pass
+    for (int base = 0; base < n; base += kWideChunk) {
+        const int m = min(kWideChunk, n - base);
+        const float* xc = xs + base;
+        const int j0 = t * kWidePer;
+        float a[kWidePer], loc[kWidePer];
+        if (j0 + kWidePer <= m && ((reinterpret_cast<uintptr_t>(xc) & 15u) == 0)) {
+            const float4 v = reinterpret_cast<const float4*>(xc)[t];
+            a[0] = sq_rn(v.x);
+            a[1] = sq_rn(v.y);
+            a[2] = sq_rn(v.z);
+            a[3] = sq_rn(v.w);
+        } else {
+#pragma unroll
+            for (int q = 0; q < kWidePer; ++q)
+                a[q] = j0 + q < m ? sq_rn(xc[j0 + q]) : 0.0f;
+        }
+        loc[0] = a[0];
+#pragma unroll
+        for (int q = 1; q < kWidePer; ++q)
+            loc[q] = add_rn(loc[q - 1], a[q]);
+        // approximate prefix before this thread's first element
+        float incl = loc[kWidePer - 1];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o)
+                incl = add_rn(incl, v);
+        }
+        float excl = __shfl_up_sync(0xffffffffu, incl, 1);
+        if (lane == 0)
+            excl = 0.0f;
+        if (lane == 31)
+            wt[warp] = incl;
+        wide_bar(bar);
+        // the earlier warps' totals, summed by a shuffle tree (any order
+        // will do for the approximate prefix; this one is wide_warp_prefix)
+        float wp = lane < warp ? wt[lane] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+            wp = add_rn(wp, __shfl_xor_sync(0xffffffffu, wp, o));
+        float pb = add_rn(add_rn(s0, wp), excl);
+        // classify, mark op starts, count
+        int tag[kWidePer];
+        uint32_t inc[kWidePer];
+#pragma unroll
+        for (int q = 0; q < kWidePer; ++q) {
+            sum_classify_one(a[q], pb, &tag[q], &inc[q]);
+            pb = add_rn(pb, a[q]);
+        }
+        int prev = __shfl_up_sync(0xffffffffu, tag[kWidePer - 1], 1);
+        if (lane == 0)
+            prev = -1;
+        bool start[kWidePer];
+        int cnt = 0;
+        uint32_t ksum = 0;
+#pragma unroll
+        for (int q = 0; q < kWidePer; ++q) {
+            const bool valid = j0 + q < m;
+            start[q] = valid && (tag[q] == kTagSingle || tag[q] != (q ? tag[q - 1] : prev));
+            cnt += start[q];
+            ksum += valid ? inc[q] : 0u;
+        }
+        int ci = cnt;
+        uint32_t ki = ksum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int vc = __shfl_up_sync(0xffffffffu, ci, o);
+            const uint32_t vk = __shfl_up_sync(0xffffffffu, ki, o);
+            if (lane >= o) {
+                ci += vc;
+                ki += vk;
+            }
+        }
+        if (lane == 31) {
+            wc[warp] = ci;
+            wk[warp] = ki;
+        }
+        wide_bar(bar);
+        const int cw = lane < kWideWarps ? wc[lane] : 0;
+        const uint32_t kw = lane < kWideWarps ? wk[lane] : 0u;
+        int coff = ci - cnt + __reduce_add_sync(0xffffffffu, lane < warp ? cw : 0);
+        uint32_t kc = ki - ksum + __reduce_add_sync(0xffffffffu, lane < warp ? kw : 0u);
+        const int total = __reduce_add_sync(0xffffffffu, cw);
+        const uint32_t kall = __reduce_add_sync(0xffffffffu, kw);
+#pragma unroll
+        for (int q = 0; q < kWidePer; ++q) {
+            if (start[q])
+                list[coff++] = SumRec{(j0 + q) | (tag[q] << 16), (int)kc};
+            kc += j0 + q < m ? inc[q] : 0u;
+        }
+        if (t == 0)  // sentinel: where the last op ends, and the final increment sum
+            list[total] = list[total + 1] = SumRec{m, (int)kall};
+        wide_bar(bar);
+        if (warp == 0) {
+            float s = s0;
+            int k = 0;
+            while (k < total) {
+                const int idx = k + lane;
+                const bool valid = idx < total;
+                const SumRec rec = list[valid ? idx : total], nx = list[(valid ? idx : total) + 1];
+                const int tg = rec_tag(rec.key);
+                const float av = sq_rn(xc[min(rec_first(rec.key), m - 1)]);
+                const uint32_t d = (uint32_t)nx.cum - (uint32_t)rec.cum;
+                const bool single = tg == kTagSingle;
+                const bool run = valid && !single && d < (1u << 24);
+                const int e = run ? tg - 128 : 0;
+                const float addend = !valid ? 0.0f : single ? av : run ? mul_rn((float)d, pow2f(e - 23)) : 0.0f;
+                // all lanes run the same chain of adds; lane j keeps the value
+                // before and after op k + j (the addends go through shared
+                // memory, read back four at a time, so the chain waits on adds
+                // only and not on 32 shuffles in turn)
+                abuf[lane] = addend;
+                __syncwarp();
+                float ad[32];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float4 v = reinterpret_cast<const float4*>(abuf)[q];
+                    ad[4 * q] = v.x;
+                    ad[4 * q + 1] = v.y;
+                    ad[4 * q + 2] = v.z;
+                    ad[4 * q + 3] = v.w;
+                }
+                float cur = s, before = s, after = s;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float next = add_rn(cur, ad[j]);
+                    before = lane == j ? cur : before;
+                    after = lane == j ? next : after;
+                    cur = next;
+                }
+                bool ok = !valid || single || run;
+                if (run)
+                    ok = before >= pow2f(e) && before < pow2f(e + 1) && after < pow2f(e + 1);
+                const unsigned badm = __ballot_sync(0xffffffffu, !ok);  // (also orders abuf's reuse)
+                if (badm == 0) {
+                    s = cur;
+                    k += 32;
+                    continue;
+                }
+                // replay the first failing op step by step, restart after it
+                const int f = __ffs(badm) - 1;
+                s = __shfl_sync(0xffffffffu, before, f);
+                s = sum_serial(xc, s, rec_first(list[k + f].key), rec_first(list[k + f + 1].key));
+                k += f + 1;
+            }
+            if (lane == 0)
+                *result = s;
+        }
+        wide_bar(bar);
+        s0 = *result;  // (the next pass rewrites result and the list only after two more barriers)
+    }
+    return s0;
 }
 #endif
 

@@ -186,6 +186,19 @@ uint32_t BNND_StepLaunches(BNND_Context ctx);
  * variable BNN_STEP_KERNEL=0 before BNND_ContextCreate turns it off. */
 uint32_t BNND_StepKernelPositions(BNND_Context ctx);
 
+/* Runs ONE greedy decode step (as BNND_Generate's next step) through the
+ * step kernel with %globaltimer stamps at its phase boundaries, for
+ * measurement; no counterpart in the reference. stamps receives
+ * [SMs][n_layers + 1][16] nanosecond stamps (0 where a CTA has no such
+ * phase): *count is set to that size, BNND_ERANGE if capacity is smaller.
+ * Per layer, contraction CTAs: 0 phase start, 1 x ready, 2 RMSNorm +
+ * quantise done, 3 q|k|v rows done, 4 y ready, 5 quantised, 6 o done,
+ * 7 x ready, 8 RMSNorm done, 9 gate|up done, 10 h ready, 11 quantised,
+ * 12 down done, 13 and 14 the two RMSNorm sums done, 15 x loaded; attention CTAs: 0 q|k|v ready, 1 norms + RoPE, 2 K/V
+ * history in, 3 scores, 4 softmax, 5 y written. Last record: 0 x ready,
+ * 1 RMSNorm done, 2 lm_head done, 14 step end (last CTA), 15 CTA start. */
+BNND_Status BNND_StepKernelTrace(BNND_Context ctx, uint64_t* stamps, size_t capacity, size_t* count);
+
 /* The CUDA stream the context's work runs on (cudaStream_t as void*). */
 void* BNND_ContextStream(BNND_Context ctx);
 

@@ -151,6 +151,144 @@ float exact_sumsq_host(const float* xs, int n) {
     return s;
 }
 
+// The same walk over a compacted op list, starting from s (the wide form's
+// walk is the 256-thread walk over its own list).
+float walk_host(const float* xs, int n, const std::vector<SumRec>& list, int total, float s) {
+    int k = 0;
+    while (k < total) {
+        float ad[32], before[32], after[32];
+        bool ok[32], run[32];
+        int e[32];
+        for (int lane = 0; lane < 32; ++lane) {
+            const int idx = k + lane;
+            const bool valid = idx < total;
+            const int ci = valid ? idx : total;
+            const SumRec rec = list[ci], nx = list[ci + 1];
+            const int tag = rec_tag(rec.key);
+            const float a = sq_rn(xs[std::min(rec_first(rec.key), n - 1)]);
+            const uint32_t d = (uint32_t)nx.cum - (uint32_t)rec.cum;
+            const bool single = tag == kTagSingle;
+            run[lane] = valid && !single && d < (1u << 24);
+            e[lane] = run[lane] ? tag - 128 : 0;
+            const uint32_t dd = d + (g_plant ? 1u : 0u);
+            ad[lane] = !valid ? 0.0f : single ? a : run[lane] ? mul_rn((float)dd, pow2f(e[lane] - 23)) : 0.0f;
+            ok[lane] = !valid || single || run[lane];
+        }
+        float cur = s;
+        for (int j = 0; j < 32; ++j) {
+            const float next = add_rn(cur, ad[j]);
+            before[j] = cur;
+            after[j] = next;
+            cur = next;
+        }
+        int f = -1;
+        for (int lane = 0; lane < 32; ++lane) {
+            if (run[lane])
+                ok[lane] = before[lane] >= pow2f(e[lane]) && before[lane] < pow2f(e[lane] + 1) &&
+                           after[lane] < pow2f(e[lane] + 1);
+            if (!ok[lane] && f < 0)
+                f = lane;
+        }
+        for (int lane = 0; lane < (f < 0 ? 32 : f); ++lane)
+            if (k + lane < total) {
+                g_runs += run[lane];
+                g_singles += !run[lane];
+            }
+        if (f < 0) {
+            s = cur;
+            k += 32;
+            continue;
+        }
+        ++g_replays;
+        s = before[f];
+        s = sum_serial(xs, s, rec_first(list[k + f].key), rec_first(list[k + f + 1].key));
+        k += f + 1;
+    }
+    return s;
+}
+
+// Host emulation of exact_sumsq_wide (512 threads, 4 elements each, passes
+// of 2048), with the device code's order of float operations.
+float exact_sumsq_wide_host(const float* xs, int n) {
+    const int T = kWideThreads, W = kWideWarps, P = kWidePer;
+    float s0 = 0.0f;
+    for (int base = 0; base < n; base += kWideChunk) {
+        const int m = std::min(kWideChunk, n - base);
+        const float* xc = xs + base;
+        std::vector<float> a((size_t)T * P), incl(T), wt(W);
+        for (int t = 0; t < T; ++t) {
+            float loc = 0.0f;
+            for (int q = 0; q < P; ++q) {
+                const int j = t * P + q;
+                a[(size_t)t * P + q] = j < m ? sq_rn(xc[j]) : 0.0f;
+                loc = q == 0 ? a[(size_t)t * P] : add_rn(loc, a[(size_t)t * P + q]);
+            }
+            incl[t] = loc;
+        }
+        for (int w = 0; w < W; ++w)
+            for (int o = 1; o < 32; o <<= 1) {
+                float prev[32];
+                for (int l = 0; l < 32; ++l)
+                    prev[l] = incl[w * 32 + l];
+                for (int l = o; l < 32; ++l)
+                    incl[w * 32 + l] = add_rn(prev[l], prev[l - o]);
+            }
+        for (int w = 0; w < W; ++w)
+            wt[w] = incl[w * 32 + 31];
+        std::vector<int> tag((size_t)T * P), cnt(T);
+        std::vector<uint32_t> inc((size_t)T * P), ksum(T);
+        std::vector<char> start((size_t)T * P);
+        // the earlier warps' totals by the device's xor-shuffle tree
+        std::vector<float> wpre(W);
+        for (int w = 0; w < W; ++w) {
+            float v[32];
+            for (int l = 0; l < 32; ++l)
+                v[l] = l < w ? wt[l] : 0.0f;
+            for (int o = 16; o > 0; o >>= 1) {
+                float nv[32];
+                for (int l = 0; l < 32; ++l)
+                    nv[l] = add_rn(v[l], v[l ^ o]);
+                std::copy(nv, nv + 32, v);
+            }
+            wpre[w] = v[0];
+        }
+        for (int t = 0; t < T; ++t) {
+            const int w = t / 32, l = t % 32;
+            float pb = add_rn(add_rn(s0, wpre[w]), l == 0 ? 0.0f : incl[t - 1]);
+            for (int q = 0; q < P; ++q) {
+                sum_classify_one(a[(size_t)t * P + q], pb, &tag[(size_t)t * P + q], &inc[(size_t)t * P + q]);
+                pb = add_rn(pb, a[(size_t)t * P + q]);
+            }
+        }
+        for (int t = 0; t < T; ++t) {
+            const int prev = t % 32 == 0 ? -1 : tag[(size_t)t * P + P - 1 - P];
+            cnt[t] = 0;
+            ksum[t] = 0;
+            for (int q = 0; q < P; ++q) {
+                const int j = t * P + q;
+                const bool valid = j < m;
+                const int pt = q ? tag[(size_t)j - 1] : prev;
+                start[j] = valid && (tag[j] == kTagSingle || tag[j] != pt);
+                cnt[t] += start[j];
+                ksum[t] += valid ? inc[j] : 0u;
+            }
+        }
+        std::vector<SumRec> list((size_t)kWideChunk + 2);
+        int total = 0;
+        uint32_t kc = 0;
+        for (int t = 0; t < T; ++t)
+            for (int q = 0; q < P; ++q) {
+                const int j = t * P + q;
+                if (start[j])
+                    list[total++] = SumRec{j | (tag[j] << 16), (int)kc};
+                kc += j < m ? inc[j] : 0u;
+            }
+        list[total] = list[total + 1] = SumRec{m, (int)kc};
+        s0 = walk_host(xc, m, list, total, s0);
+    }
+    return s0;
+}
+
 uint32_t bits_of(float v) { return fbits(v); }
 
 }  // namespace
@@ -158,7 +296,11 @@ uint32_t bits_of(float v) { return fbits(v); }
 int main(int argc, char** argv) {
     const int per = argc > 1 ? atoi(argv[1]) : 200;
     const unsigned seed = argc > 2 ? (unsigned)atoi(argv[2]) : 1u;
-    g_plant = argc > 3 && std::string(argv[3]) == "plant";
+    bool wide = false;
+    for (int i = 3; i < argc; ++i) {
+        g_plant |= std::string(argv[i]) == "plant";
+        wide |= std::string(argv[i]) == "wide";
+    }
     std::mt19937 rng(seed);
     std::normal_distribution<float> normal(0.0f, 1.0f);
     std::uniform_real_distribution<float> uni(0.0f, 1.0f);
@@ -196,7 +338,7 @@ int main(int argc, char** argv) {
                 }
             }
             const float want = sum_serial(x.data(), 0.0f, 0, n);
-            const float got = exact_sumsq_host(x.data(), n);
+            const float got = wide ? exact_sumsq_wide_host(x.data(), n) : exact_sumsq_host(x.data(), n);
             ++checked;
             if (bits_of(want) != bits_of(got)) {
                 ++fam_bad;

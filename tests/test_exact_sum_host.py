@@ -1,7 +1,7 @@
 """The exact parallel form of the reference's serial sum of squares
 (bnn-train-infer_b200/csrc/exact_sum.cuh, the RMSNorm sum of qwen3.c:361-372)
 checked on the host: tests/exact_sum_host.cpp replays the 256-thread
-algorithm with the header's own host-callable pieces and the device code's
+algorithm and the 512-thread wide form (exact_sumsq_wide) with the header's own host-callable pieces and the device code's
 order of float operations, and compares each result bit for bit with the
 serial loop, over six families of vectors (normal, outliers, 2^-60..2^50
 magnitudes, half-ulp ties, tiny/huge/zero mixes, 16K..64K lengths). The
@@ -36,9 +36,10 @@ def _run(exe, *args):
     return r, int(m.group(1)), int(m.group(2))
 
 
+@pytest.mark.parametrize("form", ["", "wide"])
 @pytest.mark.parametrize("seed", [1, 2, 3])
-def test_parallel_sum_bit_exact(exe, seed):
-    r, checked, bad = _run(exe, 300, seed)
+def test_parallel_sum_bit_exact(exe, seed, form):
+    r, checked, bad = _run(exe, 300, seed, form) if form else _run(exe, 300, seed)
     assert checked == 1800 and bad == 0, r.stdout
     assert r.returncode == 0
     # the run path (the parallel shortcut) is taken, not only serial replays
@@ -46,6 +47,7 @@ def test_parallel_sum_bit_exact(exe, seed):
     assert len(runs) == 6 and min(runs) > 100, r.stdout
 
 
-def test_planted_mistake_is_caught(exe):
-    r, checked, bad = _run(exe, 40, 7, "plant")
+@pytest.mark.parametrize("form", ["", "wide"])
+def test_planted_mistake_is_caught(exe, form):
+    r, checked, bad = _run(exe, 40, 7, "plant", form) if form else _run(exe, 40, 7, "plant")
     assert bad > 0 and r.returncode == 1, r.stdout
