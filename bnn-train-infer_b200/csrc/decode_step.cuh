@@ -845,11 +845,15 @@ __device__ __forceinline__ void contraction_role(const StepArgs& a, unsigned cha
             if (live) {
                 copy_dots(w, 2 * np, GC, act_s, tot_s, dsm);
                 named_barrier(kBarCompute, kCThreads);
+                // one ordered chain per thread (gate and up rows apart), then SwiGLU
+                float* gu_s = xs;  // the normalised row is no longer needed
+                for (uint32_t q = tid; q < 2 * np * kRowBlock; q += kCThreads)
+                    gu_s[q] = __fmul_rn(acc_of(w, GC, q / kRowBlock, q % kRowBlock), s);
+                named_barrier(kBarCompute, kCThreads);
                 const uint32_t g = gen(l, kPhH);
                 for (uint32_t q = tid; q < np * kRowBlock; q += kCThreads) {
                     const uint32_t k = q / kRowBlock, r = q % kRowBlock;
-                    const float gt = __fmul_rn(acc_of(w, GC, 2 * k, r), s);
-                    const float up = __fmul_rn(acc_of(w, GC, 2 * k + 1, r), s);
+                    const float gt = gu_s[(2 * k) * kRowBlock + r], up = gu_s[(2 * k + 1) * kRowBlock + r];
                     const float silu = __fdiv_rn(gt, __fadd_rn(1.0f, expf_cr(-gt)));
                     put_tagged(a.ht + (size_t)(p0 + k) * kRowBlock + r, __fmul_rn(silu, up), g);
                 }

@@ -203,9 +203,10 @@ __device__ inline bool attn_norm_rope(float* v, const float* gain, const float* 
     const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)HD), eps));
     if (!isfinite(rms) || rms == 0.0f)
         return false;
+    const float rr = __frcp_rn(rms);
 #pragma unroll
     for (int k = 0; k < kPer; ++k)
-        v[lane + 32 * k] = __fmul_rn(__fdiv_rn(x[k], rms), gain[lane + 32 * k]);
+        v[lane + 32 * k] = __fmul_rn(div_cr(x[k], rms, rr), gain[lane + 32 * k]);
     __syncwarp();
     constexpr int kHalf = HD / 2;
     float out[kPer];

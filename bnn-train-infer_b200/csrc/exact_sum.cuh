@@ -235,9 +235,18 @@ constexpr int kWideThreads = 512;
 constexpr int kWideWarps = kWideThreads / 32;
 constexpr int kWidePer = 4;
 constexpr int kWideChunk = kWideThreads * kWidePer;
-constexpr size_t kWideAddOffset = 256;    // [32] addends of a walk round
-constexpr size_t kWideListOffset = 384;
-constexpr size_t kWideSmemBytes = kWideListOffset + (size_t)(kWideChunk + 2) * sizeof(SumRec);
+constexpr size_t kWideAddOffset = 256;    // [64] addends of a walk round
+constexpr size_t kWideListOffset = 512;
+
+// An op of the wide form: first element | tag << 16, increments before it
+// (mod 2^32), and for a single its addend (the square).
+struct WideRec {
+    int key;
+    int cum;
+    float add;
+    int pad;
+};
+constexpr size_t kWideSmemBytes = kWideListOffset + (size_t)(kWideChunk + 2) * sizeof(WideRec);
 
 // One element's op tag (kTagSingle, or e + 128 for a run in binade e) and its
 // increment RN(a / 2^(e-23)), given the approximate sum pb before it; the
@@ -420,7 +429,7 @@ static __device__ __forceinline__ float exact_sumsq_wide(const float* xs, int n,
     uint32_t* wk = reinterpret_cast<uint32_t*>(mem + 128); // [16] warp increment sums (mod 2^32)
     float* result = reinterpret_cast<float*>(mem + 192);
     float* abuf = reinterpret_cast<float*>(mem + kWideAddOffset);
-    SumRec* list = reinterpret_cast<SumRec*>(mem + kWideListOffset);
+    WideRec* list = reinterpret_cast<WideRec*>(mem + kWideListOffset);
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     float s0 = 0.0f;  // the exact sum before this pass
     for (int base = 0; base < n; base += kWideChunk) {
@@ -510,61 +519,78 @@ static __device__ __forceinline__ float exact_sumsq_wide(const float* xs, int n,
 #pragma unroll
         for (int q = 0; q < kWidePer; ++q) {
             if (start[q])
-                list[coff++] = SumRec{(j0 + q) | (tag[q] << 16), (int)kc};
+                list[coff++] = WideRec{(j0 + q) | (tag[q] << 16), (int)kc, a[q], 0};
             kc += j0 + q < m ? inc[q] : 0u;
         }
         if (t == 0)  // sentinel: where the last op ends, and the final increment sum
-            list[total] = list[total + 1] = SumRec{m, (int)kall};
+            list[total] = list[total + 1] = WideRec{m, (int)kall, 0.0f, 0};
         wide_bar(bar);
         if (warp == 0) {
+            // 64 ops a round: lane j prepares ops k + j and k + 32 + j
             float s = s0;
             int k = 0;
             while (k < total) {
-                const int idx = k + lane;
-                const bool valid = idx < total;
-                const SumRec rec = list[valid ? idx : total], nx = list[(valid ? idx : total) + 1];
-                const int tg = rec_tag(rec.key);
-                const float av = sq_rn(xc[min(rec_first(rec.key), m - 1)]);
-                const uint32_t d = (uint32_t)nx.cum - (uint32_t)rec.cum;
-                const bool single = tg == kTagSingle;
-                const bool run = valid && !single && d < (1u << 24);
-                const int e = run ? tg - 128 : 0;
-                const float addend = !valid ? 0.0f : single ? av : run ? mul_rn((float)d, pow2f(e - 23)) : 0.0f;
-                // all lanes run the same chain of adds; lane j keeps the value
-                // before and after op k + j (the addends go through shared
-                // memory, read back four at a time, so the chain waits on adds
-                // only and not on 32 shuffles in turn)
-                abuf[lane] = addend;
-                __syncwarp();
-                float ad[32];
+                float ad[2];
+                bool run[2], okp[2];
+                int e[2];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const float4 v = reinterpret_cast<const float4*>(abuf)[q];
-                    ad[4 * q] = v.x;
-                    ad[4 * q + 1] = v.y;
-                    ad[4 * q + 2] = v.z;
-                    ad[4 * q + 3] = v.w;
+                for (int h = 0; h < 2; ++h) {
+                    const int idx = k + 32 * h + lane;
+                    const bool valid = idx < total;
+                    const WideRec rec = list[valid ? idx : total], nx = list[(valid ? idx : total) + 1];
+                    const int tg = rec_tag(rec.key);
+                    const uint32_t d = (uint32_t)nx.cum - (uint32_t)rec.cum;
+                    const bool single = tg == kTagSingle;
+                    run[h] = valid && !single && d < (1u << 24);
+                    e[h] = run[h] ? tg - 128 : 0;
+                    ad[h] = !valid ? 0.0f : single ? rec.add : run[h] ? mul_rn((float)d, pow2f(e[h] - 23)) : 0.0f;
+                    okp[h] = !valid || single || run[h];
                 }
-                float cur = s, before = s, after = s;
+                abuf[lane] = ad[0];
+                abuf[32 + lane] = ad[1];
+                __syncwarp();
+                // all lanes run the same chain of adds; lane j keeps the values
+                // before and after ops k + j and k + 32 + j
+                float av[64];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float next = add_rn(cur, ad[j]);
-                    before = lane == j ? cur : before;
-                    after = lane == j ? next : after;
+                for (int q = 0; q < 16; ++q) {
+                    const float4 v = reinterpret_cast<const float4*>(abuf)[q];
+                    av[4 * q] = v.x;
+                    av[4 * q + 1] = v.y;
+                    av[4 * q + 2] = v.z;
+                    av[4 * q + 3] = v.w;
+                }
+                float cur = s, b0 = s, a0 = s, b1 = s, a1 = s;
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) {
+                    const float next = add_rn(cur, av[jj]);
+                    b0 = lane == jj ? cur : b0;
+                    a0 = lane == jj ? next : a0;
                     cur = next;
                 }
-                bool ok = !valid || single || run;
-                if (run)
-                    ok = before >= pow2f(e) && before < pow2f(e + 1) && after < pow2f(e + 1);
-                const unsigned badm = __ballot_sync(0xffffffffu, !ok);  // (also orders abuf's reuse)
-                if (badm == 0) {
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) {
+                    const float next = add_rn(cur, av[32 + jj]);
+                    b1 = lane == jj ? cur : b1;
+                    a1 = lane == jj ? next : a1;
+                    cur = next;
+                }
+                bool ok0 = okp[0], ok1 = okp[1];
+                if (run[0])
+                    ok0 = b0 >= pow2f(e[0]) && b0 < pow2f(e[0] + 1) && a0 < pow2f(e[0] + 1);
+                if (run[1])
+                    ok1 = b1 >= pow2f(e[1]) && b1 < pow2f(e[1] + 1) && a1 < pow2f(e[1] + 1);
+                const unsigned bad0 = __ballot_sync(0xffffffffu, !ok0);
+                const unsigned bad1 = __ballot_sync(0xffffffffu, !ok1);  // (also orders abuf's reuse)
+                if ((bad0 | bad1) == 0) {
                     s = cur;
-                    k += 32;
+                    k += 64;
                     continue;
                 }
                 // replay the first failing op step by step, restart after it
-                const int f = __ffs(badm) - 1;
-                s = __shfl_sync(0xffffffffu, before, f);
+                const int f = bad0 ? __ffs(bad0) - 1 : 32 + __ffs(bad1) - 1;
+                const float bf0 = __shfl_sync(0xffffffffu, b0, f & 31), bf1 = __shfl_sync(0xffffffffu, b1, f & 31);
+                s = f < 32 ? bf0 : bf1;
                 s = sum_serial(xc, s, rec_first(list[k + f].key), rec_first(list[k + f + 1].key));
                 k += f + 1;
             }
