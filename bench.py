@@ -388,49 +388,10 @@ def run_b200(args):
         launches_per_step = 1
     else:
         roofline = None
-    # ---- roofline of the dominant kernel (instrumented replay of the same step)
-    ctx.truncate(0)
-    ctx.decode_argmax(prompt)
-    stats, total_ms = ctx.profile(args.profile_steps)
-    by_kernel = {}
-    for name, (launches, kms, kbytes) in stats.items():
-        key = "w1a8_contract_kernel" if name.startswith(("w1a8_gemv:", "w1a8_mma:")) else name
-        l0, m0, b0 = by_kernel.get(key, (0, 0.0, 0.0))
-        by_kernel[key] = (l0 + launches, m0 + kms, b0 + kbytes)
-    dominant = max(by_kernel, key=lambda k: by_kernel[k][1])
-    launches, kms, kbytes = by_kernel["w1a8_contract_kernel"]
-    peak, peak_kind = measured_peaks()
-    # The instrumented replay (an event between every pair of launches) is
-    # slower than the real step, so it gives only the kernel's SHARE of the
-    # step; the time is that share of the un-instrumented, event-timed step.
-    share = kms / total_ms
-    step_ms = ms / args.steps
-    kernel_ms = share * step_ms
-    bytes_per_step = kbytes / args.profile_steps
-    achieved = bytes_per_step / (kernel_ms / 1e3) / 1e9
-    step_gbs = bytes_per_step / (step_ms / 1e3) / 1e9
-    if roofline is None:  # the per-kernel graph is the timed step
-        assert kernel_ms <= step_ms + 1e-9, "kernel time per step exceeds the step"
-        assert step_gbs <= peak, "algorithmic bytes per step / step time above the HBM peak"
-    traffic = ncu_traffic(METRIC + ("_8ctx" if args.config5 else ""))
-    per_kernel_roofline = {
-        "kernel": "w1a8_contract_kernel", "dominant_kernel": dominant, "bound": "hbm",
-        "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-        "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-        "traffic": traffic, "launches_per_step": launches,
-        "bytes_per_launch": round(kbytes / (launches * args.profile_steps), 1),
-        "kernel_ms_per_step": round(kernel_ms, 4), "share_of_step": round(share, 4),
-        "method": ("share of the contraction in an instrumented replay of the step graph x the "
-                   "event-timed step (ms_per_step); achieved = its algorithmic bytes per step / that time"),
-        "step_gbs": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4),
-        "step_ms_instrumented": round(total_ms / args.profile_steps, 4),
-        "kernel_share": {k: round(v[1] / total_ms, 4) for k, v in sorted(by_kernel.items(), key=lambda kv: -kv[1][1])},
-    }
+    # ---- roofline of the dominant kernel of the per-kernel step graph
+    # (instrumented replay of the same step), when that graph is the timed path
     if roofline is None:
-        roofline = per_kernel_roofline
-    else:  # the per-kernel graph's figures, for comparison (not the timed path)
-        roofline["per_kernel_graph"] = {k: per_kernel_roofline[k] for k in
-                                        ("achieved", "frac", "share_of_step", "step_ms_instrumented")}
+        roofline = per_kernel_roofline(args, ctx, prompt, ms)
 
     out = None
     if rank == 0:
@@ -474,6 +435,48 @@ def run_b200(args):
         dist.barrier()
         dist.destroy_process_group()
     return out
+
+
+def per_kernel_roofline(args, ctx, prompt, ms):
+    """Roofline of the W1A8 contraction in the per-kernel step graph: its
+    share of an instrumented replay times the event-timed step."""
+    ctx.truncate(0)
+    ctx.decode_argmax(prompt)
+    stats, total_ms = ctx.profile(args.profile_steps)
+
+    by_kernel = {}
+    for name, (launches, kms, kbytes) in stats.items():
+        key = "w1a8_contract_kernel" if name.startswith(("w1a8_gemv:", "w1a8_mma:")) else name
+        l0, m0, b0 = by_kernel.get(key, (0, 0.0, 0.0))
+        by_kernel[key] = (l0 + launches, m0 + kms, b0 + kbytes)
+    dominant = max(by_kernel, key=lambda k: by_kernel[k][1])
+    launches, kms, kbytes = by_kernel["w1a8_contract_kernel"]
+    peak, peak_kind = measured_peaks()
+    # The instrumented replay (an event between every pair of launches) is
+    # slower than the real step, so it gives only the kernel's SHARE of the
+    # step; the time is that share of the un-instrumented, event-timed step.
+    share = kms / total_ms
+    step_ms = ms / args.steps
+    kernel_ms = share * step_ms
+    bytes_per_step = kbytes / args.profile_steps
+    achieved = bytes_per_step / (kernel_ms / 1e3) / 1e9
+    step_gbs = bytes_per_step / (step_ms / 1e3) / 1e9
+    assert kernel_ms <= step_ms + 1e-9, "kernel time per step exceeds the step"
+    assert step_gbs <= peak, "algorithmic bytes per step / step time above the HBM peak"
+    traffic = ncu_traffic(METRIC + ("_8ctx" if args.config5 else ""))
+    return {
+        "kernel": "w1a8_contract_kernel", "dominant_kernel": dominant, "bound": "hbm",
+        "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+        "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+        "traffic": traffic, "launches_per_step": launches,
+        "bytes_per_launch": round(kbytes / (launches * args.profile_steps), 1),
+        "kernel_ms_per_step": round(kernel_ms, 4), "share_of_step": round(share, 4),
+        "method": ("share of the contraction in an instrumented replay of the step graph x the "
+                   "event-timed step (ms_per_step); achieved = its algorithmic bytes per step / that time"),
+        "step_gbs": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4),
+        "step_ms_instrumented": round(total_ms / args.profile_steps, 4),
+        "kernel_share": {k: round(v[1] / total_ms, 4) for k, v in sorted(by_kernel.items(), key=lambda kv: -kv[1][1])},
+    }
 
 
 def run_prefill(args, ctx, info, timed, rank, world):
