@@ -102,6 +102,7 @@ struct StepArgs {
     int* status;
     float eps, scale;
     unsigned long long* trace;      // null, or [gridDim.x][n_layers + 1][kTraceSlots] %globaltimer stamps
+    uint32_t poll_ns;               // pause between two polls of a hand-off row (doubling up to 8x while nothing arrives)
 };
 
 constexpr uint32_t kTraceSlots = 16;
@@ -190,7 +191,7 @@ __device__ __forceinline__ int status_now(const int* status) {
 // the CTA should do its work; *amax_out and *bad_out (any non-finite value)
 // cover the whole row.
 __device__ __noinline__ bool poll_row(const unsigned long long* src, uint32_t K, uint32_t gen, float* xs, int* status,
-                                      int* flag, float* red, float* amax_out, int* bad_out) {
+                                      int* flag, float* red, float* amax_out, int* bad_out, uint32_t poll_ns) {
     constexpr uint32_t kMine = 16;  // 16-byte chunks per thread at most (K <= 16384)
     const uint32_t tid = threadIdx.x, chunks = K / 2;
     const ulonglong2* s2 = reinterpret_cast<const ulonglong2*>(src);
@@ -219,14 +220,16 @@ __device__ __noinline__ bool poll_row(const unsigned long long* src, uint32_t K,
     if (pending) {
         const uint64_t t0 = globaltimer_ns();
         const uint64_t limit = *reinterpret_cast<volatile unsigned long long*>(&g_wait_ns_limit);
+        uint32_t pause = poll_ns;
         for (uint32_t round = 0; pending; ++round) {
-            __nanosleep(64);
+            __nanosleep(pause);
             const uint32_t was = pending;
             pending = 0;
 #pragma unroll
             for (uint32_t i = 0; i < kMine; ++i)
                 if (was & (1u << i))
                     take(i, __ldcg(s2 + tid + i * kCThreads));
+            pause = pending == was ? min(2u * pause, 8u * poll_ns) : poll_ns;
             if (pending && (round & 15u) == 15u &&
                 (status_now(status) != 0 || globaltimer_ns() - t0 > limit)) {
                 if (status_now(status) == 0)
@@ -508,6 +511,7 @@ __device__ __forceinline__ void attention_role(const StepArgs& a, unsigned char*
             ulonglong2 v = __ldcg(src);
             const uint64_t t0 = globaltimer_ns();
             const uint64_t limit = *reinterpret_cast<volatile unsigned long long*>(&g_wait_ns_limit);
+            uint32_t pause = a.poll_ns;
             for (uint32_t round = 0; (uint32_t)(v.x >> 32) != want || (uint32_t)(v.y >> 32) != want; ++round) {
                 if ((round & 15u) == 15u && (status_now(a.status) != 0 || globaltimer_ns() - t0 > limit)) {
                     if (status_now(a.status) == 0)
@@ -515,7 +519,8 @@ __device__ __forceinline__ void attention_role(const StepArgs& a, unsigned char*
                     *flag = 1;
                     break;
                 }
-                __nanosleep(64);
+                __nanosleep(pause);
+                pause = min(2u * pause, 8u * a.poll_ns);
                 v = __ldcg(src);
             }
             dst[2 * c] = __uint_as_float((uint32_t)v.x);
@@ -728,7 +733,7 @@ __device__ __forceinline__ void contraction_role(const StepArgs& a, unsigned cha
     auto quant_prologue = [&](const unsigned long long* src, uint32_t K, uint32_t g, float* s) -> bool {
         float amax;
         int bad;
-        const bool live = poll_row(src, K, g, xs, a.status, flag, red, &amax, &bad);
+        const bool live = poll_row(src, K, g, xs, a.status, flag, red, &amax, &bad, a.poll_ns);
         // a linear rejects non-finite input (ValidateF32Input, soft :294-308)
         if (live && bad && tid == 0)
             atomicOr(a.status, kStatusBadInput);
@@ -785,7 +790,7 @@ __device__ __forceinline__ void contraction_role(const StepArgs& a, unsigned cha
             if (l > 0) {
                 float amax;
                 int bad;
-                live = poll_row(a.xt, C, gen(l - 1, kPhXd), xs, a.status, flag, red, &amax, &bad);
+                live = poll_row(a.xt, C, gen(l - 1, kPhXd), xs, a.status, flag, red, &amax, &bad, a.poll_ns);
             }
             stamp(a, l, 1);
             const float* gain = reinterpret_cast<const float*>(take());
@@ -833,7 +838,7 @@ __device__ __forceinline__ void contraction_role(const StepArgs& a, unsigned cha
         if (p1 > p0) {
             float amax;
             int bad;
-            bool live = poll_row(a.xt, C, gen(l, kPhXo), xs, a.status, flag, red, &amax, &bad);
+            bool live = poll_row(a.xt, C, gen(l, kPhXo), xs, a.status, flag, red, &amax, &bad, a.poll_ns);
             stamp(a, l, 7);
             const float* gain = reinterpret_cast<const float*>(take());
             live = live && rms_quantize(xs, gain, C, a.eps, sum_mem, red, act_s, tot_s, &s, a.status,
@@ -888,7 +893,7 @@ __device__ __forceinline__ void contraction_role(const StepArgs& a, unsigned cha
     if (v1 > v0) {
         float amax;
         int bad;
-        bool live = poll_row(a.xt, C, gen(L - 1, kPhXd), xs, a.status, flag, red, &amax, &bad);
+        bool live = poll_row(a.xt, C, gen(L - 1, kPhXd), xs, a.status, flag, red, &amax, &bad, a.poll_ns);
         stamp(a, L, 0);
         const float* gain = reinterpret_cast<const float*>(take());
         live = live && rms_quantize(xs, gain, C, a.eps, sum_mem, red, act_s, tot_s, &s, a.status);

@@ -1114,6 +1114,8 @@ void setup_step_kernel(bnnd_context* c) {
     a.status = c->status.as<int>();
     a.eps = m->eps;
     a.scale = 1.0f / sqrtf((float)HD);
+    const char* pn = std::getenv("BNN_STEP_POLL_NS");
+    a.poll_ns = pn ? (uint32_t)std::strtoul(pn, nullptr, 10) : 4u;  // measured: shorter pauses are faster (8 vs 512 ns: 1186 vs 929 tok/s)
     int occ = 0;
     if (cudaFuncSetAttribute(st::decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)st::kSmemBudget) != cudaSuccess ||
