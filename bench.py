@@ -266,16 +266,16 @@ def run_b200(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     tp = args.tp and world > 1
     dist = None
-    if tp:
-        # the engine owns the data-path NCCL communicator (bootstrap root at a
-        # fixed loopback address); the process group only coordinates the host
+    if world > 1:
+        # the engine owns the data-path NCCL communicator of the sharded runs
+        # (bootstrap root at a fixed loopback address); the process group
+        # (gloo) only coordinates the host: barriers and the max over ranks
         os.environ.setdefault("NCCL_SOCKET_IFNAME", "lo")
         os.environ.setdefault("NCCL_COMM_ID", f"127.0.0.1:{int(os.environ.get('MASTER_PORT', '29500')) + 1}")
-    if world > 1:
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("gloo" if tp else "nccl", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
     torch.cuda.set_device(local)
 
     if rank == 0 or world == 1:
@@ -304,19 +304,21 @@ def run_b200(args):
     stream = torch.cuda.ExternalStream(ctx.stream())
     launches_per_step = ctx.step_launches()
 
-    def timed(fn):
+    def timed(fn, on=None):
+        """Device time of fn() on stream `on` (the context's), max over ranks."""
+        on = stream if on is None else on
         if dist:
             dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
+        e0.record(on)
         fn()
-        e1.record(stream)
+        e1.record(on)
         e1.synchronize()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
         if dist:
-            t = torch.tensor([ms], device="cpu" if tp else "cuda")
+            t = torch.tensor([ms])
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
         return ms
@@ -393,6 +395,15 @@ def run_b200(args):
     if roofline is None:
         roofline = per_kernel_roofline(args, ctx, prompt, ms)
 
+    # ---- the sharded design on this job's GPUs: configs[4] with every linear
+    # column-sharded over the ranks (a single GPU at N = 1), so the scaling
+    # run records it at 1, 2, 4 and 8 GPUs next to the replicas
+    tp_info = None
+    if not (args.config5 or args.no_tp_block) and (info.heads % world == 0 and info.kv_heads % world == 0):
+        ctx.free()
+        tp_info = tp_block(args, dev, api, path, world, rank, dist, timed, engine)
+        ctx = None
+
     out = None
     if rank == 0:
         cpu = None
@@ -428,13 +439,57 @@ def run_b200(args):
             "clocks": clk,
             "gpu_launches": int(launches_per_step * args.steps),
         }
-    ctx.free()
+        if tp_info:
+            out["tp"] = tp_info
+    if ctx is not None:
+        ctx.free()
     model.free()
     dev.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     return out
+
+
+def tp_block(args, dev, api, path, world, rank, dist, timed, engine):
+    """BASELINE configs[4] on `world` GPUs with the model column-sharded over
+    them (one GPU at world 1): 8 contexts with 64-token seeded prompts,
+    greedy steps at ctx 4096 (the timed steps repeat the 256-step generation
+    from the end of the prompts). Returns the block for the bench line."""
+    import numpy as np
+    comm = None
+    if world > 1:
+        box = [engine.comm_id_create(api) if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        comm = box[0]
+    model = engine.Model(dev, path, api, world=world, rank=rank)
+    batch, n_prompt, gen_steps = 8, 64, GEN_STEPS_8CTX
+    prompt = np.random.default_rng(20261205).integers(0, model.info.n_vocab, size=(batch, n_prompt)).astype(np.int32)
+    ctx = engine.Context(model, n_ctx=4096, n_batch=batch, comm_id=comm)
+    try:
+        first = ctx.decode_argmax(prompt)
+
+        def generate(s):
+            api.check(api.Generate(ctx.handle, s, None))
+
+        steps = args.tp_steps
+        run_generations(ctx, generate, first, n_prompt, gen_steps, 3)
+        import torch
+        ms = timed(lambda: run_generations(ctx, generate, first, n_prompt, gen_steps, steps),
+                   torch.cuda.ExternalStream(ctx.stream()))
+        ctx.truncate(n_prompt)
+        ctx.decode_argmax(first)
+        stats, total = ctx.profile(2)
+        gather = sum(v[1] for k, v in stats.items() if k.startswith("all_gather"))
+        return {"workload": "configs[4]: 8 contexts, 64-token prompts, greedy steps at ctx 4096",
+                "world": world, "value": round(steps * batch / (ms / 1e3), 2), "unit": "tokens/s",
+                "ms_per_step": round(ms / steps, 4), "steps": steps,
+                "parallelism": (f"column-sharded linears over {world} GPUs, NCCL all-gathers" if world > 1
+                                else "single GPU"),
+                "allgather_share": round(gather / total, 4) if total > 0 else None}
+    finally:
+        ctx.free()
+        model.free()
 
 
 def per_kernel_roofline(args, ctx, prompt, ms):
@@ -883,6 +938,10 @@ def main():
     ap.add_argument("--fast", action="store_true", help="tree reductions instead of the reference order")
     ap.add_argument("--profile-steps", type=int, default=4)
     ap.add_argument("--ref-procs", type=int, default=32)
+    ap.add_argument("--tp-steps", type=int, default=32,
+                    help="timed steps of the column-sharded configs[4] block")
+    ap.add_argument("--no-tp-block", action="store_true",
+                    help="skip the column-sharded configs[4] block of the default run")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--classify", action="store_true",
                     help="BASELINE configs[0]: bnn-mlp classify, batch 64 (samples/s)")

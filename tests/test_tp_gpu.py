@@ -1,6 +1,7 @@
 """Tensor-parallel decode (column-sharded linears, NCCL all-gathers): the
-sharded engine on 2 GPUs must reproduce the single-GPU engine bit for bit.
-Runs tests/tp_worker.py as two ranks; skipped with fewer than 2 GPUs."""
+sharded engine on 2 and 4 GPUs must reproduce the single-GPU engine bit for
+bit (whose one-row steps run as the persistent step kernel). Runs
+tests/tp_worker.py as one rank per GPU; skipped with fewer GPUs."""
 import os
 import subprocess
 import sys
@@ -20,12 +21,14 @@ def _gpus():
         return 0
 
 
-@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
-def test_tensor_parallel_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("world", [2, 4])
+def test_tensor_parallel_matches_single_gpu(tmp_path, world):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
     env = dict(os.environ, BNN_TP_MODEL=str(tmp_path / "tp_model.gguf"), NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", "29513",
+           f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", str(29513 + 10 * world),
            str(ROOT / "tests" / "tp_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=360)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-6000:]
-    assert "TP OK 2" in r.stdout
+    assert f"TP OK {world}" in r.stdout
