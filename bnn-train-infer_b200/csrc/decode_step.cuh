@@ -274,14 +274,7 @@ __device__ __noinline__ void copy_dots(const unsigned char* w, uint32_t nb, uint
         if (g >= G)
             continue;
         const uint4 wv = reinterpret_cast<const uint4*>(w + (size_t)b * G * 144u)[g * kRowBlock + r];
-        uint32_t mk[32];
-        const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                mk[t * 8 + j] = words[t] & (0x01010101u << j);
-        dsm[(b * kRowBlock + r) * G + g] = (int16_t)group_dot(mk, act_s + g * kActStride, tot_s[g]);
+        dsm[(b * kRowBlock + r) * G + g] = (int16_t)group_dot_w(wv, act_s + g * kActStride, tot_s[g]);
     }
 }
 

@@ -139,8 +139,19 @@ __device__ __forceinline__ unsigned long long argmax_key(float y, uint32_t n) {
 }
 
 struct GemvSmem {
-    size_t bars, rs, act, tot, xbuf, seg, dsm, epi, stage, total;
+    size_t bars, rs, act, tot, xbuf, seg, dsm, epi, amort, stage, total;
 };
+
+// One activation row, one block per compute warp (bpt == kComputeWarps), a
+// View or residual epilogue and at most 32 groups: each warp gathers the
+// integer D and the scales of four of its blocks and then runs their 32
+// ordered FP32 chains at once, one per lane (instead of eight chains on
+// eight lanes after every block).
+constexpr uint32_t kAmortBlocks = 4;
+__host__ __device__ inline bool gemv_amortised(uint32_t groups, uint32_t mrows, uint32_t bpt, int epi) {
+    return mrows == 1 && bpt == kComputeWarps && (epi == 1 /* kEpiView */ || epi == 2 /* kEpiResidual */) &&
+           (groups == 8 || groups == 16 || groups == 32);
+}
 
 __host__ __device__ inline GemvSmem gemv_smem_plan(uint32_t groups, uint32_t mrows, uint32_t bpt,
                                                    uint32_t stages, int pro, int epi) {
@@ -154,7 +165,10 @@ __host__ __device__ inline GemvSmem gemv_smem_plan(uint32_t groups, uint32_t mro
     p.dsm = p.seg + (pro == kProRmsNorm ? kSumSmemBytes : 0);
     p.epi = p.dsm + (epi != kEpiDotGroups ? (size_t)bpt * mrows * kRowBlock * groups * 2u : 0);
     p.epi = (p.epi + 15) & ~(size_t)15;
-    p.stage = p.epi + (epi == kEpiSwiGLU ? (size_t)bpt * mrows * kRowBlock * 4u : 0);
+    p.amort = p.epi + (epi == kEpiSwiGLU ? (size_t)bpt * mrows * kRowBlock * 4u : 0);
+    // per warp: D [4 blocks][8 rows][G] int16 then scales [4][8][G] binary16
+    p.stage = p.amort + (gemv_amortised(groups, mrows, bpt, epi)
+                             ? (size_t)kComputeWarps * kAmortBlocks * kRowBlock * groups * 4u : 0);
     p.stage = (p.stage + 127) & ~(size_t)127;
     p.total = p.stage + (size_t)stages * bpt * block_bytes(groups);
     return p;
@@ -187,8 +201,64 @@ __device__ __forceinline__ int group_dot(const uint32_t (&mk)[32], const uint32_
     return (pos128 >> 6) - total;
 }
 
+// group_dot with the group's 32 sliced activation words already in registers.
+__device__ __forceinline__ int group_dot_regs(uint4 w, const uint4 (&av)[8], int total) {
+    int acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        acc[j] = 0;
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const uint4 lo = av[t * 2], hi = av[t * 2 + 1];
+        const uint32_t wd = words[t];
+        acc[0] = dp4a_us(wd & 0x01010101u, lo.x, acc[0]);
+        acc[1] = dp4a_us(wd & 0x02020202u, lo.y, acc[1]);
+        acc[2] = dp4a_us(wd & 0x04040404u, lo.z, acc[2]);
+        acc[3] = dp4a_us(wd & 0x08080808u, lo.w, acc[3]);
+        acc[4] = dp4a_us(wd & 0x10101010u, hi.x, acc[4]);
+        acc[5] = dp4a_us(wd & 0x20202020u, hi.y, acc[5]);
+        acc[6] = dp4a_us(wd & 0x40404040u, hi.z, acc[6]);
+        acc[7] = dp4a_us(wd & 0x80808080u, hi.w, acc[7]);
+    }
+    int pos128 = acc[7];
+#pragma unroll
+    for (int j = 6; j >= 0; --j)
+        pos128 += acc[j] << (7 - j);
+    return (pos128 >> 6) - total;
+}
+
+// group_dot for one activation row, the masks built word by word from the
+// weight words (fewer live registers; the same integers).
+__device__ __forceinline__ int group_dot_w(uint4 w, const uint32_t* act_s, int total) {
+    int acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        acc[j] = 0;
+    const uint4* a4 = reinterpret_cast<const uint4*>(act_s);
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const uint4 lo = a4[t * 2], hi = a4[t * 2 + 1];
+        const uint32_t wd = words[t];
+        acc[0] = dp4a_us(wd & 0x01010101u, lo.x, acc[0]);
+        acc[1] = dp4a_us(wd & 0x02020202u, lo.y, acc[1]);
+        acc[2] = dp4a_us(wd & 0x04040404u, lo.z, acc[2]);
+        acc[3] = dp4a_us(wd & 0x08080808u, lo.w, acc[3]);
+        acc[4] = dp4a_us(wd & 0x10101010u, hi.x, acc[4]);
+        acc[5] = dp4a_us(wd & 0x20202020u, hi.y, acc[5]);
+        acc[6] = dp4a_us(wd & 0x40404040u, hi.z, acc[6]);
+        acc[7] = dp4a_us(wd & 0x80808080u, hi.w, acc[7]);
+    }
+    int pos128 = acc[7];
+#pragma unroll
+    for (int j = 6; j >= 0; --j)
+        pos128 += acc[j] << (7 - j);
+    return (pos128 >> 6) - total;
+}
+
 template <int PRO, int EPI>
-__global__ void __launch_bounds__((kComputeWarps + 1) * 32, 2) w1a8_gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__((kComputeWarps + 1) * 32, 3) w1a8_gemv_kernel(GemvArgs a) {
     griddep_launch_dependents();
     extern __shared__ __align__(128) unsigned char sm[];
     const uint32_t G = a.groups;
@@ -398,6 +468,114 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, 2) w1a8_gemv_kernel(
         else
             __syncwarp();
     };
+    if (EPI == kEpiView || EPI == kEpiResidual) {
+        if (gemv_amortised(G, mrows, bpt, EPI)) {
+            // ---- amortised epilogue (see gemv_amortised)
+            int16_t* am_d = reinterpret_cast<int16_t*>(sm + plan.amort) + (size_t)warp * kAmortBlocks * kRowBlock * G * 2;
+            uint16_t* am_s = reinterpret_cast<uint16_t*>(am_d + kAmortBlocks * kRowBlock * G);
+            uint32_t pend = 0, pend_blk = 0;  // blocks gathered; block index of slot k in bits 8k..
+            uint32_t pend_live = 0;           // slot k computed (bit k)
+            uint32_t blks[kAmortBlocks];
+            // lane L works on group g = L / (32 / G), rows (L % (32 / G)) * (G / 4) .. + G / 4 - 1
+            // of every block: its group's activations stay in registers for every tile
+            const uint32_t lpg = 32u / G, rpl = G / 4u;
+            const uint32_t ga = lane / lpg, ra = (lane % lpg) * rpl;
+            uint4 av[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                av[c] = reinterpret_cast<const uint4*>(act_s + ga * kActStride)[c];
+            const int tot_a = tot_s[ga];
+            uint32_t i = 0;
+            for (uint32_t tile = blockIdx.x; tile < a.tiles; tile += gridDim.x, ++i) {
+                const uint32_t s = i % a.stages;
+                const bool ready = mbar_wait(&full[s], (i / a.stages) & 1);
+                if (!ready && lane == 0)
+                    atomicOr(a.status, kStatusTimeout);
+                const bool work = ready && !abort;
+                const uint32_t blk = tile * bpt + my_block;
+                const unsigned char* wblk = stage0 + (size_t)s * tile_bytes + (size_t)my_block * bb;
+                if (work) {
+                    const uint4* wt = reinterpret_cast<const uint4*>(wblk) + ga * kRowBlock + ra;
+                    int16_t* dcol = am_d + (size_t)(pend * kRowBlock + ra) * G + ga;
+#pragma unroll 2
+                    for (uint32_t i2 = 0; i2 < rpl; ++i2)
+                        dcol[(size_t)i2 * G] = (int16_t)group_dot_regs(wt[i2], av, tot_a);
+                    // the block's scales (8 rows x G binary16) follow it out of the stage
+                    const uint4* sc4 = reinterpret_cast<const uint4*>(wblk + (size_t)G * 128u);
+                    uint4* dst4 = reinterpret_cast<uint4*>(am_s + (size_t)pend * kRowBlock * G);
+                    for (uint32_t c = lane; c < kRowBlock * G / 8; c += 32)
+                        dst4[c] = sc4[c];
+                }
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(&empty[s]);  // this warp no longer reads the stage
+                blks[pend] = blk;
+                pend_live |= (work ? 1u : 0u) << pend;
+                ++pend;
+                if (pend == kAmortBlocks || tile + gridDim.x >= a.tiles) {
+                    // lane L: block slot L / 8, row L % 8
+                    const uint32_t k = lane >> 3, rr = lane & 7;
+                    uint32_t bk = blks[0];
+#pragma unroll
+                    for (uint32_t q = 1; q < kAmortBlocks; ++q)
+                        bk = k == q ? blks[q] : bk;
+                    const uint32_t n = bk * kRowBlock + rr;
+                    if (k < pend && ((pend_live >> k) & 1u) && n < a.n) {
+                        float acc = 0.0f;
+                        const uint16_t* sc = am_s + ((size_t)k * kRowBlock + rr) * G;
+                        const int16_t* dd = am_d + ((size_t)k * kRowBlock + rr) * G;
+                        for (uint32_t g0 = 0; g0 < G; g0 += 8) {
+                            const uint4 sv = *reinterpret_cast<const uint4*>(sc + g0);
+                            const uint4 dv = *reinterpret_cast<const uint4*>(dd + g0);
+                            const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+                            const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
+                            float pr[8];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const int d0 = (int)(int16_t)(dw[j] & 0xffffu), d1 = (int)(int16_t)(dw[j] >> 16);
+                                const float f0 = __fsub_rn(__int_as_float(0x4b400000 + d0), 12582912.0f);
+                                const float f1 = __fsub_rn(__int_as_float(0x4b400000 + d1), 12582912.0f);
+                                pr[2 * j] = __fmul_rn(h2f((uint16_t)(sw[j] & 0xffffu)), f0);
+                                pr[2 * j + 1] = __fmul_rn(h2f((uint16_t)(sw[j] >> 16)), f1);
+                            }
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                acc = __fadd_rn(acc, pr[j]);
+                        }
+                        if (PRO != kProSliced || a.row_scale)
+                            acc = __fmul_rn(acc, rs_s[0]);
+                        if (EPI == kEpiView) {
+                            store_f32_any(a.out + (size_t)m0 * a.out_stride + (size_t)n * 4u, acc);
+                            if (a.best) {
+                                if (!isfinite(acc))
+                                    atomicOr(a.status, kStatusNonFinite);
+                                const unsigned long long key = argmax_key(acc, a.index_base + n);
+                                best0 = key > best0 ? key : best0;
+                            }
+                        } else {
+                            float* dst = reinterpret_cast<float*>(a.out + (size_t)m0 * a.out_stride) + n;
+                            const float base =
+                                a.res ? reinterpret_cast<const float*>(a.res + (size_t)m0 * a.res_stride)[n] : *dst;
+                            *dst = __fadd_rn(base, acc);
+                        }
+                    }
+                    __syncwarp();  // the slots are reused
+                    pend = 0;
+                    pend_live = 0;
+                }
+            }
+            (void)pend_blk;
+            if (EPI == kEpiView && a.best != nullptr) {
+                for (int o = 16; o > 0; o >>= 1) {
+                    const unsigned long long ob = __shfl_xor_sync(0xffffffffu, best0, o);
+                    best0 = ob > best0 ? ob : best0;
+                }
+                if (lane == 0 && best0 != 0ull)
+                    atomicMax(&a.best[m0], best0);
+            }
+            return;
+        }
+    }
     uint32_t i = 0;
     for (uint32_t tile = blockIdx.x; tile < a.tiles; tile += gridDim.x, ++i) {
         const uint32_t s = i % a.stages;
