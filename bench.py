@@ -15,6 +15,8 @@ value     tokens/s of BNND_Generate with everything resident on the device,
           timed with CUDA events on the engine's stream (max over ranks).
 e2e       the same through the public per-token call BNND_DecodeArgmax with
           host token ids in and the host argmax out every step (4 B each way).
+text_stream  the same generation as streamed text (BNND_GenerateStream, a
+          host piece callback per token, device steps queued ahead), wall clock.
 roofline  the W1A8 contraction kernel (the step's dominant kernel), from an
           instrumented replay of the same step graph: algorithmic bytes
           (N*K*0.140625 + 4K + 4N per linear) / its device time, against the
@@ -145,6 +147,35 @@ def run_generations_per_token(ctx, first, n_prompt, gen_steps, total):
             tok = ctx.decode_argmax(tok)
         done += s
     return tok
+
+
+def stream_block(ctx, first, n_prompt, gen_steps):
+    """The configured generation as streamed text: BNND_GenerateStream hands
+    each token's piece to a host callback while the device runs up to four
+    steps ahead (the reference CLI's loop, bnn-infer-v2.c:253-282). Wall
+    clock around the public calls (rewind, the step at position n_prompt,
+    the stream), as a user sees it; tokens = ids handed out (the stream stops
+    early at an EOG token)."""
+    pieces = []
+
+    def on_piece(_tok, piece):
+        pieces.append(piece)
+        return False
+
+    def one():
+        pieces.clear()
+        ctx.truncate(n_prompt)
+        ctx.decode_argmax(first)
+        return ctx.generate_stream(gen_steps, on_piece)
+
+    one()
+    one()
+    t0 = time.perf_counter()
+    ids = one()
+    wall = time.perf_counter() - t0
+    return {"value": round(len(ids) / wall, 2), "unit": "tokens/s", "tokens": int(len(ids)),
+            "bytes_out": sum(len(p) for p in pieces), "wall_ms": round(wall * 1e3, 3),
+            "call": "BNND_GenerateStream with a Python piece callback, wall clock"}
 
 
 def model_path(cache):
@@ -361,6 +392,7 @@ def run_b200(args):
 
     ms_e2e = timed(e2e_loop)
     e2e_value = args.steps * streams / (ms_e2e / 1e3)
+    text_stream = stream_block(ctx, first, n_prompt, gen_steps) if batch == 1 and not tp else None
 
     step_positions = ctx.step_kernel_positions()
     timed_pos = [n_prompt + i % gen_steps for i in range(args.steps)]
@@ -439,6 +471,8 @@ def run_b200(args):
             "clocks": clk,
             "gpu_launches": int(launches_per_step * args.steps),
         }
+        if text_stream:
+            out["text_stream"] = text_stream
         if tp_info:
             out["tp"] = tp_info
     if ctx is not None:

@@ -80,6 +80,17 @@ class EngineApi:
             "BNND_StepLaunches": (c_uint32, [c_void_p]),
             "BNND_StepKernelPositions": (c_uint32, [c_void_p]),
             "BNND_StepKernelTrace": (c_int, [c_void_p, c_void_p, ctypes.c_size_t, POINTER(ctypes.c_size_t)]),
+            "BNND_GenerateStream": (c_int, [c_void_p, c_uint32, c_void_p, c_void_p, c_void_p, POINTER(c_uint32)]),
+            "BNND_Tokenize": (c_int, [c_void_p, c_char_p, c_int, c_void_p, c_uint32, POINTER(c_uint32)]),
+            "BNND_TokenPiece": (c_int, [c_void_p, c_int32, POINTER(c_void_p), POINTER(ctypes.c_size_t)]),
+            "BNND_TokenIsEog": (c_int, [c_void_p, c_int32]),
+            "BNND_TokenizerLoad": (c_int, [c_char_p, POINTER(c_void_p)]),
+            "BNND_TokenizerFree": (None, [c_void_p]),
+            "BNND_TokenizerSize": (c_uint32, [c_void_p]),
+            "BNND_TokenizerEncode": (c_int, [c_void_p, c_char_p, ctypes.c_size_t, c_int, c_void_p, c_uint32,
+                                             POINTER(c_uint32)]),
+            "BNND_TokenizerPiece": (c_int, [c_void_p, c_int32, POINTER(c_void_p), POINTER(ctypes.c_size_t)]),
+            "BNND_TokenizerIsEog": (c_int, [c_void_p, c_int32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(d, name)
@@ -93,6 +104,69 @@ class EngineApi:
     def check(self, st):
         if st != OK:
             raise EngineError(st, self.last_error())
+
+
+# int fn(void* user, int32_t id, const char* bytes, size_t len) (BNND_PieceFn)
+PIECE_FN = ctypes.CFUNCTYPE(c_int, c_void_p, c_int32, c_void_p, ctypes.c_size_t)
+
+
+def _text(text):
+    return text.encode("utf-8") if isinstance(text, str) else bytes(text)
+
+
+def _encode_raw(call, capacity):
+    """Runs one encode call (ids buffer, capacity, count pointer) -> (status, ids written)."""
+    ids = np.zeros(max(1, capacity), dtype=np.int32)
+    n = c_uint32()
+    st = call(ids.ctypes.data, capacity, ctypes.byref(n))
+    return st, ids[:n.value].copy()
+
+
+def _piece(call, token):
+    ptr, n = c_void_p(), ctypes.c_size_t()
+    st = call(token, ctypes.byref(ptr), ctypes.byref(n))
+    return st, (ctypes.string_at(ptr.value, n.value) if st == OK and n.value else b"")
+
+
+class Tokenizer:
+    """The byte-level BPE tokenizer read straight from a GGUF (no device)."""
+
+    def __init__(self, path, api: EngineApi = None):
+        self.api = api or EngineApi()
+        h = c_void_p()
+        self.api.check(self.api.TokenizerLoad(str(path).encode(), ctypes.byref(h)))
+        self.handle = h
+
+    def __len__(self):
+        return self.api.TokenizerSize(self.handle)
+
+    def encode_raw(self, text, parse_special=True, capacity=None):
+        """(status, ids written) without raising; capacity defaults to the byte count + 1."""
+        b = _text(text)
+        cap = len(b) + 1 if capacity is None else capacity
+        return _encode_raw(lambda ids, c, n: self.api.TokenizerEncode(self.handle, b, len(b), int(parse_special),
+                                                                        ids, c, n), cap)
+
+    def encode(self, text, parse_special=True):
+        st, ids = self.encode_raw(text, parse_special)
+        self.api.check(st)
+        return ids
+
+    def piece_raw(self, token):
+        return _piece(lambda t, p, n: self.api.TokenizerPiece(self.handle, t, p, n), token)
+
+    def piece(self, token):
+        st, b = self.piece_raw(token)
+        self.api.check(st)
+        return b
+
+    def is_eog(self, token):
+        return bool(self.api.TokenizerIsEog(self.handle, token))
+
+    def free(self):
+        if self.handle:
+            self.api.TokenizerFree(self.handle)
+            self.handle = None
 
 
 def shard_plan(api: EngineApi, info: ModelInfo, world: int, rank: int) -> ShardInfo:
@@ -124,6 +198,25 @@ class Model:
         shard = ShardInfo()
         self.api.check(self.api.ModelGetShard(h, ctypes.byref(shard)))
         self.shard = shard
+
+    def tokenize_raw(self, text, parse_special=True, capacity=None):
+        """BNND_Tokenize -> (status, ids written), without raising."""
+        b = _text(text)
+        cap = len(b) + 1 if capacity is None else capacity
+        return _encode_raw(lambda ids, c, n: self.api.Tokenize(self.handle, b, int(parse_special), ids, c, n), cap)
+
+    def tokenize(self, text, parse_special=True):
+        st, ids = self.tokenize_raw(text, parse_special)
+        self.api.check(st)
+        return ids
+
+    def token_piece(self, token):
+        st, b = _piece(lambda t, p, n: self.api.TokenPiece(self.handle, t, p, n), token)
+        self.api.check(st)
+        return b
+
+    def token_is_eog(self, token):
+        return bool(self.api.TokenIsEog(self.handle, token))
 
     def free(self):
         if self.handle:
@@ -178,6 +271,19 @@ class Context:
         out = np.empty((self.rows, steps), dtype=np.int32)
         self.api.check(self.api.Generate(self.handle, steps, out.ctypes.data))
         return out
+
+    def generate_stream(self, steps, on_piece=None):
+        """BNND_GenerateStream: the CLI's greedy text loop with the device
+        running ahead. on_piece(id, bytes) -> truthy stops after that token.
+        Returns the ids handed out."""
+        def cb(_user, token, ptr, n):
+            return 1 if on_piece(token, ctypes.string_at(ptr, n) if n else b"") else 0
+        fn = PIECE_FN(cb) if on_piece is not None else None
+        out = np.empty(steps, dtype=np.int32)
+        count = c_uint32()
+        self.api.check(self.api.GenerateStream(self.handle, steps, ctypes.cast(fn, c_void_p) if fn else None, None,
+                                               out.ctypes.data, ctypes.byref(count)))
+        return out[:count.value].copy()
 
     def truncate(self, pos):
         self.api.check(self.api.ContextTruncate(self.handle, pos))

@@ -267,10 +267,92 @@ def vocabulary(size):
     return tokens, types, eos
 
 
+@dataclass
+class BpeVocab:
+    tokens: list        # str or bytes per id
+    types: list         # tokenizer.ggml.token_type per id (may be shorter than tokens)
+    merges: list        # "left right" lines, rank = line number
+    eos: int
+
+
+def bpe_vocabulary(seed=7, n_merges=320):
+    """A byte-level BPE vocabulary with real merges, trained on seeded
+    synthetic text (syllable words in Latin, Greek, Cyrillic and CJK letters,
+    digits, punctuation), plus the cases a tokenizer has to get right: chat
+    specials of types 3 and 4 (one a prefix of others), a special whose text
+    is also a plain token, a repeated token string (the later id wins), a
+    repeated merge (the first rank wins), malformed merge lines, merges whose
+    result is not a token, invalid UTF-8 token bytes and tokens of types 2, 5
+    and 6. Deterministic for a seed."""
+    rng = np.random.default_rng(seed)
+    sym = _byte_symbols()
+
+    def mapped(text):
+        return [sym[b] for b in text.encode("utf-8")]
+
+    sylls = ["ka", "to", "ri", "ne", "sa", "mo", "lu", "pe", "di", "ga", "the", "ing", "er", "an", "st", "qu",
+             "ch", "sh", "αλ", "βη", "жи", "мо", "日本", "語", "ñe", "ök"]
+    chunks = {}
+    for _ in range(1500):
+        w = "".join(rng.choice(sylls, size=int(rng.integers(1, 4))))
+        if rng.random() < 0.25:
+            w = w[0].upper() + w[1:]
+        if rng.random() < 0.6:
+            w = " " + w
+        n = int(rng.zipf(1.6)) if rng.random() < 0.9 else 1
+        chunks[w] = chunks.get(w, 0) + min(n, 50)
+    for extra in (" 2024", " 1", "...", " !", "\n\n", "'s", "'re", " (", "),", " 42"):
+        chunks[extra] = chunks.get(extra, 0) + 20
+    words = [(tuple(mapped(w)), c) for w, c in sorted(chunks.items())]
+    merges, learned = [], []
+    for _ in range(n_merges):
+        counts = {}
+        for seq, c in words:
+            for a, b in zip(seq, seq[1:]):
+                counts[(a, b)] = counts.get((a, b), 0) + c
+        if not counts:
+            break
+        (a, b), _ = min(counts.items(), key=lambda kv: (-kv[1], kv[0]))
+        merges.append(f"{a} {b}")
+        learned.append(a + b)
+        out = []
+        for seq, c in words:
+            t, i = [], 0
+            while i < len(seq):
+                if i + 1 < len(seq) and seq[i] == a and seq[i + 1] == b:
+                    t.append(a + b)
+                    i += 2
+                else:
+                    t.append(seq[i])
+                    i += 1
+            out.append((tuple(t), c))
+        words = out
+    tokens = sorted(sym, key=ord)
+    seen = set(tokens)
+    for t in learned:
+        if t not in seen:
+            tokens.append(t)
+            seen.add(t)
+    types = [1] * len(tokens)
+    # result "QQ" is no token (its symbol falls back to byte tokens); "QQQ" is
+    merges += ["Q Q", "QQ Q", merges[0], "abc", "q ", " q", "", "Ġ Ġ"]
+    extra = [("QQQ", 1), (learned[3], 1), ("ka", 1), (b"\xff\xfe", 1), ("Ġx y", 2), ("ĠĠ", 5), ("Ċ", 6),
+             ("<|endoftext|>", 3), ("<|im_start|>", 3), ("<|im_end|>", 3), ("<think>", 4), ("</think>", 4),
+             ("<|im", 4), ("<|im_start|>user", 4), ("Ġhi", 4), ("the", 3)]
+    for t, ty in extra:
+        tokens.append(t)
+        types.append(ty)
+    return BpeVocab(tokens, types, merges, tokens.index("<|im_end|>"))
+
+
 def qwen3_model(path, shape=QWEN3_1_7B, seed=20261203, scale_lo=0.005, scale_hi=0.05,
-                norm_std=0.02, name="qwen3-synthetic"):
+                norm_std=0.02, name="qwen3-synthetic", vocab=None):
     """Random-init Qwen3-architecture Q1_0 model: Bernoulli sign bits, binary16
-    group scales ~U[scale_lo, scale_hi], RMSNorm gains ~N(1, norm_std)."""
+    group scales ~U[scale_lo, scale_hi], RMSNorm gains ~N(1, norm_std). The
+    tokenizer is `vocab` (a BpeVocab with len(tokens) == shape.vocab) or, by
+    default, vocabulary(shape.vocab) without merges."""
+    if vocab is not None and len(vocab.tokens) != shape.vocab:
+        raise ValueError("shape.vocab must equal the tokenizer's size")
     rng = np.random.default_rng(seed)
     w = Writer()
     w.string("general.architecture", "qwen3")
@@ -289,13 +371,20 @@ def qwen3_model(path, shape=QWEN3_1_7B, seed=20261203, scale_lo=0.005, scale_hi=
     w.string("qwen3.rope.scaling.type", "none")
     w.f32("qwen3.rope.scaling.factor", 1.0)
     w.u32("qwen3.rope.scaling.original_context_length", shape.context)
-    tokens, types, eos = vocabulary(shape.vocab)
+    if vocab is None:
+        tokens, types, eos = vocabulary(shape.vocab)
+        merges = []
+    else:
+        tokens, types, merges, eos = vocab.tokens, vocab.types, vocab.merges, vocab.eos
     w.string("tokenizer.ggml.model", "gpt2")
     w.string("tokenizer.ggml.pre", "qwen2")
     w.strings("tokenizer.ggml.tokens", tokens)
-    w.i32s("tokenizer.ggml.token_type", types)
-    w.strings("tokenizer.ggml.merges", [])
-    w.u32("tokenizer.ggml.eos_token_id", eos)
+    if types is not None:
+        w.i32s("tokenizer.ggml.token_type", types)
+    if merges is not None:
+        w.strings("tokenizer.ggml.merges", merges)
+    if eos is not None:
+        w.u32("tokenizer.ggml.eos_token_id", eos)
     w.boolean("tokenizer.ggml.add_bos_token", False)
 
     def q1(out, inp):

@@ -35,6 +35,7 @@
 #include "bnn_b200_engine.h"
 #include "bnn_b200_ext.h"
 #include "bnn_internal.h"
+#include "bpe_tokenizer.h"
 #include "decode_step.cuh"
 #include "engine_kernels.cuh"
 #include "gguf_reader.h"
@@ -231,10 +232,22 @@ struct bnnd_model {
     Linear embed;          // world > 1: the whole tied embedding, for embed_kernel
     DevMem out_norm;
     BNND_ShardInfo shard{};  // world 1: every range is the whole matrix
+    std::unique_ptr<bnn::BpeTokenizer> tok;  // qwen3: the GGUF's text tokenizer
     // bnn-mlp
     std::vector<std::unique_ptr<MlpLayer>> mlp;
     uint32_t mlp_max_dim = 0;
 };
+
+// BNND_TokenizerLoad: a tokenizer without a model or a device.
+struct bnnd_tokenizer {
+    bnn::BpeTokenizer tok;
+};
+
+// BNND_GenerateStream keeps up to kStreamAhead decode steps queued ahead of
+// the token the host is handing out; each step's token is copied into its own
+// pinned slot, so kStreamSlots covers the steps in flight plus the one read.
+constexpr uint32_t kStreamAhead = 4;
+constexpr uint32_t kStreamSlots = 2 * kStreamAhead + 2;
 
 struct bnnd_context {
     BNND_Model model = nullptr;
@@ -279,6 +292,10 @@ struct bnnd_context {
     size_t pf_meta_cap = 0;        // entries of pf_meta (ids, positions, cache rows)
     uint32_t* h_meta = nullptr;    // pinned staging of pf_meta
     size_t h_meta_cap = 0;
+    // BNND_GenerateStream: token copies on a side stream, one slot per step in flight
+    cudaStream_t aux = nullptr;
+    cudaEvent_t sv_step[kStreamSlots] = {}, sv_copy[kStreamSlots] = {};
+    int32_t* h_stream = nullptr;   // pinned [kStreamSlots]
 
     ~bnnd_context() {
         // graphs that hold NCCL work go before the communicator
@@ -302,6 +319,16 @@ struct bnnd_context {
             cudaFreeHost(h_next);
         if (h_meta)
             cudaFreeHost(h_meta);
+        for (uint32_t i = 0; i < kStreamSlots; ++i) {
+            if (sv_step[i])
+                cudaEventDestroy(sv_step[i]);
+            if (sv_copy[i])
+                cudaEventDestroy(sv_copy[i]);
+        }
+        if (h_stream)
+            cudaFreeHost(h_stream);
+        if (aux)
+            cudaStreamDestroy(aux);
     }
 };
 
@@ -1616,6 +1643,29 @@ BNND_Status decode(bnnd_context* c, const int32_t* tokens, uint32_t n, float* lo
     return BNND_OK;
 }
 
+BNND_Status tok_status(bnn::TokStatus t) {
+    switch (t) {
+    case bnn::TokStatus::kOk: return BNND_OK;
+    case bnn::TokStatus::kRange: return BNND_ERANGE;
+    case bnn::TokStatus::kFormat: return BNND_EFORMAT;
+    default: return BNND_EINVAL;
+    }
+}
+
+// A language model carries its tokenizer; a GGUF without a usable one does
+// not load (BNNE_ModelLoad, engine.c:61-67).
+BNND_Status load_tokenizer(const bnn::GgufFile& g, bnnd_model* m) {
+    auto t = std::unique_ptr<bnn::BpeTokenizer>(new (std::nothrow) bnn::BpeTokenizer());
+    if (!t)
+        return fail(BNND_ENOMEM, "out of memory");
+    std::string why;
+    const BNND_Status st = tok_status(t->build(g, &why));
+    if (st != BNND_OK)
+        return fail(st, "%s", why.c_str());
+    m->tok = std::move(t);
+    return BNND_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1648,6 +1698,8 @@ BNND_Status BNND_ModelLoadShard(BNN_Device device, const char* gguf_path, uint32
         m->shard.world = world;
         m->shard.rank = rank;
         st = load_qwen3(g, m);
+        if (st == BNND_OK)
+            st = load_tokenizer(g, m);
     } else if (arch == "bnn-mlp")
         st = load_mlp(g, m);  // whole model: classification is data-parallel
     else
@@ -1823,7 +1875,206 @@ BNND_Status BNND_Generate(BNND_Context c, uint32_t steps, int32_t* out_tokens) {
     return BNND_OK;
 }
 
+// The reference CLI's generation loop (bnn-infer-v2.c:253-282) with the
+// device kept busy: the host hands out token s while steps s+1 .. s+kStreamAhead
+// already run. The loop it reproduces, from t0 = the preceding decode's pick:
+//   for s in 0..steps-1: stop if EOG(t_s); emit t_s;
+//                        stop if s+1 == steps or the context is full;
+//                        t_{s+1} = argmax(decode(t_s))
+// so D decodes are kept, D = the number of emitted tokens, less one unless the
+// loop stopped at an EOG token. Steps queued past D are dropped afterwards:
+// the position returns to start + D and the pending pick to t_D, the state
+// the plain loop leaves (stale K/V rows past the position are rewritten
+// before any step reads them).
+BNND_Status BNND_GenerateStream(BNND_Context c, uint32_t steps, BNND_PieceFn fn, void* user, int32_t* out_tokens,
+                                uint32_t* out_count) {
+    if (out_count)
+        *out_count = 0;
+    g_last_error.clear();
+    if (!c || steps == 0)
+        return BNND_EINVAL;
+    const bnnd_model* m = c->model;
+    if (m->info.task != BNND_TASK_LLM || !m->tok)
+        return fail(BNND_ENOTSUP, "model has no text tokenizer");
+    if (c->rows != 1)
+        return fail(BNND_ENOTSUP, "streaming generation needs a one-row context");
+    if (!c->have_logits)
+        return fail(BNND_EINVAL, "BNND_GenerateStream needs a preceding decode with logits");
+    if (c->pos > c->n_ctx)
+        return fail(BNND_ERANGE, "context is past its length");
+    bnn::DeviceGuard guard(m->dev->ordinal);
+    if (!c->aux) {
+        CUDA_OR(cudaStreamCreateWithFlags(&c->aux, cudaStreamNonBlocking), BNND_EIO);
+        for (uint32_t i = 0; i < kStreamSlots; ++i) {
+            CUDA_OR(cudaEventCreateWithFlags(&c->sv_step[i], cudaEventDisableTiming), BNND_EIO);
+            CUDA_OR(cudaEventCreateWithFlags(&c->sv_copy[i], cudaEventDisableTiming), BNND_EIO);
+        }
+        CUDA_OR(cudaMallocHost(&c->h_stream, kStreamSlots * 4), BNND_ENOMEM);
+    }
+    const uint32_t start = c->pos;
+    // decodes the loop can ever run: one fewer than steps, and none past the context
+    const uint32_t d_max = std::min(steps - 1, c->n_ctx - start);
+    int32_t* tok_next = c->tok_next.as<int32_t>();
+    // slot s % kStreamSlots receives t_s: t_0 now, t_{j+1} after decode j
+    auto copy_token = [&](uint32_t s) -> cudaError_t {
+        const uint32_t k = s % kStreamSlots;
+        cudaError_t e = cudaEventRecord(c->sv_step[k], c->stream);
+        if (e == cudaSuccess)
+            e = cudaStreamWaitEvent(c->aux, c->sv_step[k], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(c->h_stream + k, c->hist.as<int32_t>() + s, 4, cudaMemcpyDeviceToHost, c->aux);
+        if (e == cudaSuccess)
+            e = cudaEventRecord(c->sv_copy[k], c->aux);
+        return e;
+    };
+    CUDA_OR(cudaMemcpyAsync(c->hist.p, tok_next, 4, cudaMemcpyDeviceToDevice, c->stream), BNND_EIO);
+    CUDA_OR(cudaMemcpyAsync(c->tok_in.p, tok_next, 4, cudaMemcpyDeviceToDevice, c->stream), BNND_EIO);
+    const uint32_t one = 1;
+    CUDA_OR(cudaMemcpyAsync(c->hist_count.p, &one, 4, cudaMemcpyHostToDevice, c->stream), BNND_EIO);
+    CUDA_OR(copy_token(0), BNND_EIO);
+    uint32_t queued = 0;  // decodes enqueued
+    auto queue_to = [&](uint32_t want) -> cudaError_t {
+        for (; queued < want; ++queued) {
+            cudaError_t e = run_step(c, start + queued, true);
+            if (e == cudaSuccess)
+                e = copy_token(queued + 1);
+            if (e != cudaSuccess)
+                return e;
+        }
+        return cudaSuccess;
+    };
+    BNND_Status st = BNND_OK;
+    uint32_t kept = 0, emitted = 0;  // D, tokens handed out
+    int32_t last = 0;                // t_D
+    cudaError_t ce = queue_to(std::min(d_max, kStreamAhead));
+    for (uint32_t s = 0; ce == cudaSuccess; ++s) {
+        ce = cudaEventSynchronize(c->sv_copy[s % kStreamSlots]);
+        if (ce != cudaSuccess)
+            break;
+        const int32_t t = c->h_stream[s % kStreamSlots];
+        last = t;
+        kept = s;
+        if (t < 0 || (uint32_t)t >= m->info.n_vocab) {
+            st = fail(BNND_ECOMPUTE, "step produced token %d outside the vocabulary", t);
+            break;
+        }
+        if (m->tok->is_eog(t))
+            break;
+        if (out_tokens)
+            out_tokens[s] = t;
+        ++emitted;
+        const char* bytes = nullptr;
+        size_t len = 0;
+        m->tok->piece(t, &bytes, &len);
+        const bool stop = fn && fn(user, t, bytes, len) != 0;
+        if (stop || s + 1 == steps || start + s >= c->n_ctx)
+            break;
+        ce = queue_to(std::min(d_max, s + 1 + kStreamAhead));
+    }
+    if (ce != cudaSuccess)
+        st = fail(BNND_EIO, "BNND_GenerateStream: %s", cudaGetErrorString(ce));
+    const cudaError_t e1 = cudaStreamSynchronize(c->stream), e2 = cudaStreamSynchronize(c->aux);
+    if (st == BNND_OK && (e1 != cudaSuccess || e2 != cudaSuccess))
+        st = fail(BNND_EIO, "BNND_GenerateStream: %s", cudaGetErrorString(e1 != cudaSuccess ? e1 : e2));
+    if (st == BNND_OK && queued)
+        st = finish(c, "BNND_GenerateStream");
+    if (out_count)
+        *out_count = emitted;
+    if (st != BNND_OK) {
+        set_pos(c, start);
+        c->have_logits = false;
+        return st;
+    }
+    if (queued != kept) {  // drop the steps queued past the loop's end
+        c->h_next[0] = last;
+        CUDA_OR(cudaMemcpyAsync(tok_next, c->h_next, 4, cudaMemcpyHostToDevice, c->stream), BNND_EIO);
+        BNND_Status ps = set_pos(c, start + kept);
+        if (ps != BNND_OK)
+            return ps;
+    }
+    c->pos = start + kept;
+    return BNND_OK;
+}
+
 uint32_t BNND_ContextPos(BNND_Context ctx) { return ctx ? ctx->pos : 0; }
+
+BNND_Status BNND_Tokenize(BNND_Model model, const char* text, int parse_special, int32_t* ids, uint32_t capacity,
+                          uint32_t* out_count) {
+    if (out_count)
+        *out_count = 0;
+    g_last_error.clear();
+    if (!model || !text || !ids || !out_count || capacity == 0)
+        return BNND_EINVAL;
+    if (!model->tok)
+        return fail(BNND_ENOTSUP, "model has no text tokenizer");
+    return tok_status(model->tok->encode(text, std::strlen(text), parse_special != 0, ids, capacity, out_count));
+}
+
+BNND_Status BNND_TokenPiece(BNND_Model model, int32_t id, const char** out_bytes, size_t* out_len) {
+    if (out_bytes)
+        *out_bytes = nullptr;
+    if (out_len)
+        *out_len = 0;
+    g_last_error.clear();
+    if (!model || !out_bytes || !out_len)
+        return BNND_EINVAL;
+    if (!model->tok)
+        return fail(BNND_ENOTSUP, "model has no text tokenizer");
+    return tok_status(model->tok->piece(id, out_bytes, out_len));
+}
+
+int BNND_TokenIsEog(BNND_Model model, int32_t id) {
+    if (!model || !model->tok || id < 0 || (uint32_t)id >= model->info.n_vocab)
+        return 0;
+    return model->tok->is_eog(id) ? 1 : 0;
+}
+
+BNND_Status BNND_TokenizerLoad(const char* gguf_path, BNND_Tokenizer* out) {
+    if (out)
+        *out = nullptr;
+    g_last_error.clear();
+    if (!gguf_path || !out)
+        return BNND_EINVAL;
+    bnn::GgufFile g;
+    if (!g.open(gguf_path))
+        return fail(BNND_EFORMAT, "%s: %s", gguf_path, g.error().c_str());
+    auto t = std::unique_ptr<bnnd_tokenizer>(new (std::nothrow) bnnd_tokenizer());
+    if (!t)
+        return fail(BNND_ENOMEM, "out of memory");
+    std::string why;
+    const BNND_Status st = tok_status(t->tok.build(g, &why));
+    if (st != BNND_OK)
+        return fail(st, "%s", why.c_str());
+    *out = t.release();
+    return BNND_OK;
+}
+
+void BNND_TokenizerFree(BNND_Tokenizer tok) { delete tok; }
+
+uint32_t BNND_TokenizerSize(BNND_Tokenizer tok) { return tok ? tok->tok.size() : 0; }
+
+BNND_Status BNND_TokenizerEncode(BNND_Tokenizer tok, const char* text, size_t len, int parse_special, int32_t* ids,
+                                 uint32_t capacity, uint32_t* out_count) {
+    if (out_count)
+        *out_count = 0;
+    g_last_error.clear();
+    if (!tok || (!text && len) || !ids || !out_count || capacity == 0)
+        return BNND_EINVAL;
+    return tok_status(tok->tok.encode(text ? text : "", len, parse_special != 0, ids, capacity, out_count));
+}
+
+BNND_Status BNND_TokenizerPiece(BNND_Tokenizer tok, int32_t id, const char** out_bytes, size_t* out_len) {
+    if (out_bytes)
+        *out_bytes = nullptr;
+    if (out_len)
+        *out_len = 0;
+    g_last_error.clear();
+    if (!tok || !out_bytes || !out_len)
+        return BNND_EINVAL;
+    return tok_status(tok->tok.piece(id, out_bytes, out_len));
+}
+
+int BNND_TokenizerIsEog(BNND_Tokenizer tok, int32_t id) { return tok && tok->tok.is_eog(id) ? 1 : 0; }
 
 BNND_Status BNND_ContextTruncate(BNND_Context ctx, uint32_t pos) {
     g_last_error.clear();

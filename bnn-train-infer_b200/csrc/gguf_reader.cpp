@@ -105,6 +105,8 @@ bool GgufFile::open(const char* path) {
             uint64_t n = c.get<uint64_t>();
             v.kind = 4;
             v.n = (size_t)n;
+            v.elem = et;
+            v.first = c.p;
             if (et == kString) {
                 for (uint64_t j = 0; j < n && c.ok; ++j)
                     c.str();
@@ -215,6 +217,33 @@ bool GgufFile::get_str(const std::string& key, std::string* out) const {
 size_t GgufFile::array_len(const std::string& key) const {
     auto it = kv_.find(key);
     return it == kv_.end() || it->second.kind != 4 ? 0 : it->second.n;
+}
+
+bool GgufFile::get_str_array(const std::string& key, std::vector<std::string_view>* out) const {
+    auto it = kv_.find(key);
+    if (it == kv_.end() || it->second.kind != 4 || it->second.elem != kString)
+        return false;
+    // open() walked these elements with bounds checks, so the walk stays inside the map.
+    const uint8_t* p = it->second.first;
+    out->clear();
+    out->reserve(it->second.n);
+    for (size_t i = 0; i < it->second.n; ++i) {
+        uint64_t len;
+        std::memcpy(&len, p, 8);
+        out->emplace_back(reinterpret_cast<const char*>(p + 8), (size_t)len);
+        p += 8 + len;
+    }
+    return true;
+}
+
+bool GgufFile::get_u32_array(const std::string& key, std::vector<uint32_t>* out) const {
+    auto it = kv_.find(key);
+    if (it == kv_.end() || it->second.kind != 4 || (it->second.elem != kI32 && it->second.elem != kU32))
+        return false;
+    out->resize(it->second.n);
+    if (it->second.n)
+        std::memcpy(out->data(), it->second.first, it->second.n * 4);
+    return true;
 }
 
 const GgufTensor* GgufFile::tensor(const std::string& name) const {

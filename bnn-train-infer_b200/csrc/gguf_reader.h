@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <map>
 #include <string>
+#include <string_view>
 #include <vector>
 
 namespace bnn {
@@ -35,6 +36,12 @@ class GgufFile {
     bool get_f32(const std::string& key, float* out) const;
     bool get_str(const std::string& key, std::string* out) const;
     size_t array_len(const std::string& key) const;
+    // Elements of a string array, as views into the mapped file (valid while
+    // this object lives). False when the key is absent or not a string array.
+    bool get_str_array(const std::string& key, std::vector<std::string_view>* out) const;
+    // Elements of an int32 or uint32 array, as their 32-bit patterns. False
+    // when the key is absent or holds another element type.
+    bool get_u32_array(const std::string& key, std::vector<uint32_t>* out) const;
 
     const GgufTensor* tensor(const std::string& name) const;
 
@@ -45,6 +52,8 @@ class GgufFile {
         double f = 0;
         std::string s;
         size_t n = 0;
+        uint32_t elem = 0;               // arrays: GGUF element type
+        const uint8_t* first = nullptr;  // arrays: first element in the map
     };
     bool fail(const std::string& why);
     std::map<std::string, Value> kv_;

@@ -31,6 +31,7 @@ extern "C" {
 
 typedef struct bnnd_model* BNND_Model;
 typedef struct bnnd_context* BNND_Context;
+typedef struct bnnd_tokenizer* BNND_Tokenizer;
 
 /* Same values as BNNE_Status (bnn-sw-v2/bnn-engine.h:36-45). */
 typedef enum {
@@ -145,6 +146,24 @@ BNND_Status BNND_DecodeLogitsAll(BNND_Context ctx, const int32_t* tokens, uint32
  * Requires a preceding BNND_Decode/BNND_DecodeArgmax. */
 BNND_Status BNND_Generate(BNND_Context ctx, uint32_t steps, int32_t* out_tokens);
 
+/* Receives one generated token and its piece (BNND_TokenPiece bytes, valid
+ * until the model is freed). A non-zero return stops the generation after
+ * this token. */
+typedef int (*BNND_PieceFn)(void* user, int32_t id, const char* bytes, size_t len);
+
+/* The reference CLI's text generation loop (bnn-infer-v2.c:253-282) with
+ * the device kept busy: starting from the argmax of the preceding
+ * BNND_Decode/BNND_DecodeArgmax, hands out up to `steps` tokens in order to
+ * fn (may be NULL) and out_tokens (may be NULL, [steps]); stops before an EOG
+ * token (BNND_TokenIsEog), after `steps` tokens, when the context is full,
+ * or when fn returns non-zero. Decode steps run up to four tokens ahead of
+ * the host; on return the context is exactly where the plain loop leaves it
+ * (position = start + tokens handed out, less one unless it stopped at an
+ * EOG token; the next pick is the token after the last one decoded).
+ * *out_count = tokens handed out. One-row contexts (n_batch 1). */
+BNND_Status BNND_GenerateStream(BNND_Context ctx, uint32_t steps, BNND_PieceFn fn, void* user,
+                                int32_t* out_tokens, uint32_t* out_count);
+
 uint32_t BNND_ContextPos(BNND_Context ctx);
 /* Replaces BNNE_ContextTruncate (bnn-engine.h:144). */
 BNND_Status BNND_ContextTruncate(BNND_Context ctx, uint32_t pos);
@@ -152,6 +171,34 @@ BNND_Status BNND_ContextTruncate(BNND_Context ctx, uint32_t pos);
 /* Replaces BNNE_Classify (bnn-engine.h:131) for bnn-mlp: input
  * [n_samples][input_size], logits [n_samples][n_classes]. */
 BNND_Status BNND_Classify(BNND_Context ctx, const float* input, uint32_t n_samples, float* logits);
+
+/* ---- text: the qwen3 GGUF's byte-level BPE tokenizer (host) ----
+ * Replace BNNE_Tokenize / BNNE_TokenPiece / BNNE_TokenIsEog
+ * (bnn-engine.h:106-116; behaviour of bnn-sw-v2/tokenizer/tokenizer-bpe.c).
+ * BNND_Tokenize: parse_special != 0 matches special tokens (types 3 and 4)
+ * as literals. *out_count always receives the ids written: on BNND_ERANGE
+ * (capacity too small) that is `capacity`, the ids written so far, as the
+ * reference engine does; text outside special tokens that is not valid UTF-8
+ * gives BNND_EINVAL. BNND_ENOTSUP for a model without a tokenizer (bnn-mlp).
+ * BNND_TokenPiece: the token's raw bytes (possibly a partial UTF-8 sequence),
+ * NUL-terminated, borrowed until BNND_ModelFree; BNND_ERANGE for a bad id.
+ * BNND_TokenIsEog: 1 for eos_token_id, <|endoftext|> and <|im_end|>; 0 for
+ * other ids, ids outside the vocabulary and models without a tokenizer. */
+BNND_Status BNND_Tokenize(BNND_Model model, const char* text, int parse_special, int32_t* ids, uint32_t capacity,
+                          uint32_t* out_count);
+BNND_Status BNND_TokenPiece(BNND_Model model, int32_t id, const char** out_bytes, size_t* out_len);
+int BNND_TokenIsEog(BNND_Model model, int32_t id);
+
+/* The same tokenizer read straight from a GGUF, without a model or a device
+ * (host text pipelines, tests). BNND_TokenizerEncode takes an explicit byte
+ * length; otherwise the rules above apply. */
+BNND_Status BNND_TokenizerLoad(const char* gguf_path, BNND_Tokenizer* out);
+void BNND_TokenizerFree(BNND_Tokenizer tok);
+uint32_t BNND_TokenizerSize(BNND_Tokenizer tok);
+BNND_Status BNND_TokenizerEncode(BNND_Tokenizer tok, const char* text, size_t len, int parse_special, int32_t* ids,
+                                 uint32_t capacity, uint32_t* out_count);
+BNND_Status BNND_TokenizerPiece(BNND_Tokenizer tok, int32_t id, const char** out_bytes, size_t* out_len);
+int BNND_TokenizerIsEog(BNND_Tokenizer tok, int32_t id);
 
 /* Thread-local text of the last failure (BNNE_LastError, bnn-engine.h:157). */
 const char* BNND_LastError(void);

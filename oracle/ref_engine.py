@@ -51,6 +51,9 @@ def dll(fast=False):
         d.BNNE_Classify.argtypes = [c_void_p, c_void_p, c_uint32, c_void_p]
         d.BNNE_ContextTruncate.argtypes = [c_void_p, c_uint32]
         d.BNNE_LastError.restype = c_char_p
+        d.BNNE_Tokenize.argtypes = [c_void_p, c_char_p, c_int, c_void_p, c_uint32, POINTER(c_uint32)]
+        d.BNNE_TokenPiece.argtypes = [c_void_p, c_int32, POINTER(c_void_p), POINTER(ctypes.c_size_t)]
+        d.BNNE_TokenIsEog.argtypes = [c_void_p, c_int32]
         _dlls[fast] = d
     return _dlls[fast]
 
@@ -92,6 +95,25 @@ class RefEngine:
             logits = self.decode([out[-1]])
             out.append(int(np.argmax(logits)))
         return out
+
+    def tokenize_raw(self, text, parse_special=True, capacity=None):
+        """BNNE_Tokenize (bnn-engine.h:106) -> (status, ids written). text is
+        bytes without NUL (the call takes a C string)."""
+        b = text.encode("utf-8") if isinstance(text, str) else bytes(text)
+        cap = len(b) + 1 if capacity is None else capacity
+        ids = np.zeros(max(1, cap), dtype=np.int32)
+        n = c_uint32()
+        st = self._d.BNNE_Tokenize(self.model, b, int(parse_special), ids.ctypes.data, cap, ctypes.byref(n))
+        return st, ids[:n.value].copy()
+
+    def piece_raw(self, token):
+        """BNNE_TokenPiece (bnn-engine.h:113) -> (status, bytes)."""
+        ptr, n = c_void_p(), ctypes.c_size_t()
+        st = self._d.BNNE_TokenPiece(self.model, token, ctypes.byref(ptr), ctypes.byref(n))
+        return st, (ctypes.string_at(ptr.value, n.value) if st == 0 and n.value else b"")
+
+    def is_eog(self, token):
+        return bool(self._d.BNNE_TokenIsEog(self.model, token))
 
     def classify(self, x):
         x = np.ascontiguousarray(x, dtype=np.float32)
