@@ -20,10 +20,10 @@ PROMPT = "<|im_start|>user\nkato's RIne 2024 — 日本語?<|im_end|>\n<|im_star
 SHAPE = dict(layers=2, hidden=256, heads=2, kv_heads=1, head_dim=128, ffn=512, context=96)
 
 
-def _model(path, vocab):
+def _model(path, vocab, seed=19):
     from bnn_b200 import gguf
     shape = gguf.Qwen3Shape(vocab=len(vocab.tokens), **SHAPE)
-    return gguf.qwen3_model(path, shape, seed=19, vocab=vocab)
+    return gguf.qwen3_model(path, shape, seed=seed, vocab=vocab)
 
 
 def _cli_loop(ref, prompt, steps, n_ctx, stop_after=None):
@@ -124,14 +124,15 @@ def test_stream_step_limit(b200_device, vocab, tmp_path):
 
 def test_stream_stops_at_eog(b200_device, vocab, tmp_path):
     from bnn_b200 import gguf
-    # the greedy continuation of the default model, then the same weights with
-    # eos_token_id set to a token that first appears a few steps in
-    seq = _run_case(b200_device, _model(tmp_path / "a.gguf", vocab), steps=24, n_ctx=96)
+    # the greedy continuation of a model whose output changes token after a
+    # few steps (seed 22: three of one token, then another), then the same
+    # weights with eos_token_id set to that second token: the stream stops
+    # with steps already queued past it, which must be dropped
+    seq = _run_case(b200_device, _model(tmp_path / "a.gguf", vocab, seed=22), steps=24, n_ctx=96)
     k = next((i for i in range(3, len(seq)) if seq[i] not in seq[:i]), None)
-    if k is None:
-        pytest.skip("greedy sequence repeats one token")
+    assert k is not None, seq
     v = gguf.BpeVocab(vocab.tokens, vocab.types, vocab.merges, seq[k])
-    ids = _run_case(b200_device, _model(tmp_path / "b.gguf", v), steps=24, n_ctx=96)
+    ids = _run_case(b200_device, _model(tmp_path / "b.gguf", v, seed=22), steps=24, n_ctx=96)
     assert ids == seq[:k]
 
 
