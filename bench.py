@@ -17,6 +17,10 @@ e2e       the same through the public per-token call BNND_DecodeArgmax with
           host token ids in and the host argmax out every step (4 B each way).
 text_stream  the same generation as streamed text (BNND_GenerateStream, a
           host piece callback per token, device steps queued ahead), wall clock.
+other_configs  (one-GPU runs) short timed runs of configs[3] (--prefill),
+          configs[0] (--classify) and configs[1]'s 2048x151669 GEMV_F32
+          (--sweep), each with its own roofline, e2e and clocks, so every
+          BASELINE config is measured in the default line.
 roofline  the W1A8 contraction kernel (the step's dominant kernel), from an
           instrumented replay of the same step graph: algorithmic bytes
           (N*K*0.140625 + 4K + 4N per linear) / its device time, against the
@@ -427,6 +431,12 @@ def run_b200(args):
     if roofline is None:
         roofline = per_kernel_roofline(args, ctx, prompt, ms)
 
+    # ---- configs[3] on the same model and GPU (one GPU jobs only): the
+    # batched 512-token prefill, a short timed run inside this line
+    others = {}
+    if world == 1 and not (args.config5 or args.no_other_configs):
+        others["configs[3]"] = _brief(run_prefill(_sub_args(args), ctx, info, timed, rank, world))
+
     # ---- the sharded design on this job's GPUs: configs[4] with every linear
     # column-sharded over the ranks (a single GPU at N = 1), so the scaling
     # run records it at 1, 2, 4 and 8 GPUs next to the replicas
@@ -479,10 +489,35 @@ def run_b200(args):
         ctx.free()
     model.free()
     dev.close()
+    if others:
+        # configs[0] and configs[1] need their own model / matrices: after
+        # this model is gone, each a short timed run of its own mode
+        others["configs[0]"] = _brief(run_classify(_sub_args(args)))
+        others["configs[1]"] = _brief(run_sweep(_sub_args(args, sweep_shape="2048x151669")))
+        if out is not None:
+            out["other_configs"] = others
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     return out
+
+
+def _sub_args(args, **kw):
+    """The options of a short block inside the default line: 8 timed steps
+    after 3 warm-up steps."""
+    sub = argparse.Namespace(**vars(args))
+    sub.steps, sub.warmup, sub.sweep_shape = 8, 3, None
+    for k, v in kw.items():
+        setattr(sub, k, v)
+    return sub
+
+
+def _brief(line):
+    """A mode's JSON line without the keys the enclosing line already holds."""
+    if line is None:
+        return None
+    keep = ("metric", "value", "unit", "steps", "warmup", "ms_per_step", "config", "roofline", "e2e", "clocks")
+    return {k: line[k] for k in keep if k in line}
 
 
 def tp_block(args, dev, api, path, world, rank, dist, timed, engine):
@@ -977,6 +1012,8 @@ def main():
     ap.add_argument("--no-tp-block", action="store_true",
                     help="skip the column-sharded configs[4] block of the default run")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-other-configs", action="store_true",
+                    help="skip the short configs[0], configs[1] and configs[3] blocks of the default run")
     ap.add_argument("--classify", action="store_true",
                     help="BASELINE configs[0]: bnn-mlp classify, batch 64 (samples/s)")
     ap.add_argument("--sweep", action="store_true",
