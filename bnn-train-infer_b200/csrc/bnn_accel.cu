@@ -471,8 +471,9 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
         return BNN_OK;
     }
     // From kMmaMinRows rows the group dots run on the tensor cores
-    // (w1a8_mma.cuh); below, on the dp4a contraction (w1a8_gemv.cuh).
-    const bool mma = M >= bnn::kMmaMinRows;
+    // (w1a8_mma.cuh); below, and for K beyond the tensor-core kernel's
+    // shared memory, on the dp4a contraction (w1a8_gemv.cuh).
+    const bool mma = M >= bnn::kMmaMinRows && bnn::mma_fits(G);
     const size_t act_bytes = align256(mma ? bnn::mma_a_bytes(M, G) : (size_t)M * K);
     const size_t tot_bytes = mma ? 0 : align256((size_t)M * G * 4u);
     const size_t scl_bytes = align256((size_t)M * 4u);
