@@ -619,7 +619,9 @@ BNN_Status bnn_b200_test_wait_limit(BNN_Device device, uint64_t limit_ns, int st
     // no job of this handle may run while the limits change
     if (cudaStreamSynchronize(device->stream) != cudaSuccess ||
         cudaMemcpyToSymbol(bnn::g_wait_ns_limit, &limit, sizeof limit) != cudaSuccess ||
-        cudaMemcpyToSymbol(bnn::g_test_starve_producer, &starve, sizeof starve) != cudaSuccess) {
+        cudaMemcpyToSymbol(bnn::g_test_starve_producer, &starve, sizeof starve) != cudaSuccess ||
+        bnn::set_test_hooks_engine(limit, starve) != cudaSuccess ||
+        bnn::set_test_hooks_noalloc(limit, starve) != cudaSuccess) {
         cudaGetLastError();
         return BNN_EIO;
     }

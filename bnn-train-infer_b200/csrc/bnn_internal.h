@@ -64,4 +64,12 @@ class DeviceGuard {
     bool ok_ = false;
 };
 
+// The kernels' test hooks (the wait limit and the starved copy producer,
+// bnn_sync.cuh and w1a8_gemv.cuh) are device globals, one copy per
+// translation unit. The contraction templates are instantiated in several
+// units and the host link keeps one launch stub of each, so a launch may run
+// another unit's instance: bnn_b200_test_wait_limit sets every unit's copy.
+cudaError_t set_test_hooks_engine(unsigned long long limit_ns, int starve);
+cudaError_t set_test_hooks_noalloc(unsigned long long limit_ns, int starve);
+
 }  // namespace bnn

@@ -149,3 +149,12 @@ extern "C" BNN_Status bnn_b200_gemm_f32_noalloc(BNN_Matrix matrix, const float* 
         return BNN_ETIMEOUT;
     return verdict ? BNN_ERANGE : BNN_OK;
 }
+
+namespace bnn {
+cudaError_t set_test_hooks_noalloc(unsigned long long limit_ns, int starve) {
+    cudaError_t e = cudaMemcpyToSymbol(g_wait_ns_limit, &limit_ns, sizeof limit_ns);
+    if (e == cudaSuccess)
+        e = cudaMemcpyToSymbol(g_test_starve_producer, &starve, sizeof starve);
+    return e;
+}
+}  // namespace bnn

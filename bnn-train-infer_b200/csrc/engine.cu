@@ -2273,3 +2273,12 @@ const char* BNND_LastError(void) { return g_last_error.c_str(); }
 void* BNND_ContextStream(BNND_Context ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
 
 }  // extern "C"
+
+namespace bnn {
+cudaError_t set_test_hooks_engine(unsigned long long limit_ns, int starve) {
+    cudaError_t e = cudaMemcpyToSymbol(g_wait_ns_limit, &limit_ns, sizeof limit_ns);
+    if (e == cudaSuccess)
+        e = cudaMemcpyToSymbol(g_test_starve_producer, &starve, sizeof starve);
+    return e;
+}
+}  // namespace bnn
