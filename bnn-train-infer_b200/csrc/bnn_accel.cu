@@ -150,7 +150,8 @@ BNN_Status BNN_DeviceOpen(uint32_t device_index, BNN_Device* out_device) {
         delete d;
         return BNN_EIO;
     }
-    if (cudaMalloc(&d->d_status, sizeof(int)) != cudaSuccess ||
+    if (cudaMalloc(&d->d_status, 3 * sizeof(int)) != cudaSuccess ||
+        cudaMemset(d->d_status, 0, 3 * sizeof(int)) != cudaSuccess ||
         cudaMallocHost(&d->h_status, sizeof(int)) != cudaSuccess) {
         cudaGetLastError();
         if (d->d_status)
@@ -159,6 +160,8 @@ BNN_Status BNN_DeviceOpen(uint32_t device_index, BNN_Device* out_device) {
         delete d;
         return BNN_ENOMEM;
     }
+    d->last_status = d->d_status;
+    d->single_jobs = 0;
     *out_device = d;
     return BNN_OK;
 }
@@ -445,12 +448,16 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
     // F32 jobs of at most kRowsPerCta rows in 16-byte aligned rows: every
     // contraction CTA loads, validates and quantises all of them in its
     // prologue (kProQuant) before it writes anything, so a rejected row still
-    // leaves the output untouched and no separate prep pass is needed.
+    // leaves the output untouched and no separate prep pass is needed. The
+    // job is one kernel: launched with programmatic dependent launch, its
+    // weight stream starts while the previous kernel of the stream drains
+    // (weights are immutable; activations and outputs are touched only after
+    // the kernel's grid-dependency wait), and its verdict goes to the slot
+    // that the previous single-kernel job cleared.
     const unsigned char* in_ptr = job->input.buffer->data + job->input.offset;
     if (in_type == BNN_TYPE_F32 && M <= (uint32_t)bnn::kRowsPerCta && K <= bnn::kMaxPrologueK &&
         (reinterpret_cast<uintptr_t>(in_ptr) & 15u) == 0 && (M == 1 || in_stride % 16 == 0)) {
-        if (cudaMemsetAsync(device->d_status, 0, sizeof(int), s) != cudaSuccess)
-            return BNN_EIO;
+        const uint32_t slot = 1u + (device->single_jobs & 1u);
         const bnn::GemvLaunch cl = bnn::plan_gemv(device->sm_count, m->out_features, G, M, bnn::kProQuant,
                                                   bnn::kEpiView);
         bnn::GemvArgs ga = {};
@@ -465,11 +472,15 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
         ga.x_stride = M == 1 ? K : in_stride / 4u;
         ga.out = job->output.buffer->data + job->output.offset;
         ga.out_stride = out_stride;
-        ga.status = device->d_status;
-        if (bnn::launch_gemv(cl, M, ga, s, false) != cudaSuccess)
+        ga.status = device->d_status + slot;
+        ga.status_next = device->d_status + (3u - slot);
+        if (bnn::launch_gemv(cl, M, ga, s, true) != cudaSuccess)
             return BNN_EIO;
+        device->single_jobs++;
+        device->last_status = device->d_status + slot;
         return BNN_OK;
     }
+    device->last_status = device->d_status;
     // From kMmaMinRows rows the group dots run on the tensor cores
     // (w1a8_mma.cuh); below, and for K beyond the tensor-core kernel's
     // shared memory, on the dp4a contraction (w1a8_gemv.cuh).
@@ -597,7 +608,7 @@ BNN_Status bnn_b200_sync(BNN_Device device) {
         return BNN_EINVAL;
     bnn::DeviceGuard guard(device->ordinal);
     cudaStream_t s = device->stream;
-    if (cudaMemcpyAsync(device->h_status, device->d_status, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+    if (cudaMemcpyAsync(device->h_status, device->last_status, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
         cudaStreamSynchronize(s) != cudaSuccess) {
         cudaGetLastError();
         return BNN_EIO;

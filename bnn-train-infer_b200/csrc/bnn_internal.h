@@ -16,8 +16,14 @@ struct bnn_accel_device {
     // Per-job scratch: sliced int8 activations, group totals, row scales.
     void* scratch;
     size_t scratch_bytes;
-    int* d_status;            // prep-kernel verdict (device)
+    int* d_status;            // [0] verdict of prep + contraction jobs (reset per job);
+                              // [1], [2] verdicts of single-kernel jobs, used in turn:
+                              // each such job clears the other slot for the next one,
+                              // so no reset sits between two of them and the next
+                              // job's launch overlaps this one's tail (PDL)
     int* h_status;            // pinned host mirror
+    int* last_status;         // the verdict word of the last enqueued job
+    uint32_t single_jobs;     // single-kernel jobs enqueued (picks the slot)
 };
 
 struct bnn_accel_matrix {
