@@ -162,6 +162,8 @@ BNN_Status BNN_DeviceOpen(uint32_t device_index, BNN_Device* out_device) {
     }
     d->last_status = d->d_status;
     d->single_jobs = 0;
+    d->inflight_count = 0;
+    d->inflight_overflow = false;
     *out_device = d;
     return BNN_OK;
 }
@@ -436,6 +438,31 @@ static BNN_Status check_job(BNN_Device device, const BNN_Job* job, BNN_Type* in_
     return BNN_OK;
 }
 
+// Outputs of the jobs in flight (see bnn_accel_device::inflight_out).
+static bool inflight_meets(const bnn_accel_device* d, uintptr_t begin, uintptr_t end) {
+    if (d->inflight_overflow)
+        return true;
+    for (uint32_t i = 0; i < d->inflight_count; ++i)
+        if (begin < d->inflight_out[i][1] && d->inflight_out[i][0] < end)
+            return true;
+    return false;
+}
+
+static void inflight_add(bnn_accel_device* d, uintptr_t begin, uintptr_t end) {
+    if (d->inflight_count == bnn_accel_device::kMaxInflightOutputs) {
+        d->inflight_overflow = true;
+        return;
+    }
+    d->inflight_out[d->inflight_count][0] = begin;
+    d->inflight_out[d->inflight_count][1] = end;
+    d->inflight_count++;
+}
+
+static void inflight_clear(bnn_accel_device* d) {
+    d->inflight_count = 0;
+    d->inflight_overflow = false;
+}
+
 // Enqueues prep + contraction for a validated job on the device stream,
 // without synchronising. Rows are processed in chunks so the grid's y
 // dimension stays within limits; the prep pass over ALL rows runs before
@@ -445,6 +472,12 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
     const BNN_Matrix m = job->matrix;
     const uint32_t K = m->in_features, G = m->groups, M = job->rows;
     cudaStream_t s = device->stream;
+    // every job's output joins the in-flight set (whatever path runs it)
+    {
+        const uintptr_t ob = reinterpret_cast<uintptr_t>(job->output.buffer->data + job->output.offset);
+        inflight_add(device, ob, ob + (size_t)(M - 1) * out_stride +
+                                     (size_t)m->out_features * (job->operation == BNN_OP_DOT_GROUPS ? 2u * G : 4u));
+    }
     // F32 jobs of at most kRowsPerCta rows in 16-byte aligned rows: every
     // contraction CTA loads, validates and quantises all of them in its
     // prologue (kProQuant) before it writes anything, so a rejected row still
@@ -470,6 +503,12 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
         ga.blocks_per_tile = cl.blocks_per_tile;
         ga.x = reinterpret_cast<const float*>(in_ptr);
         ga.x_stride = M == 1 ? K : in_stride / 4u;
+        {
+            // the input may be read early when no job in flight writes it
+            // (this job's own output is in the set already: in place never is)
+            const uintptr_t ib = reinterpret_cast<uintptr_t>(in_ptr);
+            ga.early_input = inflight_meets(device, ib, ib + (size_t)(M - 1) * ga.x_stride * 4u + (size_t)K * 4u) ? 0 : 1;
+        }
         ga.out = job->output.buffer->data + job->output.offset;
         ga.out_stride = out_stride;
         ga.status = device->d_status + slot;
@@ -613,6 +652,7 @@ BNN_Status bnn_b200_sync(BNN_Device device) {
         cudaGetLastError();
         return BNN_EIO;
     }
+    inflight_clear(device);
     const int st = *device->h_status;
     if (st & bnn::kStatusTimeout)
         return BNN_ETIMEOUT;

@@ -24,6 +24,13 @@ struct bnn_accel_device {
     int* h_status;            // pinned host mirror
     int* last_status;         // the verdict word of the last enqueued job
     uint32_t single_jobs;     // single-kernel jobs enqueued (picks the slot)
+    // Output byte ranges [begin, end) of the jobs enqueued since the stream
+    // was last drained: a single-kernel job whose input meets none of them
+    // reads it before its grid-dependency wait (GemvArgs::early_input).
+    static constexpr uint32_t kMaxInflightOutputs = 256;
+    uintptr_t inflight_out[kMaxInflightOutputs][2];
+    uint32_t inflight_count;
+    bool inflight_overflow;   // more outputs than the table holds: no early reads until drained
 };
 
 struct bnn_accel_matrix {

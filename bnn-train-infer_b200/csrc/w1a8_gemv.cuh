@@ -119,6 +119,11 @@ struct GemvArgs {
     size_t out_stride;             // bytes between output rows
     int* status;
     int* status_next;              // when set: cleared for the next job of the stream (once, after the wait)
+    // kProQuant: 1 when no kernel that may still be running writes x (the
+    // host tracks the outputs of the jobs in flight): the prologue then
+    // loads and quantises x before the grid-dependency wait, under the
+    // previous kernel's tail; status words are touched only after the wait
+    int early_input;
     // kEpiView: when set, best[m] collects max over the row's outputs of
     // (order-preserving bits of the value) << 32 | ~(index_base + index),
     // i.e. the greedy pick (first index of the maximum); non-finite outputs
@@ -321,11 +326,19 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, 3) w1a8_gemv_kernel(
     }
 
     // ---- consumers: wait for the producers of our activations, then build them
-    griddep_wait();
-    if (tid == 0 && *a.status != 0)
-        flags[0] = 1;  // an earlier kernel failed: skip the work, keep the protocol
-    if (tid == 0 && a.status_next != nullptr && blockIdx.x == 0 && blockIdx.y == 0)
-        *a.status_next = 0;
+    const bool early = PRO == kProQuant && a.early_input != 0;
+    auto after_wait = [&]() {
+        if (tid == 0) {
+            if (*a.status != 0 && flags[0] != 2)
+                flags[0] = 1;  // an earlier kernel failed: skip the work, keep the protocol
+            if (a.status_next != nullptr && blockIdx.x == 0 && blockIdx.y == 0)
+                *a.status_next = 0;
+        }
+    };
+    if (!early) {
+        griddep_wait();
+        after_wait();
+    }
     if (PRO == kProSliced) {
         for (uint32_t i = tid; i < mrows * G * (kWordsPerGroup / 4); i += cthreads) {
             const uint32_t mm = i / (G * 8), rest = i % (G * 8), g = rest / 8, c = rest % 8;
@@ -453,6 +466,10 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, 3) w1a8_gemv_kernel(
             if (tid == 0)
                 rs_s[mm] = s;
             named_barrier(1, cthreads);  // xbuf and red are reused by the next row
+        }
+        if (early) {
+            griddep_wait();  // the row loop's last barrier made every flag visible to thread 0
+            after_wait();
         }
         if (tid == 0 && flags[0] == 2)
             atomicOr(a.status, kStatusBadInput);

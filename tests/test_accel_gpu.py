@@ -267,3 +267,65 @@ def test_multi_round_tiles(b200_device, oracle_mod):
         for b in (bi, bq, bo, bd):
             b.free()
         m.destroy()
+
+
+def test_async_jobs_read_inputs_in_order(b200_device, oracle_mod):
+    """Single-kernel F32 jobs enqueued back to back (bnn_b200_execute_async):
+    a job may load and quantise its input before the previous kernel ends
+    only when no job in flight writes that input. Chains (each job reading
+    the previous job's output, through the fixed-G kernel and the general
+    one) and independent jobs sharing one input all stay bit-exact."""
+    import ctypes
+    dll = b200_device.api.dll
+    dll.bnn_b200_execute_async.restype = ctypes.c_int
+    dll.bnn_b200_execute_async.argtypes = [ctypes.c_void_p, ctypes.POINTER(accel.Job)]
+    dll.bnn_b200_sync.restype = ctypes.c_int
+    dll.bnn_b200_sync.argtypes = [ctypes.c_void_p]
+    rng = synth.rng_for(10, salt=3)
+    k, n_big = 2048, 8 * 2600  # 2600 blocks: one block per compute warp, the G = 16 kernel
+    sq_bits, sq_scales = (np.ascontiguousarray(a) for a in synth.w1_matrix(rng, k, k))
+    big_bits, big_scales = (np.ascontiguousarray(a) for a in synth.w1_matrix(rng, k, n_big))
+    sq = accel.Matrix(b200_device, sq_bits, sq_scales)
+    big = _unbounded_matrix(b200_device, big_bits, big_scales)
+    x = np.ascontiguousarray(synth.activations(rng, 1, k)[0], dtype=np.float32)
+    bufs = {}
+
+    def buf(name, n):
+        bufs[name] = accel.Buffer(b200_device, n * 4)
+        return bufs[name]
+
+    def enqueue(m, src, dst):
+        job = accel.Job(operation=accel.OP_GEMV_F32, matrix=m.handle,
+                        input=accel.BufferView(src.handle, accel.TYPE_F32, 0, 0),
+                        output=accel.BufferView(dst.handle, accel.TYPE_F32, 0, 0), rows=1)
+        assert dll.bnn_b200_execute_async(b200_device.handle, ctypes.byref(job)) == accel.OK
+
+    def ref(bits, scales, v):
+        out, _, _ = oracle_mod.gemm_f32(bits, scales, v.reshape(1, -1))
+        return out[0]
+
+    try:
+        buf("x", k).write(x)
+        # x -> a -> b -> c through the square matrix; x -> big0; a -> big1 (a in
+        # flight); x -> big2 (x is no job's output); c -> big3
+        enqueue(sq, bufs["x"], buf("a", k))
+        enqueue(big, bufs["x"], buf("big0", n_big))
+        enqueue(sq, bufs["a"], buf("b", k))
+        enqueue(big, bufs["a"], buf("big1", n_big))
+        enqueue(sq, bufs["b"], buf("c", k))
+        enqueue(big, bufs["x"], buf("big2", n_big))
+        enqueue(big, bufs["c"], buf("big3", n_big))
+        assert dll.bnn_b200_sync(b200_device.handle) == accel.OK
+        a = ref(sq_bits, sq_scales, x)
+        b = ref(sq_bits, sq_scales, a)
+        c = ref(sq_bits, sq_scales, b)
+        want = {"a": a, "b": b, "c": c, "big0": ref(big_bits, big_scales, x), "big1": ref(big_bits, big_scales, a),
+                "big2": ref(big_bits, big_scales, x), "big3": ref(big_bits, big_scales, c)}
+        for name, w in want.items():
+            got = bufs[name].read(w.size * 4).view(np.float32)
+            assert bits_equal(got.view(np.uint32), w.view(np.uint32)), name
+    finally:
+        for bb in bufs.values():
+            bb.free()
+        sq.destroy()
+        big.destroy()
