@@ -70,9 +70,9 @@ BNN_Status bnn_b200_test_wait_limit(BNN_Device device, uint64_t limit_ns, int st
  *
  * The first call on a device (after each BNN_DeviceOpen there) looks up the
  * scratch's device address (cudaGetSymbolAddress) and sets the prep kernel's
- * shared-memory limit; make that first call before any stream capture. Every
- * call is synchronous: it waits for its own kernels on the device's stream
- * before it returns. After cudaDeviceReset every handle of that device is
+ * shared-memory limit. Every call is synchronous: it waits for its own
+ * kernels on the device's stream before it returns, so no call can be
+ * recorded into a CUDA graph (stream capture). After cudaDeviceReset every handle of that device is
  * dead; open a new device handle (which also renews this set-up) before the
  * next call. All calls share the one scratch array and it keeps the last
  * call's contents: calls that overlap on the GPU race and must be
