@@ -47,6 +47,7 @@ struct RowsPrepArgs {
     int32_t* totals;     //   group totals [m][k/128] for the dp4a contraction (kProSliced)
     float* row_scale;    // [m]
     int* status;
+    int early_next;      // 1: let the next kernel of the stream launch at once (PDL)
 };
 
 inline size_t rows_prep_smem(uint32_t k, bool exact) {
@@ -67,6 +68,11 @@ __global__ void __launch_bounds__(kRowsPrepThreads) rows_prep_kernel(RowsPrepArg
     const uint32_t row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t K = a.k, G = K / kGroup;
     constexpr uint32_t nt = kRowsPrepThreads, nw = kRowsPrepThreads / 32;
+    // everything below reads what earlier kernels wrote (a no-op unless
+    // launched with programmatic dependent launch)
+    if (a.early_next)
+        griddep_launch_dependents();
+    griddep_wait();
 
     if (tid == 0)
         s_flag = *a.status != 0;  // an earlier kernel failed: nothing more is written
@@ -198,6 +204,8 @@ __global__ void kv_append_kernel(KvAppendArgs a) {
     float* rs = rc + HD / 2;        // [HD/2]
     float* kb = rs + HD / 2;        // [kv_heads][HD]
     const uint32_t row = blockIdx.x, tid = threadIdx.x, g = tid >> 5, lane = tid & 31;
+    griddep_launch_dependents();
+    griddep_wait();
     if (*a.status != 0)
         return;
     const uint32_t pos = a.pos[row];
@@ -304,6 +312,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttn
         return sc_smem ? reinterpret_cast<float*>(pf_smem + plan.sc) + (size_t)(qi * KVM + h) * a.sc_stride
                        : a.scores + ((size_t)(p0 + qi) * a.heads + g * KVM + h) * a.sc_stride;
     };
+    griddep_launch_dependents();
+    griddep_wait();
     if (*a.status != 0)
         return;
     const uint32_t pos0 = a.pos[p0];

@@ -270,9 +270,39 @@ static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs
     const uint32_t nt = blockIdx.x, mt = blockIdx.y;
     const uint32_t nchunks = (G + kMmaChunk - 1) / kMmaChunk;
     const uint32_t nblocks = (a.n + kRowBlock - 1) / kRowBlock;  // weight blocks that exist
+    __shared__ int skip_cta;
+    // With programmatic dependent launch the set-up below (barriers, TMEM,
+    // the first weight bits) overlaps the previous kernel; nothing that an
+    // earlier kernel writes is read before the grid-dependency wait.
+    griddep_launch_dependents();
 
-    if (*a.status != 0)
-        return;  // an input row was rejected: no output is written
+    // ---- warps 2..5: weight bits kMmaXDepth chunks ahead (each thread its
+    // own kXRows 16-byte rows): where they come from and where they go
+    const uint32_t xt = tid - 64;  // 0 .. kMmaXThreads - 1 on those warps
+    auto row_src = [&](uint32_t c, uint32_t k, uint32_t* gi, uint32_t* n) -> const unsigned char* {
+        const uint32_t rg = xt + k * kMmaXThreads;
+        *gi = rg / NT;
+        *n = rg % NT;
+        const uint32_t g = c * kMmaChunk + *gi, blk = nt * kBlk + *n / kRowBlock;
+        if (g >= G || blk >= nblocks)
+            return nullptr;
+        return a.wblocks + (size_t)blk * G * 144u + (size_t)g * 128u + (*n % kRowBlock) * 16u;
+    };
+    auto slot = [&](uint32_t c, uint32_t k) {
+        return w_slots + (((size_t)(c % kMmaXDepth) * kXRows + k) * kMmaXThreads + xt) * 16u;
+    };
+    auto fetch = [&](uint32_t c) {  // one commit group per chunk, empty past the end
+        if (c < nchunks)
+#pragma unroll
+            for (uint32_t k = 0; k < kXRows; ++k) {
+                uint32_t gi, n;
+                const unsigned char* src = row_src(c, k, &gi, &n);
+                if (src)
+                    cp_async16(slot(c, k), src);
+            }
+        cp_async_commit();
+    };
+    const bool expander = warp >= 2 && warp < kMmaEpiWarp0;
 
     if (tid == 0) {
         for (uint32_t s = 0; s < kMmaAStages; ++s) {
@@ -302,6 +332,27 @@ static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+
+    // weights never depend on earlier kernels
+    if (expander)
+#pragma unroll
+        for (uint32_t c = 0; c < kMmaXDepth; ++c)
+            fetch(c);
+    griddep_wait();
+    if (tid == 0)
+        skip_cta = *a.status != 0;  // an input row was rejected: no output is written
+    __syncthreads();
+    if (skip_cta) {
+        if (expander)
+            cp_async_wait<0>();  // no copy in flight when the CTA exits
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 1) {  // no MMA was issued
+            tc_fence_after();
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kMmaTmemCols));
+        }
+        return;
+    }
 
     if (warp == 0) {
         // ---- producer: one bulk copy of A per chunk (its groups are adjacent)
@@ -354,35 +405,11 @@ static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs
             mma_commit(mdone);  // completes when every MMA issued above has completed
         }
         __syncwarp();
-    } else if (warp < kMmaEpiWarp0) {
-        // ---- warps 2..5: weight bits kMmaXDepth chunks ahead (each thread
-        // its own kXRows 16-byte rows), B chunk by chunk; after the first
+    } else if (expander) {
+        // ---- warps 2..5: B chunk by chunk from the fetched weight bits (the
+        // first kMmaXDepth chunks are in flight already); after the first
         // chunk, the tile's FP32 scales (the epilogue's first read comes after
         // that chunk's MMAs)
-        const uint32_t xt = tid - 64;  // 0 .. kMmaXThreads - 1
-        auto row_src = [&](uint32_t c, uint32_t k, uint32_t* gi, uint32_t* n) -> const unsigned char* {
-            const uint32_t rg = xt + k * kMmaXThreads;
-            *gi = rg / NT;
-            *n = rg % NT;
-            const uint32_t g = c * kMmaChunk + *gi, blk = nt * kBlk + *n / kRowBlock;
-            if (g >= G || blk >= nblocks)
-                return nullptr;
-            return a.wblocks + (size_t)blk * G * 144u + (size_t)g * 128u + (*n % kRowBlock) * 16u;
-        };
-        auto slot = [&](uint32_t c, uint32_t k) {
-            return w_slots + (((size_t)(c % kMmaXDepth) * kXRows + k) * kMmaXThreads + xt) * 16u;
-        };
-        auto fetch = [&](uint32_t c) {  // one commit group per chunk, empty past the end
-            if (c < nchunks)
-#pragma unroll
-                for (uint32_t k = 0; k < kXRows; ++k) {
-                    uint32_t gi, n;
-                    const unsigned char* src = row_src(c, k, &gi, &n);
-                    if (src)
-                        cp_async16(slot(c, k), src);
-                }
-            cp_async_commit();
-        };
         bool scaled = false;
         auto convert_scales = [&]() {
             scaled = true;
@@ -398,9 +425,6 @@ static __global__ void __launch_bounds__(kMmaThreads, 1) w1a8_mma_kernel(MmaArgs
             }
             mbar_arrive(sready);
         };
-#pragma unroll
-        for (uint32_t c = 0; c < kMmaXDepth; ++c)
-            fetch(c);
         bool ok = true;
         for (uint32_t c = 0; c < nchunks && ok; ++c) {
             if (c == 1)
@@ -607,7 +631,9 @@ inline bool mma_fits(uint32_t groups) { return mma_smem_plan(kMmaNarrow, groups)
 // Launches the contraction of `a.m` rows (a.m <= 65535 * kMmaM, mma_fits)
 // on `s`: 128-wide tiles, or 64-wide when the wide grid would leave SMs idle
 // on a device of `sms` streaming multiprocessors or its scales do not fit.
-inline cudaError_t launch_mma(const MmaArgs& a, int sms, cudaStream_t s) {
+// With pdl the launch may overlap the previous kernel of the stream (the
+// kernel waits for it before it reads anything but the weights).
+inline cudaError_t launch_mma(const MmaArgs& a, int sms, cudaStream_t s, bool pdl = false) {
     const uint32_t mtiles = (a.m + kMmaM - 1) / kMmaM;
     const bool narrow = (size_t)((a.n + kMmaN - 1) / kMmaN) * mtiles < (size_t)sms ||
                         mma_smem_plan(kMmaN, a.groups).total > kMmaSmemMax;
@@ -617,12 +643,18 @@ inline cudaError_t launch_mma(const MmaArgs& a, int sms, cudaStream_t s) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.total);
     if (e != cudaSuccess)
         return e;
-    const dim3 grid((a.n + nt - 1) / nt, mtiles);
-    if (narrow)
-        w1a8_mma_kernel<kMmaNarrow><<<grid, kMmaThreads, p.total, s>>>(a);
-    else
-        w1a8_mma_kernel<kMmaN><<<grid, kMmaThreads, p.total, s>>>(a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((a.n + nt - 1) / nt, mtiles);
+    cfg.blockDim = dim3(kMmaThreads);
+    cfg.dynamicSmemBytes = p.total;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return narrow ? cudaLaunchKernelEx(&cfg, w1a8_mma_kernel<kMmaNarrow>, a)
+                  : cudaLaunchKernelEx(&cfg, w1a8_mma_kernel<kMmaN>, a);
 }
 
 }  // namespace bnn
