@@ -478,21 +478,26 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
         inflight_add(device, ob, ob + (size_t)(M - 1) * out_stride +
                                      (size_t)m->out_features * (job->operation == BNN_OP_DOT_GROUPS ? 2u * G : 4u));
     }
-    // F32 jobs of at most kRowsPerCta rows in 16-byte aligned rows: every
-    // contraction CTA loads, validates and quantises all of them in its
-    // prologue (kProQuant) before it writes anything, so a rejected row still
-    // leaves the output untouched and no separate prep pass is needed. The
-    // job is one kernel: launched with programmatic dependent launch, its
-    // weight stream starts while the previous kernel of the stream drains
-    // (weights are immutable; activations and outputs are touched only after
-    // the kernel's grid-dependency wait), and its verdict goes to the slot
-    // that the previous single-kernel job cleared.
+    // Jobs of at most kRowsPerCta rows (F32 rows 16-byte aligned, int8 rows
+    // 4-byte aligned): every contraction CTA loads, validates and quantises
+    // (kProQuant) or slices (kProI8) all of them in its prologue before it
+    // writes anything, so a rejected row still leaves the output untouched
+    // and no separate prep pass is needed. The job is one kernel: launched
+    // with programmatic dependent launch, its weight stream starts while the
+    // previous kernel of the stream drains (weights are immutable;
+    // activations and outputs are touched only after the kernel's
+    // grid-dependency wait, or activations before it when no job in flight
+    // writes them), and its verdict goes to the slot that the previous
+    // single-kernel job cleared.
     const unsigned char* in_ptr = job->input.buffer->data + job->input.offset;
-    if (in_type == BNN_TYPE_F32 && M <= (uint32_t)bnn::kRowsPerCta && K <= bnn::kMaxPrologueK &&
-        (reinterpret_cast<uintptr_t>(in_ptr) & 15u) == 0 && (M == 1 || in_stride % 16 == 0)) {
+    const bool f32 = in_type == BNN_TYPE_F32;
+    const uint32_t in_align = f32 ? 16u : 4u;
+    if (M <= (uint32_t)bnn::kRowsPerCta && K <= bnn::kMaxPrologueK &&
+        (reinterpret_cast<uintptr_t>(in_ptr) & (in_align - 1u)) == 0 && (M == 1 || in_stride % in_align == 0)) {
         const uint32_t slot = 1u + (device->single_jobs & 1u);
-        const bnn::GemvLaunch cl = bnn::plan_gemv(device->sm_count, m->out_features, G, M, bnn::kProQuant,
-                                                  bnn::kEpiView);
+        const int pro = f32 ? bnn::kProQuant : bnn::kProI8;
+        const int epi = job->operation == BNN_OP_DOT_GROUPS ? bnn::kEpiDotGroups : bnn::kEpiView;
+        const bnn::GemvLaunch cl = bnn::plan_gemv(device->sm_count, m->out_features, G, M, pro, epi);
         bnn::GemvArgs ga = {};
         ga.wblocks = m->wblocks;
         ga.n = m->out_features;
@@ -501,13 +506,18 @@ static BNN_Status enqueue_job(BNN_Device device, const BNN_Job* job, BNN_Type in
         ga.tiles = cl.tiles;
         ga.stages = cl.stages;
         ga.blocks_per_tile = cl.blocks_per_tile;
-        ga.x = reinterpret_cast<const float*>(in_ptr);
-        ga.x_stride = M == 1 ? K : in_stride / 4u;
+        const size_t elem = f32 ? 4u : 1u;
+        if (f32)
+            ga.x = reinterpret_cast<const float*>(in_ptr);
+        else
+            ga.xq = reinterpret_cast<const int8_t*>(in_ptr);
+        ga.x_stride = M == 1 ? K : in_stride / elem;
         {
             // the input may be read early when no job in flight writes it
             // (this job's own output is in the set already: in place never is)
             const uintptr_t ib = reinterpret_cast<uintptr_t>(in_ptr);
-            ga.early_input = inflight_meets(device, ib, ib + (size_t)(M - 1) * ga.x_stride * 4u + (size_t)K * 4u) ? 0 : 1;
+            ga.early_input =
+                inflight_meets(device, ib, ib + (size_t)(M - 1) * ga.x_stride * elem + (size_t)K * elem) ? 0 : 1;
         }
         ga.out = job->output.buffer->data + job->output.offset;
         ga.out_stride = out_stride;

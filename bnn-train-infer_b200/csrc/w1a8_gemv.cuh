@@ -21,6 +21,7 @@
 //   kProSliced   pre-sliced words/totals/row scales in global memory (BNN_Execute)
 //   kProQuant    FP32 rows, quantised in the CTA (QuantizeRow, soft :175-211)
 //   kProRmsNorm  FP32 rows, RMSNorm (qwen3.c:361-372) then quantised
+//   kProI8       int8 rows as given, validated (no -128) and sliced in the CTA
 // Epilogues (what is written):
 //   kEpiDotGroups  int16 D into a BNN view          (DOT_GROUPS)
 //   kEpiView       FP32 Z or Z*s into a BNN view    (GEMV/GEMM[_F32])
@@ -62,7 +63,7 @@ constexpr uint32_t kMaxPrologueK = 8192;
 // barrier, so every consumer wait for a weight tile runs out.
 static __device__ int g_test_starve_producer = 0;
 
-enum Prologue : int { kProSliced = 0, kProQuant = 1, kProRmsNorm = 2 };
+enum Prologue : int { kProSliced = 0, kProQuant = 1, kProRmsNorm = 2, kProI8 = 3 };
 enum Epilogue : int { kEpiDotGroups = 0, kEpiView = 1, kEpiResidual = 2, kEpiSwiGLU = 3 };
 
 __host__ __device__ inline size_t block_bytes(uint32_t groups) { return (size_t)groups * 144u; }
@@ -110,7 +111,8 @@ struct GemvArgs {
     const float* row_scale;        // [M]; nullptr: the I8 ops return Z unscaled
     // kProQuant / kProRmsNorm
     const float* x;                // FP32 rows
-    size_t x_stride;               // floats between rows
+    size_t x_stride;               // floats (kProI8: bytes) between rows
+    const int8_t* xq;              // kProI8: int8 rows, 4-byte aligned
     const float* gain;             // kProRmsNorm gains [K]
     float eps;
     int exact;                     // 1: the reference's serial sum for RMSNorm
@@ -119,7 +121,7 @@ struct GemvArgs {
     size_t out_stride;             // bytes between output rows
     int* status;
     int* status_next;              // when set: cleared for the next job of the stream (once, after the wait)
-    // kProQuant: 1 when no kernel that may still be running writes x (the
+    // kProQuant / kProI8: 1 when no kernel that may still be running writes x (the
     // host tracks the outputs of the jobs in flight): the prologue then
     // loads and quantises x before the grid-dependency wait, under the
     // previous kernel's tail; status words are touched only after the wait
@@ -159,6 +161,15 @@ __host__ __device__ inline bool gemv_amortised(uint32_t groups, uint32_t mrows, 
            (groups == 8 || groups == 16 || groups == 32);
 }
 
+// One activation row, one block per compute warp and G = 8/16/32: the lane
+// layout of the amortised epilogue (each lane keeps one group's sliced
+// activations in registers); DOT_GROUPS stores its integers directly.
+__host__ __device__ inline bool gemv_one_row_lanes(uint32_t groups, uint32_t mrows, uint32_t bpt, int epi) {
+    return gemv_amortised(groups, mrows, bpt, epi) ||
+           (epi == 0 /* kEpiDotGroups */ && mrows == 1 && bpt == kComputeWarps &&
+            (groups == 8 || groups == 16 || groups == 32));
+}
+
 __host__ __device__ inline GemvSmem gemv_smem_plan(uint32_t groups, uint32_t mrows, uint32_t bpt,
                                                    uint32_t stages, int pro, int epi) {
     GemvSmem p;
@@ -167,7 +178,7 @@ __host__ __device__ inline GemvSmem gemv_smem_plan(uint32_t groups, uint32_t mro
     p.act = 448;  // after the row scales, flags and 64 reduction slots
     p.tot = p.act + (size_t)mrows * groups * kActStride * 4u;
     p.xbuf = (p.tot + (size_t)mrows * groups * 4u + 15) & ~(size_t)15;  // float4 stores
-    p.seg = p.xbuf + (pro != kProSliced ? (size_t)groups * kGroup * 4u : 0);  // FP32 row
+    p.seg = p.xbuf + (pro == kProQuant || pro == kProRmsNorm ? (size_t)groups * kGroup * 4u : 0);  // FP32 row
     p.dsm = p.seg + (pro == kProRmsNorm ? kSumSmemBytes : 0);
     p.epi = p.dsm + (epi != kEpiDotGroups ? (size_t)bpt * mrows * kRowBlock * groups * 2u : 0);
     p.epi = (p.epi + 15) & ~(size_t)15;
@@ -326,7 +337,7 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, 3) w1a8_gemv_kernel(
     }
 
     // ---- consumers: wait for the producers of our activations, then build them
-    const bool early = PRO == kProQuant && a.early_input != 0;
+    const bool early = (PRO == kProQuant || PRO == kProI8) && a.early_input != 0;
     auto after_wait = [&]() {
         if (tid == 0) {
             if (*a.status != 0 && flags[0] != 2)
@@ -350,6 +361,41 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, 3) w1a8_gemv_kernel(
             tot_s[i] = a.totals[(size_t)m0 * G + i];
         if (tid < mrows)
             rs_s[tid] = a.row_scale ? a.row_scale[m0 + tid] : 1.0f;
+        named_barrier(1, cthreads);
+    } else if constexpr (PRO == kProI8) {
+        // int8 rows as given (ValidateI8Input, soft :279-292: no -128). One
+        // warp slices one group per pass: lane L holds the group's bytes
+        // 4L .. 4L+3, the same 4x4 byte transpose as the FP32 prologue leaves
+        // lane L with its slice word; totals with one dp4a and a reduction.
+        const uint32_t slot = (lane >> 3) * 8u + (lane & 1u) * 4u + ((lane >> 1) & 3u);
+        int bad = 0;
+        for (uint32_t mm = 0; mm < mrows; ++mm) {
+            const uint32_t* xr = reinterpret_cast<const uint32_t*>(a.xq + (size_t)(m0 + mm) * a.x_stride);
+#pragma unroll 1
+            for (uint32_t g = warp; g < G; g += consumers) {
+                uint32_t w = xr[g * 32u + lane];
+                bad |= __vcmpeq4(w, 0x80808080u) != 0u;
+                const int total = __reduce_add_sync(0xffffffffu, __dp4a((int)w, 0x01010101, 0));
+                uint32_t o = __shfl_xor_sync(0xffffffffu, w, 4);
+                w = (lane & 4u) ? __byte_perm(w, o, 0x3276) : __byte_perm(w, o, 0x5410);
+                o = __shfl_xor_sync(0xffffffffu, w, 2);
+                w = (lane & 2u) ? __byte_perm(w, o, 0x3715) : __byte_perm(w, o, 0x6240);
+                act_s[(mm * G + g) * kActStride + slot] = w;
+                if (lane == 0)
+                    tot_s[mm * G + g] = total;
+            }
+        }
+        if (bad)
+            flags[0] = 2;
+        if (tid < mrows)
+            rs_s[tid] = 1.0f;
+        named_barrier(1, cthreads);
+        if (early) {
+            griddep_wait();
+            after_wait();
+        }
+        if (tid == 0 && flags[0] == 2)
+            atomicOr(a.status, kStatusBadInput);
         named_barrier(1, cthreads);
     } else {
         // The row is staged in shared memory once; every later pass is a
@@ -501,6 +547,44 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, 3) w1a8_gemv_kernel(
         else
             __syncwarp();
     };
+    if (EPI == kEpiDotGroups && gemv_one_row_lanes(G, mrows, bpt, EPI)) {
+        // ---- one row, DOT_GROUPS: lane L works on group L / (32 / G), rows
+        // (L % (32 / G)) * (G / 4) .. + G / 4 - 1 of every block, its group's
+        // activations in registers; each int16 D goes straight to the output
+        const uint32_t lpg = 32u / G, rpl = G / 4u;
+        const uint32_t ga = lane / lpg, ra = (lane % lpg) * rpl;
+        uint4 av[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+            av[c] = reinterpret_cast<const uint4*>(act_s + ga * kActStride)[c];
+        const int tot_a = tot_s[ga];
+        unsigned char* orow = a.out + (size_t)m0 * a.out_stride;
+        uint32_t s = 0, phase = 0;
+        for (uint32_t tile = blockIdx.x; tile < a.tiles; tile += gridDim.x) {
+            const bool ready = mbar_wait(&full[s], phase);
+            if (!ready && lane == 0)
+                atomicOr(a.status, kStatusTimeout);
+            if (ready && !abort) {
+                const uint4* wt = reinterpret_cast<const uint4*>(stage0 + (size_t)s * tile_bytes +
+                                                                 (size_t)my_block * bb) + ga * kRowBlock + ra;
+                const uint32_t n0 = (tile * bpt + my_block) * kRowBlock + ra;
+#pragma unroll 2
+                for (uint32_t i2 = 0; i2 < rpl; ++i2) {
+                    const int d = group_dot_regs(wt[i2], av, tot_a);
+                    if (n0 + i2 < a.n)
+                        store_i16_any(orow + ((size_t)(n0 + i2) * G + ga) * 2u, (int16_t)d);
+                }
+            }
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&empty[s]);  // this warp no longer reads the stage
+            if (++s == a.stages) {
+                s = 0;
+                phase ^= 1u;
+            }
+        }
+        return;
+    }
     if (EPI == kEpiView || EPI == kEpiResidual) {
         if (gemv_amortised(G, mrows, bpt, EPI)) {
             // ---- amortised epilogue (see gemv_amortised)
@@ -575,7 +659,7 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, 3) w1a8_gemv_kernel(
                             for (int j = 0; j < 8; ++j)
                                 acc = __fadd_rn(acc, pr[j]);
                         }
-                        if (PRO != kProSliced || a.row_scale)
+                        if ((PRO != kProSliced && PRO != kProI8) || a.row_scale)
                             acc = __fmul_rn(acc, rs_s[0]);
                         if (EPI == kEpiView) {
                             store_f32_any(a.out + (size_t)m0 * a.out_stride + (size_t)n * 4u, acc);
@@ -683,7 +767,7 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, 3) w1a8_gemv_kernel(
                             for (uint32_t g = 0; g < G; ++g)
                                 acc = __fadd_rn(acc, __fmul_rn(h2f(sc[g]), (float)dd[g]));
                         }
-                        if (PRO != kProSliced || a.row_scale)
+                        if ((PRO != kProSliced && PRO != kProI8) || a.row_scale)
                             acc = __fmul_rn(acc, rs_s[mm]);
                         if (EPI == kEpiView) {
                             store_f32_any(a.out + (size_t)(m0 + mm) * a.out_stride + (size_t)n * 4u, acc);
@@ -764,6 +848,8 @@ inline GemvFn gemv_fn_fixed(int pro, int epi) {
     if (pro == kProSliced && epi == kEpiResidual) return w1a8_gemv_kernel<kProSliced, kEpiResidual, 16>;
     if (pro == kProQuant && epi == kEpiView) return w1a8_gemv_kernel<kProQuant, kEpiView, 16>;
     if (pro == kProRmsNorm && epi == kEpiView) return w1a8_gemv_kernel<kProRmsNorm, kEpiView, 16>;
+    if (pro == kProI8 && epi == kEpiView) return w1a8_gemv_kernel<kProI8, kEpiView, 16>;
+    if (pro == kProI8 && epi == kEpiDotGroups) return w1a8_gemv_kernel<kProI8, kEpiDotGroups, 16>;
     return nullptr;
 }
 
@@ -778,6 +864,8 @@ inline GemvFn gemv_fn(int pro, int epi, int gc = 0) {
     if (pro == kProQuant && epi == kEpiResidual) return w1a8_gemv_kernel<kProQuant, kEpiResidual>;
     if (pro == kProRmsNorm && epi == kEpiView) return w1a8_gemv_kernel<kProRmsNorm, kEpiView>;
     if (pro == kProRmsNorm && epi == kEpiSwiGLU) return w1a8_gemv_kernel<kProRmsNorm, kEpiSwiGLU>;
+    if (pro == kProI8 && epi == kEpiDotGroups) return w1a8_gemv_kernel<kProI8, kEpiDotGroups>;
+    if (pro == kProI8 && epi == kEpiView) return w1a8_gemv_kernel<kProI8, kEpiView>;
     return nullptr;
 }
 
@@ -864,7 +952,7 @@ inline GemvLaunch plan_gemv(int sm_count, uint32_t n, uint32_t groups, uint32_t 
     }
     c.grid_x = c.tiles < slots ? c.tiles : slots;
     c.gc = 0;
-    if (groups == kGemvFixedGroups && gemv_amortised(groups, mrows, c.blocks_per_tile, epi)) {
+    if (groups == kGemvFixedGroups && gemv_one_row_lanes(groups, mrows, c.blocks_per_tile, epi)) {
         const GemvFn fixed = gemv_fn_fixed(pro, epi);
         if (fixed != nullptr &&
             cudaFuncSetAttribute((const void*)fixed, cudaFuncAttributeMaxDynamicSharedMemorySize,
