@@ -922,7 +922,7 @@ def run_sweep(args):
                    "shapes": results},
         "roofline": {"bound": "hbm", "achieved": head_gbs, "peak": hbm, "unit": "GB/s",
                      "frac": round(head_gbs / hbm, 4), "peak_source": hbm_kind, "traffic": None,
-                     "what": "prep + contraction of one GEMV_F32 job (kernel time), algorithmic bytes"},
+                     "what": "one GEMV_F32 job = one kernel (in-CTA quantise + contraction), per-job time in the stream of jobs, algorithmic bytes"},
         "e2e": {"value": round(head["bytes"] / (head["e2e_us"] * 1e-6) / 1e9, 1), "unit": "GB/s",
                 "h2d_bytes_per_step": 2048 * 4, "d2h_bytes_per_step": 151669 * 4,
                 "call": "BufferWrite + 19 x BNN_Execute (<= 8192 rows) + BufferRead, host buffers"},
