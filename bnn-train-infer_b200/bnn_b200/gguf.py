@@ -424,9 +424,10 @@ class MlpShape:
 MNIST_MLP = MlpShape()
 
 
-def bnn_mlp_model(path, shape=MNIST_MLP, seed=20261201, scale_lo=0.005, scale_hi=0.05):
+def bnn_mlp_model(path, shape=MNIST_MLP, seed=20261201, scale_lo=0.005, scale_hi=0.05, post_scale_mul=1.0):
     """Random-init bnn-mlp classifier with the reference exporter's schema:
-    Q1_0 blocks, post_scale ~N(1, 0.1), post_bias ~N(0, 0.1)."""
+    Q1_0 blocks, post_scale ~N(1, 0.1) (times post_scale_mul: a test can make
+    hidden activations overflow), post_bias ~N(0, 0.1)."""
     rng = np.random.default_rng(seed)
     w = Writer()
     n_layers = len(shape.dims) - 1
@@ -448,6 +449,6 @@ def bnn_mlp_model(path, shape=MNIST_MLP, seed=20261201, scale_lo=0.005, scale_hi
         scales = rng.uniform(scale_lo, scale_hi, size=(out_pad, inp // GROUP)).astype(np.float16).view(np.uint16)
         w.tensor(f"blk.{i}.weight", [inp, out], TENSOR_Q1_0, q1_0_encode(bits, scales))
         w.tensor(f"blk.{i}.post_scale", [out], TENSOR_F32,
-                 (1.0 + 0.1 * rng.standard_normal(out)).astype("<f4"))
+                 (post_scale_mul * (1.0 + 0.1 * rng.standard_normal(out))).astype("<f4"))
         w.tensor(f"blk.{i}.post_bias", [out], TENSOR_F32, (0.1 * rng.standard_normal(out)).astype("<f4"))
     return w.write(path)

@@ -39,6 +39,7 @@
 #include "decode_step.cuh"
 #include "engine_kernels.cuh"
 #include "gguf_reader.h"
+#include "mlp_fused.cuh"
 #include "prefill_kernels.cuh"
 #include "w1a8_gemv.cuh"
 #include "w1a8_mma.cuh"
@@ -236,6 +237,8 @@ struct bnnd_model {
     // bnn-mlp
     std::vector<std::unique_ptr<MlpLayer>> mlp;
     uint32_t mlp_max_dim = 0;
+    uint32_t mlp_max_in = 0;  // widest layer input
+    DevMem mlp_desc;          // bnn::eng::MlpLayerDev per layer, for mlp_fused_kernel
 };
 
 // BNND_TokenizerLoad: a tokenizer without a model or a device.
@@ -274,6 +277,9 @@ struct bnnd_context {
     StepRecorder recorder;
     uint32_t step_launches = 0;
     int* h_status = nullptr;
+    float* h_mlp_in = nullptr;     // pinned staging of a fused classify call's samples / logits
+    float* h_mlp_out = nullptr;
+    size_t mlp_fused_smem = 0;     // 0: no fused classify (mlp_fused.cuh) in this context
     int32_t* h_tokens = nullptr;   // pinned staging of input ids
     size_t h_tokens_cap = 0;
     int32_t* h_next = nullptr;     // pinned staging of greedy picks
@@ -313,6 +319,10 @@ struct bnnd_context {
             cudaEventDestroy(e);
         if (h_status)
             cudaFreeHost(h_status);
+        if (h_mlp_in)
+            cudaFreeHost(h_mlp_in);
+        if (h_mlp_out)
+            cudaFreeHost(h_mlp_out);
         if (h_tokens)
             cudaFreeHost(h_tokens);
         if (h_next)
@@ -632,6 +642,24 @@ BNND_Status load_mlp(const bnn::GgufFile& g, bnnd_model* m) {
     m->info.eos_token = -1;
     m->info.weight_count = weights;
     m->mlp_max_dim = max_dim;
+    // the layers as the fused classifier kernel reads them
+    std::vector<bnn::eng::MlpLayerDev> desc;
+    for (const auto& layer : m->mlp) {
+        bnn::eng::MlpLayerDev d = {};
+        d.wblocks = layer->w.m->wblocks;
+        d.post_scale = layer->post_scale.as<float>();
+        d.post_bias = layer->post_bias.as<float>();
+        d.in = layer->w.in;
+        d.out = layer->w.out;
+        d.relu = layer->relu;
+        desc.push_back(d);
+        m->mlp_max_in = std::max(m->mlp_max_in, layer->w.in);
+    }
+    BNND_Status st = dev_alloc(m->mlp_desc, desc.size() * sizeof(desc[0]));
+    if (st != BNND_OK)
+        return st;
+    if (cudaMemcpy(m->mlp_desc.p, desc.data(), desc.size() * sizeof(desc[0]), cudaMemcpyHostToDevice) != cudaSuccess)
+        return fail(BNND_EIO, "bnn-mlp layer table upload failed");
     return BNND_OK;
 }
 
@@ -1323,6 +1351,17 @@ BNND_Status create_mlp_context(bnnd_context* c) {
         if (c->plan_mlp.back().smem > bnn::kGemvSmemBudget)
             return fail(BNND_ENOTSUP, "layer width too large for the contraction kernel");
     }
+    // calls of up to kMlpFusedMaxSamples samples: one fused launch, pinned staging
+    const size_t fused = bnn::eng::mlp_fused_smem(m->mlp_max_in);
+    if (fused <= 200u * 1024u) {
+        const size_t rows = std::min<size_t>(R, bnn::eng::kMlpFusedMaxSamples);
+        CUDA_OR(cudaFuncSetAttribute(bnn::eng::mlp_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)fused),
+                BNND_EIO);
+        CUDA_OR(cudaMallocHost(&c->h_mlp_in, rows * m->info.input_size * 4), BNND_ENOMEM);
+        CUDA_OR(cudaMallocHost(&c->h_mlp_out, rows * m->info.n_classes * 4), BNND_ENOMEM);
+        c->mlp_fused_smem = fused;
+    }
     return BNND_OK;
 }
 
@@ -1336,6 +1375,8 @@ BNND_Status finish(bnnd_context* c, const char* what) {
         cudaStreamSynchronize(c->stream);
         if (st & bnn::kStatusTimeout)
             return fail(BNND_EIO, "%s: device wait timed out", what);
+        if (st & bnn::eng::kStatusInputNotFinite)  // checked on the device (fused classify)
+            return fail(BNND_EINVAL, "input contains NaN or Inf");
         if (st == bnn::kStatusBadInput)  // a linear's FP32 input held NaN/Inf (BNN_ERANGE)
             return fail(BNND_ERANGE, "%s: linear input contains NaN or Inf", what);
         return fail(BNND_ECOMPUTE, "%s: model produced NaN or Inf values", what);
@@ -2120,13 +2161,34 @@ BNND_Status BNND_Classify(BNND_Context c, const float* input, uint32_t n_samples
     if (n_samples > c->rows)
         return fail(BNND_ERANGE, "sample count exceeds context batch size");
     const size_t inputs = (size_t)n_samples * m->info.input_size;
-    for (size_t i = 0; i < inputs; ++i)
-        if (!std::isfinite(input[i]))
-            return fail(BNND_EINVAL, "input contains NaN or Inf");
+    const size_t outputs = (size_t)n_samples * m->info.n_classes;
     bnn::DeviceGuard guard(m->dev->ordinal);
     cudaStream_t s = c->stream;
     float* cur = c->mlp_a.as<float>();
     float* nxt = c->mlp_b.as<float>();
+    if (n_samples <= bnn::eng::kMlpFusedMaxSamples && c->mlp_fused_smem) {
+        // every layer of a sample in one CTA (mlp_fused.cuh): one launch per
+        // call, the input check on the device, copies through pinned staging
+        std::memcpy(c->h_mlp_in, input, inputs * 4);
+        CUDA_OR(cudaMemcpyAsync(cur, c->h_mlp_in, inputs * 4, cudaMemcpyHostToDevice, s), BNND_EIO);
+        bnn::eng::MlpFusedArgs fa = {};
+        fa.layers = m->mlp_desc.as<bnn::eng::MlpLayerDev>();
+        fa.n_layers = (uint32_t)m->mlp.size();
+        fa.max_in = m->mlp_max_in;
+        fa.x = cur;
+        fa.logits = nxt;
+        fa.status = c->status.as<int>();
+        bnn::eng::mlp_fused_kernel<<<n_samples, bnn::eng::kMlpThreads, c->mlp_fused_smem, s>>>(fa);
+        CUDA_OR(cudaGetLastError(), BNND_EIO);
+        CUDA_OR(cudaMemcpyAsync(c->h_mlp_out, nxt, outputs * 4, cudaMemcpyDeviceToHost, s), BNND_EIO);
+        const BNND_Status st = finish(c, "BNND_Classify");
+        if (st == BNND_OK)
+            std::memcpy(logits, c->h_mlp_out, outputs * 4);
+        return st;
+    }
+    for (size_t i = 0; i < inputs; ++i)
+        if (!std::isfinite(input[i]))
+            return fail(BNND_EINVAL, "input contains NaN or Inf");
     CUDA_OR(cudaMemcpyAsync(cur, input, inputs * 4, cudaMemcpyHostToDevice, s), BNND_EIO);
     const bool mma = n_samples >= bnn::kMmaMinRows;  // the batch on the tensor cores (BNN_Execute's threshold)
     for (size_t i = 0; i < m->mlp.size(); ++i) {
@@ -2168,7 +2230,6 @@ BNND_Status BNND_Classify(BNND_Context c, const float* input, uint32_t n_samples
                                                      L.w.out, n_samples, L.relu);
         std::swap(cur, nxt);
     }
-    const size_t outputs = (size_t)n_samples * m->info.n_classes;
     bnn::eng::finite_check_kernel<<<16, 256, 0, s>>>(cur, outputs, c->status.as<int>(), bnn::kStatusNonFinite);
     CUDA_OR(cudaMemcpyAsync(logits, cur, outputs * 4, cudaMemcpyDeviceToHost, s), BNND_EIO);
     return finish(c, "BNND_Classify");

@@ -655,8 +655,12 @@ __global__ void mlp_post_kernel(float* y, const float* ps, const float* pb, uint
     }
 }
 
-// Non-finite check of an FP32 array (BNNE_Classify's input/logit checks).
+// Non-finite check of an FP32 array (BNNE_Classify's logit check). After an
+// earlier kernel failed (a rejected layer input, whose layer was skipped) the
+// array is stale and the first error stands, as the reference stops at it.
 __global__ void finite_check_kernel(const float* v, size_t n, int* status, int bit) {
+    if (*status != 0)
+        return;
     int bad = 0;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x)

@@ -246,3 +246,58 @@ def test_multi_round_lm_head_logits(b200_device, ref_engine_mod, tmp_path):
         ctx.free()
         m.free()
         ref.close()
+
+
+@pytest.mark.parametrize("n", [1, 7, 64, 256, 300])
+def test_classify_batch_sizes(b200_device, ref_engine_mod, models, n):
+    """Up to 256 samples a call runs as one fused kernel (every layer of a
+    sample in one CTA); larger batches run layer by layer on the tensor
+    cores. Both are bit-identical to the reference."""
+    rng = np.random.default_rng(100 + n)
+    x = np.zeros((n, 896), dtype=np.float32)
+    x[:, :784] = rng.standard_normal((n, 784))
+    ref = ref_engine_mod.RefEngine(models["mlp"], n_batch=n)
+    want = ref.classify(x)
+    ref.close()
+    m = engine.Model(b200_device, models["mlp"])
+    ctx = engine.Context(m, n_batch=max(n, 64))
+    try:
+        got = ctx.classify(x)
+        assert np.array_equal(bits(got), bits(want))
+    finally:
+        ctx.free()
+        m.free()
+
+
+def test_classify_hidden_overflow_rejected(b200_device, ref_engine_mod, tmp_path):
+    """post_scale ~1e30: the first layer's outputs overflow to infinity, so
+    the second layer's input is rejected as the accelerator rejects a
+    non-finite row, by the fused kernel and by the per-layer path alike (and
+    the reference fails the call too)."""
+    path = gguf.bnn_mlp_model(tmp_path / "big.gguf", seed=5, post_scale_mul=1e30)
+    rng = np.random.default_rng(8)
+    x = np.zeros((300, 896), dtype=np.float32)
+    x[:, :784] = rng.standard_normal((300, 784))
+    ref = ref_engine_mod.RefEngine(path, n_batch=8)
+    with pytest.raises(RuntimeError):
+        ref.classify(x[:8])
+    ref.close()
+    m = engine.Model(b200_device, path)
+    ctx = engine.Context(m, n_batch=300)
+    try:
+        for n in (8, 300):
+            with pytest.raises(engine.EngineError) as e:
+                ctx.classify(x[:n])
+            assert e.value.status == engine.ERANGE, n
+        # the context stays usable
+        ok = gguf.bnn_mlp_model(tmp_path / "ok.gguf", seed=5)
+        m2 = engine.Model(b200_device, ok)
+        ctx2 = engine.Context(m2, n_batch=8)
+        try:
+            assert np.isfinite(ctx2.classify(x[:8])).all()
+        finally:
+            ctx2.free()
+            m2.free()
+    finally:
+        ctx.free()
+        m.free()
