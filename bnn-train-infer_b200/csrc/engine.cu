@@ -238,6 +238,7 @@ struct bnnd_model {
     std::vector<std::unique_ptr<MlpLayer>> mlp;
     uint32_t mlp_max_dim = 0;
     uint32_t mlp_max_in = 0;  // widest layer input
+    uint32_t mlp_max_wbytes = 0;  // largest layer's packed weights
     DevMem mlp_desc;          // bnn::eng::MlpLayerDev per layer, for mlp_fused_kernel
 };
 
@@ -654,6 +655,7 @@ BNND_Status load_mlp(const bnn::GgufFile& g, bnnd_model* m) {
         d.relu = layer->relu;
         desc.push_back(d);
         m->mlp_max_in = std::max(m->mlp_max_in, layer->w.in);
+        m->mlp_max_wbytes = std::max(m->mlp_max_wbytes, bnn::eng::mlp_layer_wbytes(layer->w.in, layer->w.out));
     }
     BNND_Status st = dev_alloc(m->mlp_desc, desc.size() * sizeof(desc[0]));
     if (st != BNND_OK)
@@ -1352,7 +1354,7 @@ BNND_Status create_mlp_context(bnnd_context* c) {
             return fail(BNND_ENOTSUP, "layer width too large for the contraction kernel");
     }
     // calls of up to kMlpFusedMaxSamples samples: one fused launch, pinned staging
-    const size_t fused = bnn::eng::mlp_fused_smem(m->mlp_max_in);
+    const size_t fused = bnn::eng::mlp_fused_smem(m->mlp_max_in, m->mlp_max_wbytes);
     if (fused <= 200u * 1024u) {
         const size_t rows = std::min<size_t>(R, bnn::eng::kMlpFusedMaxSamples);
         CUDA_OR(cudaFuncSetAttribute(bnn::eng::mlp_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -2175,6 +2177,7 @@ BNND_Status BNND_Classify(BNND_Context c, const float* input, uint32_t n_samples
         fa.layers = m->mlp_desc.as<bnn::eng::MlpLayerDev>();
         fa.n_layers = (uint32_t)m->mlp.size();
         fa.max_in = m->mlp_max_in;
+        fa.max_wbytes = m->mlp_max_wbytes;
         fa.x = cur;
         fa.logits = nxt;
         fa.status = c->status.as<int>();
