@@ -244,10 +244,10 @@ __global__ void kv_append_kernel(KvAppendArgs a) {
 // serially over the positions 0 .. pos. So outputs are bit-identical to one
 // decode step per position.
 constexpr uint32_t kPfQT = 16;        // query positions per CTA
-constexpr uint32_t kPfKT = 32;        // K/V positions per shared-memory tile
-constexpr uint32_t kPfThreads = 512;  // (query, key) and (query, 4 dims) per thread
+constexpr uint32_t kPfKT = 64;        // K/V positions per shared-memory tile
+constexpr uint32_t kPfThreads = 512;  // (query pair, key) and (query, 4 dims) per thread
 constexpr uint32_t kPfSmemBudget = 200u * 1024u;
-static_assert(kPfThreads == kPfQT * kPfKT && kPfThreads == kPfQT * 32, "thread maps of the score and V phases");
+static_assert(kPfThreads == kPfQT / 2 * kPfKT && kPfThreads == kPfQT * 32, "thread maps of the score and V phases");
 
 struct PfAttnArgs {
     const float* qkv;       // [rows][c + 2kv]
@@ -376,9 +376,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttn
     };
     auto kvb = [&](uint32_t b) { return kv_s + (b ? (size_t)kPfKT * kStride : (size_t)0); };
 
-    // ---- scores: thread (query sq, key kp of the tile), all KVM heads
-    const uint32_t sq = tid / kPfKT, kp = tid % kPfKT;
-    const uint32_t sq_n = pos0 + sq + 1;  // keys of query sq
+    // ---- scores: thread (queries 2sp and 2sp + 1, key kp of the tile), all
+    // KVM heads: each K row read from shared memory serves both queries
+    const uint32_t sp = tid / kPfKT, kp = tid % kPfKT;
+    const uint32_t sq0 = 2 * sp, sq1 = sq0 + 1;
+    const uint32_t n0 = pos0 + sq0 + 1, n1 = n0 + 1;  // keys of each query
     int bad = 0;
     tile_load(kc, kcache_row(HD), 0);
     tile_store(kvb(0), 0);
@@ -388,29 +390,42 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(PfAttn
         if (more)
             tile_load(kc, kcache_row(HD), t0 + kPfKT);
         const uint32_t ta = t0 + kp;
-        if (sq < nq && ta < sq_n) {
+        const bool v0 = sq0 < nq && ta < n0, v1 = sq1 < nq && ta < n1;
+        if (v0 || v1) {
             const float4* ka = reinterpret_cast<const float4*>(kvb(buf) + (size_t)kp * kStride);
-            float da[KVM];
+            float d0[KVM], d1[KVM];
 #pragma unroll
             for (int h = 0; h < KVM; ++h)
-                da[h] = 0.0f;
+                d0[h] = d1[h] = 0.0f;
 #pragma unroll 4
             for (uint32_t i = 0; i < HD / 4; ++i) {
                 const float4 x = ka[i];
 #pragma unroll
                 for (int h = 0; h < KVM; ++h) {
-                    const float4 q = reinterpret_cast<const float4*>(q_s + (size_t)(sq * KVM + h) * HD)[i];
-                    da[h] = __fadd_rn(da[h], __fmul_rn(q.x, x.x));
-                    da[h] = __fadd_rn(da[h], __fmul_rn(q.y, x.y));
-                    da[h] = __fadd_rn(da[h], __fmul_rn(q.z, x.z));
-                    da[h] = __fadd_rn(da[h], __fmul_rn(q.w, x.w));
+                    const float4 q0 = reinterpret_cast<const float4*>(q_s + (size_t)(sq0 * KVM + h) * HD)[i];
+                    const float4 q1 = reinterpret_cast<const float4*>(q_s + (size_t)(sq1 * KVM + h) * HD)[i];
+                    d0[h] = __fadd_rn(d0[h], __fmul_rn(q0.x, x.x));
+                    d1[h] = __fadd_rn(d1[h], __fmul_rn(q1.x, x.x));
+                    d0[h] = __fadd_rn(d0[h], __fmul_rn(q0.y, x.y));
+                    d1[h] = __fadd_rn(d1[h], __fmul_rn(q1.y, x.y));
+                    d0[h] = __fadd_rn(d0[h], __fmul_rn(q0.z, x.z));
+                    d1[h] = __fadd_rn(d1[h], __fmul_rn(q1.z, x.z));
+                    d0[h] = __fadd_rn(d0[h], __fmul_rn(q0.w, x.w));
+                    d1[h] = __fadd_rn(d1[h], __fmul_rn(q1.w, x.w));
                 }
             }
 #pragma unroll
             for (int h = 0; h < KVM; ++h) {
-                const float sa = __fmul_rn(da[h], a.scale);
-                bad |= !isfinite(sa);
-                sc_row(sq, h)[ta] = sa;
+                if (v0) {
+                    const float sa = __fmul_rn(d0[h], a.scale);
+                    bad |= !isfinite(sa);
+                    sc_row(sq0, h)[ta] = sa;
+                }
+                if (v1) {
+                    const float sa = __fmul_rn(d1[h], a.scale);
+                    bad |= !isfinite(sa);
+                    sc_row(sq1, h)[ta] = sa;
+                }
             }
         }
         if (more)
