@@ -33,7 +33,7 @@
 namespace bnn {
 namespace eng {
 
-constexpr uint32_t kRowsPrepThreads = kSumThreads;  // the decode prologue's RMSNorm sum threads
+constexpr uint32_t kRowsPrepThreads = kWideThreads;  // the wide exact sum's threads
 
 struct RowsPrepArgs {
     const float* x;      // [m][k] F32 rows, x_stride floats apart
@@ -51,7 +51,7 @@ struct RowsPrepArgs {
 };
 
 inline size_t rows_prep_smem(uint32_t k, bool exact) {
-    return (size_t)k * 5u + (exact ? kSumSmemBytes : 0);  // row, its int8 codes, the sum's scratch
+    return (size_t)k * 5u + (exact ? kWideSmemBytes : 0);  // row, its int8 codes, the sum's scratch
 }
 
 // One CTA of kRowsPrepThreads per row. A non-finite input without RMSNorm is
@@ -59,7 +59,7 @@ inline size_t rows_prep_smem(uint32_t k, bool exact) {
 // non-finite divisor (kStatusNonFinite), as in the decode step.
 __global__ void __launch_bounds__(kRowsPrepThreads) rows_prep_kernel(RowsPrepArgs a) {
     extern __shared__ __align__(16) unsigned char rp_smem[];
-    __shared__ float red[16];
+    __shared__ float red[32];  // [1..8] fast-mode warp sums, [16..31] warp maxima
     __shared__ int s_flag;
     float* xb = reinterpret_cast<float*>(rp_smem);
     float4* xb4 = reinterpret_cast<float4*>(rp_smem);
@@ -95,18 +95,21 @@ __global__ void __launch_bounds__(kRowsPrepThreads) rows_prep_kernel(RowsPrepArg
     if (a.gain) {
         float sum;
         if (a.exact) {
-            sum = exact_sumsq(xb, (int)K, sum_mem, 1);
+            sum = exact_sumsq_wide(xb, (int)K, sum_mem, 1);
         } else {
-            float t = 0.0f;
-            for (uint32_t i = tid; i < K; i += nt)
-                t = __fadd_rn(t, __fmul_rn(xb[i], xb[i]));
-            for (int o = 16; o > 0; o >>= 1)
-                t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
-            if (lane == 0)
-                red[1 + warp] = t;
+            // the decode prologue's tree: kSumThreads lane-strided sums
+            if (tid < kSumThreads) {
+                float t = 0.0f;
+                for (uint32_t i = tid; i < K; i += kSumThreads)
+                    t = __fadd_rn(t, __fmul_rn(xb[i], xb[i]));
+                for (int o = 16; o > 0; o >>= 1)
+                    t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
+                if (lane == 0)
+                    red[1 + warp] = t;
+            }
             __syncthreads();
             sum = 0.0f;
-            for (uint32_t w = 0; w < nw; ++w)
+            for (uint32_t w = 0; w < (uint32_t)kSumWarpsN; ++w)
                 sum = __fadd_rn(sum, red[1 + w]);
         }
         const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)K), a.eps));
@@ -116,14 +119,15 @@ __global__ void __launch_bounds__(kRowsPrepThreads) rows_prep_kernel(RowsPrepArg
             return;  // uniform: every thread computed the same rms
         }
         amax = 0.0f;
+        const float rr = __frcp_rn(rms);  // div_cr: x / rms correctly rounded, as __fdiv_rn
         const float4* gr = reinterpret_cast<const float4*>(a.gain);
         for (uint32_t i = tid; i < K / 4; i += nt) {
             float4 v = xb4[i];
             const float4 gn = gr[i];
-            v.x = __fmul_rn(__fdiv_rn(v.x, rms), gn.x);
-            v.y = __fmul_rn(__fdiv_rn(v.y, rms), gn.y);
-            v.z = __fmul_rn(__fdiv_rn(v.z, rms), gn.z);
-            v.w = __fmul_rn(__fdiv_rn(v.w, rms), gn.w);
+            v.x = __fmul_rn(div_cr(v.x, rms, rr), gn.x);
+            v.y = __fmul_rn(div_cr(v.y, rms, rr), gn.y);
+            v.z = __fmul_rn(div_cr(v.z, rms, rr), gn.z);
+            v.w = __fmul_rn(div_cr(v.w, rms, rr), gn.w);
             amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
             xb4[i] = v;
         }
@@ -131,11 +135,11 @@ __global__ void __launch_bounds__(kRowsPrepThreads) rows_prep_kernel(RowsPrepArg
     for (int o = 16; o > 0; o >>= 1)
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     if (lane == 0)
-        red[8 + warp] = amax;
+        red[16 + warp] = amax;
     __syncthreads();
-    amax = red[8];
+    amax = red[16];
     for (uint32_t w = 1; w < nw; ++w)
-        amax = fmaxf(amax, red[8 + w]);
+        amax = fmaxf(amax, red[16 + w]);
     const float s = row_scale_from_absmax(amax);
     const RowQuantizer quant(s);
     if (!a.a_sw) {
