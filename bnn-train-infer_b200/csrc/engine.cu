@@ -2171,19 +2171,20 @@ BNND_Status BNND_Classify(BNND_Context c, const float* input, uint32_t n_samples
     if (n_samples <= bnn::eng::kMlpFusedMaxSamples && c->mlp_fused_smem) {
         // every layer of a sample in one CTA (mlp_fused.cuh): one launch per
         // call, the input check on the device, copies through pinned staging
+        // the kernel reads the samples from, and writes the logits to, the
+        // pinned staging buffers directly (device-addressable host memory):
+        // no copy operations on the stream
         std::memcpy(c->h_mlp_in, input, inputs * 4);
-        CUDA_OR(cudaMemcpyAsync(cur, c->h_mlp_in, inputs * 4, cudaMemcpyHostToDevice, s), BNND_EIO);
         bnn::eng::MlpFusedArgs fa = {};
         fa.layers = m->mlp_desc.as<bnn::eng::MlpLayerDev>();
         fa.n_layers = (uint32_t)m->mlp.size();
         fa.max_in = m->mlp_max_in;
         fa.max_wbytes = m->mlp_max_wbytes;
-        fa.x = cur;
-        fa.logits = nxt;
+        fa.x = c->h_mlp_in;
+        fa.logits = c->h_mlp_out;
         fa.status = c->status.as<int>();
         bnn::eng::mlp_fused_kernel<<<n_samples, bnn::eng::kMlpThreads, c->mlp_fused_smem, s>>>(fa);
         CUDA_OR(cudaGetLastError(), BNND_EIO);
-        CUDA_OR(cudaMemcpyAsync(c->h_mlp_out, nxt, outputs * 4, cudaMemcpyDeviceToHost, s), BNND_EIO);
         const BNND_Status st = finish(c, "BNND_Classify");
         if (st == BNND_OK)
             std::memcpy(logits, c->h_mlp_out, outputs * 4);
