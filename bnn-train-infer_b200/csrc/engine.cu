@@ -1672,13 +1672,17 @@ BNND_Status decode(bnnd_context* c, const int32_t* tokens, uint32_t n, float* lo
             set_pos(c, start);
             return pst;
         }
+    } else if (n == 1) {
+        // one token per row: straight into the step's input slot
+        CUDA_OR(cudaMemcpyAsync(c->tok_in.p, seq, count * 4, cudaMemcpyHostToDevice, c->stream), BNND_EIO);
     } else {
         CUDA_OR(cudaMemcpyAsync(c->tok_seq.p, seq, count * 4, cudaMemcpyHostToDevice, c->stream), BNND_EIO);
     }
     for (uint32_t i = 0; i < (batched ? 0u : n); ++i) {
-        CUDA_OR(cudaMemcpyAsync(c->tok_in.p, c->tok_seq.as<int32_t>() + (size_t)i * c->rows, c->rows * 4,
-                                cudaMemcpyDeviceToDevice, c->stream),
-                BNND_EIO);
+        if (n > 1)
+            CUDA_OR(cudaMemcpyAsync(c->tok_in.p, c->tok_seq.as<int32_t>() + (size_t)i * c->rows, c->rows * 4,
+                                    cudaMemcpyDeviceToDevice, c->stream),
+                    BNND_EIO);
         const bool last = i + 1 == n;
         CUDA_OR(run_step(c, start + i, (last && want) || all), BNND_EIO);
         if (all)
