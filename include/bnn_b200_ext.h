@@ -30,7 +30,12 @@ BNN_Status bnn_b200_execute_async(BNN_Device device, const BNN_Job* job);
  * job rejected its input, BNN_EIO on a CUDA failure, else BNN_OK. */
 BNN_Status bnn_b200_sync(BNN_Device device);
 
-/* The cudaStream_t every call of this handle runs on (for CUDA events). */
+/* The cudaStream_t every call of this handle runs on (for CUDA events). A
+ * one-row job whose input no job of this handle still in flight writes may
+ * read that input as soon as the previous kernel on the stream lets it start
+ * (programmatic dependent launch): a kernel of the caller's own on this
+ * stream that calls griddepcontrol.launch_dependents before it has finished
+ * writing a job's input must not come right before that job. */
 void* bnn_b200_device_stream(BNN_Device device);
 
 /* CUDA ordinal behind the handle. */
