@@ -103,6 +103,9 @@ def test_gemm_f32_rows(b200_device, oracle_mod, m):
     assert bits_equal(got.view(np.uint32), want.view(np.uint32))
     z = accel.run_op(b200_device, accel.OP_GEMM, bits, scales, q)
     assert bits_equal(z.view(np.uint32), oracle_mod.gemm_i8(bits, scales, q).view(np.uint32))
+    # up to 8 rows the int8 ops run as one kernel that slices the rows itself
+    d = accel.run_op(b200_device, accel.OP_DOT_GROUPS, bits, scales, q)
+    assert np.array_equal(d, oracle_mod.dot_groups(bits, scales, q))
 
 
 @pytest.mark.parametrize("op", [accel.OP_GEMM_F32, accel.OP_GEMM, accel.OP_DOT_GROUPS])
