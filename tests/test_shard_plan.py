@@ -1,5 +1,5 @@
 """Host side of tensor parallelism: BNND_ShardPlan's row ranges, computed by
-two gloo ranks on CPU, partition every matrix exactly (whole GQA groups for
+2, 4 and 8 gloo ranks on CPU, partition every matrix exactly (whole GQA groups for
 q|k|v, matching gate/up ranges, 8-row lm_head stride), and shapes that do not
 split are refused. No GPU is needed."""
 import datetime
@@ -23,12 +23,19 @@ def _info(engine, heads=16, kv_heads=8, hd=128, hidden=2048, ffn=6144, vocab=151
     return info
 
 
+SHAPES = (dict(), dict(vocab=3000, hidden=1024, heads=8, kv_heads=4, ffn=2048))
+
+
+def _splits(shape, world):
+    return shape.get("kv_heads", 8) % world == 0 and shape.get("heads", 16) % world == 0
+
+
 def _rank(rank, world, port, out):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     from bnn_b200 import _lib, engine
     api = engine.EngineApi(_lib.load())
-    for shape in (dict(), dict(vocab=3000, hidden=1024, heads=8, kv_heads=4, ffn=2048)):
+    for shape in (s for s in SHAPES if _splits(s, world)):
         info = _info(engine, **shape)
         p = engine.shard_plan(api, info, world, rank)
         mine = {f: getattr(p, f) for f, _ in engine.ShardInfo._fields_}
@@ -40,15 +47,16 @@ def _rank(rank, world, port, out):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_plans_partition_every_matrix(world):
     from bnn_b200 import engine
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, 29641, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, 29641 + world, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = [q.get(timeout=120) for _ in range(2)]
+    results = [q.get(timeout=120) for s in SHAPES if _splits(s, world)]
+    assert results
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
