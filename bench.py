@@ -402,8 +402,8 @@ def run_b200(args):
     timed_pos = [n_prompt + i % gen_steps for i in range(args.steps)]
     if batch == 1 and not tp and step_positions > max(timed_pos):
         # ---- the whole step is ONE kernel (decode_step_kernel): its time is the
-        # event-timed step; algorithmic bytes per token as SURVEY d(3) counts
-        # them: weights + K/V history read + K/V append + norm gains + embed row
+        # event-timed step; algorithmic bytes per token: Q1_0 weights (0.140625
+        # bytes each) + K/V history read + K/V append + norm gains + embed row
         peak, peak_kind = measured_peaks()
         kv_row = info.n_layers * info.kv_heads * info.head_dim * 4 * 2
         gains = (2 * info.n_layers + 1) * info.hidden * 4 + 2 * info.n_layers * info.head_dim * 4
