@@ -544,8 +544,11 @@ __device__ __forceinline__ void attention_role(const StepArgs& a, unsigned char*
             live = false;
         }
         stamp(a, l, 2);
-        // scores: one position per thread, each dot serial over the head dimension
+        // scores: one position per thread, each dot serial over the head
+        // dimension; their maximum is reduced on the way (per warp here, across
+        // the warps after the barrier)
         int bad = 0;
+        float mx = -INFINITY;
         if (live) {
             for (uint32_t t = tid; t < n; t += kCThreads) {
                 const float4* k4 = reinterpret_cast<const float4*>(t < pos ? kres + (size_t)t * kstride : k_s);
@@ -562,9 +565,14 @@ __device__ __forceinline__ void attention_role(const StepArgs& a, unsigned char*
                 const float score = __fmul_rn(dot, a.scale);
                 bad |= !isfinite(score);
                 sc[t] = score;
+                mx = fmaxf(mx, score);
             }
         }
         bad = __reduce_or_sync(0xffffffffu, bad);
+        for (int o = 16; o > 0; o >>= 1)
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0)
+            red[32 + warp] = mx;  // read after the barrier; rewritten only in the next layer
         if (bad && lane == 0) {
             *flag = 1;
             atomicOr(a.status, kStatusNonFinite);  // "attention score is not finite"
@@ -572,29 +580,29 @@ __device__ __forceinline__ void attention_role(const StepArgs& a, unsigned char*
         named_barrier(kBarCompute, kCThreads);
         live = live && *reinterpret_cast<volatile int*>(flag) == 0;
         stamp(a, l, 3);
-        // softmax: max, expf(s - max), serial sum, division
-        float mx = -INFINITY;
-        if (live)
-            for (uint32_t t = tid; t < n; t += kCThreads)
-                mx = fmaxf(mx, sc[t]);
-        mx = compute_max(mx, red);
+        // softmax: max (the scores are finite here), expf(s - max), serial sum, division
+        mx = red[32];
+        for (uint32_t w = 1; w < kWarps; ++w)
+            mx = fmaxf(mx, red[32 + w]);
         if (live)
             for (uint32_t t = tid; t < n; t += kCThreads)
                 sc[t] = expf_cr(__fsub_rn(sc[t], mx));
         named_barrier(kBarCompute, kCThreads);
         if (live && tid == 0) {
-            // serial in index order; the next four terms load while the current four are added
+            // serial in index order; terms load two float4s ahead of their adds
             const float4* e4 = reinterpret_cast<const float4*>(sc);
             const uint32_t n4 = n / 4;
             float sum = 0.0f;
-            float4 cur = n4 ? e4[0] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            float4 cur = n4 > 0 ? e4[0] : zero, nxt = n4 > 1 ? e4[1] : zero;
             for (uint32_t b = 0; b < n4; ++b) {
-                const float4 nx = b + 1 < n4 ? e4[b + 1] : cur;
+                const float4 ahead = b + 2 < n4 ? e4[b + 2] : nxt;
                 sum = __fadd_rn(sum, cur.x);
                 sum = __fadd_rn(sum, cur.y);
                 sum = __fadd_rn(sum, cur.z);
                 sum = __fadd_rn(sum, cur.w);
-                cur = nx;
+                cur = nxt;
+                nxt = ahead;
             }
             for (uint32_t t = n4 * 4; t < n; ++t)
                 sum = __fadd_rn(sum, sc[t]);

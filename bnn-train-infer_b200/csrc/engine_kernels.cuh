@@ -446,18 +446,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
             float sum = 0.0f;
             if (a.exact) {
                 if (lane == 0) {
-                    // serial in index order; the next four terms load while
-                    // the current four are added (rows are float4-aligned)
+                    // serial in index order; terms load two float4s ahead of
+                    // their adds (rows are float4-aligned)
                     const float4* e4 = reinterpret_cast<const float4*>(e);
                     const uint32_t n4 = n / 4;
-                    float4 cur = n4 ? e4[0] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    float4 cur = n4 > 0 ? e4[0] : zero, nxt = n4 > 1 ? e4[1] : zero;
                     for (uint32_t b = 0; b < n4; ++b) {
-                        const float4 nx = b + 1 < n4 ? e4[b + 1] : cur;
+                        const float4 ahead = b + 2 < n4 ? e4[b + 2] : nxt;
                         sum = __fadd_rn(sum, cur.x);
                         sum = __fadd_rn(sum, cur.y);
                         sum = __fadd_rn(sum, cur.z);
                         sum = __fadd_rn(sum, cur.w);
-                        cur = nx;
+                        cur = nxt;
+                        nxt = ahead;
                     }
                     for (uint32_t t = n4 * 4; t < n; ++t)
                         sum = __fadd_rn(sum, e[t]);
